@@ -1,0 +1,404 @@
+// Forward kernel of the block-sparse masked flash attention (sm_100a, tcgen05 + TMA).
+//
+// Replaces the Pallas-Triton `_kernel` (src/faster_weathernext/pallas_attn.py:112-141). Same math:
+// per query row, an online softmax over the allowed keys of the row's query block's active 32-key
+// tiles; masked logits contribute exactly 0 (the reference sets them to -1e30 so exp underflows to
+// 0, pallas_attn.py:123-125); O = acc / l; LSE = m + log(l).
+//
+// Work item = (batch, head, 128-query block of the paired tile list). Persistent CTAs walk items
+// blockIdx.x, +gridDim.x, ... Roles (192 threads):
+//   warp 0      TMA producer: Q tile once per item; per chunk of up to two 32-key tiles, the K and V
+//               tiles (4D tensor maps over [B, n, H, D], 128-byte swizzle) and the tiles' mask words.
+//   warp 1      TMEM allocation; one thread issues the tcgen05 MMAs:
+//                 S[buf] = Q K^T  (M=128, N=32|64, K=D)        -> TMEM, fp32
+//                 O     += P V    (M=128, N=D,     K=32|64)     -> TMEM, fp32 (P from shared memory)
+//               S of chunk c+1 is issued before P V of chunk c, so the tensor core overlaps softmax.
+//   warps 2-5   softmax: thread = query row = TMEM lane. Reads S with tcgen05.ld, applies the row's
+//               mask word, keeps a running max m (log2 domain) and sum l, writes P (bf16 / fp32) to
+//               shared memory for the P V MMA. O is rescaled in TMEM only when the row max grows by
+//               more than 2^8 (the final O / l is exact either way). Exponentials are issued only for
+//               columns that some row of the warp may attend to.
+//               Epilogue: O / l -> global, LSE -> global.
+// Every mbarrier wait is bounded (common.cuh); on expiry the CTA drains and returns with the device
+// error word set.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace fwn {
+
+struct FwdParams {
+  const int32_t* ptr2;    // [NP + 1] paired (128-row) list
+  const int32_t* kb2;     // [T2]
+  const uint32_t* bits2;  // [T2 * 128]
+  void* o;                // [B, n, H, D]
+  float* lse;             // [B, H, lse_rows] or null
+  int64_t o_sb, o_sn, o_sh;
+  int batch, heads, n, np, lse_rows, n_items;
+  float scale_log2;       // scale * log2(e)
+};
+
+template <int D, bool F32>
+struct FwdCfg {
+  static constexpr int ES = F32 ? 4 : 2;
+  static constexpr int EPB = 128 / ES;        // elements per 128-byte column block
+  static constexpr int CB = D / EPB;          // column blocks of a head_dim row
+  static constexpr int ROWS = 128;            // query rows per item
+  static constexpr int SUB = 32;              // keys per tile
+  static constexpr int KEYS = 64;             // keys per chunk (two tiles)
+  static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
+  static constexpr int NS = 3;                // K/V pipeline stages
+  static constexpr int Q_BYTES = CB * ROWS * 128;
+  static constexpr int KV_BYTES = CB * KEYS * 128;
+  static constexpr int BITS_BYTES = 2 * 128 * 4;
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES + BITS_BYTES;
+  static constexpr int PCB = KEYS * ES / 128;  // column blocks of a P row
+  static constexpr int P_BYTES = PCB * ROWS * 128;
+  static constexpr int OFF_STAGE = Q_BYTES;
+  static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment
+  static constexpr int TMEM_COLS = 256;
+  static constexpr int O_COL = 128;
+  static constexpr int THREADS = 192;
+  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
+  static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
+  static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
+};
+
+template <int D, bool F32>
+__global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using C = FwdCfg<D, F32>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t q_smem = sbase;
+  auto stage_k = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES; };
+  auto stage_v = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + C::KV_BYTES; };
+  auto stage_bits = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + 2 * C::KV_BYTES; };
+  auto p_smem = [&](int b) { return sbase + C::OFF_P + b * C::P_BYTES; };
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  const uint32_t q_full = bar0, q_empty = bar0 + 8;
+  auto kv_full = [&](int s) { return bar0 + 16 + 8 * s; };
+  auto kv_empty = [&](int s) { return bar0 + 16 + 8 * (C::NS + s); };
+  const uint32_t bar1 = bar0 + 16 + 16 * C::NS;
+  auto s_full = [&](int b) { return bar1 + 8 * b; };
+  auto s_empty = [&](int b) { return bar1 + 16 + 8 * b; };
+  auto p_full = [&](int b) { return bar1 + 32 + 8 * b; };
+  auto p_empty = [&](int b) { return bar1 + 48 + 8 * b; };
+  const uint32_t o_full = bar1 + 64, o_empty = bar1 + 72, drain = bar1 + 80;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(s_empty(b), 4);
+      mbar_init(p_full(b), 4);
+      mbar_init(p_empty(b), 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const int per_bh = p.np;
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      int pending_q = 0;
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + 1) >> 1;
+        if (nch == 0) continue;
+        if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+        for (int cb = 0; cb < C::CB; ++cb)
+          tma_load_4d(q_smem + cb * C::ROWS * 128, &tm_q, cb * C::EPB, h, pb * C::ROWS, b, q_full);
+        pending_q = 1;
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int st = g % C::NS;
+          if (!(ok = mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
+          const int n_in = min(2, n_sub - 2 * c);
+          mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
+          for (int s = 0; s < n_in; ++s) {
+            const int t = t0 + 2 * c + s;
+            const int key0 = p.kb2[t] * C::SUB;
+            for (int cb = 0; cb < C::CB; ++cb) {
+              tma_load_4d(stage_k(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_k, cb * C::EPB, h, key0, b,
+                          kv_full(st));
+              tma_load_4d(stage_v(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_v, cb * C::EPB, h, key0, b,
+                          kv_full(st));
+            }
+            bulk_load(stage_bits(st) + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, kv_full(st));
+          }
+        }
+        ++qc;
+      }
+      if (!ok) {
+        // Drain: wait (bounded, ignoring the abort flag) for every copy this thread issued.
+        volatile int never = 0;
+        for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
+          mbar_wait(kv_full(k % C::NS), (k / C::NS) & 1, &never);
+        if (pending_q) mbar_wait(q_full, (qc & 1), &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescPV = instr_desc(F32, 128, D, false, true);
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      auto issue_pv = [&](uint32_t gg, bool first) -> bool {
+        const int pbuf = gg & 1, st = gg % C::NS;
+        if (!mbar_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag)) return false;
+        if (first && !mbar_wait(o_empty, (qc & 1) ^ 1, abort_flag)) return false;
+        tc_fence_after();
+        return true;
+        (void)st;
+      };
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + 1) >> 1;
+        if (nch == 0) continue;
+        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+        const uint32_t g0 = g;
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {
+            const uint32_t gg = g0 + c;
+            const int st = gg % C::NS, sb = gg & 1;
+            const int n_in = min(2, n_sub - 2 * c);
+            if (!(ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
+            if (!(ok = mbar_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
+            const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
+#pragma unroll
+            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              const uint64_t a = smem_desc(q_smem + cb * C::ROWS * 128 + within, 16, 1024);
+              const uint64_t bdesc = smem_desc(stage_k(st) + cb * C::KEYS * 128 + within, 16, 1024);
+              mma_ss<F32>(tmem + sb * 64, a, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(s_full(sb));
+            if (c == nch - 1) mma_commit(q_empty);
+          }
+          if (c >= 1) {
+            const uint32_t gg = g0 + c - 1;
+            const int st = gg % C::NS, pbuf = gg & 1;
+            const int n_in = min(2, n_sub - 2 * (c - 1));
+            if (!(ok = issue_pv(gg, c == 1))) break;
+            const int ksteps = n_in * C::SUB / C::KSTEP;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              const uint64_t a = smem_desc(p_smem(pbuf) + cb * C::ROWS * 128 + within, 16, 1024);
+              const uint64_t bdesc = smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
+              mma_ss<F32>(tmem + C::O_COL, a, bdesc, kIdescPV, (c == 1 && kk == 0) ? 0u : 1u);
+            }
+            mma_commit(p_empty(pbuf));
+            mma_commit(kv_empty(st));
+            if (c == nch) mma_commit(o_full);
+          }
+        }
+        g = g0 + nch;
+        ++qc;
+      }
+      // Drain the tensor pipe before TMEM is released.
+      mma_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + 1) >> 1;
+      const int qrow = pb * C::ROWS + row;
+      float m_ref = -INFINITY, l = 0.f;
+      const uint32_t g0 = g;
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t gg = g0 + c;
+        const int sb = gg & 1, st = gg % C::NS;
+        const int n_in = min(2, n_sub - 2 * c);
+        float s[64];
+        if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
+        tc_fence_after();
+        tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
+        if (n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty(sb));
+        if (!(ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
+        const uint32_t w0 = ld_shared_u32(stage_bits(st) + row * 4);
+        const uint32_t w1 = n_in == 2 ? ld_shared_u32(stage_bits(st) + 512 + row * 4) : 0u;
+        const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
+        const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = ((w0 >> j) & 1u) ? fmaxf(mx, s[j]) : mx;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = ((w1 >> j) & 1u) ? fmaxf(mx, s[32 + j]) : mx;
+        const float m_new = mx * p.scale_log2;
+        const float m_old = m_ref;
+        const bool grow = m_new > m_ref + 8.0f;
+        float corr = 1.f;
+        if (grow) {
+          corr = ex2(m_old - m_new);
+          m_ref = m_new;
+          l *= corr;
+        }
+        const float neg_m = -m_ref;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float e = 0.f;
+          if ((any0 >> j) & 1u) {
+            const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
+            e = ((w0 >> j) & 1u) ? t : 0.f;
+          }
+          s[j] = e;
+          l += e;
+        }
+        if (n_in == 2) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float e = 0.f;
+            if ((any1 >> j) & 1u) {
+              const float t = ex2(fmaf(s[32 + j], p.scale_log2, neg_m));
+              e = ((w1 >> j) & 1u) ? t : 0.f;
+            }
+            s[32 + j] = e;
+            l += e;
+          }
+        }
+        // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
+        if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+        const uint32_t pbase = p_smem(sb);
+        if constexpr (!F32) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            if (cc < 4 * n_in)
+              st_shared_v4(pbase + sw128_offset(row, cc), pack_bf16(s[8 * cc], s[8 * cc + 1]),
+                           pack_bf16(s[8 * cc + 2], s[8 * cc + 3]), pack_bf16(s[8 * cc + 4], s[8 * cc + 5]),
+                           pack_bf16(s[8 * cc + 6], s[8 * cc + 7]));
+          }
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) {
+            if (cc < 8 * n_in) {
+              const int blk = cc >> 3, ch = cc & 7;
+              st_shared_v4(pbase + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(s[4 * cc]),
+                           __float_as_uint(s[4 * cc + 1]), __float_as_uint(s[4 * cc + 2]),
+                           __float_as_uint(s[4 * cc + 3]));
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        // Rescale O rows whose reference max grew (rows that saw no allowed key yet hold O = 0).
+        const bool rescale = grow && m_old != -INFINITY;
+        if (__any_sync(0xffffffffu, rescale)) {
+          const uint32_t prev = gg - 1;
+          if (!(ok = mbar_wait(p_empty(prev & 1), (prev >> 1) & 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) {
+            float o[32];
+            tmem_ld32(trow + C::O_COL + 32 * j, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(trow + C::O_COL + 32 * j, o);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(sb));
+      }
+      if (!ok) break;
+      g = g0 + nch;
+      // ---------------------------------------------------------------- epilogue
+      const bool has = l > 0.f;
+      const float inv = has ? 1.f / l : 0.f;
+      if (p.lse != nullptr) {
+        const float lse = has ? (m_ref + lg2(l)) * 0.69314718055994530942f : -INFINITY;
+        p.lse[static_cast<size_t>(bh) * p.lse_rows + qrow] = lse;
+      }
+      const bool store = qrow < p.n;
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
+                      (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(qrow) * p.o_sn +
+                       static_cast<int64_t>(h) * p.o_sh) * C::ES;
+      if (nch == 0) {
+        if (store) {
+          for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(orow)[i] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      if (!(ok = mbar_wait(o_full, qc & 1, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int j = 0; j < D / 32; ++j) {
+        float o[32];
+        tmem_ld32(trow + C::O_COL + 32 * j, o);
+        tmem_wait_ld();
+        if (store) {
+          if constexpr (!F32) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<uint4*>(orow + j * 64)[i] =
+                  make_uint4(pack_bf16(o[8 * i] * inv, o[8 * i + 1] * inv), pack_bf16(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
+                             pack_bf16(o[8 * i + 4] * inv, o[8 * i + 5] * inv), pack_bf16(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              reinterpret_cast<float4*>(orow + j * 128)[i] =
+                  make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_empty);
+      ++qc;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+}  // namespace fwn

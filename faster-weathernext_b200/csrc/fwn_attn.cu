@@ -1,0 +1,310 @@
+// C ABI of libfwn_attn.so (include/fwn_attn.h): argument checks, TMA descriptors, kernel launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/fwn_attn.h"
+#include "common.cuh"
+
+#include "attn_bwd.cuh"
+#include "attn_fwd.cuh"
+#include "tiles.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+fwn_status fail(fwn_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+fwn_status ok() {
+  g_last_error.clear();
+  return FWN_OK;
+}
+
+fwn_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(FWN_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4D map over a [B, n, H, D] tensor (D contiguous): box = 128 bytes of D x 1 head x `rows` nodes x 1.
+fwn_status make_map(CUtensorMap* map, const void* base, const fwn_attn_desc& d, int rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FWN_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  const int es = d.dtype == FWN_DTYPE_BF16 ? 2 : 4;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d.head_dim), static_cast<cuuint64_t>(d.heads),
+                        static_cast<cuuint64_t>(d.n), static_cast<cuuint64_t>(d.batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d.stride_h) * es, static_cast<cuuint64_t>(d.stride_n) * es,
+                           static_cast<cuuint64_t>(d.stride_b) * es};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 1, static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, d.dtype == FWN_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                   4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FWN_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return FWN_OK;
+}
+
+fwn_status check_desc(const fwn_attn_desc* d) {
+  if (!d) return fail(FWN_ERR_INVALID_ARGUMENT, "desc is null");
+  if (d->batch <= 0 || d->heads <= 0 || d->n <= 0)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "batch, heads and n must be positive (got %d, %d, %d)", d->batch, d->heads, d->n);
+  if (d->head_dim != 64 && d->head_dim != 128)
+    return fail(FWN_ERR_UNSUPPORTED, "head_dim %d not built (64 or 128)", d->head_dim);
+  if (d->dtype != FWN_DTYPE_BF16 && d->dtype != FWN_DTYPE_F32)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown dtype %d", d->dtype);
+  if (d->mode == FWN_MODE_BF16 && d->dtype != FWN_DTYPE_BF16)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "mode BF16 takes bf16 tensors");
+  if ((d->mode == FWN_MODE_TF32 || d->mode == FWN_MODE_TF32X3) && d->dtype != FWN_DTYPE_F32)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "modes TF32/TF32X3 take float32 tensors");
+  if (d->mode < 0 || d->mode > 2) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown mode %d", d->mode);
+  if (!(d->scale > 0.f)) return fail(FWN_ERR_INVALID_ARGUMENT, "scale must be positive");
+  const int64_t es = d->dtype == FWN_DTYPE_BF16 ? 2 : 4;
+  if ((d->stride_h * es) % 16 || (d->stride_n * es) % 16 || (d->stride_b * es) % 16)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "strides must be multiples of 16 bytes");
+  if (d->stride_h < d->head_dim || d->stride_n <= 0 || d->stride_b <= 0)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "strides must be positive and rows must not overlap");
+  return FWN_OK;
+}
+
+fwn_status check_tiles(const fwn_tile_list* t, const fwn_attn_desc* d, const char* name) {
+  if (!t) return fail(FWN_ERR_INVALID_ARGUMENT, "%s is null", name);
+  if (t->block_rows != 128)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "%s: attention kernels take the 128-row list (fwn_tiles_pair_*), got %d rows",
+                name, t->block_rows);
+  if (t->n_blocks != (d->n + 127) / 128)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "%s: %d blocks for n=%d (expected %d)", name, t->n_blocks, d->n, (d->n + 127) / 128);
+  if (!t->ptr || (t->n_tiles > 0 && (!t->kb || !t->bits)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned16(t->bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "%s: bits must be 16-byte aligned", name);
+  if (t->n_cols > d->n) return fail(FWN_ERR_INVALID_ARGUMENT, "%s: %d mask columns > n=%d", name, t->n_cols, d->n);
+  return FWN_OK;
+}
+
+int num_sms() {
+  static int sms = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  });
+  return sms;
+}
+
+template <typename Kernel>
+fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, int items, int* grid) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (per_sm < 1) return fail(FWN_ERR_LAUNCH, "kernel does not fit on an SM");
+  // Resident CTAs must never ask for more tensor memory than an SM has (512 columns): an allocation
+  // that cannot be satisfied would wait for a CTA that never exits.
+  if (per_sm * tmem_cols > 512) per_sm = 512 / tmem_cols;
+  *grid = items < per_sm * num_sms() ? items : per_sm * num_sms();
+  return FWN_OK;
+}
+
+template <int D, bool F32>
+fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
+                      void* o, float* lse, cudaStream_t stream) {
+  using C = fwn::FwdCfg<D, F32>;
+  CUtensorMap tq, tk, tv;
+  fwn_status s;
+  if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
+  if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&tv, v, d, C::SUB)) != FWN_OK) return s;
+  fwn::FwdParams p{};
+  p.ptr2 = t.ptr;
+  p.kb2 = t.kb;
+  p.bits2 = t.bits;
+  p.o = o;
+  p.lse = lse;
+  p.o_sb = d.stride_b;
+  p.o_sn = d.stride_n;
+  p.o_sh = d.stride_h;
+  p.batch = d.batch;
+  p.heads = d.heads;
+  p.n = d.n;
+  p.np = t.n_blocks;
+  p.lse_rows = fwn_lse_rows(d.n);
+  p.n_items = d.batch * d.heads * t.n_blocks;
+  p.scale_log2 = d.scale * 1.4426950408889634f;
+  auto kernel = fwn::attn_fwd_kernel<D, F32>;
+  int grid = 0;
+  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fwn_version(void) { return "fwn_attn 0.1.0 (sm_100a)"; }
+
+const char* fwn_last_error_string(void) { return g_last_error.c_str(); }
+
+int32_t fwn_lse_rows(int32_t n) { return ((n + 127) / 128) * 128; }
+
+fwn_status fwn_device_error(void* stream, int32_t* code) {
+  if (!code) return fail(FWN_ERR_INVALID_ARGUMENT, "code is null");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  unsigned int word = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&word, fwn::g_device_error, sizeof(word));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  e = cudaMemcpyToSymbol(fwn::g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
+  *code = word ? FWN_ERR_DEVICE_TIMEOUT : 0;
+  return ok();
+}
+
+fwn_status fwn_tiles_workspace_size(int32_t n_rows, int32_t n_cols, int32_t block_q, size_t* bytes) {
+  if (!bytes) return fail(FWN_ERR_INVALID_ARGUMENT, "bytes is null");
+  if (n_rows < 0 || n_cols < 0 || (block_q != 64 && block_q != 128))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape (n_rows=%d, n_cols=%d, block_q=%d)", n_rows, n_cols, block_q);
+  const size_t nqb = (static_cast<size_t>(n_rows) + block_q - 1) / block_q;
+  *bytes = ((nqb * 4 + 255) / 256) * 256 + 256;
+  return ok();
+}
+
+static fwn_status check_csr(const int32_t* indptr, const int32_t* indices, int32_t n_rows, int32_t n_cols,
+                            int32_t block_q) {
+  if (n_rows < 0 || n_cols < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "negative shape");
+  if (block_q != 64 && block_q != 128) return fail(FWN_ERR_INVALID_ARGUMENT, "block_q must be 64 or 128 (got %d)", block_q);
+  if (n_cols > (1 << 24)) return fail(FWN_ERR_UNSUPPORTED, "n_cols %d > 2^24", n_cols);
+  if (!indptr || (!indices && n_rows > 0)) return fail(FWN_ERR_INVALID_ARGUMENT, "null CSR pointer");
+  return FWN_OK;
+}
+
+fwn_status fwn_tiles_count(const int32_t* indptr, const int32_t* indices, int32_t n_rows, int32_t n_cols,
+                           int32_t block_q, int32_t* tile_ptr, void* ws, size_t ws_bytes, void* stream) {
+  fwn_status s = check_csr(indptr, indices, n_rows, n_cols, block_q);
+  if (s != FWN_OK) return s;
+  if (!tile_ptr) return fail(FWN_ERR_INVALID_ARGUMENT, "tile_ptr is null");
+  size_t need = 0;
+  fwn_tiles_workspace_size(n_rows, n_cols, block_q, &need);
+  if (!ws || ws_bytes < need) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaError_t e = fwn::launch_tiles_count(indptr, indices, n_rows, n_cols, block_q, tile_ptr,
+                                          static_cast<int32_t*>(ws), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tiles_count");
+  return ok();
+}
+
+fwn_status fwn_tiles_fill(const int32_t* indptr, const int32_t* indices, int32_t n_rows, int32_t n_cols,
+                          int32_t block_q, const int32_t* tile_ptr, int32_t* tile_kb, uint32_t* tile_bits,
+                          void* stream) {
+  fwn_status s = check_csr(indptr, indices, n_rows, n_cols, block_q);
+  if (s != FWN_OK) return s;
+  if (!tile_ptr || !tile_kb || !tile_bits) return fail(FWN_ERR_INVALID_ARGUMENT, "null output pointer");
+  cudaError_t e = fwn::launch_tiles_fill(indptr, indices, n_rows, n_cols, block_q, tile_ptr, tile_kb, tile_bits,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tiles_fill");
+  return ok();
+}
+
+fwn_status fwn_tiles_pair_count(const fwn_tile_list* t, int32_t* ptr2, void* ws, size_t ws_bytes, void* stream) {
+  if (!t || !ptr2) return fail(FWN_ERR_INVALID_ARGUMENT, "null argument");
+  if (t->block_rows != 64) return fail(FWN_ERR_INVALID_ARGUMENT, "pairing takes a 64-row list (got %d)", t->block_rows);
+  if (!t->ptr || (t->n_tiles > 0 && !t->kb)) return fail(FWN_ERR_INVALID_ARGUMENT, "null tile pointer");
+  if (t->n_cols < 0 || t->n_cols > (1 << 24)) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n_cols %d", t->n_cols);
+  const size_t need = ((static_cast<size_t>((t->n_blocks + 1) / 2) * 4 + 255) / 256) * 256 + 256;
+  if (!ws || ws_bytes < need) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaError_t e = fwn::launch_pair_count(t->ptr, t->kb, t->n_blocks, t->n_cols, ptr2, static_cast<int32_t*>(ws),
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pair_count");
+  return ok();
+}
+
+fwn_status fwn_tiles_pair_fill(const fwn_tile_list* t, const int32_t* ptr2, int32_t* kb2, uint32_t* bits2,
+                               void* stream) {
+  if (!t || !ptr2 || !kb2 || !bits2) return fail(FWN_ERR_INVALID_ARGUMENT, "null argument");
+  if (t->block_rows != 64) return fail(FWN_ERR_INVALID_ARGUMENT, "pairing takes a 64-row list (got %d)", t->block_rows);
+  if (!t->ptr || (t->n_tiles > 0 && (!t->kb || !t->bits))) return fail(FWN_ERR_INVALID_ARGUMENT, "null tile pointer");
+  cudaError_t e = fwn::launch_pair_fill(t->ptr, t->kb, t->bits, t->n_blocks, t->n_cols, ptr2, kb2, bits2,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pair_fill");
+  return ok();
+}
+
+fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32_t n, int32_t bits, int64_t* codes,
+                             void* stream) {
+  if (n < 0 || bits < 1 || bits > 20) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n=%d or bits=%d", n, bits);
+  if (n > 0 && (!lat_deg || !lon_deg || !codes)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaError_t e = fwn::launch_hilbert_codes(lat_deg, lon_deg, n, bits, reinterpret_cast<long long*>(codes),
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "hilbert_codes");
+  return ok();
+}
+
+fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                        const fwn_tile_list* tiles, void* o, float* lse, void* stream) {
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  if ((s = check_tiles(tiles, desc, "tiles")) != FWN_OK) return s;
+  if (!q || !k || !v || !o) return fail(FWN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const fwn_attn_desc& d = *desc;
+  if (d.mode == FWN_MODE_BF16) {
+    if (d.head_dim == 64) return launch_fwd<64, false>(d, q, k, v, *tiles, o, lse, st);
+    return launch_fwd<128, false>(d, q, k, v, *tiles, o, lse, st);
+  }
+  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64) return launch_fwd<64, true>(d, q, k, v, *tiles, o, lse, st);
+  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
+}
+
+fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes) {
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  if (!bytes) return fail(FWN_ERR_INVALID_ARGUMENT, "bytes is null");
+  *bytes = static_cast<size_t>(desc->batch) * desc->heads * fwn_lse_rows(desc->n) * sizeof(float);
+  return ok();
+}
+
+fwn_status fwn_attn_bwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
+                        const float* lse, const void* d_o, const fwn_tile_list* tiles, const fwn_tile_list* tiles_t,
+                        void* dq, void* dk, void* dv, void* ws, size_t ws_bytes, void* stream) {
+  (void)q; (void)k; (void)v; (void)o; (void)lse; (void)d_o; (void)tiles; (void)tiles_t;
+  (void)dq; (void)dk; (void)dv; (void)ws; (void)ws_bytes; (void)stream;
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  return fail(FWN_ERR_UNSUPPORTED, "backward not built yet");
+}
+
+}  // extern "C"

@@ -1,0 +1,29 @@
+// Host launchers of the tile-list builder kernels (tiles.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fwn {
+
+// 32-bit words of the per-block key-block bitmap for a mask with n_cols columns.
+int tiles_bitmap_words(int n_cols);
+
+// tile_ptr[nqb + 1] (exclusive scan of per-block tile counts; `counts` is nqb ints of workspace).
+cudaError_t launch_tiles_count(const int32_t* indptr, const int32_t* indices, int n_rows, int n_cols, int block_q,
+                               int32_t* tile_ptr, int32_t* counts, cudaStream_t stream);
+
+cudaError_t launch_tiles_fill(const int32_t* indptr, const int32_t* indices, int n_rows, int n_cols, int block_q,
+                              const int32_t* tile_ptr, int32_t* tile_kb, uint32_t* tile_bits, cudaStream_t stream);
+
+cudaError_t launch_pair_count(const int32_t* ptr, const int32_t* kb, int n_blocks, int n_cols, int32_t* ptr2,
+                              int32_t* counts, cudaStream_t stream);
+
+cudaError_t launch_pair_fill(const int32_t* ptr, const int32_t* kb, const uint32_t* bits, int n_blocks, int n_cols,
+                             const int32_t* ptr2, int32_t* kb2, uint32_t* bits2, cudaStream_t stream);
+
+// Hilbert-curve codes of (lat, lon) points in degrees (bits per axis <= 20); INT64_MAX for non-finite.
+cudaError_t launch_hilbert_codes(const double* lat_deg, const double* lon_deg, int n, int bits, long long* codes,
+                                 cudaStream_t stream);
+
+}  // namespace fwn

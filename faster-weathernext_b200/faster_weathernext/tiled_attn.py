@@ -1,0 +1,339 @@
+"""Block-sparse masked flash attention on B200, the drop-in for faster_weathernext.pallas_attn.
+
+Public API (names and argument meanings follow src/faster_weathernext/pallas_attn.py):
+
+  build_tile_mask(mask, block_q=64, block_k=32)  pallas_attn.py:85-109, computed by the CUDA builder;
+                                                 returns NumPy (tile_ptr int32, tile_kb int32, tile_bits uint32)
+  hilbert_order(lat_deg, lon_deg, bits=10)       pallas_attn.py:71-82 (host, NumPy)
+  tiled_flash_attention(q, k, v, tile_ptr, tile_kb, tile_bits, *, scale, strict_fp32=False, tiles_t=None, ...)
+                                                 pallas_attn.py:317-354; differentiable (torch.autograd),
+                                                 the analogue of the reference's jax.custom_vjp
+
+Device-side building blocks (torch tensors on the current CUDA device):
+
+  build_tiles_device(indptr, indices, n_rows, n_cols)     -> TileList64 (64-row list, bit-exact with the reference)
+  pair_tiles(tiles64)                                     -> TileList128 (what the kernels walk)
+  AttentionTiles.from_mask(mask) / .from_lists(...)       -> forward + transposed paired lists, cached
+  attention_forward(q, k, v, tiles, scale, mode, with_lse) / attention_backward(...)
+
+Precision: bf16 tensors run in bf16; float32 tensors run in TF32 (the reference's default precision,
+pallas_attn.py:342) or, with precision="highest" / strict_fp32=True, in 3xTF32 (pallas_attn.py:338-340).
+"""
+
+import ctypes
+import dataclasses
+from typing import Optional
+
+import numpy as np
+import torch
+from scipy import sparse
+
+from faster_weathernext import _lib
+from faster_weathernext._hilbert import hilbert_order  # noqa: F401  (re-exported)
+
+BLOCK_Q = 64
+BLOCK_K = 32
+MASK_VALUE = -1e30
+
+
+def _stream() -> int:
+  return torch.cuda.current_stream().cuda_stream
+
+
+def _device(device=None) -> torch.device:
+  if device is None:
+    if not torch.cuda.is_available():
+      raise RuntimeError("faster_weathernext attention needs a CUDA device (sm_100a); none is available")
+    return torch.device("cuda", torch.cuda.current_device())
+  return torch.device(device)
+
+
+@dataclasses.dataclass
+class TileList64:
+  """A build_tile_mask list on the device: ptr [nqb+1], kb [T], bits [T, 64] (int32 storage of uint32)."""
+  ptr: torch.Tensor
+  kb: torch.Tensor
+  bits: torch.Tensor
+  n_rows: int
+  n_cols: int
+
+  @property
+  def n_blocks(self):
+    return self.ptr.numel() - 1
+
+  @property
+  def n_tiles(self):
+    return self.kb.numel()
+
+  def struct(self) -> _lib.TileList:
+    return _lib.TileList(self.ptr.data_ptr(), self.kb.data_ptr() if self.n_tiles else 0,
+                         self.bits.data_ptr() if self.n_tiles else 0, self.n_blocks, self.n_tiles, 64, self.n_cols)
+
+  def numpy(self):
+    """(tile_ptr int32, tile_kb int32, tile_bits uint32 [T, 64]) — the reference's return types."""
+    return (self.ptr.cpu().numpy(), self.kb.cpu().numpy(),
+            self.bits.cpu().numpy().view(np.uint32).reshape(-1, 64))
+
+
+@dataclasses.dataclass
+class TileList128:
+  """Paired list (128 query rows per block) the attention kernels walk."""
+  ptr: torch.Tensor
+  kb: torch.Tensor
+  bits: torch.Tensor
+  n_cols: int
+
+  @property
+  def n_blocks(self):
+    return self.ptr.numel() - 1
+
+  @property
+  def n_tiles(self):
+    return self.kb.numel()
+
+  def struct(self) -> _lib.TileList:
+    return _lib.TileList(self.ptr.data_ptr(), self.kb.data_ptr() if self.n_tiles else 0,
+                         self.bits.data_ptr() if self.n_tiles else 0, self.n_blocks, self.n_tiles, 128, self.n_cols)
+
+  def numpy(self):
+    return (self.ptr.cpu().numpy(), self.kb.cpu().numpy(),
+            self.bits.cpu().numpy().view(np.uint32).reshape(-1, 128))
+
+
+def _read_last(ptr: torch.Tensor) -> int:
+  return int(ptr[-1].item())
+
+
+def build_tiles_device(indptr: torch.Tensor, indices: torch.Tensor, n_rows: int, n_cols: int,
+                       block_q: int = BLOCK_Q) -> TileList64:
+  """CUDA tile-list builder over a device CSR (int32 indptr [n_rows+1], indices [nnz])."""
+  lib = _lib.lib()
+  dev = indptr.device
+  indptr = indptr.to(torch.int32).contiguous()
+  indices = indices.to(torch.int32).contiguous()
+  nqb = -(-n_rows // block_q)
+  ws_bytes = ctypes.c_size_t(0)
+  _lib.check(lib.fwn_tiles_workspace_size(n_rows, n_cols, block_q, ctypes.byref(ws_bytes)))
+  ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=dev)
+  ptr = torch.empty(nqb + 1, dtype=torch.int32, device=dev)
+  s = _stream()
+  _lib.check(lib.fwn_tiles_count(indptr.data_ptr(), indices.data_ptr() if indices.numel() else 0, n_rows, n_cols,
+                                 block_q, ptr.data_ptr(), ws.data_ptr(), ws_bytes.value, s))
+  n_tiles = _read_last(ptr)
+  kb = torch.empty(max(n_tiles, 1), dtype=torch.int32, device=dev)[:n_tiles]
+  bits = torch.empty(max(n_tiles, 1) * block_q, dtype=torch.int32, device=dev)[:n_tiles * block_q]
+  if n_tiles:
+    _lib.check(lib.fwn_tiles_fill(indptr.data_ptr(), indices.data_ptr(), n_rows, n_cols, block_q, ptr.data_ptr(),
+                                  kb.data_ptr(), bits.data_ptr(), s))
+  return TileList64(ptr, kb, bits.view(n_tiles, block_q), n_rows, n_cols)
+
+
+def pair_tiles(t: TileList64) -> TileList128:
+  """128-row list derived from a 64-row list (union of the two blocks' key tiles)."""
+  lib = _lib.lib()
+  dev = t.ptr.device
+  npb = (t.n_blocks + 1) // 2
+  st = t.struct()
+  ws = torch.empty(npb * 4 + 512, dtype=torch.uint8, device=dev)
+  ptr2 = torch.empty(npb + 1, dtype=torch.int32, device=dev)
+  s = _stream()
+  _lib.check(lib.fwn_tiles_pair_count(ctypes.byref(st), ptr2.data_ptr(), ws.data_ptr(), ws.numel(), s))
+  n2 = _read_last(ptr2)
+  kb2 = torch.empty(max(n2, 1), dtype=torch.int32, device=dev)[:n2]
+  bits2 = torch.empty(max(n2, 1) * 128, dtype=torch.int32, device=dev)[:n2 * 128]
+  if n2:
+    _lib.check(lib.fwn_tiles_pair_fill(ctypes.byref(st), ptr2.data_ptr(), kb2.data_ptr(), bits2.data_ptr(), s))
+  return TileList128(ptr2, kb2, bits2.view(n2, 128), t.n_cols)
+
+
+def _csr_to_device(mask, device):
+  m = sparse.csr_matrix(mask)
+  m.sum_duplicates()
+  indptr = torch.from_numpy(np.asarray(m.indptr, np.int32)).to(device)
+  indices = torch.from_numpy(np.asarray(m.indices, np.int32)).to(device)
+  return indptr, indices, m.shape
+
+
+def build_tile_mask(mask, block_q: int = BLOCK_Q, block_k: int = BLOCK_K, device=None):
+  """Drop-in for pallas_attn.build_tile_mask: NumPy (tile_ptr, tile_kb, tile_bits) built on the GPU."""
+  assert block_k == 32, "one uint32 mask word per query row per tile"
+  if block_q != 64:
+    raise ValueError("the reference's tile lists use 64-row query blocks")
+  dev = _device(device)
+  m = sparse.csr_matrix(mask).astype(bool)
+  m.eliminate_zeros()
+  indptr, indices, (n_rows, n_cols) = _csr_to_device(m, dev)
+  return build_tiles_device(indptr, indices, n_rows, n_cols, block_q).numpy()
+
+
+def _tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n_cols, device) -> TileList64:
+  ptr = torch.as_tensor(np.asarray(tile_ptr, np.int32), device=device)
+  kb = torch.as_tensor(np.asarray(tile_kb, np.int32), device=device)
+  bits = torch.as_tensor(np.ascontiguousarray(np.asarray(tile_bits, np.uint32)).view(np.int32), device=device)
+  return TileList64(ptr, kb, bits.reshape(-1, 64), (ptr.numel() - 1) * 64, n_cols)
+
+
+class AttentionTiles:
+  """Forward and transposed paired lists of one mask, resident on the device (built once per mask,
+  like the reference's tile constants, patch.py:208-219)."""
+
+  def __init__(self, fwd: TileList128, bwd: TileList128, n: int, symmetric: bool):
+    self.fwd = fwd
+    self.bwd = bwd
+    self.n = n
+    self.symmetric = symmetric
+
+  @classmethod
+  def from_mask(cls, mask, device=None) -> "AttentionTiles":
+    dev = _device(device)
+    m = sparse.csr_matrix(mask).astype(bool)
+    m.eliminate_zeros()
+    n = m.shape[0]
+    assert m.shape == (n, n), "attention masks are square [n, n]"
+    indptr, indices, _ = _csr_to_device(m, dev)
+    fwd = pair_tiles(build_tiles_device(indptr, indices, n, n))
+    symmetric = (m != m.T).nnz == 0
+    if symmetric:
+      bwd = fwd
+    else:
+      mt = m.T.tocsr()
+      ip, ix, _ = _csr_to_device(mt, dev)
+      bwd = pair_tiles(build_tiles_device(ip, ix, n, n))
+    return cls(fwd, bwd, n, symmetric)
+
+  @classmethod
+  def from_lists(cls, tile_ptr, tile_kb, tile_bits, n: int, tiles_t=None, device=None) -> "AttentionTiles":
+    """From the reference's (tile_ptr, tile_kb, tile_bits) arrays (and optionally the transposed triple)."""
+    dev = _device(device)
+    fwd = pair_tiles(_tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n, dev))
+    if tiles_t is None:
+      return cls(fwd, fwd, n, True)
+    bwd = pair_tiles(_tiles64_from_arrays(*tiles_t, n, dev))
+    return cls(fwd, bwd, n, False)
+
+
+def _mode_for(dtype: torch.dtype, precision: Optional[str], strict_fp32: bool) -> int:
+  if dtype == torch.bfloat16:
+    return _lib.MODE_BF16
+  if dtype != torch.float32:
+    raise TypeError(f"q/k/v must be bfloat16 or float32, got {dtype}")
+  if strict_fp32 or precision in ("highest", "float32"):
+    return _lib.MODE_TF32X3
+  return _lib.MODE_TF32
+
+
+def _desc(q: torch.Tensor, scale: float, mode: int) -> _lib.AttnDesc:
+  b, n, h, d = q.shape
+  sb, sn, sh, sd = q.stride()
+  if sd != 1:
+    raise ValueError("head_dim must be contiguous")
+  dt = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_F32
+  return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh)
+
+
+def _same_layout(*ts):
+  ref = ts[0]
+  return all(t.shape == ref.shape and t.stride() == ref.stride() and t.dtype == ref.dtype for t in ts)
+
+
+def _canon(*ts):
+  """Make tensors share one [B, n, H, D] layout with head_dim contiguous."""
+  if _same_layout(*ts) and ts[0].stride(-1) == 1:
+    return ts
+  return tuple(t.contiguous() for t in ts)
+
+
+def attention_forward(q, k, v, tiles: AttentionTiles, scale: float, mode: int, with_lse: bool = True):
+  """o [B, n, H, D] (q's dtype) and lse float32 [B, H, lse_rows] (or None)."""
+  lib = _lib.lib()
+  q, k, v = _canon(q, k, v)
+  o = torch.empty_like(q)
+  desc = _desc(q, scale, mode)
+  lse = None
+  if with_lse:
+    b, n, h, _ = q.shape
+    lse = torch.empty(b, h, lib.fwn_lse_rows(n), dtype=torch.float32, device=q.device)
+  st = tiles.fwd.struct()
+  _lib.check(lib.fwn_attn_fwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), ctypes.byref(st),
+                              o.data_ptr(), lse.data_ptr() if lse is not None else 0, _stream()))
+  return o, lse
+
+
+def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float, mode: int):
+  """(dq, dk, dv), each [B, n, H, D] in q's dtype."""
+  lib = _lib.lib()
+  q, k, v, o, do = _canon(q, k, v, o, do)
+  desc = _desc(q, scale, mode)
+  ws_bytes = ctypes.c_size_t(0)
+  _lib.check(lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)))
+  ws = torch.empty(max(ws_bytes.value, 16), dtype=torch.uint8, device=q.device)
+  dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+  sf, sb = tiles.fwd.struct(), tiles.bwd.struct()
+  _lib.check(lib.fwn_attn_bwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                              lse.data_ptr(), do.data_ptr(), ctypes.byref(sf), ctypes.byref(sb), dq.data_ptr(),
+                              dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(), _stream()))
+  return dq, dk, dv
+
+
+class _TiledAttention(torch.autograd.Function):
+  """custom VJP (pallas_attn.py:260-314): forward saves (q, k, v, o, lse); backward runs the dQ and
+  dK/dV kernels, recomputing P from the saved log-sum-exp."""
+
+  @staticmethod
+  def forward(ctx, q, k, v, tiles, scale, mode):
+    needs = any(ctx.needs_input_grad[:3])
+    o, lse = attention_forward(q, k, v, tiles, scale, mode, with_lse=needs)
+    if needs:
+      ctx.save_for_backward(q, k, v, o, lse)
+    ctx.tiles, ctx.scale, ctx.mode = tiles, scale, mode
+    return o
+
+  @staticmethod
+  def backward(ctx, do):
+    q, k, v, o, lse = ctx.saved_tensors
+    dq, dk, dv = attention_backward(q, k, v, o, lse, do, ctx.tiles, ctx.scale, ctx.mode)
+    return dq, dk, dv, None, None, None
+
+
+def attention(q, k, v, tiles: AttentionTiles, *, scale: float, precision: Optional[str] = None,
+              strict_fp32: bool = False):
+  """Differentiable masked attention over prepared tiles: q, k, v [B, n, H, D] -> [B, n, H, D]."""
+  mode = _mode_for(q.dtype, precision, strict_fp32)
+  return _TiledAttention.apply(q, k, v, tiles, float(scale), mode)
+
+
+_TILE_CACHE = {}
+
+
+def tiled_flash_attention(q, k, v, tile_ptr, tile_kb, tile_bits, *, scale, strict_fp32=False, tiles_t=None,
+                          block_q=BLOCK_Q, block_k=BLOCK_K, num_warps=None, num_stages=None, bwd_num_warps=None,
+                          bwd_split=None, interpret=False, precision=None):
+  """Drop-in for pallas_attn.tiled_flash_attention: q, k, v [batch, n, heads, head_dim] -> same shape.
+
+  tile lists are the reference's (build_tile_mask) 64-row lists, NumPy or torch; tiles_t is the
+  transposed mask's list (None: the mask is symmetric). The Triton launch knobs (num_warps,
+  num_stages, bwd_num_warps, bwd_split) have no meaning here and are accepted for compatibility;
+  `interpret` (Pallas interpret mode) is refused: there is no CPU path.
+  """
+  if interpret:
+    raise NotImplementedError("interpret mode: this implementation has no CPU path")
+  if block_q != BLOCK_Q or block_k != BLOCK_K:
+    raise ValueError("the tile lists use 64-row query blocks and 32-key tiles")
+  n = q.shape[1]
+  key = tuple(id(x) for x in (tile_ptr, tile_kb, tile_bits)) + ((tuple(id(x) for x in tiles_t),) if tiles_t else ())
+  hit = _TILE_CACHE.get(key)
+  if hit is None or hit[0] is not tile_ptr:
+    tiles = AttentionTiles.from_lists(_np(tile_ptr), _np(tile_kb), _np(tile_bits), n,
+                                      tiles_t=tuple(_np(x) for x in tiles_t) if tiles_t else None, device=q.device)
+    _TILE_CACHE.clear()
+    _TILE_CACHE[key] = (tile_ptr, tiles)
+  else:
+    tiles = hit[1]
+  return attention(q, k, v, tiles, scale=scale, precision=precision, strict_fp32=strict_fp32)
+
+
+def _np(x):
+  if isinstance(x, torch.Tensor):
+    x = x.detach().cpu().numpy()
+  x = np.asarray(x)
+  return x.view(np.uint32) if x.dtype == np.int32 and x.ndim == 2 else x

@@ -1,0 +1,152 @@
+/*
+ * fwn_attn.h — C ABI of libfwn_attn.so, the B200 (sm_100a) block-sparse masked flash attention of
+ * faster-weathernext's mesh-transformer processor.
+ *
+ * Reference interfaces replaced (Raymondlol/Faster-WeatherNext v0.2.0):
+ *   fwn_tiles_count / fwn_tiles_fill      <- pallas_attn.build_tile_mask   (src/faster_weathernext/pallas_attn.py:85-109)
+ *   fwn_tiles_pair_count / _fill          <- (no counterpart: derives the 128-query-row list the kernels walk
+ *                                             from build_tile_mask's 64-row list; see pallas_attn.py:112-141)
+ *   fwn_attn_fwd                          <- pallas_attn._forward / _kernel (pallas_attn.py:112-141, 235-257)
+ *                                             and the custom-VJP forward rule _attention_fwd (pallas_attn.py:267-271)
+ *   fwn_attn_bwd                          <- pallas_attn._attention_bwd with _bwd_dq_kernel / _bwd_dkv_kernel
+ *                                             (pallas_attn.py:161-215, 274-311)
+ *   fwn_attn_desc                         <- the static arguments of tiled_flash_attention (pallas_attn.py:317-354):
+ *                                             shapes, `scale`, precision preset (TF32 / 3xTF32) and layout
+ *
+ * Conventions
+ *   - Every pointer is device memory owned by the caller; nothing here allocates, frees or synchronises
+ *     (except fwn_device_error, which synchronises the stream to read the device error word).
+ *   - Calls are stateless and may be issued concurrently on different streams.
+ *   - Tensors q, k, v, o, d_o, dq, dk, dv use the reference's public layout [batch, n, heads, head_dim] with
+ *     head_dim contiguous and arbitrary element strides for batch / node / head (multiples of 16 bytes).
+ *   - lse is float32 [batch, heads, fwn_lse_rows(n)] (natural-log log-sum-exp of the scaled logits).
+ *   - Tile lists follow build_tile_mask: block b owns tiles ptr[b]..ptr[b+1]-1 in ascending key-block
+ *     order; tile t covers keys kb[t]*32 + [0, 32); bit j of bits[t*rows + r] allows (row b*rows + r,
+ *     key kb[t]*32 + j). The attention kernels take the 128-row ("paired") form.
+ *   - Errors are returned as fwn_status; fwn_last_error_string() describes the last failure of the calling
+ *     thread.
+ */
+#ifndef FWN_ATTN_H_
+#define FWN_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FWN_API __attribute__((visibility("default")))
+#else
+#define FWN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fwn_status {
+  FWN_OK = 0,
+  FWN_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, stride or alignment */
+  FWN_ERR_UNSUPPORTED = 2,      /* head_dim / dtype / mode combination not built */
+  FWN_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  FWN_ERR_LAUNCH = 4,           /* CUDA runtime / driver error */
+  FWN_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait expired; the kernel returned early */
+  FWN_ERR_NO_DEVICE = 6         /* no sm_100 device is current */
+} fwn_status;
+
+typedef enum fwn_dtype { FWN_DTYPE_BF16 = 0, FWN_DTYPE_F32 = 1 } fwn_dtype;
+
+/* Arithmetic of the attention MMAs. BF16 takes bf16 tensors; TF32 and TF32X3 take float32 tensors.
+ * TF32 <-> the reference's default precision (DotAlgorithmPreset.TF32_TF32_F32, pallas_attn.py:342);
+ * TF32X3 <-> jax.default_matmul_precision("highest") (TF32_TF32_F32_X3, pallas_attn.py:338-340). */
+typedef enum fwn_mode { FWN_MODE_BF16 = 0, FWN_MODE_TF32 = 1, FWN_MODE_TF32X3 = 2 } fwn_mode;
+
+typedef struct fwn_attn_desc {
+  int32_t batch;
+  int32_t heads;
+  int32_t n;          /* nodes (rows of q and k) */
+  int32_t head_dim;   /* 64 or 128 */
+  float scale;        /* softmax scale; the reference passes key_size ** -0.5 (patch.py:174) */
+  int32_t dtype;      /* fwn_dtype of q, k, v, o, d_o, dq, dk, dv */
+  int32_t mode;       /* fwn_mode */
+  int32_t reserved;
+  int64_t stride_b;   /* element strides of the [batch, n, heads, head_dim] tensors */
+  int64_t stride_n;
+  int64_t stride_h;
+} fwn_attn_desc;
+
+typedef struct fwn_tile_list {
+  const int32_t* ptr;   /* [n_blocks + 1] */
+  const int32_t* kb;    /* [n_tiles] */
+  const uint32_t* bits; /* [n_tiles * block_rows] */
+  int32_t n_blocks;
+  int32_t n_tiles;
+  int32_t block_rows;   /* 64: build_tile_mask layout; 128: paired layout (attention kernels) */
+  int32_t n_cols;       /* columns of the mask (keys); key blocks are < ceil(n_cols / 32) */
+} fwn_tile_list;
+
+/* Version string of the library build. */
+FWN_API const char* fwn_version(void);
+
+/* Description of the last error returned to the calling thread ("" if none). */
+FWN_API const char* fwn_last_error_string(void);
+
+/* Synchronises `stream`, reads and clears the device error word written by bounded waits.
+ * *code receives 0 or FWN_ERR_DEVICE_TIMEOUT. */
+FWN_API fwn_status fwn_device_error(void* stream, int32_t* code);
+
+/* Rows of the lse buffer per (batch, head): n rounded up to a multiple of 128. */
+FWN_API int32_t fwn_lse_rows(int32_t n);
+
+/* ---- tile-list builder (replaces pallas_attn.build_tile_mask, pallas_attn.py:85-109) -------------------- */
+
+/* Workspace bytes fwn_tiles_count needs for an [n_rows, n_cols] mask with block_q-row blocks. */
+FWN_API fwn_status fwn_tiles_workspace_size(int32_t n_rows, int32_t n_cols, int32_t block_q, size_t* bytes);
+
+/* Pass 1: tile_ptr[ceil(n_rows/block_q) + 1] from the CSR (indptr[n_rows+1], indices[nnz]) of a boolean
+ * mask (duplicates allowed, any column order). The tile count is tile_ptr[last]. block_q in {64, 128};
+ * key tiles are 32 columns (one uint32 word per row per tile). */
+FWN_API fwn_status fwn_tiles_count(const int32_t* indptr, const int32_t* indices, int32_t n_rows, int32_t n_cols,
+                           int32_t block_q, int32_t* tile_ptr, void* ws, size_t ws_bytes, void* stream);
+
+/* Pass 2: tile_kb[n_tiles] and tile_bits[n_tiles * block_q] for the tile_ptr of pass 1. Bit-exact with
+ * build_tile_mask for block_q = 64. The transposed list (pallas_attn.py:351-352, patch.py:215-218) is
+ * the same two passes over the CSR of the transposed mask. */
+FWN_API fwn_status fwn_tiles_fill(const int32_t* indptr, const int32_t* indices, int32_t n_rows, int32_t n_cols,
+                          int32_t block_q, const int32_t* tile_ptr, int32_t* tile_kb, uint32_t* tile_bits,
+                          void* stream);
+
+/* Paired 128-row list from a 64-row list: block p = rows of blocks 2p and 2p+1; its tiles are the union
+ * of their key blocks (ascending); words of rows 0-63 come from block 2p, rows 64-127 from 2p+1 (0 where
+ * that block lacks the key block). pass 1 writes ptr2[ceil(n_blocks/2) + 1]; pass 2 kb2 and bits2. */
+FWN_API fwn_status fwn_tiles_pair_count(const fwn_tile_list* tiles64, int32_t* ptr2, void* ws, size_t ws_bytes,
+                                void* stream);
+FWN_API fwn_status fwn_tiles_pair_fill(const fwn_tile_list* tiles64, const int32_t* ptr2, int32_t* kb2,
+                               uint32_t* bits2, void* stream);
+
+/* Hilbert-curve codes (3D, `bits` per axis, 1..20) of unit-sphere points given in degrees; non-finite
+ * points get INT64_MAX. A stable argsort of the codes is pallas_attn.hilbert_order (pallas_attn.py:41-82). */
+FWN_API fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32_t n, int32_t bits,
+                                     int64_t* codes, void* stream);
+
+/* ---- attention --------------------------------------------------------------------------------------- */
+
+/* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)
+ * receives m + log(l) per row, the residual of the custom-VJP forward rule. Rows with no allowed key get
+ * o = 0 and lse = -inf. */
+FWN_API fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                        const fwn_tile_list* tiles, void* o, float* lse, void* stream);
+
+/* Workspace bytes of fwn_attn_bwd (the per-row delta = rowsum(o * d_o), float32). */
+FWN_API fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes);
+
+/* Backward: dq over `tiles` (the forward's 128-row list), dk/dv over `tiles_t` (the 128-row list of the
+ * transposed mask; pass `tiles` again for a symmetric mask, pallas_attn.py:351-352). */
+FWN_API fwn_status fwn_attn_bwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                        const void* o, const float* lse, const void* d_o, const fwn_tile_list* tiles,
+                        const fwn_tile_list* tiles_t, void* dq, void* dk, void* dv, void* ws,
+                        size_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FWN_ATTN_H_ */

@@ -1,0 +1,196 @@
+"""Masked-softmax attention on the CPU (test infrastructure; see oracle/__init__.py).
+
+Tensors use the reference's public layout [batch, n, heads, head_dim]; the mask is a boolean
+[n, n] matrix with mask[query, key].
+
+  chunked_attention    — the reference's XLA attention path, patch.py:130-162 (per chunk of queries:
+                         einsum over the chunk's key window * scale, where(mask, ., -1e30), softmax
+                         upcast to float32, einsum with V), in float32 or float64.
+  sparse_attention     — the same masked softmax evaluated only on allowed pairs (masked pairs get
+                         weight exp(-1e30 - max) == 0 exactly), float64, with the forward's
+                         log-sum-exp lse = m + log(max(l, 1e-30)) (pallas_attn.py:138-140).
+  sparse_attention_vjp — dQ, dK, dV of the masked softmax: dS = P * (dP - rowsum(dP * P))
+                         (tests/test_pallas_kernel.py:58-69), float64.
+  dense_attention(_vjp)— the float64 dense references of tests/test_pallas_kernel.py:15-21, 58-69.
+  rel_rms              — RMS(x - ref) / std(ref) (scripts/attn_bench.py:122).
+"""
+
+import numpy as np
+from scipy import sparse
+
+from oracle.tiles import build_chunked_mask
+
+MASK_VALUE = -1e30
+
+
+def rel_rms(x, ref) -> float:
+  x = np.asarray(x, np.float64)
+  ref = np.asarray(ref, np.float64)
+  return float(np.sqrt(np.mean((x - ref) ** 2)) / ref.std())
+
+
+def max_rel(x, ref) -> float:
+  """max|x - ref| / max|ref| (the metric of tests/test_pallas_kernel.py:54)."""
+  x = np.asarray(x, np.float64)
+  ref = np.asarray(ref, np.float64)
+  return float(np.abs(x - ref).max() / np.abs(ref).max())
+
+
+def _softmax_lastaxis(x):
+  m = x.max(-1, keepdims=True)
+  e = np.exp(x - m)
+  return e / e.sum(-1, keepdims=True)
+
+
+def chunked_attention(q, k, v, mask, scale, chunk=512, dtype=np.float32, chunks=None):
+  """The XLA chunked path (patch.py:130-162). Returns [B, n, H, D] in `dtype`.
+
+  `chunks` (optional iterable of chunk indices) evaluates only those query chunks (rows of other
+  chunks are left zero) — used to time a bounded sample of a large workload.
+  """
+  starts, packed, window, n_kv = build_chunked_mask(mask, chunk)
+  b, n, h, d = q.shape
+  nc = len(starts)
+  qp = np.zeros((b, nc * chunk, h, d), dtype)
+  qp[:, :n] = q
+  kp = np.zeros((b, n_kv, h, d), dtype)
+  vp = np.zeros((b, n_kv, h, d), dtype)
+  kp[:, :n] = k
+  vp[:, :n] = v
+  out = np.zeros((b, nc * chunk, h, d), dtype)
+  # Head-major copies so each chunk is a batched matmul.
+  qh = np.ascontiguousarray(qp.transpose(0, 2, 1, 3))
+  kh = np.ascontiguousarray(kp.transpose(0, 2, 1, 3))
+  vh = np.ascontiguousarray(vp.transpose(0, 2, 1, 3))
+  for c in (range(nc) if chunks is None else chunks):
+    s0 = int(starts[c])
+    qc = qh[:, :, c * chunk:(c + 1) * chunk]                       # [B, H, chunk, D]
+    kc = kh[:, :, s0:s0 + window]
+    vc = vh[:, :, s0:s0 + window]
+    logits = np.matmul(qc, kc.transpose(0, 1, 3, 2)) * dtype(scale)  # [B, H, chunk, W]
+    m = np.unpackbits(packed[c], axis=-1, count=window, bitorder="little").astype(bool)
+    logits = np.where(m[None, None], logits, dtype(MASK_VALUE))
+    w = _softmax_lastaxis(logits.astype(np.float32) if dtype != np.float64 else logits).astype(dtype)
+    out[:, c * chunk:(c + 1) * chunk] = np.matmul(w, vc).transpose(0, 2, 1, 3)
+  return out[:, :n]
+
+
+def _pairs(mask):
+  m = sparse.csr_matrix(mask).astype(bool).tocsr()
+  m.sum_duplicates()
+  m.sort_indices()
+  rows = np.repeat(np.arange(m.shape[0], dtype=np.int64), np.diff(m.indptr))
+  return m, rows, m.indices.astype(np.int64)
+
+
+def _row_blocks(indptr, max_pairs):
+  """Split rows into contiguous ranges with at most ~max_pairs allowed pairs each."""
+  n = len(indptr) - 1
+  r0 = 0
+  while r0 < n:
+    target = indptr[r0] + max_pairs
+    r1 = int(np.searchsorted(indptr, target, side="right")) - 1
+    r1 = max(r1, r0 + 1)
+    yield r0, min(r1, n)
+    r0 = min(r1, n)
+
+
+def sparse_attention(q, k, v, mask, scale, max_pairs=1 << 21):
+  """float64 masked softmax attention on allowed pairs. Returns (out [B,n,H,D], lse [B,H,n])."""
+  m, rows_all, cols_all = _pairs(mask)
+  b, n, h, d = q.shape
+  out = np.zeros((b, n, h, d))
+  lse = np.zeros((b, h, n))
+  for bi in range(b):
+    for hi in range(h):
+      qq = np.asarray(q[bi, :, hi], np.float64)
+      kk = np.asarray(k[bi, :, hi], np.float64)
+      vv = np.asarray(v[bi, :, hi], np.float64)
+      for r0, r1 in _row_blocks(m.indptr, max_pairs):
+        e0, e1 = m.indptr[r0], m.indptr[r1]
+        if e1 == e0:
+          continue
+        rows, cols = rows_all[e0:e1], cols_all[e0:e1]
+        s = np.einsum("ed,ed->e", qq[rows], kk[cols]) * scale
+        seg = m.indptr[r0:r1] - e0
+        nonempty = np.diff(m.indptr[r0:r1 + 1]) > 0
+        mx = np.full(r1 - r0, -np.inf)
+        mx[nonempty] = np.maximum.reduceat(s, seg[nonempty])
+        p = np.exp(s - mx[rows - r0])
+        l = np.zeros(r1 - r0)
+        l[nonempty] = np.add.reduceat(p, seg[nonempty])
+        pm = sparse.csr_matrix((p, cols, m.indptr[r0:r1 + 1] - e0), shape=(r1 - r0, n))
+        out[bi, r0:r1, hi] = (pm @ vv) / np.maximum(l, 1e-30)[:, None]
+        lse[bi, hi, r0:r1] = mx + np.log(np.maximum(l, 1e-30))
+  return out, lse
+
+
+def sparse_attention_vjp(q, k, v, do, mask, scale, max_pairs=1 << 21):
+  """float64 (dq, dk, dv) of masked softmax attention, each [B, n, H, D]."""
+  m, rows_all, cols_all = _pairs(mask)
+  b, n, h, d = q.shape
+  dq = np.zeros((b, n, h, d))
+  dk = np.zeros((b, n, h, d))
+  dv = np.zeros((b, n, h, d))
+  for bi in range(b):
+    for hi in range(h):
+      qq = np.asarray(q[bi, :, hi], np.float64)
+      kk = np.asarray(k[bi, :, hi], np.float64)
+      vv = np.asarray(v[bi, :, hi], np.float64)
+      gg = np.asarray(do[bi, :, hi], np.float64)
+      for r0, r1 in _row_blocks(m.indptr, max_pairs):
+        e0, e1 = m.indptr[r0], m.indptr[r1]
+        if e1 == e0:
+          continue
+        rows, cols = rows_all[e0:e1], cols_all[e0:e1]
+        s = np.einsum("ed,ed->e", qq[rows], kk[cols]) * scale
+        seg = m.indptr[r0:r1] - e0
+        nonempty = np.diff(m.indptr[r0:r1 + 1]) > 0
+        mx = np.full(r1 - r0, -np.inf)
+        mx[nonempty] = np.maximum.reduceat(s, seg[nonempty])
+        p = np.exp(s - mx[rows - r0])
+        l = np.zeros(r1 - r0)
+        l[nonempty] = np.add.reduceat(p, seg[nonempty])
+        p = p / l[rows - r0]
+        dp = np.einsum("ed,ed->e", gg[rows], vv[cols])
+        delta = np.zeros(r1 - r0)
+        delta[nonempty] = np.add.reduceat(p * dp, seg[nonempty])
+        ds = p * (dp - delta[rows - r0])
+        indptr = m.indptr[r0:r1 + 1] - e0
+        dsm = sparse.csr_matrix((ds, cols, indptr), shape=(r1 - r0, n))
+        pm = sparse.csr_matrix((p, cols, indptr), shape=(r1 - r0, n))
+        dq[bi, r0:r1, hi] = (dsm @ kk) * scale
+        dk[bi, :, hi] += (dsm.T @ qq[r0:r1]) * scale
+        dv[bi, :, hi] += pm.T @ gg[r0:r1]
+  return dq, dk, dv
+
+
+def dense_attention(q, k, v, mask, scale):
+  """float64 dense masked softmax for one batch element, q/k/v [n, H, D] (test_pallas_kernel.py:15-21)."""
+  s = np.einsum("nhd,mhd->hnm", q.astype(np.float64), k.astype(np.float64)) * scale
+  s = np.where(mask[None], s, -np.inf)
+  p = np.exp(s - s.max(-1, keepdims=True))
+  p /= p.sum(-1, keepdims=True)
+  return np.einsum("hnm,mhd->nhd", p, v.astype(np.float64))
+
+
+def dense_attention_vjp(q, k, v, do, mask, scale):
+  """float64 dQ, dK, dV for one batch element (test_pallas_kernel.py:58-69)."""
+  q, k, v, do = (x.astype(np.float64) for x in (q, k, v, do))
+  s = np.where(mask[None], np.einsum("nhd,mhd->hnm", q, k) * scale, -np.inf)
+  p = np.exp(s - s.max(-1, keepdims=True))
+  p /= p.sum(-1, keepdims=True)
+  dp = np.einsum("nhd,mhd->hnm", do, v)
+  ds = p * (dp - (dp * p).sum(-1, keepdims=True))
+  dq = np.einsum("hnm,mhd->nhd", ds, k) * scale
+  dk = np.einsum("hnm,nhd->mhd", ds, q) * scale
+  dv = np.einsum("hnm,nhd->mhd", p, do)
+  return dq, dk, dv
+
+
+def bf16_round(x):
+  """Round float32/float64 values to bfloat16 (round to nearest even), returned as float32."""
+  a = np.ascontiguousarray(np.asarray(x, np.float32))
+  u = a.view(np.uint32).astype(np.uint64)
+  r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+  return r.astype(np.uint32).view(np.float32).reshape(a.shape)
