@@ -219,7 +219,10 @@ __global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
             for (int kk = 0; kk < ksteps; ++kk) {
               const uint32_t cb = kk / 4, within = (kk % 4) * 32;
               const uint64_t a = smem_desc(p_smem(pbuf) + cb * C::ROWS * 128 + within, 16, 1024);
-              const uint64_t bdesc = smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
+              // V is the MN-major B operand: 128-byte swizzle for bf16, the 32-byte-atom variant for tf32.
+              const uint64_t bdesc = F32 ? smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 512,
+                                                     kLayoutSW128Base32B)
+                                         : smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
               mma_ss<F32>(tmem + C::O_COL, a, bdesc, kIdescPV, (c == 1 && kk == 0) ? 0u : 1u);
             }
             mma_commit(p_empty(pbuf));

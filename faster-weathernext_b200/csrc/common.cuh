@@ -193,15 +193,18 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // Shared-memory matrix descriptor (tcgen05 format: version 1 at bits 46-47, layout type at 61-63).
 // Swizzled layouts: K-major operands use 8-row x 128-byte atoms stacked at SBO; MN-major operands use
 // atoms of 8 K-rows x 128 bytes of MN, stacked along K at SBO and along MN at LBO.
-enum : uint32_t { kLayoutSW128 = 2 };
+// 32-bit MN-major operands (tf32) use SWIZZLE_128B_BASE32B: 32-byte chunks of a 128-byte row XOR
+// (row & 3), atoms of 4 K-rows (TMA: CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+enum : uint32_t { kLayoutSW128 = 2, kLayoutSW128Base32B = 1 };
 
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout = kLayoutSW128) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
-  d |= static_cast<uint64_t>(kLayoutSW128) << 61;
+  d |= static_cast<uint64_t>(layout) << 61;
   return d;
 }
 

@@ -57,19 +57,24 @@ EncodeTiledFn encode_fn() {
 }
 
 // 4D map over a [B, n, H, D] tensor (D contiguous): box = 128 bytes of D x 1 head x `rows` nodes x 1.
-fwn_status make_map(CUtensorMap* map, const void* base, const fwn_attn_desc& d, int rows) {
+// `atom32` selects the 128-byte swizzle with 32-byte atoms (tf32 operands read MN-major by the MMA).
+fwn_status make_map(CUtensorMap* map, const void* base, const fwn_attn_desc& d, int rows, bool atom32 = false,
+                    bool out = false) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FWN_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
   const int es = d.dtype == FWN_DTYPE_BF16 ? 2 : 4;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(d.head_dim), static_cast<cuuint64_t>(d.heads),
                         static_cast<cuuint64_t>(d.n), static_cast<cuuint64_t>(d.batch)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d.stride_h) * es, static_cast<cuuint64_t>(d.stride_n) * es,
-                           static_cast<cuuint64_t>(d.stride_b) * es};
+  const int64_t sh = out ? d.out_stride_h : d.stride_h, sn = out ? d.out_stride_n : d.stride_n,
+                sb = out ? d.out_stride_b : d.stride_b;
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(sh) * es, static_cast<cuuint64_t>(sn) * es,
+                           static_cast<cuuint64_t>(sb) * es};
   cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 1, static_cast<cuuint32_t>(rows), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, d.dtype == FWN_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                    4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FWN_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return FWN_OK;
 }
@@ -89,9 +94,11 @@ fwn_status check_desc(const fwn_attn_desc* d) {
   if (d->mode < 0 || d->mode > 2) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown mode %d", d->mode);
   if (!(d->scale > 0.f)) return fail(FWN_ERR_INVALID_ARGUMENT, "scale must be positive");
   const int64_t es = d->dtype == FWN_DTYPE_BF16 ? 2 : 4;
-  if ((d->stride_h * es) % 16 || (d->stride_n * es) % 16 || (d->stride_b * es) % 16)
+  if ((d->stride_h * es) % 16 || (d->stride_n * es) % 16 || (d->stride_b * es) % 16 ||
+      (d->out_stride_h * es) % 16 || (d->out_stride_n * es) % 16 || (d->out_stride_b * es) % 16)
     return fail(FWN_ERR_INVALID_ARGUMENT, "strides must be multiples of 16 bytes");
-  if (d->stride_h < d->head_dim || d->stride_n <= 0 || d->stride_b <= 0)
+  if (d->stride_h < d->head_dim || d->stride_n <= 0 || d->stride_b <= 0 || d->out_stride_h < d->head_dim ||
+      d->out_stride_n <= 0 || d->out_stride_b <= 0)
     return fail(FWN_ERR_INVALID_ARGUMENT, "strides must be positive and rows must not overlap");
   return FWN_OK;
 }
@@ -144,16 +151,16 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   fwn_status s;
   if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
   if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
-  if ((s = make_map(&tv, v, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&tv, v, d, C::SUB, F32)) != FWN_OK) return s;
   fwn::FwdParams p{};
   p.ptr2 = t.ptr;
   p.kb2 = t.kb;
   p.bits2 = t.bits;
   p.o = o;
   p.lse = lse;
-  p.o_sb = d.stride_b;
-  p.o_sn = d.stride_n;
-  p.o_sh = d.stride_h;
+  p.o_sb = d.out_stride_b;
+  p.o_sn = d.out_stride_n;
+  p.o_sh = d.out_stride_h;
   p.batch = d.batch;
   p.heads = d.heads;
   p.n = d.n;
@@ -207,7 +214,8 @@ static fwn_status check_csr(const int32_t* indptr, const int32_t* indices, int32
   if (n_rows < 0 || n_cols < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "negative shape");
   if (block_q != 64 && block_q != 128) return fail(FWN_ERR_INVALID_ARGUMENT, "block_q must be 64 or 128 (got %d)", block_q);
   if (n_cols > (1 << 24)) return fail(FWN_ERR_UNSUPPORTED, "n_cols %d > 2^24", n_cols);
-  if (!indptr || (!indices && n_rows > 0)) return fail(FWN_ERR_INVALID_ARGUMENT, "null CSR pointer");
+  // indices may be null when the mask has no entries (indptr all zero): it is only read at [indptr[r], indptr[r+1]).
+  if (!indptr) return fail(FWN_ERR_INVALID_ARGUMENT, "indptr is null");
   return FWN_OK;
 }
 

@@ -33,7 +33,8 @@ class AttnDesc(ctypes.Structure):
   _fields_ = [("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("n", ctypes.c_int32),
               ("head_dim", ctypes.c_int32), ("scale", ctypes.c_float), ("dtype", ctypes.c_int32),
               ("mode", ctypes.c_int32), ("reserved", ctypes.c_int32), ("stride_b", ctypes.c_int64),
-              ("stride_n", ctypes.c_int64), ("stride_h", ctypes.c_int64)]
+              ("stride_n", ctypes.c_int64), ("stride_h", ctypes.c_int64), ("out_stride_b", ctypes.c_int64),
+              ("out_stride_n", ctypes.c_int64), ("out_stride_h", ctypes.c_int64)]
 
 
 class TileList(ctypes.Structure):

@@ -222,13 +222,15 @@ def _mode_for(dtype: torch.dtype, precision: Optional[str], strict_fp32: bool) -
   return _lib.MODE_TF32
 
 
-def _desc(q: torch.Tensor, scale: float, mode: int) -> _lib.AttnDesc:
+def _desc(q: torch.Tensor, o: torch.Tensor, scale: float, mode: int) -> _lib.AttnDesc:
+  """q's strides for q, k, v; o's strides for o, d_o, dq, dk, dv."""
   b, n, h, d = q.shape
   sb, sn, sh, sd = q.stride()
-  if sd != 1:
+  ob, on, oh, od = o.stride()
+  if sd != 1 or od != 1:
     raise ValueError("head_dim must be contiguous")
   dt = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_F32
-  return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh)
+  return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh, ob, on, oh)
 
 
 def _same_layout(*ts):
@@ -247,8 +249,8 @@ def attention_forward(q, k, v, tiles: AttentionTiles, scale: float, mode: int, w
   """o [B, n, H, D] (q's dtype) and lse float32 [B, H, lse_rows] (or None)."""
   lib = _lib.lib()
   q, k, v = _canon(q, k, v)
-  o = torch.empty_like(q)
-  desc = _desc(q, scale, mode)
+  o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+  desc = _desc(q, o, scale, mode)
   lse = None
   if with_lse:
     b, n, h, _ = q.shape
@@ -262,12 +264,13 @@ def attention_forward(q, k, v, tiles: AttentionTiles, scale: float, mode: int, w
 def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float, mode: int):
   """(dq, dk, dv), each [B, n, H, D] in q's dtype."""
   lib = _lib.lib()
-  q, k, v, o, do = _canon(q, k, v, o, do)
-  desc = _desc(q, scale, mode)
+  q, k, v = _canon(q, k, v)
+  o, do = _canon(o.contiguous(), do.contiguous())
+  desc = _desc(q, o, scale, mode)
   ws_bytes = ctypes.c_size_t(0)
   _lib.check(lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)))
   ws = torch.empty(max(ws_bytes.value, 16), dtype=torch.uint8, device=q.device)
-  dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+  dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
   sf, sb = tiles.fwd.struct(), tiles.bwd.struct()
   _lib.check(lib.fwn_attn_bwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                               lse.data_ptr(), do.data_ptr(), ctypes.byref(sf), ctypes.byref(sb), dq.data_ptr(),

@@ -18,7 +18,8 @@
  *     (except fwn_device_error, which synchronises the stream to read the device error word).
  *   - Calls are stateless and may be issued concurrently on different streams.
  *   - Tensors q, k, v, o, d_o, dq, dk, dv use the reference's public layout [batch, n, heads, head_dim] with
- *     head_dim contiguous and arbitrary element strides for batch / node / head (multiples of 16 bytes).
+ *     head_dim contiguous and arbitrary element strides for batch / node / head (multiples of 16 bytes):
+ *     one set for the inputs q, k, v, one for o, d_o, dq, dk, dv.
  *   - lse is float32 [batch, heads, fwn_lse_rows(n)] (natural-log log-sum-exp of the scaled logits).
  *   - Tile lists follow build_tile_mask: block b owns tiles ptr[b]..ptr[b+1]-1 in ascending key-block
  *     order; tile t covers keys kb[t]*32 + [0, 32); bit j of bits[t*rows + r] allows (row b*rows + r,
@@ -68,9 +69,12 @@ typedef struct fwn_attn_desc {
   int32_t dtype;      /* fwn_dtype of q, k, v, o, d_o, dq, dk, dv */
   int32_t mode;       /* fwn_mode */
   int32_t reserved;
-  int64_t stride_b;   /* element strides of the [batch, n, heads, head_dim] tensors */
+  int64_t stride_b;   /* element strides of q, k, v ([batch, n, heads, head_dim], head_dim contiguous) */
   int64_t stride_n;
   int64_t stride_h;
+  int64_t out_stride_b; /* element strides of o, d_o, dq, dk, dv */
+  int64_t out_stride_n;
+  int64_t out_stride_h;
 } fwn_attn_desc;
 
 typedef struct fwn_tile_list {
