@@ -1,1 +1,462 @@
+// Backward kernels of the block-sparse masked flash attention (sm_100a, tcgen05 + TMA).
+//
+// Replaces _attention_bwd with _bwd_dq_kernel / _bwd_dkv_kernel (src/faster_weathernext/pallas_attn.py:
+// 161-215, 274-311). Same algorithm: delta = rowsum(O * dO) first; then P is recomputed tile by tile
+// from the forward's log-sum-exp, P = where(valid, exp(S - lse), 0), dS = P * (dP - delta), and
+//   dQ  = scale * sum dS K        per query block over the forward list      (kDKV = false)
+//   dK  = scale * sum dS^T Q,  dV = sum P^T dO
+//                                 per key block over the transposed list     (kDKV = true)
+// so every output row is owned by one CTA: no atomics, deterministic (as pallas_attn.py:297-311).
+//
+// One kernel template serves both: "rows" are the 128 rows of the work item (queries for dQ, keys for
+// dK/dV) held in shared memory for the whole item (R0, R1), "columns" are walked in chunks of CH
+// 32-wide tiles (C0, C1):
+//               dQ kernel           dK/dV kernel
+//   R0, R1      Q, dO               K, V
+//   C0, C1      K, V                Q, dO
+//   S  = R0 C0^T (TMEM)             dP = R1 C1^T (TMEM)
+//   acc0 += dS C0 (MN-major B)      acc1 += P C1 (dK/dV only)
+// Roles (192 threads): warp 0 TMA producer; warp 1 TMEM allocation + single-thread MMA issue; warps
+// 2-5 the elementwise stage (thread = row = TMEM lane) and the epilogue. S / dP of chunk c+1 are
+// issued before the accumulating MMAs of chunk c. tf32 operands read MN-major use a second copy of
+// the column tile with the 32-byte-atom swizzle (SWIZZLE_128B_BASE32B).
 #pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace fwn {
+
+struct BwdParams {
+  const int32_t* ptr2;
+  const int32_t* kb2;
+  const uint32_t* bits2;
+  const float* lse;    // [B, H, lse_rows] natural log
+  const float* delta;  // [B, H, lse_rows]
+  void* out0;          // dQ (dq kernel) or dK (dkv kernel)
+  void* out1;          // dV (dkv kernel)
+  int64_t o_sb, o_sn, o_sh;
+  int heads, n, np, lse_rows, n_items;
+  float scale;         // softmax scale (applied to acc0)
+  float scale_log2;    // scale * log2(e)
+};
+
+template <bool kDKV, int D, bool F32, int CH>
+struct BwdCfg {
+  static constexpr int ES = F32 ? 4 : 2;
+  static constexpr int EPB = 128 / ES;
+  static constexpr int CB = D / EPB;
+  static constexpr int ROWS = 128;
+  static constexpr int SUB = 32;
+  static constexpr int COLS = 32 * CH;       // columns per chunk
+  static constexpr int KSTEP = F32 ? 8 : 16;
+  static constexpr int NS = 2;
+  static constexpr int NMN = F32 ? (kDKV ? 2 : 1) : 0;  // extra MN-major copies of column tiles (tf32)
+  static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
+  static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
+  static constexpr int BITS_OFF = (2 + NMN) * C_BYTES;
+  static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (dK/dV)
+  static constexpr int STAGE_RAW = VEC_OFF + (kDKV ? CH * 256 : 0);
+  static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
+  static constexpr int PCB = COLS * ES / 128 > 0 ? COLS * ES / 128 : 1;  // 128-byte column blocks of dS / P
+  static constexpr int G_BYTES = ((COLS * ES + 127) / 128) * ROWS * 128; // one dS (or P) tile
+  static constexpr int NG = kDKV ? 2 : 1;              // tiles per buffer (dS; dS and P)
+  // dS / P buffers: one for the bf16 dK/dV kernel at head_dim 64 (keeps two CTAs per SM), else two.
+  static constexpr int NB = (kDKV && !F32 && D == 64) ? 1 : 2;
+  static constexpr int OFF_C = 2 * R_BYTES;
+  static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_G + NB * NG * G_BYTES;
+  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 * NB + 2 + 1;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
+  static constexpr int ACC0 = 128;
+  static constexpr int ACC1 = 128 + D;
+  static constexpr int TMEM_NEED = kDKV ? 128 + 2 * D : 128 + D;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
+  static constexpr int THREADS = 192;
+  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256) ? 2 : 1;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(COLS * ES % 128 == 0, "dS rows must fill 128-byte column blocks");
+};
+
+// delta[b, h, r] = sum_d O[b, r, h, d] * dO[b, r, h, d] (fp32); rows r in [n, lse_rows) get 0.
+template <bool F32, int D>
+__global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ o, const void* __restrict__ d_o,
+                                                    float* __restrict__ delta, int heads, int n, int lse_rows,
+                                                    int64_t sb, int64_t sn, int64_t sh, int total_rows) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= total_rows) return;
+  const int r = warp % lse_rows, bh = warp / lse_rows, h = bh % heads, b = bh / heads;
+  float acc = 0.f;
+  if (r < n) {
+    const int64_t off = static_cast<int64_t>(b) * sb + static_cast<int64_t>(r) * sn + static_cast<int64_t>(h) * sh;
+    if constexpr (F32) {
+      const float* po = static_cast<const float*>(o) + off;
+      const float* pd = static_cast<const float*>(d_o) + off;
+#pragma unroll
+      for (int i = lane * 2; i < D; i += 64) {
+        const float2 a = *reinterpret_cast<const float2*>(po + i), c = *reinterpret_cast<const float2*>(pd + i);
+        acc += a.x * c.x + a.y * c.y;
+      }
+    } else {
+      const __nv_bfloat16* po = static_cast<const __nv_bfloat16*>(o) + off;
+      const __nv_bfloat16* pd = static_cast<const __nv_bfloat16*>(d_o) + off;
+#pragma unroll
+      for (int i = lane * 2; i < D; i += 64) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + i));
+        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + i));
+        acc += a.x * c.x + a.y * c.y;
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+  }
+  if (lane == 0) delta[warp] = acc;
+}
+
+template <bool kDKV, int D, bool F32, int CH>
+__global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
+                    const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
+                    const __grid_constant__ CUtensorMap tm_c0mn, const __grid_constant__ CUtensorMap tm_c1mn,
+                    const BwdParams p) {
+  using C = BwdCfg<kDKV, D, F32, CH>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t r0_smem = sbase, r1_smem = sbase + C::R_BYTES;
+  auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };
+  auto g_tile = [&](int b, int which) { return sbase + C::OFF_G + (b * C::NG + which) * C::G_BYTES; };
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  const uint32_t r_full = bar0, r_empty = bar0 + 8;
+  auto c_full = [&](int s) { return bar0 + 16 + 8 * s; };
+  auto c_empty = [&](int s) { return bar0 + 16 + 8 * (C::NS + s); };
+  const uint32_t bar1 = bar0 + 16 + 16 * C::NS;
+  const uint32_t sd_full = bar1, sd_empty = bar1 + 8;
+  auto g_full = [&](int b) { return bar1 + 16 + 8 * b; };
+  auto g_empty = [&](int b) { return bar1 + 16 + 8 * (C::NB + b); };
+  const uint32_t bar2 = bar1 + 16 + 16 * C::NB;
+  const uint32_t acc_full = bar2, acc_empty = bar2 + 8, drain = bar2 + 16;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(r_full, 1);
+    mbar_init(r_empty, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(c_full(s), 1);
+      mbar_init(c_empty(s), 1);
+    }
+    mbar_init(sd_full, 1);
+    mbar_init(sd_empty, 4);
+    for (int b = 0; b < C::NB; ++b) {
+      mbar_init(g_full(b), 4);
+      mbar_init(g_empty(b), 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_r0);
+    tma_prefetch_desc(&tm_r1);
+    tma_prefetch_desc(&tm_c0);
+    tma_prefetch_desc(&tm_c1);
+    if (C::NMN >= 1) tma_prefetch_desc(&tm_c0mn);
+    if (C::NMN >= 2) tma_prefetch_desc(&tm_c1mn);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int per_bh = p.np;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      int pending_r = 0;
+      constexpr uint32_t kColBytes = C::SUB * D * C::ES;  // one 32-wide tile of one column operand
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + CH - 1) / CH;
+        if (nch == 0) continue;
+        if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(r_full, 2 * C::R_BYTES);
+        for (int cb = 0; cb < C::CB; ++cb) {
+          tma_load_4d(r0_smem + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+          tma_load_4d(r1_smem + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+        }
+        pending_r = 1;
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int st = g % C::NS;
+          if (!(ok = mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
+          const int n_in = min(CH, n_sub - CH * c);
+          const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + (kDKV ? 256 : 0);
+          mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
+          const uint32_t sb = stage(st);
+          for (int s = 0; s < n_in; ++s) {
+            const int t = t0 + CH * c + s;
+            const int col0 = p.kb2[t] * C::SUB;
+            for (int cb = 0; cb < C::CB; ++cb) {
+              const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
+              tma_load_4d(sb + off, &tm_c0, cb * C::EPB, h, col0, b, c_full(st));
+              tma_load_4d(sb + C::C_BYTES + off, &tm_c1, cb * C::EPB, h, col0, b, c_full(st));
+              if (C::NMN >= 1) tma_load_4d(sb + 2 * C::C_BYTES + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
+              if (C::NMN >= 2) tma_load_4d(sb + 3 * C::C_BYTES + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
+            }
+            bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
+            if (kDKV) {
+              const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col0;
+              bulk_load(sb + C::VEC_OFF + s * 256, p.lse + vo, 128, c_full(st));
+              bulk_load(sb + C::VEC_OFF + s * 256 + 128, p.delta + vo, 128, c_full(st));
+            }
+          }
+        }
+        ++qc;
+      }
+      if (!ok) {
+        volatile int never = 0;
+        for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
+          mbar_wait(c_full(k % C::NS), (k / C::NS) & 1, &never);
+        if (pending_r) mbar_wait(r_full, qc & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescAcc = instr_desc(F32, 128, D, false, true);
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + CH - 1) / CH;
+        if (nch == 0) continue;
+        if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
+        const uint32_t g0 = g;
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {
+            const uint32_t gg = g0 + c;
+            const int st = gg % C::NS;
+            const int n_in = min(CH, n_sub - CH * c);
+            if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
+            if (!(ok = mbar_wait(sd_empty, (gg & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
+            const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
+            const uint32_t sb = stage(st);
+#pragma unroll
+            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<F32>(tmem, smem_desc(r0_smem + cb * C::ROWS * 128 + within, 16, 1024),
+                          smem_desc(sb + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<F32>(tmem + 64, smem_desc(r1_smem + cb * C::ROWS * 128 + within, 16, 1024),
+                          smem_desc(sb + C::C_BYTES + cb * C::COLS * 128 + within, 16, 1024), idesc,
+                          kk > 0 ? 1u : 0u);
+            }
+            mma_commit(sd_full);
+            if (c == nch - 1) mma_commit(r_empty);
+          }
+          if (c >= 1) {
+            const uint32_t gg = g0 + c - 1;
+            const int st = gg % C::NS, gb = gg % C::NB;
+            const int n_in = min(CH, n_sub - CH * (c - 1));
+            if (!(ok = mbar_wait(g_full(gb), (gg / C::NB) & 1, abort_flag))) break;
+            if (c == 1 && !(ok = mbar_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
+            const uint32_t sb = stage(st);
+            // MN-major B operands: the K-major tile itself (bf16) or its 32-byte-atom copy (tf32).
+            const uint32_t b0 = F32 ? sb + 2 * C::C_BYTES : sb;
+            const uint32_t b1 = F32 ? sb + 3 * C::C_BYTES : sb + C::C_BYTES;
+            const int ksteps = n_in * C::SUB / C::KSTEP;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              const uint64_t a = smem_desc(g_tile(gb, 0) + cb * C::ROWS * 128 + within, 16, 1024);
+              const uint64_t bd = F32 ? smem_desc(b0 + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
+                                      : smem_desc(b0 + kk * C::KSTEP * 128, C::COLS * 128, 1024);
+              mma_ss<F32>(tmem + C::ACC0, a, bd, kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
+            }
+            if constexpr (kDKV) {
+              for (int kk = 0; kk < ksteps; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = smem_desc(g_tile(gb, 1) + cb * C::ROWS * 128 + within, 16, 1024);
+                const uint64_t bd = F32 ? smem_desc(b1 + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
+                                        : smem_desc(b1 + kk * C::KSTEP * 128, C::COLS * 128, 1024);
+                mma_ss<F32>(tmem + C::ACC1, a, bd, kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
+              }
+            }
+            mma_commit(g_empty(gb));
+            mma_commit(c_empty(st));
+            if (c == nch) mma_commit(acc_full);
+          }
+        }
+        g = g0 + nch;
+        ++qc;
+      }
+      mma_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    constexpr float kLog2e = 1.4426950408889634f;
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + CH - 1) / CH;
+      const int grow = pb * C::ROWS + row;
+      float lse2_row = 0.f, delta_row = 0.f;
+      if (!kDKV) {
+        lse2_row = p.lse[static_cast<size_t>(bh) * p.lse_rows + grow] * kLog2e;
+        delta_row = p.delta[static_cast<size_t>(bh) * p.lse_rows + grow];
+      }
+      const uint32_t g0 = g;
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t gg = g0 + c;
+        const int st = gg % C::NS, gb = gg % C::NB;
+        const int n_in = min(CH, n_sub - CH * c);
+        float s[C::COLS], dp[C::COLS];
+        if (!(ok = mbar_wait(sd_full, gg & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          if (j < n_in) {
+            tmem_ld32(trow + 32 * j, *reinterpret_cast<float(*)[32]>(&s[32 * j]));
+            tmem_ld32(trow + 64 + 32 * j, *reinterpret_cast<float(*)[32]>(&dp[32 * j]));
+          }
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sd_empty);
+        if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
+        const uint32_t sb = stage(st);
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          if (j < n_in) {
+            const uint32_t w = ld_shared_u32(sb + C::BITS_OFF + j * 512 + row * 4);
+            const uint32_t any = __reduce_or_sync(0xffffffffu, w);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float pv = 0.f, dsv = 0.f;
+              if ((any >> i) & 1u) {
+                float l2, dl;
+                if constexpr (kDKV) {
+                  l2 = ld_shared_f32(sb + C::VEC_OFF + j * 256 + i * 4) * kLog2e;
+                  dl = ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4);
+                } else {
+                  l2 = lse2_row;
+                  dl = delta_row;
+                }
+                const float e = ex2(fmaf(s[32 * j + i], p.scale_log2, -l2));
+                pv = ((w >> i) & 1u) ? e : 0.f;
+                dsv = pv * (dp[32 * j + i] - dl);
+              }
+              s[32 * j + i] = pv;
+              dp[32 * j + i] = dsv;
+            }
+          }
+        }
+        // dS (and P) -> shared memory buffer gb.
+        if (!(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
+#pragma unroll
+        for (int which = 0; which < C::NG; ++which) {
+          const float* src = which == 0 ? dp : s;
+          const uint32_t base = g_tile(gb, which);
+          if constexpr (!F32) {
+#pragma unroll
+            for (int cc = 0; cc < C::COLS / 8; ++cc) {
+              if (cc < 4 * n_in)
+                st_shared_v4(base + sw128_offset(row, cc), pack_bf16(src[8 * cc], src[8 * cc + 1]),
+                             pack_bf16(src[8 * cc + 2], src[8 * cc + 3]), pack_bf16(src[8 * cc + 4], src[8 * cc + 5]),
+                             pack_bf16(src[8 * cc + 6], src[8 * cc + 7]));
+            }
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < C::COLS / 4; ++cc) {
+              if (cc < 8 * n_in) {
+                const int blk = cc >> 3, ch = cc & 7;
+                st_shared_v4(base + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(src[4 * cc]),
+                             __float_as_uint(src[4 * cc + 1]), __float_as_uint(src[4 * cc + 2]),
+                             __float_as_uint(src[4 * cc + 3]));
+              }
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(g_full(gb));
+      }
+      if (!ok) break;
+      g = g0 + nch;
+      // ---------------------------------------------------------------- epilogue
+      const bool store = grow < p.n;
+      const int64_t roff = (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sn +
+                            static_cast<int64_t>(h) * p.o_sh) * C::ES;
+      uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.out0) + roff;
+      uint8_t* dst1 = kDKV ? reinterpret_cast<uint8_t*>(p.out1) + roff : nullptr;
+      if (nch == 0) {
+        if (store) {
+          for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst0)[i] = make_uint4(0, 0, 0, 0);
+          if (kDKV)
+            for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst1)[i] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      if (!(ok = mbar_wait(acc_full, qc & 1, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < (kDKV ? 2 : 1); ++which) {
+        uint8_t* dst = which == 0 ? dst0 : dst1;
+        const float mul = which == 0 ? p.scale : 1.f;
+        const uint32_t col = which == 0 ? C::ACC0 : C::ACC1;
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) {
+          float o[32];
+          tmem_ld32(trow + col + 32 * j, o);
+          tmem_wait_ld();
+          if (store) {
+            if constexpr (!F32) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                reinterpret_cast<uint4*>(dst + j * 64)[i] =
+                    make_uint4(pack_bf16(o[8 * i] * mul, o[8 * i + 1] * mul), pack_bf16(o[8 * i + 2] * mul, o[8 * i + 3] * mul),
+                               pack_bf16(o[8 * i + 4] * mul, o[8 * i + 5] * mul), pack_bf16(o[8 * i + 6] * mul, o[8 * i + 7] * mul));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                reinterpret_cast<float4*>(dst + j * 128)[i] =
+                    make_float4(o[4 * i] * mul, o[4 * i + 1] * mul, o[4 * i + 2] * mul, o[4 * i + 3] * mul);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      ++qc;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+}  // namespace fwn

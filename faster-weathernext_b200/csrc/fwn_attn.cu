@@ -177,6 +177,74 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   return ok();
 }
 
+template <bool kDKV, int D, bool F32, int CH>
+fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
+                           const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
+                           cudaStream_t stream) {
+  using C = fwn::BwdCfg<kDKV, D, F32, CH>;
+  CUtensorMap r0, r1, c0, c1, c0mn, c1mn;
+  fwn_status s;
+  // dq kernel: rows Q, dO; columns K, V.   dkv kernel: rows K, V; columns Q, dO.
+  const void* rp0 = kDKV ? k : q;
+  const void* rp1 = kDKV ? v : d_o;
+  const void* cp0 = kDKV ? q : k;
+  const void* cp1 = kDKV ? d_o : v;
+  const bool r1_out = !kDKV, c1_out = kDKV;
+  if ((s = make_map(&r0, rp0, d, C::ROWS)) != FWN_OK) return s;
+  if ((s = make_map(&r1, rp1, d, C::ROWS, false, r1_out)) != FWN_OK) return s;
+  if ((s = make_map(&c0, cp0, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&c1, cp1, d, C::SUB, false, c1_out)) != FWN_OK) return s;
+  c0mn = c0;
+  c1mn = c1;
+  if (F32) {
+    if ((s = make_map(&c0mn, cp0, d, C::SUB, true)) != FWN_OK) return s;
+    if ((s = make_map(&c1mn, cp1, d, C::SUB, true, c1_out)) != FWN_OK) return s;
+  }
+  fwn::BwdParams p{};
+  p.ptr2 = t.ptr;
+  p.kb2 = t.kb;
+  p.bits2 = t.bits;
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = out0;
+  p.out1 = out1;
+  p.o_sb = d.out_stride_b;
+  p.o_sn = d.out_stride_n;
+  p.o_sh = d.out_stride_h;
+  p.heads = d.heads;
+  p.n = d.n;
+  p.np = t.n_blocks;
+  p.lse_rows = fwn_lse_rows(d.n);
+  p.n_items = d.batch * d.heads * t.n_blocks;
+  p.scale = d.scale;
+  p.scale_log2 = d.scale * 1.4426950408889634f;
+  auto kernel = fwn::attn_bwd_kernel<kDKV, D, F32, CH>;
+  int grid = 0;
+  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, kDKV ? "attn_bwd dkv launch" : "attn_bwd dq launch");
+  return FWN_OK;
+}
+
+template <int D, bool F32>
+fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
+                      const float* lse, const void* d_o, const fwn_tile_list& t, const fwn_tile_list& tt, void* dq,
+                      void* dk, void* dv, float* delta, cudaStream_t stream) {
+  const int lse_rows = fwn_lse_rows(d.n);
+  const int total = d.batch * d.heads * lse_rows;
+  fwn::delta_kernel<F32, D><<<(total * 32 + 255) / 256, 256, 0, stream>>>(
+      o, d_o, delta, d.heads, d.n, lse_rows, d.out_stride_b, d.out_stride_n, d.out_stride_h, total);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "delta launch");
+  constexpr int CH = F32 ? 1 : 2;
+  fwn_status s = launch_bwd_pass<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, t, dq, nullptr, stream);
+  if (s != FWN_OK) return s;
+  s = launch_bwd_pass<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, tt, dk, dv, stream);
+  if (s != FWN_OK) return s;
+  return ok();
+}
+
 }  // namespace
 
 extern "C" {
@@ -308,11 +376,28 @@ fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes)
 fwn_status fwn_attn_bwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
                         const float* lse, const void* d_o, const fwn_tile_list* tiles, const fwn_tile_list* tiles_t,
                         void* dq, void* dk, void* dv, void* ws, size_t ws_bytes, void* stream) {
-  (void)q; (void)k; (void)v; (void)o; (void)lse; (void)d_o; (void)tiles; (void)tiles_t;
-  (void)dq; (void)dk; (void)dv; (void)ws; (void)ws_bytes; (void)stream;
   fwn_status s = check_desc(desc);
   if (s != FWN_OK) return s;
-  return fail(FWN_ERR_UNSUPPORTED, "backward not built yet");
+  if ((s = check_tiles(tiles, desc, "tiles")) != FWN_OK) return s;
+  if ((s = check_tiles(tiles_t, desc, "tiles_t")) != FWN_OK) return s;
+  if (!q || !k || !v || !o || !lse || !d_o || !dq || !dk || !dv)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(d_o) || !aligned16(dq) ||
+      !aligned16(dk) || !aligned16(dv) || !aligned16(lse))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  size_t need = 0;
+  fwn_attn_bwd_workspace_size(desc, &need);
+  if (!ws || ws_bytes < need || !aligned16(ws)) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed", need);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const fwn_attn_desc& d = *desc;
+  float* delta = static_cast<float*>(ws);
+  if (d.mode == FWN_MODE_BF16) {
+    if (d.head_dim == 64) return launch_bwd<64, false>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
+    return launch_bwd<128, false>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
+  }
+  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
+    return launch_bwd<64, true>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
+  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
 }
 
 }  // extern "C"

@@ -1,0 +1,137 @@
+"""GPU: backward kernels (delta, dQ over the forward list, dK/dV over the transposed list) against the
+oracle's analytic float64 gradient (tests/test_pallas_kernel.py:58-69) and the golden vectors.
+
+Tolerances: rel RMS <= 5e-3 in bf16 / TF32 (the stated bound for outputs and dQ/dK/dV), and for TF32
+the reference test's max-abs metric max|err| / max|ref| < 3e-2 (tests/test_pallas_kernel.py:98).
+"""
+import numpy as np
+import pytest
+import torch
+from scipy import sparse
+
+from oracle import attention as oa
+from tests.helpers import golden_mask, kernel_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"bf16": 5e-3, "tf32": 5e-3, "tf32x3": 2e-5}
+
+
+def _grads(q, k, v, do, mask, scale, mode, device, tiles=None):
+  from faster_weathernext import _lib
+  from faster_weathernext import tiled_attn as ta
+  dt = torch.bfloat16 if mode == "bf16" else torch.float32
+  if tiles is None:
+    tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  m = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[mode]
+  tq, tk, tv, tdo = (torch.from_numpy(x).to(device=device, dtype=dt) for x in (q, k, v, do))
+  o, lse = ta.attention_forward(tq, tk, tv, tiles, scale, m, with_lse=True)
+  dq, dk, dv = ta.attention_backward(tq, tk, tv, o, lse, tdo, tiles, scale, m)
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  return [x.float().cpu().numpy() for x in (dq, dk, dv)]
+
+
+def _rounded(mode, arrays):
+  return [oa.bf16_round(a) if mode == "bf16" else a for a in arrays]
+
+
+@pytest.mark.parametrize("mode", ["bf16", "tf32"])
+@pytest.mark.parametrize("symmetric", [True, False])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_grads_reference_test_case(golden, cuda, mode, symmetric, batch):
+  """tests/test_pallas_kernel.py:72-99: n=300 (padding rows), h=2, d=64, density 0.08, sym / non-sym."""
+  q, k, v, do = kernel_inputs(2, (1, 300, 2, 64), 4)
+  if batch == 2:
+    q2, k2, v2, do2 = kernel_inputs(12, (1, 300, 2, 64), 4)
+    q, k, v, do = (np.concatenate([a, b]) for a, b in zip((q, k, v, do), (q2, k2, v2, do2)))
+  m = golden_mask(golden["tiles"], "k_sym" if symmetric else "k_nonsym")
+  got = _grads(q, k, v, do, m, 0.125, mode, cuda)
+  ref = oa.sparse_attention_vjp(*_rounded(mode, (q, k, v, do)), m, 0.125)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL[mode], (name, oa.rel_rms(a, r))
+    assert oa.max_rel(a, r) < 3e-2, (name, oa.max_rel(a, r))
+  if mode == "tf32":
+    gold = golden["attention"]
+    ev = int(gold["every"])
+    tag = "sym" if symmetric else "nonsym"
+    for name, a in zip(("dq", "dk", "dv"), got):
+      assert oa.max_rel(a[0][::ev], gold[f"grad_{tag}/{name}"]) < 3e-2, name
+
+
+def test_nonsymmetric_mask_needs_transposed_tiles(golden, cuda):
+  """tests/test_pallas_kernel.py:102-118: reusing the forward list for dK/dV of a non-symmetric mask is wrong."""
+  from faster_weathernext import tiled_attn as ta
+  q, k, v, do = kernel_inputs(4, (1, 130, 1, 32), 4)
+  # head_dim 32 is not built: pad the head dimension with zeros (identical logits and outputs).
+  pad = lambda x: np.concatenate([x, np.zeros(x.shape[:-1] + (32,), np.float32)], -1)
+  q, k, v, do = (pad(x) for x in (q, k, v, do))
+  m = golden_mask(golden["tiles"], "k_guard")
+  scale = 32 ** -0.5
+  good = ta.AttentionTiles.from_mask(m, device=cuda)
+  wrong = ta.AttentionTiles(good.fwd, good.fwd, 130, True)
+  ref_dk = golden["attention"]["guard/dk"]
+  _, dk_good, _ = _grads(q, k, v, do, m, scale, "tf32", cuda, tiles=good)
+  _, dk_bad, _ = _grads(q, k, v, do, m, scale, "tf32", cuda, tiles=wrong)
+  assert oa.max_rel(dk_good[0][..., :32], ref_dk) < 3e-2
+  assert oa.max_rel(dk_bad[0][..., :32], ref_dk) > 1e-2
+
+
+@pytest.mark.parametrize("mode", ["bf16", "tf32"])
+def test_grads_config1(golden, cuda, mode):
+  """Configuration 1 VJP (upstream gradient from seed 1) against the reference's float64 gradient."""
+  from faster_weathernext import mesh
+  m, _, _ = mesh.config_mask(1)
+  rng = np.random.default_rng(0)
+  q, k, v = (rng.standard_normal((1, 642, 4, 64)).astype(np.float32) for _ in range(3))
+  do = np.random.default_rng(1).standard_normal((1, 642, 4, 64)).astype(np.float32)
+  got = _grads(q, k, v, do, m, 0.125, mode, cuda)
+  ref = oa.sparse_attention_vjp(*_rounded(mode, (q, k, v, do)), m, 0.125)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL[mode], (name, oa.rel_rms(a, r))
+  if mode == "tf32":
+    gold = golden["attention"]
+    for name, a in zip(("dq", "dk", "dv"), got):
+      assert oa.max_rel(a[0][::int(gold["every"])], gold[f"cfg1/{name}"]) < 3e-2, name
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_grads_bf16_odd_sizes_nonsymmetric(cuda, head_dim):
+  n = 457
+  m = sparse.random(n, n, density=0.05, random_state=11, format="csr").astype(bool)
+  m = (m + sparse.identity(n, dtype=bool)).tocsr()
+  q, k, v, do = kernel_inputs(6, (2, n, 3, head_dim), 4)
+  got = _grads(q, k, v, do, m, head_dim ** -0.5, "bf16", cuda)
+  ref = oa.sparse_attention_vjp(*_rounded("bf16", (q, k, v, do)), m, head_dim ** -0.5)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL["bf16"], (name, oa.rel_rms(a, r))
+
+
+@pytest.mark.parametrize("mode", ["bf16", "tf32"])
+def test_grads_full_size_config3(cuda, mode):
+  from faster_weathernext import mesh
+  m, _, _ = mesh.config_mask(3)
+  n = m.shape[0]
+  rng = np.random.default_rng(0)
+  q, k, v = (rng.standard_normal((1, n, 8, 64)).astype(np.float32) for _ in range(3))
+  do = np.random.default_rng(1).standard_normal((1, n, 8, 64)).astype(np.float32)
+  got = _grads(q, k, v, do, m, 0.125, mode, cuda)
+  ref = oa.sparse_attention_vjp(*_rounded(mode, (q, k, v, do)), m, 0.125)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL[mode], (name, oa.rel_rms(a, r))
+
+
+def test_autograd_matches_explicit_backward(cuda):
+  """torch.autograd through attention() (the custom-VJP analogue) gives the kernels' gradients."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  m, _, _ = mesh.config_mask(1)
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(0)
+  q, k, v, do = (torch.randn(1, 642, 4, 64, device=cuda, generator=g, dtype=torch.bfloat16) for _ in range(4))
+  qq, kk, vv = (x.clone().requires_grad_(True) for x in (q, k, v))
+  out = ta.attention(qq, kk, vv, tiles, scale=0.125)
+  out.backward(do)
+  ref = oa.sparse_attention_vjp(*(x.float().cpu().numpy() for x in (q, k, v, do)), m, 0.125)
+  for t, r in zip((qq.grad, kk.grad, vv.grad), ref):
+    assert oa.rel_rms(t.float().cpu().numpy(), r) < TOL["bf16"]
