@@ -1,0 +1,437 @@
+#!/usr/bin/env python
+"""Benchmark of the block-sparse masked flash attention (forward + custom-VJP backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--mode bf16|tf32]
+
+Metric: block-sparse attention useful TFLOP/s, forward + backward. Workload:
+configuration 3 — icosahedral mesh refined 6 times (40,962 nodes) in Morton order, great-circle mask
+<= 0.06 rad, batch 1 x 8 heads x head_dim 64 per GPU (one ensemble member per GPU: weak scaling,
+no inter-GPU communication). Useful FLOPs per step = 14 * B * H * nnz * D (forward 4, backward 10).
+
+One step = fwn_attn_fwd (with LSE) + fwn_attn_bwd (delta, dQ, dK/dV) over inputs already in HBM; three
+rotating input sets of 168 MB each keep every step's inputs out of the 126 MB L2. Under torchrun
+(N > 1) every rank runs its own member; the step time is the max over ranks.
+
+--impl reference times the reference's CPU path for this op — its XLA chunked attention
+(patch.py:106-162) with its autodiff backward, as the NumPy restatement in oracle/ (JAX is not
+installed) — on the host cores, each step a bounded sample of query chunks of the same workload.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "faster-weathernext_b200"), ROOT]
+
+import numpy as np  # noqa: E402
+
+METRIC = "block-sparse attn useful TFLOP/s fwd+bwd"
+UNIT = "TFLOP/s"
+CFG = 3
+# Kernel FLOP counts per allowed (query, key) pair per head and head_dim element: forward S and P V (4);
+# dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
+USEFUL_PER_PAIR = 14
+# DRAM bytes per launch of the dominant kernel at this workload from one ncu capture
+# (profiles/ncu_cfg3_bf16.md); None until captured for the current build.
+NCU_TRAFFIC = {}
+
+
+def peaks():
+  path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+  if os.path.exists(path):
+    with open(path) as f:
+      p = json.load(f)
+    return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+  return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+  """nvidia-smi clocks and throttle reasons sampled every 100 ms while running."""
+
+  FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+  def __init__(self, gpu_index):
+    self.gpu = gpu_index
+    self.proc = None
+    self.lines = []
+    self.t0 = self.t1 = None
+
+  def start(self):
+    try:
+      self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                    "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                   stderr=subprocess.DEVNULL, text=True)
+      threading.Thread(target=self._read, daemon=True).start()
+    except OSError:
+      self.proc = None
+
+  def _read(self):
+    for line in self.proc.stdout:
+      self.lines.append((time.time(), line.strip()))
+
+  def mark(self, which):
+    setattr(self, which, time.time())
+
+  def stop(self):
+    if self.proc is not None:
+      time.sleep(0.25)
+      self.proc.terminate()
+      try:
+        self.proc.wait(timeout=5)
+      except subprocess.TimeoutExpired:
+        self.proc.kill()
+
+  def summary(self):
+    rows = []
+    for t, line in self.lines:
+      parts = [x.strip() for x in line.split(",")]
+      if len(parts) < 9:
+        continue
+      try:
+        rows.append((t, float(parts[1]), float(parts[2]), parts[4:9]))
+      except ValueError:
+        continue
+    if not rows:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+    inside = [r for r in rows if self.t0 and self.t1 and self.t0 - 0.15 <= r[0] <= self.t1 + 0.15] or rows
+    names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for r in inside for i in range(1, 5) if "Active" in r[3][i]})
+    return {"sm_mhz": float(np.median([r[1] for r in inside])), "sm_max_mhz": max(r[2] for r in inside),
+            "reasons": reasons, "samples": len(inside)}
+
+
+def workload(device, seed, mode):
+  import torch
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  mask, _, _ = mesh.config_mask(CFG)
+  _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
+  n = mask.shape[0]
+  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  dt = torch.bfloat16 if mode == "bf16" else torch.float32
+  g = torch.Generator(device=device).manual_seed(seed)
+  sets = [[torch.randn(1, n, heads, head_dim, device=device, dtype=dt, generator=g) for _ in range(4)]
+          for _ in range(3)]
+  return mask, tiles, sets, heads, head_dim
+
+
+def kernel_costs(nnz, n, heads, head_dim, es, tiles):
+  """Algorithmic FLOPs and DRAM bytes per launch (one batch element)."""
+  t = heads * n * head_dim * es                 # one [1, n, H, D] tensor
+  vec = heads * ((n + 127) // 128 * 128) * 4     # one lse / delta vector set
+  fwd_list = 4 * (tiles.fwd.n_blocks + 1) + 4 * tiles.fwd.n_tiles + 512 * tiles.fwd.n_tiles
+  bwd_list = 4 * (tiles.bwd.n_blocks + 1) + 4 * tiles.bwd.n_tiles + 512 * tiles.bwd.n_tiles
+  pair = heads * nnz * head_dim
+  return {
+      "attn_fwd": (4 * pair, 3 * t + t + vec + fwd_list),
+      "attn_bwd_delta": (2 * heads * n * head_dim, 2 * t + vec),
+      "attn_bwd_dq": (6 * pair, 4 * t + 2 * vec + t + fwd_list),
+      "attn_bwd_dkv": (8 * pair, 4 * t + 2 * vec + 2 * t + bwd_list),
+  }
+
+
+def run_ours(args):
+  import torch
+  import torch.distributed as dist
+  from faster_weathernext import _lib
+  from faster_weathernext import tiled_attn as ta
+
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  torch.cuda.set_device(local)
+  device = torch.device("cuda", local)
+  if world > 1:
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+  mode = _lib.MODE_BF16 if args.mode == "bf16" else _lib.MODE_TF32
+  mask, tiles, sets, heads, head_dim = workload(device, 1000 + rank, args.mode)
+  n, nnz = mask.shape[0], mask.nnz
+  scale = head_dim ** -0.5
+  es = 2 if args.mode == "bf16" else 4
+  useful = USEFUL_PER_PAIR * heads * nnz * head_dim
+  stream = torch.cuda.current_stream()
+  lib = _lib.lib()
+
+  q0 = sets[0][0]
+  o_like = torch.empty_like(q0)
+  desc = ta._desc(q0, o_like, scale, mode)
+  lse_rows = lib.fwn_lse_rows(n)
+  outs = [dict(o=torch.empty_like(q0), lse=torch.empty(1, heads, lse_rows, device=device),
+               dq=torch.empty_like(q0), dk=torch.empty_like(q0), dv=torch.empty_like(q0)) for _ in sets]
+  ws_bytes = heads * lse_rows * 4
+  ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+  import ctypes
+  sf, sb = tiles.fwd.struct(), tiles.bwd.struct()
+  dref = ctypes.byref(desc)
+
+  def launch(i, events=None):
+    q, k, v, do = sets[i % 3]
+    ob = outs[i % 3]
+    s = stream.cuda_stream
+    calls = (
+        ("attn_fwd", lambda: lib.fwn_attn_fwd(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(), ctypes.byref(sf),
+                                              ob["o"].data_ptr(), ob["lse"].data_ptr(), s)),
+        ("attn_bwd_delta", lambda: lib.fwn_attn_bwd_delta(dref, ob["o"].data_ptr(), do.data_ptr(), ws.data_ptr(),
+                                                          ws_bytes, s)),
+        ("attn_bwd_dq", lambda: lib.fwn_attn_bwd_dq(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                    ob["lse"].data_ptr(), do.data_ptr(), ctypes.byref(sf),
+                                                    ob["dq"].data_ptr(), ws.data_ptr(), ws_bytes, s)),
+        ("attn_bwd_dkv", lambda: lib.fwn_attn_bwd_dkv(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                      ob["lse"].data_ptr(), do.data_ptr(), ctypes.byref(sb),
+                                                      ob["dk"].data_ptr(), ob["dv"].data_ptr(), ws.data_ptr(),
+                                                      ws_bytes, s)),
+    )
+    for name, fn in calls:
+      if events is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+      _lib.check(fn())
+      if events is not None:
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record(stream)
+        events.setdefault(name, []).append((e0, e1))
+    return len(calls)
+
+  def barrier():
+    torch.cuda.synchronize()
+    if world > 1:
+      dist.barrier()
+
+  def max_over_ranks(x):
+    if world == 1:
+      return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+  clocks = ClockSampler(local)
+  clocks.start()
+  for i in range(args.warmup):
+    launch(i)
+  barrier()
+  if _lib.device_error(stream.cuda_stream):
+    raise RuntimeError("device timeout during warm-up")
+  start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  clocks.mark("t0")
+  start.record(stream)
+  launches = 0
+  for i in range(args.steps):
+    launches += launch(i)
+  end.record(stream)
+  barrier()
+  clocks.mark("t1")
+  ms = max_over_ranks(start.elapsed_time(end)) / args.steps
+  clocks.stop()
+  value = world * useful / (ms * 1e-3) / 1e12
+
+  # Per-kernel durations (events on the launching stream around each C-ABI call), outside the timed region.
+  events = {}
+  barrier()
+  per_kernel_steps = min(args.steps, 200)
+  for i in range(per_kernel_steps):
+    launch(i, events)
+  barrier()
+  kernel_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in events.items()}
+  costs = kernel_costs(nnz, n, heads, head_dim, es, tiles)
+  hbm, tc, peak_kind = peaks()
+  kernels = {}
+  for k, ms_k in kernel_ms.items():
+    flops, nbytes = costs[k]
+    kernels[k] = {"ms": round(ms_k, 5), "useful_tflops": round(flops / (ms_k * 1e-3) / 1e12, 2),
+                  "algorithmic_gbs": round(nbytes / (ms_k * 1e-3) / 1e9, 1),
+                  "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm"}
+  dom = max(kernel_ms, key=kernel_ms.get)
+  flops, nbytes = costs[dom]
+  bound = kernels[dom]["bound"]
+  if bound == "hbm":
+    achieved = nbytes / (kernel_ms[dom] * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
+            "algorithmic_bytes": nbytes, "traffic": NCU_TRAFFIC.get(dom)}
+  else:
+    achieved = flops / (kernel_ms[dom] * 1e-3) / 1e12
+    roof = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 2), "peak": tc, "unit": "TFLOP/s",
+            "frac": round(achieved / tc, 4), "peak_source": peak_kind,
+            "algorithmic_flops": flops, "traffic": NCU_TRAFFIC.get(dom)}
+  # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile.
+  issued = 2 * heads * head_dim * 128 * 32 * (5 * tiles.fwd.n_tiles + 4 * tiles.bwd.n_tiles)
+
+  # End to end through the public API with host buffers: pinned H2D of q, k, v, dO, forward + backward
+  # through torch.autograd, D2H of o, dq, dk, dv, every step.
+  e2e = None
+  if not args.no_e2e:
+    dt = torch.bfloat16 if args.mode == "bf16" else torch.float32
+    host_in = [[x.cpu().pin_memory() for x in s] for s in sets[:2]]
+    host_out = [torch.empty(q0.shape, dtype=dt).pin_memory() for _ in range(4)]
+    e2e_steps = min(args.steps, 50)
+
+    def e2e_step(i):
+      hq, hk, hv, hdo = host_in[i % 2]
+      q, k, v = (x.to(device, non_blocking=True).requires_grad_(True) for x in (hq, hk, hv))
+      do = hdo.to(device, non_blocking=True)
+      o = ta.attention(q, k, v, tiles, scale=scale, precision=None)
+      dq, dk, dv = torch.autograd.grad(o, (q, k, v), do)
+      for dst, src in zip(host_out, (o, dq, dk, dv)):
+        dst.copy_(src.detach(), non_blocking=True)
+
+    for i in range(3):
+      e2e_step(i)
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(e2e_steps):
+      e2e_step(i)
+    b.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(a.elapsed_time(b)) / e2e_steps
+    tb = q0.numel() * q0.element_size()
+    e2e = {"value": round(world * useful / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
+           "h2d_bytes_per_step": 4 * tb, "d2h_bytes_per_step": 4 * tb}
+
+  cpu = None
+  if rank == 0 and world == 1 and not args.no_cpu:
+    cpu = cpu_baseline(mask, heads, head_dim, seconds=args.cpu_seconds)
+
+  if world > 1:
+    dist.barrier()
+  if rank == 0:
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": args.mode, "data": "synthetic: Q/K/V/dO ~ N(0,1) seeded per rank; "
+        "icosphere level-6 great-circle mask built on the host",
+        "config": {"workload": f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({nnz} pairs), "
+                               f"B1 H{heads} D{head_dim} per GPU", "global_batch": world, "nodes": n,
+                   "heads": heads, "head_dim": head_dim, "parallelism": f"replicas x{world} (no communication)",
+                   "l2": "inputs larger than L2: 3 rotating input sets of 168 MB"},
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+        "clocks": clocks.summary(), "kernels": kernels,
+        "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2),
+    }
+    print(json.dumps(line), flush=True)
+  if world > 1:
+    dist.destroy_process_group()
+
+
+def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None):
+  """The reference's CPU path (XLA chunked attention fwd + autodiff bwd, float32, NumPy/BLAS on all
+  host cores) timed on a bounded sample of query chunks; returned in useful TFLOP/s."""
+  from oracle import attention as oa
+  try:
+    from threadpoolctl import threadpool_info
+    cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count()])
+  except Exception:
+    cores = os.cpu_count()
+  n = mask.shape[0]
+  rng = np.random.default_rng(0)
+  q, k, v, do = (rng.standard_normal((1, n, heads, head_dim)).astype(np.float32) for _ in range(4))
+  path = oa.ChunkedPath(mask, 512, np.float32)
+  t = path.layout(q, k, v, do)
+  out = np.zeros_like(t["q"])
+  dq, dk, dv = np.zeros_like(t["q"]), np.zeros_like(t["k"]), np.zeros_like(t["v"])
+  rows_nnz = np.diff(mask.indptr)
+  order = [(7 * i + 3) % path.n_chunks for i in range(path.n_chunks)]
+  path.forward_chunk(t, order[0], head_dim ** -0.5, out)   # warm-up
+  done, flops, t0 = 0, 0, time.perf_counter()
+  while True:
+    c = order[done % len(order)]
+    path.forward_chunk(t, c, head_dim ** -0.5, out)
+    path.vjp_chunk(t, c, head_dim ** -0.5, dq, dk, dv)
+    flops += USEFUL_PER_PAIR * heads * head_dim * int(rows_nnz[c * 512:(c + 1) * 512].sum())
+    done += 1
+    el = time.perf_counter() - t0
+    if (steps is None and el > seconds) or (steps is not None and done >= steps):
+      break
+  return {"value": round(flops / el / 1e12, 6), "unit": UNIT, "cores": cores, "kind": "port",
+          "sample": f"{done} of {path.n_chunks} query chunks (512 queries, key window {path.window}) of cfg3, "
+                    f"fwd + bwd, float32, {el:.1f} s"}
+
+
+def run_reference(args):
+  """CPU reference arm: rank 0 only, the oracle's restatement of the reference XLA path on the host."""
+  rank = int(os.environ.get("RANK", "0"))
+  if rank != 0:
+    return
+  from faster_weathernext import mesh
+  from oracle import attention as oa
+  mask, _, _ = mesh.config_mask(CFG)
+  _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
+  n = mask.shape[0]
+  rng = np.random.default_rng(0)
+  q, k, v, do = (rng.standard_normal((1, n, heads, head_dim)).astype(np.float32) for _ in range(4))
+  path = oa.ChunkedPath(mask, 512, np.float32)
+  t = path.layout(q, k, v, do)
+  out = np.zeros_like(t["q"])
+  dq, dk, dv = np.zeros_like(t["q"]), np.zeros_like(t["k"]), np.zeros_like(t["v"])
+  rows_nnz = np.diff(mask.indptr)
+  scale = head_dim ** -0.5
+
+  # Each step is one query chunk, or a slice of its rows with the same key window, sized so that the
+  # whole --warmup W --steps K run takes about a minute and a half.
+  chunk_s = time.perf_counter()
+  path.forward_chunk(t, 3, scale, out)
+  path.vjp_chunk(t, 3, scale, dq, dk, dv)
+  chunk_s = time.perf_counter() - chunk_s
+  rows = int(np.clip(512 * 90.0 / max(args.steps + args.warmup, 1) / chunk_s, 8, 512)) // 8 * 8
+
+  def step(i):
+    c = (7 * i + 3) % path.n_chunks
+    path.forward_chunk(t, c, scale, out, 0, rows)
+    path.vjp_chunk(t, c, scale, dq, dk, dv, 0, rows)
+    return USEFUL_PER_PAIR * heads * head_dim * int(rows_nnz[c * 512:min(c * 512 + rows, n)].sum())
+
+  for i in range(args.warmup):
+    step(i)
+  t0 = time.perf_counter()
+  flops = sum(step(args.warmup + i) for i in range(args.steps))
+  el = time.perf_counter() - t0
+  value = flops / el / 1e12
+  try:
+    from threadpoolctl import threadpool_info
+    cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count()])
+  except Exception:
+    cores = os.cpu_count()
+  sample = (f"per step {rows} query rows of one of the {path.n_chunks} query chunks (key window {path.window}) "
+            "of cfg3, fwd + autodiff bwd, float32 NumPy/BLAS restatement of the XLA path (JAX absent)")
+  print(json.dumps({
+      "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": args.gpus,
+      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+      "data": "synthetic: Q/K/V/dO ~ N(0,1); icosphere level-6 great-circle mask",
+      "config": {"workload": f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({mask.nnz} pairs), "
+                             f"B1 H{heads} D{head_dim}", "nodes": n, "heads": heads, "head_dim": head_dim,
+                 "parallelism": "host CPU"},
+      "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+      "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+  }), flush=True)
+
+
+def main():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=2000)
+  ap.add_argument("--warmup", type=int, default=20)
+  ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+  ap.add_argument("--mode", choices=["bf16", "tf32"], default="bf16")
+  ap.add_argument("--no-e2e", action="store_true")
+  ap.add_argument("--no-cpu", action="store_true")
+  ap.add_argument("--cpu-seconds", type=float, default=15.0)
+  args = ap.parse_args()
+  if args.warmup < 3:
+    ap.error("--warmup must be >= 3")
+  if args.impl == "reference":
+    run_reference(args)
+  else:
+    run_ours(args)
+
+
+if __name__ == "__main__":
+  main()

@@ -228,22 +228,36 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
 }
 
 template <int D, bool F32>
-fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
-                      const float* lse, const void* d_o, const fwn_tile_list& t, const fwn_tile_list& tt, void* dq,
-                      void* dk, void* dv, float* delta, cudaStream_t stream) {
+fwn_status launch_delta(const fwn_attn_desc& d, const void* o, const void* d_o, float* delta, cudaStream_t stream) {
   const int lse_rows = fwn_lse_rows(d.n);
   const int total = d.batch * d.heads * lse_rows;
   fwn::delta_kernel<F32, D><<<(total * 32 + 255) / 256, 256, 0, stream>>>(
       o, d_o, delta, d.heads, d.n, lse_rows, d.out_stride_b, d.out_stride_n, d.out_stride_h, total);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "delta launch");
+  return FWN_OK;
+}
+
+// Which backward launches to issue.
+enum BwdParts { kDelta = 1, kDq = 2, kDkv = 4, kAll = 7 };
+
+template <int D, bool F32>
+fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
+                      const float* lse, const void* d_o, const fwn_tile_list* t, const fwn_tile_list* tt, void* dq,
+                      void* dk, void* dv, float* delta, int parts, cudaStream_t stream) {
   constexpr int CH = F32 ? 1 : 2;
-  fwn_status s = launch_bwd_pass<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, t, dq, nullptr, stream);
-  if (s != FWN_OK) return s;
-  s = launch_bwd_pass<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, tt, dk, dv, stream);
-  if (s != FWN_OK) return s;
+  fwn_status s;
+  if ((parts & kDelta) && (s = launch_delta<D, F32>(d, o, d_o, delta, stream)) != FWN_OK) return s;
+  if ((parts & kDq) && (s = launch_bwd_pass<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
+    return s;
+  if ((parts & kDkv) && (s = launch_bwd_pass<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) != FWN_OK)
+    return s;
   return ok();
 }
+
+fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
+                        const float* lse, const void* d_o, const fwn_tile_list* tiles, const fwn_tile_list* tiles_t,
+                        void* dq, void* dk, void* dv, const void* ws, size_t ws_bytes, int parts, void* stream);
 
 }  // namespace
 
@@ -376,28 +390,60 @@ fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes)
 fwn_status fwn_attn_bwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
                         const float* lse, const void* d_o, const fwn_tile_list* tiles, const fwn_tile_list* tiles_t,
                         void* dq, void* dk, void* dv, void* ws, size_t ws_bytes, void* stream) {
-  fwn_status s = check_desc(desc);
-  if (s != FWN_OK) return s;
-  if ((s = check_tiles(tiles, desc, "tiles")) != FWN_OK) return s;
-  if ((s = check_tiles(tiles_t, desc, "tiles_t")) != FWN_OK) return s;
-  if (!q || !k || !v || !o || !lse || !d_o || !dq || !dk || !dv)
-    return fail(FWN_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(d_o) || !aligned16(dq) ||
-      !aligned16(dk) || !aligned16(dv) || !aligned16(lse))
-    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
-  size_t need = 0;
-  fwn_attn_bwd_workspace_size(desc, &need);
-  if (!ws || ws_bytes < need || !aligned16(ws)) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed", need);
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const fwn_attn_desc& d = *desc;
-  float* delta = static_cast<float*>(ws);
-  if (d.mode == FWN_MODE_BF16) {
-    if (d.head_dim == 64) return launch_bwd<64, false>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
-    return launch_bwd<128, false>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
-  }
-  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
-    return launch_bwd<64, true>(d, q, k, v, o, lse, d_o, *tiles, *tiles_t, dq, dk, dv, delta, st);
-  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
+  return bwd_dispatch(desc, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, ws, ws_bytes, kAll, stream);
+}
+
+fwn_status fwn_attn_bwd_delta(const fwn_attn_desc* desc, const void* o, const void* d_o, void* ws, size_t ws_bytes,
+                              void* stream) {
+  return bwd_dispatch(desc, nullptr, nullptr, nullptr, o, nullptr, d_o, nullptr, nullptr, nullptr, nullptr, nullptr, ws,
+                      ws_bytes, kDelta, stream);
+}
+
+fwn_status fwn_attn_bwd_dq(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const float* lse,
+                           const void* d_o, const fwn_tile_list* tiles, void* dq, const void* ws, size_t ws_bytes,
+                           void* stream) {
+  return bwd_dispatch(desc, q, k, v, nullptr, lse, d_o, tiles, nullptr, dq, nullptr, nullptr, ws, ws_bytes, kDq, stream);
+}
+
+fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const float* lse,
+                            const void* d_o, const fwn_tile_list* tiles_t, void* dk, void* dv, const void* ws,
+                            size_t ws_bytes, void* stream) {
+  return bwd_dispatch(desc, q, k, v, nullptr, lse, d_o, nullptr, tiles_t, nullptr, dk, dv, ws, ws_bytes, kDkv, stream);
 }
 
 }  // extern "C"
+
+namespace {
+
+fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
+                        const float* lse, const void* d_o, const fwn_tile_list* tiles, const fwn_tile_list* tiles_t,
+                        void* dq, void* dk, void* dv, const void* ws, size_t ws_bytes, int parts, void* stream) {
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  if ((parts & kDq) && (s = check_tiles(tiles, desc, "tiles")) != FWN_OK) return s;
+  if ((parts & kDkv) && (s = check_tiles(tiles_t, desc, "tiles_t")) != FWN_OK) return s;
+  const void* need_ptrs[] = {(parts & kDelta) ? o : d_o, d_o, (parts & (kDq | kDkv)) ? q : d_o,
+                             (parts & (kDq | kDkv)) ? k : d_o, (parts & (kDq | kDkv)) ? v : d_o,
+                             (parts & (kDq | kDkv)) ? static_cast<const void*>(lse) : d_o, (parts & kDq) ? dq : d_o,
+                             (parts & kDkv) ? dk : d_o, (parts & kDkv) ? dv : d_o};
+  for (const void* ptr : need_ptrs) {
+    if (!ptr) return fail(FWN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(ptr)) return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  }
+  size_t need = 0;
+  fwn_attn_bwd_workspace_size(desc, &need);
+  if (!ws || ws_bytes < need || !aligned16(ws))
+    return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed", need);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const fwn_attn_desc& d = *desc;
+  float* delta = static_cast<float*>(const_cast<void*>(ws));
+  if (d.mode == FWN_MODE_BF16) {
+    if (d.head_dim == 64) return launch_bwd<64, false>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
+    return launch_bwd<128, false>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
+  }
+  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
+    return launch_bwd<64, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
+  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
+}
+
+}  // namespace

@@ -149,6 +149,19 @@ FWN_API fwn_status fwn_attn_bwd(const fwn_attn_desc* desc, const void* q, const 
                         const fwn_tile_list* tiles_t, void* dq, void* dk, void* dv, void* ws,
                         size_t ws_bytes, void* stream);
 
+/* The three launches of fwn_attn_bwd, one by one (same arguments; ws holds delta between them):
+ *   fwn_attn_bwd_delta  delta = rowsum(o * d_o)                      <- pallas_attn.py:278 (XLA reduction)
+ *   fwn_attn_bwd_dq     dq over `tiles`                              <- _bwd_dq_kernel, pallas_attn.py:161-184, 286-295
+ *   fwn_attn_bwd_dkv    dk, dv over `tiles_t`                        <- _bwd_dkv_kernel, pallas_attn.py:187-215, 297-311 */
+FWN_API fwn_status fwn_attn_bwd_delta(const fwn_attn_desc* desc, const void* o, const void* d_o, void* ws,
+                                      size_t ws_bytes, void* stream);
+FWN_API fwn_status fwn_attn_bwd_dq(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                                   const float* lse, const void* d_o, const fwn_tile_list* tiles, void* dq,
+                                   const void* ws, size_t ws_bytes, void* stream);
+FWN_API fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                                    const float* lse, const void* d_o, const fwn_tile_list* tiles_t, void* dk,
+                                    void* dv, const void* ws, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,9 +3,10 @@
 Tensors use the reference's public layout [batch, n, heads, head_dim]; the mask is a boolean
 [n, n] matrix with mask[query, key].
 
-  chunked_attention    — the reference's XLA attention path, patch.py:130-162 (per chunk of queries:
+  ChunkedPath / chunked_attention / chunked_attention_vjp
+                       — the reference's XLA attention path, patch.py:130-162 (per chunk of queries:
                          einsum over the chunk's key window * scale, where(mask, ., -1e30), softmax
-                         upcast to float32, einsum with V), in float32 or float64.
+                         upcast to float32, einsum with V) and its autodiff, in float32 or float64.
   sparse_attention     — the same masked softmax evaluated only on allowed pairs (masked pairs get
                          weight exp(-1e30 - max) == 0 exactly), float64, with the forward's
                          log-sum-exp lse = m + log(max(l, 1e-30)) (pallas_attn.py:138-140).
@@ -42,37 +43,82 @@ def _softmax_lastaxis(x):
   return e / e.sum(-1, keepdims=True)
 
 
-def chunked_attention(q, k, v, mask, scale, chunk=512, dtype=np.float32, chunks=None):
-  """The XLA chunked path (patch.py:130-162). Returns [B, n, H, D] in `dtype`.
+class ChunkedPath:
+  """The reference's XLA chunked attention path (patch.py:106-162) on the CPU, split into the layout
+  step (pad to whole chunks / the key window, head-major copies; patch.py:137-142) and the per-chunk
+  work (patch.py:144-152 and its autodiff), so a bounded sample of chunks can be timed."""
 
-  `chunks` (optional iterable of chunk indices) evaluates only those query chunks (rows of other
-  chunks are left zero) — used to time a bounded sample of a large workload.
-  """
-  starts, packed, window, n_kv = build_chunked_mask(mask, chunk)
-  b, n, h, d = q.shape
-  nc = len(starts)
-  qp = np.zeros((b, nc * chunk, h, d), dtype)
-  qp[:, :n] = q
-  kp = np.zeros((b, n_kv, h, d), dtype)
-  vp = np.zeros((b, n_kv, h, d), dtype)
-  kp[:, :n] = k
-  vp[:, :n] = v
-  out = np.zeros((b, nc * chunk, h, d), dtype)
-  # Head-major copies so each chunk is a batched matmul.
-  qh = np.ascontiguousarray(qp.transpose(0, 2, 1, 3))
-  kh = np.ascontiguousarray(kp.transpose(0, 2, 1, 3))
-  vh = np.ascontiguousarray(vp.transpose(0, 2, 1, 3))
-  for c in (range(nc) if chunks is None else chunks):
-    s0 = int(starts[c])
-    qc = qh[:, :, c * chunk:(c + 1) * chunk]                       # [B, H, chunk, D]
-    kc = kh[:, :, s0:s0 + window]
-    vc = vh[:, :, s0:s0 + window]
-    logits = np.matmul(qc, kc.transpose(0, 1, 3, 2)) * dtype(scale)  # [B, H, chunk, W]
-    m = np.unpackbits(packed[c], axis=-1, count=window, bitorder="little").astype(bool)
-    logits = np.where(m[None, None], logits, dtype(MASK_VALUE))
-    w = _softmax_lastaxis(logits.astype(np.float32) if dtype != np.float64 else logits).astype(dtype)
-    out[:, c * chunk:(c + 1) * chunk] = np.matmul(w, vc).transpose(0, 2, 1, 3)
-  return out[:, :n]
+  def __init__(self, mask, chunk=512, dtype=np.float32):
+    self.starts, self.packed, self.window, self.n_kv = build_chunked_mask(mask, chunk)
+    self.chunk, self.dtype = chunk, dtype
+    self.n = mask.shape[0]
+    self.n_chunks = len(self.starts)
+
+  def layout(self, q, k, v, do=None):
+    b, n, h, d = q.shape
+    def head_major(x, rows):
+      out = np.zeros((b, h, rows, d), self.dtype)
+      out[:, :, :n] = np.asarray(x, self.dtype).transpose(0, 2, 1, 3)
+      return out
+    rows_q = self.n_chunks * self.chunk
+    t = {"q": head_major(q, rows_q), "k": head_major(k, self.n_kv), "v": head_major(v, self.n_kv)}
+    if do is not None:
+      t["do"] = head_major(do, rows_q)
+    return t
+
+  def _probs(self, t, c, scale, r0=0, r1=None):
+    s0 = int(self.starts[c])
+    rows = slice(c * self.chunk + r0, c * self.chunk + (self.chunk if r1 is None else r1))
+    keys = slice(s0, s0 + self.window)
+    qc, kc, vc = t["q"][:, :, rows], t["k"][:, :, keys], t["v"][:, :, keys]
+    logits = np.matmul(qc, kc.transpose(0, 1, 3, 2)) * self.dtype(scale)
+    m = np.unpackbits(self.packed[c], axis=-1, count=self.window, bitorder="little").astype(bool)
+    m = m[r0:self.chunk if r1 is None else r1]
+    logits = np.where(m[None, None], logits, self.dtype(MASK_VALUE))
+    # wrap_fn_for_upcast_downcast: the softmax runs in float32 at least.
+    p = _softmax_lastaxis(logits.astype(np.float32) if self.dtype != np.float64 else logits).astype(self.dtype)
+    return rows, keys, p
+
+  def forward_chunk(self, t, c, scale, out, r0=0, r1=None):
+    """Chunk c (optionally only its query rows [r0, r1)): out[rows] = softmax(mask(q k^T)) v."""
+    rows, keys, p = self._probs(t, c, scale, r0, r1)
+    out[:, :, rows] = np.matmul(p, t["v"][:, :, keys])
+
+  def vjp_chunk(self, t, c, scale, dq, dk, dv, r0=0, r1=None):
+    """Autodiff of one chunk (or its rows [r0, r1)): dP = dO V^T, dS = P (dP - rowsum(dP P)), then dQ, dK, dV."""
+    rows, keys, p = self._probs(t, c, scale, r0, r1)
+    sc = self.dtype(scale)
+    gc, qc = t["do"][:, :, rows], t["q"][:, :, rows]
+    kc, vc = t["k"][:, :, keys], t["v"][:, :, keys]
+    dp = np.matmul(gc, vc.transpose(0, 1, 3, 2))
+    ds = p * (dp - (dp * p).sum(-1, keepdims=True))
+    dq[:, :, rows] = np.matmul(ds, kc) * sc
+    dk[:, :, keys] += np.matmul(ds.transpose(0, 1, 3, 2), qc) * sc
+    dv[:, :, keys] += np.matmul(p.transpose(0, 1, 3, 2), gc)
+
+  def back(self, x):
+    return x[:, :, :self.n].transpose(0, 2, 1, 3)
+
+
+def chunked_attention(q, k, v, mask, scale, chunk=512, dtype=np.float32, chunks=None):
+  """The XLA chunked path's forward (patch.py:130-162). Returns [B, n, H, D] in `dtype`;
+  `chunks` evaluates only those query chunks (rows of other chunks stay zero)."""
+  path = ChunkedPath(mask, chunk, dtype)
+  t = path.layout(q, k, v)
+  out = np.zeros_like(t["q"])
+  for c in (range(path.n_chunks) if chunks is None else chunks):
+    path.forward_chunk(t, c, scale, out)
+  return path.back(out)
+
+
+def chunked_attention_vjp(q, k, v, do, mask, scale, chunk=512, dtype=np.float32, chunks=None):
+  """dQ, dK, dV of the XLA chunked path (JAX autodiff of patch.py:144-159). Returns [B, n, H, D] arrays."""
+  path = ChunkedPath(mask, chunk, dtype)
+  t = path.layout(q, k, v, do)
+  dq, dk, dv = np.zeros_like(t["q"]), np.zeros_like(t["k"]), np.zeros_like(t["v"])
+  for c in (range(path.n_chunks) if chunks is None else chunks):
+    path.vjp_chunk(t, c, scale, dq, dk, dv)
+  return path.back(dq), path.back(dk), path.back(dv)
 
 
 def _pairs(mask):

@@ -137,3 +137,14 @@ def test_config1_golden(golden):
   np.testing.assert_allclose(out[0][::ev], a["cfg1/out"], rtol=1e-5, atol=1e-6)
   for nm, x in zip(("dq", "dk", "dv"), oa.sparse_attention_vjp(q, k, v, do, m, 0.125)):
     np.testing.assert_allclose(x[0][::ev], a[f"cfg1/{nm}"], rtol=1e-5, atol=1e-6, err_msg=nm)
+
+
+def test_chunked_vjp_matches_analytic_gradient(golden):
+  """The XLA-path backward restatement (autodiff of patch.py:144-159) equals the reference tests' gradient."""
+  a = golden["attention"]
+  ev = int(a["every"])
+  m = golden_mask(golden["tiles"], "k_sym")
+  q, k, v, do = kernel_inputs(2, (1, 300, 2, 64), 4)
+  got = oa.chunked_attention_vjp(q, k, v, do, m, 0.125, chunk=64, dtype=np.float64)
+  for nm, x in zip(("dq", "dk", "dv"), got):
+    np.testing.assert_allclose(x[0][::ev], a[f"grad_sym/{nm}"], rtol=1e-5, atol=1e-6, err_msg=nm)
