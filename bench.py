@@ -103,7 +103,7 @@ class ClockSampler:
       return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
     inside = [r for r in rows if self.t0 and self.t1 and self.t0 - 0.15 <= r[0] <= self.t1 + 0.15] or rows
     names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    reasons = sorted({names[i] for r in inside for i in range(1, 5) if "Active" in r[3][i]})
+    reasons = sorted({names[i] for r in inside for i in range(1, 5) if r[3][i].strip() == "Active"})
     return {"sm_mhz": float(np.median([r[1] for r in inside])), "sm_max_mhz": max(r[2] for r in inside),
             "reasons": reasons, "samples": len(inside)}
 
@@ -123,12 +123,12 @@ def workload(device, seed, mode):
   return mask, tiles, sets, heads, head_dim
 
 
-def kernel_costs(nnz, n, heads, head_dim, es, tiles):
-  """Algorithmic FLOPs and DRAM bytes per launch (one batch element)."""
+def kernel_costs(nnz, n, heads, head_dim, es, lf, lb):
+  """Algorithmic FLOPs and DRAM bytes per launch (one batch element); lf / lb the lists walked."""
   t = heads * n * head_dim * es                 # one [1, n, H, D] tensor
   vec = heads * ((n + 127) // 128 * 128) * 4     # one lse / delta vector set
-  fwd_list = 4 * (tiles.fwd.n_blocks + 1) + 4 * tiles.fwd.n_tiles + 512 * tiles.fwd.n_tiles
-  bwd_list = 4 * (tiles.bwd.n_blocks + 1) + 4 * tiles.bwd.n_tiles + 512 * tiles.bwd.n_tiles
+  size = lambda l: 4 * (l.n_blocks + 1) + (128 if l.cols is not None else 4) * l.n_tiles + 512 * l.n_tiles
+  fwd_list, bwd_list = size(lf), size(lb)
   pair = heads * nnz * head_dim
   return {
       "attn_fwd": (4 * pair, 3 * t + t + vec + fwd_list),
@@ -169,7 +169,8 @@ def run_ours(args):
   ws_bytes = heads * lse_rows * 4
   ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
   import ctypes
-  sf, sb = tiles.fwd.struct(), tiles.bwd.struct()
+  lf, lb = (tiles.fwd_g, tiles.bwd_g) if args.lists == "gathered" else (tiles.fwd, tiles.bwd)
+  sf, sb = lf.struct(), lb.struct()
   dref = ctypes.byref(desc)
 
   def launch(i, events=None):
@@ -240,7 +241,7 @@ def run_ours(args):
     launch(i, events)
   barrier()
   kernel_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in events.items()}
-  costs = kernel_costs(nnz, n, heads, head_dim, es, tiles)
+  costs = kernel_costs(nnz, n, heads, head_dim, es, lf, lb)
   hbm, tc, peak_kind = peaks()
   kernels = {}
   for k, ms_k in kernel_ms.items():
@@ -262,7 +263,7 @@ def run_ours(args):
             "frac": round(achieved / tc, 4), "peak_source": peak_kind,
             "algorithmic_flops": flops, "traffic": NCU_TRAFFIC.get(dom)}
   # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile.
-  issued = 2 * heads * head_dim * 128 * 32 * (5 * tiles.fwd.n_tiles + 4 * tiles.bwd.n_tiles)
+  issued = 2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + 4 * lb.n_tiles)
 
   # End to end through the public API with host buffers: pinned H2D of q, k, v, dO, forward + backward
   # through torch.autograd, D2H of o, dq, dk, dv, every step.
@@ -311,7 +312,7 @@ def run_ours(args):
         "config": {"workload": f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({nnz} pairs), "
                                f"B1 H{heads} D{head_dim} per GPU", "global_batch": world, "nodes": n,
                    "heads": heads, "head_dim": head_dim, "parallelism": f"replicas x{world} (no communication)",
-                   "l2": "inputs larger than L2: 3 rotating input sets of 168 MB"},
+                   "l2": "inputs larger than L2: 3 rotating input sets of 168 MB", "tile_lists": args.lists},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
         "clocks": clocks.summary(), "kernels": kernels,
         "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2),
@@ -421,6 +422,8 @@ def main():
   ap.add_argument("--warmup", type=int, default=20)
   ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
   ap.add_argument("--mode", choices=["bf16", "tf32"], default="bf16")
+  ap.add_argument("--lists", choices=["gathered", "paired"], default="gathered",
+                  help="tile lists the kernels walk: gathered (distinct keys per block) or paired 32-key tiles")
   ap.add_argument("--no-e2e", action="store_true")
   ap.add_argument("--no-cpu", action="store_true")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)

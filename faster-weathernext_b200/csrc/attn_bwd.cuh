@@ -30,8 +30,10 @@ namespace fwn {
 
 struct BwdParams {
   const int32_t* ptr2;
-  const int32_t* kb2;
+  const int32_t* kb2;     // tile mode: column block of each tile
+  const int32_t* cols;    // gathered mode: column of each slot [T * 32]
   const uint32_t* bits2;
+  int head_major;         // gathered mode: rows of the 2D column-operand views are (b, h, node)
   const float* lse;    // [B, H, lse_rows] natural log
   const float* delta;  // [B, H, lse_rows]
   void* out0;          // dQ (dq kernel) or dK (dkv kernel)
@@ -75,6 +77,7 @@ struct BwdCfg {
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int THREADS = 192;
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256) ? 2 : 1;
+  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 255;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(COLS * ES % 128 == 0, "dS rows must fill 128-byte column blocks");
 };
@@ -114,8 +117,8 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ o, 
   if (lane == 0) delta[warp] = acc;
 }
 
-template <bool kDKV, int D, bool F32, int CH>
-__global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
+template <bool kDKV, int D, bool F32, int CH, bool GATHER>
+__global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MAX_REGS))
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
                     const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
                     const __grid_constant__ CUtensorMap tm_c0mn, const __grid_constant__ CUtensorMap tm_c1mn,
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
-      mbar_init(c_full(s), 1);
+      mbar_init(c_full(s), (GATHER && kDKV) ? 2 : 1);
       mbar_init(c_empty(s), 1);
     }
     mbar_init(sd_full, 1);
@@ -176,33 +179,62 @@ __global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
   const int per_bh = p.np;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t g = 0, qc = 0;
-      bool ok = true;
-      int pending_r = 0;
-      constexpr uint32_t kColBytes = C::SUB * D * C::ES;  // one 32-wide tile of one column operand
-      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-        const int nch = (n_sub + CH - 1) / CH;
-        if (nch == 0) continue;
-        if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+    // ------------------------------------------------------------------ TMA producer (whole warp)
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    int pending_r = 0;
+    constexpr uint32_t kColBytes = C::SUB * D * C::ES;  // one 32-wide tile of one column operand
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + CH - 1) / CH;
+      if (nch == 0) continue;
+      if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+      if (lane == 0) {
         mbar_arrive_expect_tx(r_full, 2 * C::R_BYTES);
         for (int cb = 0; cb < C::CB; ++cb) {
           tma_load_4d(r0_smem + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
           tma_load_4d(r1_smem + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
         }
-        pending_r = 1;
-        for (int c = 0; c < nch; ++c, ++g) {
-          const int st = g % C::NS;
-          if (!(ok = mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
-          const int n_in = min(CH, n_sub - CH * c);
-          const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + (kDKV ? 256 : 0);
-          mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
-          const uint32_t sb = stage(st);
-          for (int s = 0; s < n_in; ++s) {
-            const int t = t0 + CH * c + s;
+      }
+      pending_r = 1;
+      const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
+      const int row_mul = p.head_major ? 1 : p.heads;
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
+        const int n_in = min(CH, n_sub - CH * c);
+        // Gathered dK/dV: lse / delta of the gathered queries are stored by the lanes, not copied.
+        const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + ((kDKV && !GATHER) ? 256 : 0);
+        if (lane == 0) mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
+        __syncwarp();
+        const uint32_t sb = stage(st);
+        for (int s = 0; s < n_in; ++s) {
+          const int t = t0 + CH * c + s;
+          if constexpr (GATHER) {
+            const int col = p.cols[static_cast<size_t>(t) * 32 + lane];
+            const int row = col * row_mul + row_base;
+            const int j = lane & 7, which = lane >> 3;  // which: 0 C0, 1 C1, 2 C0 (MN copy), 3 C1 (MN copy)
+            const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
+            const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
+            if (which < 2 + C::NMN) {
+              const void* tm = which == 0 ? static_cast<const void*>(&tm_c0)
+                               : which == 1 ? static_cast<const void*>(&tm_c1)
+                               : which == 2 ? static_cast<const void*>(&tm_c0mn)
+                                            : static_cast<const void*>(&tm_c1mn);
+              const uint32_t dst = sb + which * C::C_BYTES + s * C::SUB * 128 + j * 512;
+              for (int cb = 0; cb < C::CB; ++cb)
+                tma_gather4(dst + cb * C::COLS * 128, tm, cb * C::EPB, r0, r1, r2, r3, c_full(st));
+            }
+            if constexpr (kDKV) {
+              const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col;
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(p.lse[vo])
+                           : "memory");
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + 128 + lane * 4),
+                           "f"(p.delta[vo])
+                           : "memory");
+            }
+          } else if (lane == 0) {
             const int col0 = p.kb2[t] * C::SUB;
             for (int cb = 0; cb < C::CB; ++cb) {
               const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
@@ -211,22 +243,27 @@ __global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
               if (C::NMN >= 1) tma_load_4d(sb + 2 * C::C_BYTES + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
               if (C::NMN >= 2) tma_load_4d(sb + 3 * C::C_BYTES + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
             }
-            bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
             if (kDKV) {
               const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col0;
               bulk_load(sb + C::VEC_OFF + s * 256, p.lse + vo, 128, c_full(st));
               bulk_load(sb + C::VEC_OFF + s * 256 + 128, p.delta + vo, 128, c_full(st));
             }
           }
+          if (lane == 0) bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
         }
-        ++qc;
+        if constexpr (GATHER && kDKV) {
+          // Second arrival of c_full: publishes the lanes' lse / delta stores.
+          __syncwarp();
+          if (lane == 0) mbar_arrive(c_full(st));
+        }
       }
-      if (!ok) {
-        volatile int never = 0;
-        for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
-          mbar_wait(c_full(k % C::NS), (k / C::NS) & 1, &never);
-        if (pending_r) mbar_wait(r_full, qc & 1, &never);
-      }
+      ++qc;
+    }
+    if (!ok && lane == 0) {
+      volatile int never = 0;
+      for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
+        mbar_wait(c_full(k % C::NS), (k / C::NS) & 1, &never);
+      if (pending_r) mbar_wait(r_full, qc & 1, &never);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -330,70 +367,73 @@ __global__ void __launch_bounds__(192, BwdCfg<kDKV, D, F32, CH>::MIN_BLOCKS)
         const uint32_t gg = g0 + c;
         const int st = gg % C::NS, gb = gg % C::NB;
         const int n_in = min(CH, n_sub - CH * c);
-        float s[C::COLS], dp[C::COLS];
         if (!(ok = mbar_wait(sd_full, gg & 1, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          if (j < n_in) {
-            tmem_ld32(trow + 32 * j, *reinterpret_cast<float(*)[32]>(&s[32 * j]));
-            tmem_ld32(trow + 64 + 32 * j, *reinterpret_cast<float(*)[32]>(&dp[32 * j]));
-          }
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sd_empty);
         if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
+        tc_fence_after();
         const uint32_t sb = stage(st);
+        // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into the shared-memory
+        // tiles of buffer gb (TMEM is released once the last tile's values are in registers).
 #pragma unroll
         for (int j = 0; j < CH; ++j) {
           if (j < n_in) {
+            float s[32], dp[32];
+            tmem_ld32(trow + 32 * j, s);
+            tmem_ld32(trow + 64 + 32 * j, dp);
+            tmem_wait_ld();
+            if (j == n_in - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(sd_empty);
+            }
             const uint32_t w = ld_shared_u32(sb + C::BITS_OFF + j * 512 + row * 4);
             const uint32_t any = __reduce_or_sync(0xffffffffu, w);
+            // Groups of 8 columns that no row of the warp may attend to are skipped by the whole warp.
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              float pv = 0.f, dsv = 0.f;
-              if ((any >> i) & 1u) {
-                float l2, dl;
-                if constexpr (kDKV) {
-                  l2 = ld_shared_f32(sb + C::VEC_OFF + j * 256 + i * 4) * kLog2e;
-                  dl = ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4);
-                } else {
-                  l2 = lse2_row;
-                  dl = delta_row;
+            for (int g = 0; g < 4; ++g) {
+              if ((any >> (8 * g)) & 0xFFu) {
+#pragma unroll
+                for (int ii = 0; ii < 8; ++ii) {
+                  const int i = 8 * g + ii;
+                  float l2, dl;
+                  if constexpr (kDKV) {
+                    l2 = ld_shared_f32(sb + C::VEC_OFF + j * 256 + i * 4) * kLog2e;
+                    dl = ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4);
+                  } else {
+                    l2 = lse2_row;
+                    dl = delta_row;
+                  }
+                  const float e = ex2(fmaf(s[i], p.scale_log2, -l2));
+                  const float pv = (w & (1u << i)) ? e : 0.f;
+                  s[i] = pv;
+                  dp[i] = pv * (dp[i] - dl);
                 }
-                const float e = ex2(fmaf(s[32 * j + i], p.scale_log2, -l2));
-                pv = ((w >> i) & 1u) ? e : 0.f;
-                dsv = pv * (dp[32 * j + i] - dl);
+              } else {
+#pragma unroll
+                for (int ii = 0; ii < 8; ++ii) {
+                  s[8 * g + ii] = 0.f;
+                  dp[8 * g + ii] = 0.f;
+                }
               }
-              s[32 * j + i] = pv;
-              dp[32 * j + i] = dsv;
             }
-          }
-        }
-        // dS (and P) -> shared memory buffer gb.
-        if (!(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
 #pragma unroll
-        for (int which = 0; which < C::NG; ++which) {
-          const float* src = which == 0 ? dp : s;
-          const uint32_t base = g_tile(gb, which);
-          if constexpr (!F32) {
+            for (int which = 0; which < C::NG; ++which) {
+              const float* src = which == 0 ? dp : s;
+              const uint32_t base = g_tile(gb, which);
+              if constexpr (!F32) {
+                // 32 bf16 columns = chunks 4j .. 4j+3 of the 128-byte row.
 #pragma unroll
-            for (int cc = 0; cc < C::COLS / 8; ++cc) {
-              if (cc < 4 * n_in)
-                st_shared_v4(base + sw128_offset(row, cc), pack_bf16(src[8 * cc], src[8 * cc + 1]),
-                             pack_bf16(src[8 * cc + 2], src[8 * cc + 3]), pack_bf16(src[8 * cc + 4], src[8 * cc + 5]),
-                             pack_bf16(src[8 * cc + 6], src[8 * cc + 7]));
-            }
-          } else {
+                for (int cc = 0; cc < 4; ++cc)
+                  st_shared_v4(base + sw128_offset(row, 4 * j + cc), pack_bf16(src[8 * cc], src[8 * cc + 1]),
+                               pack_bf16(src[8 * cc + 2], src[8 * cc + 3]), pack_bf16(src[8 * cc + 4], src[8 * cc + 5]),
+                               pack_bf16(src[8 * cc + 6], src[8 * cc + 7]));
+              } else {
+                // 32 fp32 columns = one whole 128-byte column block.
 #pragma unroll
-            for (int cc = 0; cc < C::COLS / 4; ++cc) {
-              if (cc < 8 * n_in) {
-                const int blk = cc >> 3, ch = cc & 7;
-                st_shared_v4(base + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(src[4 * cc]),
-                             __float_as_uint(src[4 * cc + 1]), __float_as_uint(src[4 * cc + 2]),
-                             __float_as_uint(src[4 * cc + 3]));
+                for (int cc = 0; cc < 8; ++cc)
+                  st_shared_v4(base + j * C::ROWS * 128 + sw128_offset(row, cc), __float_as_uint(src[4 * cc]),
+                               __float_as_uint(src[4 * cc + 1]), __float_as_uint(src[4 * cc + 2]),
+                               __float_as_uint(src[4 * cc + 3]));
               }
             }
           }

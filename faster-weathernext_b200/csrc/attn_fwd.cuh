@@ -8,7 +8,11 @@
 // Work item = (batch, head, 128-query block of the paired tile list). Persistent CTAs walk items
 // blockIdx.x, +gridDim.x, ... Roles (192 threads):
 //   warp 0      TMA producer: Q tile once per item; per chunk of up to two 32-key tiles, the K and V
-//               tiles (4D tensor maps over [B, n, H, D], 128-byte swizzle) and the tiles' mask words.
+//               tiles and the tiles' mask words. Tile mode: 32 consecutive keys per tile (4D tensor
+//               maps over [B, n, H, D], 128-byte swizzle). Gathered mode: the 32 keys of a tile are the
+//               block's distinct keys in ascending order (cols), fetched 4 rows at a time with TMA
+//               tile::gather4 from a 2D view of K / V; the swizzle is by shared-memory address, so
+//               8 gathers at 512-byte steps build the same 32-row tile.
 //   warp 1      TMEM allocation; one thread issues the tcgen05 MMAs:
 //                 S[buf] = Q K^T  (M=128, N=32|64, K=D)        -> TMEM, fp32
 //                 O     += P V    (M=128, N=D,     K=32|64)     -> TMEM, fp32 (P from shared memory)
@@ -30,9 +34,11 @@
 namespace fwn {
 
 struct FwdParams {
-  const int32_t* ptr2;    // [NP + 1] paired (128-row) list
-  const int32_t* kb2;     // [T2]
+  const int32_t* ptr2;    // [NP + 1] 128-row list
+  const int32_t* kb2;     // [T2] key block of each tile (tile mode)
+  const int32_t* cols;    // [T2 * 32] key of each slot (gathered mode)
   const uint32_t* bits2;  // [T2 * 128]
+  int head_major;         // gathered mode: rows of the 2D K/V view are (b, h, node) instead of (b, node, h)
   void* o;                // [B, n, H, D]
   float* lse;             // [B, H, lse_rows] or null
   int64_t o_sb, o_sn, o_sh;
@@ -65,12 +71,15 @@ struct FwdCfg {
   static constexpr int O_COL = 128;
   static constexpr int THREADS = 192;
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
+  // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
+  // 192-thread CTAs share an SM's 65,536.
+  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 255;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
 };
 
-template <int D, bool F32>
-__global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
+template <int D, bool F32, bool GATHER>
+__global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   using C = FwdCfg<D, F32>;
@@ -128,28 +137,46 @@ __global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
 
   const int per_bh = p.np;
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t g = 0, qc = 0;
-      bool ok = true;
-      int pending_q = 0;
-      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-        const int nch = (n_sub + 1) >> 1;
-        if (nch == 0) continue;
-        if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+    // ------------------------------------------------------------------ TMA producer (whole warp)
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    int pending_q = 0;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + 1) >> 1;
+      if (nch == 0) continue;
+      if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+      if (lane == 0) {
         mbar_arrive_expect_tx(q_full, C::Q_BYTES);
         for (int cb = 0; cb < C::CB; ++cb)
           tma_load_4d(q_smem + cb * C::ROWS * 128, &tm_q, cb * C::EPB, h, pb * C::ROWS, b, q_full);
-        pending_q = 1;
-        for (int c = 0; c < nch; ++c, ++g) {
-          const int st = g % C::NS;
-          if (!(ok = mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
-          const int n_in = min(2, n_sub - 2 * c);
-          mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
-          for (int s = 0; s < n_in; ++s) {
-            const int t = t0 + 2 * c + s;
+      }
+      pending_q = 1;
+      // Gathered mode: row of the 2D view of K / V holding (batch b, node `key`, head h).
+      const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
+      const int row_mul = p.head_major ? 1 : p.heads;
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
+        const int n_in = min(2, n_sub - 2 * c);
+        if (lane == 0) mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
+        __syncwarp();
+        for (int s = 0; s < n_in; ++s) {
+          const int t = t0 + 2 * c + s;
+          if constexpr (GATHER) {
+            // Lane i holds slot i's row; lanes 0-7 gather K rows 4j..4j+3, lanes 8-15 V rows.
+            const int row = p.cols[static_cast<size_t>(t) * 32 + lane] * row_mul + row_base;
+            const int j = lane & 7;
+            const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
+            const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
+            if (lane < 16) {
+              const uint32_t dst = (lane < 8 ? stage_k(st) : stage_v(st)) + s * C::SUB * 128 + j * 512;
+              const void* tm = lane < 8 ? static_cast<const void*>(&tm_k) : static_cast<const void*>(&tm_v);
+              for (int cb = 0; cb < C::CB; ++cb)
+                tma_gather4(dst + cb * C::KEYS * 128, tm, cb * C::EPB, r0, r1, r2, r3, kv_full(st));
+            }
+          } else if (lane == 0) {
             const int key0 = p.kb2[t] * C::SUB;
             for (int cb = 0; cb < C::CB; ++cb) {
               tma_load_4d(stage_k(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_k, cb * C::EPB, h, key0, b,
@@ -157,18 +184,18 @@ __global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
               tma_load_4d(stage_v(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_v, cb * C::EPB, h, key0, b,
                           kv_full(st));
             }
-            bulk_load(stage_bits(st) + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, kv_full(st));
           }
+          if (lane == 0) bulk_load(stage_bits(st) + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, kv_full(st));
         }
-        ++qc;
       }
-      if (!ok) {
-        // Drain: wait (bounded, ignoring the abort flag) for every copy this thread issued.
-        volatile int never = 0;
-        for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
-          mbar_wait(kv_full(k % C::NS), (k / C::NS) & 1, &never);
-        if (pending_q) mbar_wait(q_full, (qc & 1), &never);
-      }
+      ++qc;
+    }
+    if (!ok && lane == 0) {
+      // Drain: wait (bounded, ignoring the abort flag) for every copy this warp issued.
+      volatile int never = 0;
+      for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
+        mbar_wait(kv_full(k % C::NS), (k / C::NS) & 1, &never);
+      if (pending_q) mbar_wait(q_full, (qc & 1), &never);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -270,11 +297,21 @@ __global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
         const uint32_t w1 = n_in == 2 ? ld_shared_u32(stage_bits(st) + 512 + row * 4) : 0u;
         const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
         const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
+        // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
+        // of the warp may attend to is skipped by the whole warp.
         float mx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = ((w0 >> j) & 1u) ? fmaxf(mx, s[j]) : mx;
+        for (int g = 0; g < 8; ++g) {
+          const uint32_t w = g < 4 ? w0 : w1;
+          const uint32_t any = g < 4 ? any0 : any1;
+          if ((any >> (8 * (g & 3))) & 0xFFu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = ((w1 >> j) & 1u) ? fmaxf(mx, s[32 + j]) : mx;
+            for (int i = 0; i < 8; ++i) {
+              const int j = 8 * g + i;
+              mx = (w & (1u << (j & 31))) ? fmaxf(mx, s[j]) : mx;
+            }
+          }
+        }
         const float m_new = mx * p.scale_log2;
         const float m_old = m_ref;
         const bool grow = m_new > m_ref + 8.0f;
@@ -286,25 +323,21 @@ __global__ void __launch_bounds__(192, FwdCfg<D, F32>::MIN_BLOCKS)
         }
         const float neg_m = -m_ref;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float e = 0.f;
-          if ((any0 >> j) & 1u) {
-            const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
-            e = ((w0 >> j) & 1u) ? t : 0.f;
-          }
-          s[j] = e;
-          l += e;
-        }
-        if (n_in == 2) {
+        for (int g = 0; g < 8; ++g) {
+          const uint32_t w = g < 4 ? w0 : w1;
+          const uint32_t any = g < 4 ? any0 : any1;
+          if ((any >> (8 * (g & 3))) & 0xFFu) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float e = 0.f;
-            if ((any1 >> j) & 1u) {
-              const float t = ex2(fmaf(s[32 + j], p.scale_log2, neg_m));
-              e = ((w1 >> j) & 1u) ? t : 0.f;
+            for (int i = 0; i < 8; ++i) {
+              const int j = 8 * g + i;
+              const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
+              const float e = (w & (1u << (j & 31))) ? t : 0.f;
+              s[j] = e;
+              l += e;
             }
-            s[32 + j] = e;
-            l += e;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s[8 * g + i] = 0.f;
           }
         }
         // P -> shared memory (wait until P V of chunk gg-2 released this buffer).

@@ -79,6 +79,37 @@ fwn_status make_map(CUtensorMap* map, const void* base, const fwn_attn_desc& d, 
   return FWN_OK;
 }
 
+// Row layout of the 2D view used by gathered loads: 0 node-major, 1 head-major, -1 not expressible.
+int gather_layout(const fwn_attn_desc& d, bool out) {
+  const int64_t sh = out ? d.out_stride_h : d.stride_h, sn = out ? d.out_stride_n : d.stride_n,
+                sb = out ? d.out_stride_b : d.stride_b;
+  if ((d.heads == 1 || sn == static_cast<int64_t>(d.heads) * sh) && (d.batch == 1 || sb == static_cast<int64_t>(d.n) * sn))
+    return 0;
+  if ((d.n == 1 || sh == static_cast<int64_t>(d.n) * sn) && (d.batch == 1 || sb == static_cast<int64_t>(d.heads) * sh))
+    return 1;
+  return -1;
+}
+
+// 2D map over the (batch, node, head) rows of a tensor for tile::gather4: box = 128 bytes x 1 row.
+fwn_status make_map_rows(CUtensorMap* map, const void* base, const fwn_attn_desc& d, int layout, bool atom32,
+                         bool out) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FWN_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  const int es = d.dtype == FWN_DTYPE_BF16 ? 2 : 4;
+  const int64_t row_stride = layout == 0 ? (out ? d.out_stride_h : d.stride_h) : (out ? d.out_stride_n : d.stride_n);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.head_dim),
+                        static_cast<cuuint64_t>(d.batch) * static_cast<cuuint64_t>(d.n) * static_cast<cuuint64_t>(d.heads)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * es};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, d.dtype == FWN_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                   2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FWN_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled (rows) failed (%d)", static_cast<int>(r));
+  return FWN_OK;
+}
+
 fwn_status check_desc(const fwn_attn_desc* d) {
   if (!d) return fail(FWN_ERR_INVALID_ARGUMENT, "desc is null");
   if (d->batch <= 0 || d->heads <= 0 || d->n <= 0)
@@ -113,6 +144,8 @@ fwn_status check_tiles(const fwn_tile_list* t, const fwn_attn_desc* d, const cha
   if (!t->ptr || (t->n_tiles > 0 && (!t->kb || !t->bits)))
     return fail(FWN_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (!aligned16(t->bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "%s: bits must be 16-byte aligned", name);
+  if (t->cols && t->n_tiles > 0 && !aligned16(t->cols))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "%s: cols must be 16-byte aligned", name);
   if (t->n_cols > d->n) return fail(FWN_ERR_INVALID_ARGUMENT, "%s: %d mask columns > n=%d", name, t->n_cols, d->n);
   return FWN_OK;
 }
@@ -132,6 +165,9 @@ template <typename Kernel>
 fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, int items, int* grid) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  // Ask for the full shared-memory carveout so that the occupancy below is the one the launch gets.
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
   int per_sm = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
@@ -143,19 +179,26 @@ fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, 
   return FWN_OK;
 }
 
-template <int D, bool F32>
+template <int D, bool F32, bool GATHER>
 fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
-                      void* o, float* lse, cudaStream_t stream) {
+                      void* o, float* lse, int layout, cudaStream_t stream) {
   using C = fwn::FwdCfg<D, F32>;
   CUtensorMap tq, tk, tv;
   fwn_status s;
   if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
-  if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
-  if ((s = make_map(&tv, v, d, C::SUB, F32)) != FWN_OK) return s;
+  if (GATHER) {
+    if ((s = make_map_rows(&tk, k, d, layout, false, false)) != FWN_OK) return s;
+    if ((s = make_map_rows(&tv, v, d, layout, F32, false)) != FWN_OK) return s;
+  } else {
+    if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
+    if ((s = make_map(&tv, v, d, C::SUB, F32)) != FWN_OK) return s;
+  }
   fwn::FwdParams p{};
   p.ptr2 = t.ptr;
   p.kb2 = t.kb;
+  p.cols = t.cols;
   p.bits2 = t.bits;
+  p.head_major = layout == 1;
   p.o = o;
   p.lse = lse;
   p.o_sb = d.out_stride_b;
@@ -168,7 +211,7 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   p.lse_rows = fwn_lse_rows(d.n);
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale_log2 = d.scale * 1.4426950408889634f;
-  auto kernel = fwn::attn_fwd_kernel<D, F32>;
+  auto kernel = fwn::attn_fwd_kernel<D, F32, GATHER>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
@@ -177,10 +220,10 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   return ok();
 }
 
-template <bool kDKV, int D, bool F32, int CH>
+template <bool kDKV, int D, bool F32, int CH, bool GATHER>
 fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
                            const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
-                           cudaStream_t stream) {
+                           int layout, cudaStream_t stream) {
   using C = fwn::BwdCfg<kDKV, D, F32, CH>;
   CUtensorMap r0, r1, c0, c1, c0mn, c1mn;
   fwn_status s;
@@ -192,18 +235,30 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   const bool r1_out = !kDKV, c1_out = kDKV;
   if ((s = make_map(&r0, rp0, d, C::ROWS)) != FWN_OK) return s;
   if ((s = make_map(&r1, rp1, d, C::ROWS, false, r1_out)) != FWN_OK) return s;
-  if ((s = make_map(&c0, cp0, d, C::SUB)) != FWN_OK) return s;
-  if ((s = make_map(&c1, cp1, d, C::SUB, false, c1_out)) != FWN_OK) return s;
+  if (GATHER) {
+    if ((s = make_map_rows(&c0, cp0, d, layout, false, false)) != FWN_OK) return s;
+    if ((s = make_map_rows(&c1, cp1, d, layout, false, c1_out)) != FWN_OK) return s;
+  } else {
+    if ((s = make_map(&c0, cp0, d, C::SUB)) != FWN_OK) return s;
+    if ((s = make_map(&c1, cp1, d, C::SUB, false, c1_out)) != FWN_OK) return s;
+  }
   c0mn = c0;
   c1mn = c1;
   if (F32) {
-    if ((s = make_map(&c0mn, cp0, d, C::SUB, true)) != FWN_OK) return s;
-    if ((s = make_map(&c1mn, cp1, d, C::SUB, true, c1_out)) != FWN_OK) return s;
+    if (GATHER) {
+      if ((s = make_map_rows(&c0mn, cp0, d, layout, true, false)) != FWN_OK) return s;
+      if ((s = make_map_rows(&c1mn, cp1, d, layout, true, c1_out)) != FWN_OK) return s;
+    } else {
+      if ((s = make_map(&c0mn, cp0, d, C::SUB, true)) != FWN_OK) return s;
+      if ((s = make_map(&c1mn, cp1, d, C::SUB, true, c1_out)) != FWN_OK) return s;
+    }
   }
   fwn::BwdParams p{};
   p.ptr2 = t.ptr;
   p.kb2 = t.kb;
+  p.cols = t.cols;
   p.bits2 = t.bits;
+  p.head_major = layout == 1;
   p.lse = lse;
   p.delta = delta;
   p.out0 = out0;
@@ -218,13 +273,33 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale = d.scale;
   p.scale_log2 = d.scale * 1.4426950408889634f;
-  auto kernel = fwn::attn_bwd_kernel<kDKV, D, F32, CH>;
+  auto kernel = fwn::attn_bwd_kernel<kDKV, D, F32, CH, GATHER>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, kDKV ? "attn_bwd dkv launch" : "attn_bwd dq launch");
   return FWN_OK;
+}
+
+// Gathered-mode layout for the column operands of one pass (-1: not gatherable).
+int pass_layout(const fwn_attn_desc& d, bool dkv) {
+  const int a = gather_layout(d, false);
+  if (!dkv) return a;                    // columns K, V (input strides)
+  const int b = gather_layout(d, true);  // columns Q (input) and dO (output strides)
+  return (a >= 0 && a == b) ? a : -1;
+}
+
+template <bool kDKV, int D, bool F32, int CH>
+fwn_status launch_bwd_pass_any(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
+                               const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
+                               cudaStream_t stream) {
+  if (t.cols) {
+    const int layout = pass_layout(d, kDKV);
+    if (layout < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "gathered lists need a node-major or head-major packed layout");
+    return launch_bwd_pass<kDKV, D, F32, CH, true>(d, q, k, v, d_o, lse, delta, t, out0, out1, layout, stream);
+  }
+  return launch_bwd_pass<kDKV, D, F32, CH, false>(d, q, k, v, d_o, lse, delta, t, out0, out1, 0, stream);
 }
 
 template <int D, bool F32>
@@ -248,9 +323,9 @@ fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   constexpr int CH = F32 ? 1 : 2;
   fwn_status s;
   if ((parts & kDelta) && (s = launch_delta<D, F32>(d, o, d_o, delta, stream)) != FWN_OK) return s;
-  if ((parts & kDq) && (s = launch_bwd_pass<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
+  if ((parts & kDq) && (s = launch_bwd_pass_any<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
     return s;
-  if ((parts & kDkv) && (s = launch_bwd_pass<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) != FWN_OK)
+  if ((parts & kDkv) && (s = launch_bwd_pass_any<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) != FWN_OK)
     return s;
   return ok();
 }
@@ -351,6 +426,32 @@ fwn_status fwn_tiles_pair_fill(const fwn_tile_list* t, const int32_t* ptr2, int3
   return ok();
 }
 
+fwn_status fwn_tiles_gather_count(const fwn_tile_list* t, int32_t* ptr_g, void* ws, size_t ws_bytes, void* stream) {
+  if (!t || !ptr_g) return fail(FWN_ERR_INVALID_ARGUMENT, "null argument");
+  if (t->block_rows != 128 || t->cols) return fail(FWN_ERR_INVALID_ARGUMENT, "gathering takes a 128-row (paired) list");
+  if (!t->ptr || (t->n_tiles > 0 && !t->bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "null tile pointer");
+  if (t->n_tiles > 0 && !aligned16(t->bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "bits must be 16-byte aligned");
+  const size_t need = ((static_cast<size_t>(t->n_blocks) * 4 + 255) / 256) * 256 + 256;
+  if (!ws || ws_bytes < need) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaError_t e = fwn::launch_gather_count(t->ptr, t->bits, t->n_blocks, ptr_g, static_cast<int32_t*>(ws),
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather_count");
+  return ok();
+}
+
+fwn_status fwn_tiles_gather_fill(const fwn_tile_list* t, int32_t max_block_tiles, const int32_t* ptr_g, int32_t* cols_g,
+                                 uint32_t* bits_g, void* stream) {
+  if (!t || !ptr_g || !cols_g || !bits_g) return fail(FWN_ERR_INVALID_ARGUMENT, "null argument");
+  if (t->block_rows != 128 || t->cols) return fail(FWN_ERR_INVALID_ARGUMENT, "gathering takes a 128-row (paired) list");
+  if (!t->ptr || (t->n_tiles > 0 && (!t->kb || !t->bits))) return fail(FWN_ERR_INVALID_ARGUMENT, "null tile pointer");
+  if (max_block_tiles < 0 || max_block_tiles > 40960)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "max_block_tiles %d outside [0, 40960]", max_block_tiles);
+  cudaError_t e = fwn::launch_gather_fill(t->ptr, t->kb, t->bits, t->n_blocks, max_block_tiles, ptr_g, cols_g, bits_g,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather_fill");
+  return ok();
+}
+
 fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32_t n, int32_t bits, int64_t* codes,
                              void* stream) {
   if (n < 0 || bits < 1 || bits > 20) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n=%d or bits=%d", n, bits);
@@ -371,11 +472,22 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
     return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const fwn_attn_desc& d = *desc;
-  if (d.mode == FWN_MODE_BF16) {
-    if (d.head_dim == 64) return launch_fwd<64, false>(d, q, k, v, *tiles, o, lse, st);
-    return launch_fwd<128, false>(d, q, k, v, *tiles, o, lse, st);
+  int layout = 0;
+  if (tiles->cols) {
+    layout = gather_layout(d, false);
+    if (layout < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "gathered lists need a node-major or head-major packed layout");
   }
-  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64) return launch_fwd<64, true>(d, q, k, v, *tiles, o, lse, st);
+  const bool g = tiles->cols != nullptr;
+  if (d.mode == FWN_MODE_BF16) {
+    if (d.head_dim == 64)
+      return g ? launch_fwd<64, false, true>(d, q, k, v, *tiles, o, lse, layout, st)
+               : launch_fwd<64, false, false>(d, q, k, v, *tiles, o, lse, layout, st);
+    return g ? launch_fwd<128, false, true>(d, q, k, v, *tiles, o, lse, layout, st)
+             : launch_fwd<128, false, false>(d, q, k, v, *tiles, o, lse, layout, st);
+  }
+  if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
+    return g ? launch_fwd<64, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
+             : launch_fwd<64, true, false>(d, q, k, v, *tiles, o, lse, layout, st);
   return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
 }
 

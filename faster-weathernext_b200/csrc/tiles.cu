@@ -279,6 +279,95 @@ __global__ void __launch_bounds__(kThreads) pair_fill_kernel(const int32_t* __re
   }
 }
 
+// Column mask of a 128-row tile: OR of its 128 words (which of the tile's 32 columns any row uses).
+__device__ __forceinline__ uint32_t tile_colmask(const uint32_t* __restrict__ bits2, int e, int lane) {
+  const uint4 w = reinterpret_cast<const uint4*>(bits2 + static_cast<size_t>(e) * 128)[lane];
+  uint32_t m = w.x | w.y | w.z | w.w;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, d);
+  return m;
+}
+
+// Gathered list, pass 1: per 128-row block, ceil(distinct used columns / 32) tiles.
+__global__ void __launch_bounds__(kThreads) gather_count_kernel(const int32_t* __restrict__ ptr2,
+                                                                 const uint32_t* __restrict__ bits2,
+                                                                 int32_t* __restrict__ counts) {
+  const int p = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = ptr2[p], e1 = ptr2[p + 1];
+  int used = 0;
+  for (int e = e0 + warp; e < e1; e += kWarps) used += __popc(tile_colmask(bits2, e, lane));
+  __shared__ int part[kWarps];
+  if (lane == 0) part[warp] = used;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < kWarps; ++w) s += part[w];
+    counts[p] = (s + 31) / 32;
+  }
+}
+
+// Gathered list, pass 2. Shared memory: colmask[n_sub], base[n_sub], then (if they fit) the block's
+// words. A block with more tiles than `max_sub` falls back to recomputing column masks on the fly.
+__global__ void __launch_bounds__(kThreads) gather_fill_kernel(const int32_t* __restrict__ ptr2,
+                                                                const int32_t* __restrict__ kb2,
+                                                                const uint32_t* __restrict__ bits2,
+                                                                const int32_t* __restrict__ ptr_g,
+                                                                int32_t* __restrict__ cols_g,
+                                                                uint32_t* __restrict__ bits_g, int max_sub,
+                                                                int word_cap) {
+  extern __shared__ uint32_t smem[];
+  uint32_t* cm = smem;                                   // [max_sub]
+  int* base = reinterpret_cast<int*>(smem + max_sub);    // [max_sub]
+  uint32_t* acc = smem + 2 * max_sub;                    // [word_cap]
+  __shared__ int scratch[kWarps];
+  const int p = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = ptr2[p], n_sub = ptr2[p + 1] - e0;
+  const int g0 = ptr_g[p], ng = ptr_g[p + 1] - g0;
+  if (n_sub == 0) return;
+  if (n_sub > max_sub) return;  // the host sizes max_sub from the largest block, so this never happens
+  for (int e = warp; e < n_sub; e += kWarps) {
+    const uint32_t m = tile_colmask(bits2, e0 + e, lane);
+    if (lane == 0) cm[e] = m;
+  }
+  __syncthreads();
+  // Exclusive scan of popcount(cm) over the block's tiles (reuses the bitmap prefix helper).
+  bitmap_prefix(cm, base, n_sub, scratch);
+  // Columns: slot base[e] + rank of bit j in cm[e]; padding slots repeat the block's last column.
+  int last = 0;
+  {
+    const int e = n_sub - 1;
+    last = kb2[e0 + e] * 32 + (31 - __clz(cm[e] ? cm[e] : 1u));
+  }
+  int32_t* cols = cols_g + static_cast<size_t>(g0) * 32;
+  for (int i = threadIdx.x; i < ng * 32; i += kThreads) cols[i] = last;
+  __syncthreads();
+  for (int e = warp; e < n_sub; e += kWarps) {
+    const uint32_t m = cm[e];
+    if ((m >> lane) & 1u) cols[base[e] + __popc(m & ((1u << lane) - 1u))] = kb2[e0 + e] * 32 + lane;
+  }
+  // Words: OR each (tile, row) word's bits into the slots of its columns.
+  const bool in_smem = ng * 128 <= word_cap;
+  uint32_t* out = bits_g + static_cast<size_t>(g0) * 128;
+  uint32_t* dst = in_smem ? acc : out;
+  for (int i = threadIdx.x; i < ng * 128; i += kThreads) dst[i] = 0;
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < n_sub * 128; idx += kThreads) {
+    const int e = idx >> 7, r = idx & 127;
+    uint32_t w = bits2[static_cast<size_t>(e0 + e) * 128 + r];
+    const uint32_t m = cm[e];
+    const int b0 = base[e];
+    while (w) {
+      const int j = __ffs(w) - 1;
+      w &= w - 1;
+      const int slot = b0 + __popc(m & ((1u << j) - 1u));
+      atomicOr(&dst[(slot >> 5) * 128 + r], 1u << (slot & 31));
+    }
+  }
+  __syncthreads();
+  if (in_smem)
+    for (int i = threadIdx.x; i < ng * 128; i += kThreads) out[i] = acc[i];
+}
+
 // Hilbert-curve index of unit-sphere points (Skilling, "Programming the Hilbert curve", 2004: axes ->
 // transpose by undoing excess work per bit plane, Gray encoding, then bit interleaving), the device
 // counterpart of hilbert_order's key (pallas_attn.py:41-82). Non-finite points get INT64_MAX.
@@ -340,6 +429,29 @@ cudaError_t launch_hilbert_codes(const double* lat_deg, const double* lon_deg, i
 }
 
 int tiles_bitmap_words(int n_cols) { return ((n_cols + 31) / 32 + 31) / 32; }
+
+cudaError_t launch_gather_count(const int32_t* ptr2, const uint32_t* bits2, int n_blocks, int32_t* ptr_g,
+                                int32_t* counts, cudaStream_t stream) {
+  if (n_blocks > 0) gather_count_kernel<<<n_blocks, kThreads, 0, stream>>>(ptr2, bits2, counts);
+  exclusive_scan_kernel<<<1, 1024, 0, stream>>>(counts, n_blocks, ptr_g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_fill(const int32_t* ptr2, const int32_t* kb2, const uint32_t* bits2, int n_blocks,
+                               int max_sub, const int32_t* ptr_g, int32_t* cols_g, uint32_t* bits_g,
+                               cudaStream_t stream) {
+  if (n_blocks == 0) return cudaSuccess;
+  max_sub = max_sub < 1 ? 1 : max_sub;
+  const size_t fixed = static_cast<size_t>(2 * max_sub) * 4;
+  if (fixed > 160 * 1024) return cudaErrorInvalidValue;
+  int cap = static_cast<int>((200 * 1024 - fixed) / 4);
+  const size_t smem = fixed + static_cast<size_t>(cap) * 4;
+  cudaError_t e = cudaFuncSetAttribute(gather_fill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  gather_fill_kernel<<<n_blocks, kThreads, smem, stream>>>(ptr2, kb2, bits2, ptr_g, cols_g, bits_g, max_sub, cap);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_tiles_count(const int32_t* indptr, const int32_t* indices, int n_rows, int n_cols,
                                int block_q, int32_t* tile_ptr, int32_t* counts, cudaStream_t stream) {

@@ -22,6 +22,14 @@ cudaError_t launch_pair_count(const int32_t* ptr, const int32_t* kb, int n_block
 cudaError_t launch_pair_fill(const int32_t* ptr, const int32_t* kb, const uint32_t* bits, int n_blocks, int n_cols,
                              const int32_t* ptr2, int32_t* kb2, uint32_t* bits2, cudaStream_t stream);
 
+// Gathered list from a 128-row list: pass 1 (ptr_g via per-block tile counts) and pass 2 (cols, bits).
+// max_sub = the largest number of tiles of one block in the 128-row list.
+cudaError_t launch_gather_count(const int32_t* ptr2, const uint32_t* bits2, int n_blocks, int32_t* ptr_g,
+                                int32_t* counts, cudaStream_t stream);
+cudaError_t launch_gather_fill(const int32_t* ptr2, const int32_t* kb2, const uint32_t* bits2, int n_blocks,
+                               int max_sub, const int32_t* ptr_g, int32_t* cols_g, uint32_t* bits_g,
+                               cudaStream_t stream);
+
 // Hilbert-curve codes of (lat, lon) points in degrees (bits per axis <= 20); INT64_MAX for non-finite.
 cudaError_t launch_hilbert_codes(const double* lat_deg, const double* lon_deg, int n, int bits, long long* codes,
                                  cudaStream_t stream);

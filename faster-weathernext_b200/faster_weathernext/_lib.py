@@ -26,7 +26,7 @@ MODE_TF32X3 = 2
 # Every symbol include/fwn_attn.h declares.
 SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_rows",
            "fwn_tiles_workspace_size", "fwn_tiles_count", "fwn_tiles_fill", "fwn_tiles_pair_count",
-           "fwn_tiles_pair_fill", "fwn_hilbert_codes", "fwn_attn_fwd", "fwn_attn_bwd_workspace_size", "fwn_attn_bwd",
+           "fwn_tiles_pair_fill", "fwn_tiles_gather_count", "fwn_tiles_gather_fill", "fwn_hilbert_codes", "fwn_attn_fwd", "fwn_attn_bwd_workspace_size", "fwn_attn_bwd",
            "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv")
 
 
@@ -41,7 +41,7 @@ class AttnDesc(ctypes.Structure):
 class TileList(ctypes.Structure):
   _fields_ = [("ptr", ctypes.c_void_p), ("kb", ctypes.c_void_p), ("bits", ctypes.c_void_p),
               ("n_blocks", ctypes.c_int32), ("n_tiles", ctypes.c_int32), ("block_rows", ctypes.c_int32),
-              ("n_cols", ctypes.c_int32)]
+              ("n_cols", ctypes.c_int32), ("cols", ctypes.c_void_p)]
 
 
 class FwnError(RuntimeError):
@@ -67,6 +67,8 @@ def _declare(lib):
       "fwn_tiles_fill": [_P, _P, _I, _I, _I, _P, _P, _P, _P],
       "fwn_tiles_pair_count": [ctypes.POINTER(TileList), _P, _P, _SZ, _P],
       "fwn_tiles_pair_fill": [ctypes.POINTER(TileList), _P, _P, _P, _P],
+      "fwn_tiles_gather_count": [ctypes.POINTER(TileList), _P, _P, _SZ, _P],
+      "fwn_tiles_gather_fill": [ctypes.POINTER(TileList), _I, _P, _P, _P, _P],
       "fwn_hilbert_codes": [_P, _P, _I, _I, _P, _P],
       "fwn_attn_fwd": [ctypes.POINTER(AttnDesc), _P, _P, _P, ctypes.POINTER(TileList), _P, _P, _P],
       "fwn_attn_bwd_workspace_size": [ctypes.POINTER(AttnDesc), ctypes.POINTER(_SZ)],

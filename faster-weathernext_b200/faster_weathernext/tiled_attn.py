@@ -67,7 +67,7 @@ class TileList64:
 
   def struct(self) -> _lib.TileList:
     return _lib.TileList(self.ptr.data_ptr(), self.kb.data_ptr() if self.n_tiles else 0,
-                         self.bits.data_ptr() if self.n_tiles else 0, self.n_blocks, self.n_tiles, 64, self.n_cols)
+                         self.bits.data_ptr() if self.n_tiles else 0, self.n_blocks, self.n_tiles, 64, self.n_cols, 0)
 
   def numpy(self):
     """(tile_ptr int32, tile_kb int32, tile_bits uint32 [T, 64]) — the reference's return types."""
@@ -77,11 +77,13 @@ class TileList64:
 
 @dataclasses.dataclass
 class TileList128:
-  """Paired list (128 query rows per block) the attention kernels walk."""
+  """128-row list the attention kernels walk: paired (kb: key block of each tile) or gathered
+  (cols: the column of each of a tile's 32 slots)."""
   ptr: torch.Tensor
   kb: torch.Tensor
   bits: torch.Tensor
   n_cols: int
+  cols: Optional[torch.Tensor] = None
 
   @property
   def n_blocks(self):
@@ -89,15 +91,17 @@ class TileList128:
 
   @property
   def n_tiles(self):
-    return self.kb.numel()
+    return self.bits.shape[0]
 
   def struct(self) -> _lib.TileList:
-    return _lib.TileList(self.ptr.data_ptr(), self.kb.data_ptr() if self.n_tiles else 0,
-                         self.bits.data_ptr() if self.n_tiles else 0, self.n_blocks, self.n_tiles, 128, self.n_cols)
+    n = self.n_tiles
+    return _lib.TileList(self.ptr.data_ptr(), self.kb.data_ptr() if n and self.kb.numel() else 0,
+                         self.bits.data_ptr() if n else 0, self.n_blocks, n, 128, self.n_cols,
+                         self.cols.data_ptr() if (self.cols is not None and n) else 0)
 
   def numpy(self):
-    return (self.ptr.cpu().numpy(), self.kb.cpu().numpy(),
-            self.bits.cpu().numpy().view(np.uint32).reshape(-1, 128))
+    second = self.cols.cpu().numpy().reshape(-1, 32) if self.cols is not None else self.kb.cpu().numpy()
+    return (self.ptr.cpu().numpy(), second, self.bits.cpu().numpy().view(np.uint32).reshape(-1, 128))
 
 
 def _read_last(ptr: torch.Tensor) -> int:
@@ -146,6 +150,26 @@ def pair_tiles(t: TileList64) -> TileList128:
   return TileList128(ptr2, kb2, bits2.view(n2, 128), t.n_cols)
 
 
+def gather_tiles(t: TileList128) -> TileList128:
+  """Gathered list from a paired list: each block's distinct columns packed into 32-slot tiles."""
+  lib = _lib.lib()
+  dev = t.ptr.device
+  st = t.struct()
+  ws = torch.empty(t.n_blocks * 4 + 512, dtype=torch.uint8, device=dev)
+  ptr_g = torch.empty(t.n_blocks + 1, dtype=torch.int32, device=dev)
+  s = _stream()
+  _lib.check(lib.fwn_tiles_gather_count(ctypes.byref(st), ptr_g.data_ptr(), ws.data_ptr(), ws.numel(), s))
+  ng = _read_last(ptr_g)
+  max_block = int(torch.diff(t.ptr).max().item()) if t.n_blocks else 0
+  cols = torch.empty(max(ng, 1) * 32, dtype=torch.int32, device=dev)[:ng * 32]
+  bits = torch.empty(max(ng, 1) * 128, dtype=torch.int32, device=dev)[:ng * 128]
+  if ng:
+    _lib.check(lib.fwn_tiles_gather_fill(ctypes.byref(st), max_block, ptr_g.data_ptr(), cols.data_ptr(),
+                                         bits.data_ptr(), s))
+  empty = torch.empty(0, dtype=torch.int32, device=dev)
+  return TileList128(ptr_g, empty, bits.view(ng, 128), t.n_cols, cols)
+
+
 def _csr_to_device(mask, device):
   m = sparse.csr_matrix(mask)
   m.sum_duplicates()
@@ -174,17 +198,20 @@ def _tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n_cols, device) -> TileLi
 
 
 class AttentionTiles:
-  """Forward and transposed paired lists of one mask, resident on the device (built once per mask,
-  like the reference's tile constants, patch.py:208-219)."""
+  """Forward and transposed 128-row lists of one mask, resident on the device (built once per mask,
+  like the reference's tile constants, patch.py:208-219): paired lists (fwd, bwd) and their gathered
+  forms (fwd_g, bwd_g), which the kernels use whenever q/k/v/o have a node- or head-major layout."""
 
-  def __init__(self, fwd: TileList128, bwd: TileList128, n: int, symmetric: bool):
+  def __init__(self, fwd: TileList128, bwd: TileList128, n: int, symmetric: bool, gather: bool = True):
     self.fwd = fwd
     self.bwd = bwd
     self.n = n
     self.symmetric = symmetric
+    self.fwd_g = gather_tiles(fwd) if gather else None
+    self.bwd_g = (self.fwd_g if bwd is fwd else gather_tiles(bwd)) if gather else None
 
   @classmethod
-  def from_mask(cls, mask, device=None) -> "AttentionTiles":
+  def from_mask(cls, mask, device=None, gather: bool = True) -> "AttentionTiles":
     dev = _device(device)
     m = sparse.csr_matrix(mask).astype(bool)
     m.eliminate_zeros()
@@ -199,17 +226,18 @@ class AttentionTiles:
       mt = m.T.tocsr()
       ip, ix, _ = _csr_to_device(mt, dev)
       bwd = pair_tiles(build_tiles_device(ip, ix, n, n))
-    return cls(fwd, bwd, n, symmetric)
+    return cls(fwd, bwd, n, symmetric, gather)
 
   @classmethod
-  def from_lists(cls, tile_ptr, tile_kb, tile_bits, n: int, tiles_t=None, device=None) -> "AttentionTiles":
+  def from_lists(cls, tile_ptr, tile_kb, tile_bits, n: int, tiles_t=None, device=None,
+                 gather: bool = True) -> "AttentionTiles":
     """From the reference's (tile_ptr, tile_kb, tile_bits) arrays (and optionally the transposed triple)."""
     dev = _device(device)
     fwd = pair_tiles(_tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n, dev))
     if tiles_t is None:
-      return cls(fwd, fwd, n, True)
+      return cls(fwd, fwd, n, True, gather)
     bwd = pair_tiles(_tiles64_from_arrays(*tiles_t, n, dev))
-    return cls(fwd, bwd, n, False)
+    return cls(fwd, bwd, n, False, gather)
 
 
 def _mode_for(dtype: torch.dtype, precision: Optional[str], strict_fp32: bool) -> int:
@@ -231,6 +259,26 @@ def _desc(q: torch.Tensor, o: torch.Tensor, scale: float, mode: int) -> _lib.Att
     raise ValueError("head_dim must be contiguous")
   dt = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_F32
   return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh, ob, on, oh)
+
+
+def _gather_layout(t: torch.Tensor) -> int:
+  """0: (batch, node, head) rows form one strided 2D view; 1: (batch, head, node) rows do; -1: neither."""
+  b, n, h, _ = t.shape
+  sb, sn, sh, _ = t.stride()
+  if (h == 1 or sn == h * sh) and (b == 1 or sb == n * sn):
+    return 0
+  if (n == 1 or sh == n * sn) and (b == 1 or sb == h * sh):
+    return 1
+  return -1
+
+
+def _lists(tiles: "AttentionTiles", q: torch.Tensor, o: torch.Tensor):
+  """(forward list, transposed list): gathered when the layouts allow gathered row loads."""
+  if tiles.fwd_g is not None:
+    a, c = _gather_layout(q), _gather_layout(o)
+    if a >= 0 and a == c:
+      return tiles.fwd_g, tiles.bwd_g
+  return tiles.fwd, tiles.bwd
 
 
 def _same_layout(*ts):
@@ -255,7 +303,7 @@ def attention_forward(q, k, v, tiles: AttentionTiles, scale: float, mode: int, w
   if with_lse:
     b, n, h, _ = q.shape
     lse = torch.empty(b, h, lib.fwn_lse_rows(n), dtype=torch.float32, device=q.device)
-  st = tiles.fwd.struct()
+  st = _lists(tiles, q, o)[0].struct()
   _lib.check(lib.fwn_attn_fwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), ctypes.byref(st),
                               o.data_ptr(), lse.data_ptr() if lse is not None else 0, _stream()))
   return o, lse
@@ -271,7 +319,8 @@ def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float,
   _lib.check(lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)))
   ws = torch.empty(max(ws_bytes.value, 16), dtype=torch.uint8, device=q.device)
   dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
-  sf, sb = tiles.fwd.struct(), tiles.bwd.struct()
+  lf, lb = _lists(tiles, q, o)
+  sf, sb = lf.struct(), lb.struct()
   _lib.check(lib.fwn_attn_bwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                               lse.data_ptr(), do.data_ptr(), ctypes.byref(sf), ctypes.byref(sb), dq.data_ptr(),
                               dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(), _stream()))

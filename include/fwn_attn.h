@@ -83,8 +83,13 @@ typedef struct fwn_tile_list {
   const uint32_t* bits; /* [n_tiles * block_rows] */
   int32_t n_blocks;
   int32_t n_tiles;
-  int32_t block_rows;   /* 64: build_tile_mask layout; 128: paired layout (attention kernels) */
+  int32_t block_rows;   /* 64: build_tile_mask layout; 128: paired or gathered layout (attention kernels) */
   int32_t n_cols;       /* columns of the mask (keys); key blocks are < ceil(n_cols / 32) */
+  const int32_t* cols;  /* NULL, or [n_tiles * 32]: gathered list, slot j of tile t is column cols[t*32 + j]
+                           (kb unused). Gathered lists need q/k/v (and o/d_o) laid out so that (batch, node,
+                           head) rows form one strided 2D view: node-major (stride_n = heads * stride_h,
+                           stride_b = n * stride_n) or head-major (stride_h = n * stride_n, stride_b =
+                           heads * stride_h). */
 } fwn_tile_list;
 
 /* Version string of the library build. */
@@ -125,6 +130,16 @@ FWN_API fwn_status fwn_tiles_pair_count(const fwn_tile_list* tiles64, int32_t* p
                                 void* stream);
 FWN_API fwn_status fwn_tiles_pair_fill(const fwn_tile_list* tiles64, const int32_t* ptr2, int32_t* kb2,
                                uint32_t* bits2, void* stream);
+
+/* Gathered list from a 128-row list (no counterpart in the reference; derived from build_tile_mask's list):
+ * per block, the distinct columns its rows may attend to, ascending, packed into tiles of 32 slots (the
+ * last tile padded with the block's last column, whose padding slots carry no bits). Pass 1 writes
+ * ptr_g[n_blocks + 1]; pass 2 cols_g[T_g * 32] and bits_g[T_g * 128]. max_block_tiles >= the largest
+ * ptr[b+1] - ptr[b] of the 128-row list (at most 40,960). */
+FWN_API fwn_status fwn_tiles_gather_count(const fwn_tile_list* tiles128, int32_t* ptr_g, void* ws, size_t ws_bytes,
+                                          void* stream);
+FWN_API fwn_status fwn_tiles_gather_fill(const fwn_tile_list* tiles128, int32_t max_block_tiles,
+                                         const int32_t* ptr_g, int32_t* cols_g, uint32_t* bits_g, void* stream);
 
 /* Hilbert-curve codes (3D, `bits` per axis, 1..20) of unit-sphere points given in degrees; non-finite
  * points get INT64_MAX. A stable argsort of the codes is pallas_attn.hilbert_order (pallas_attn.py:41-82). */

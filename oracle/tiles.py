@@ -72,6 +72,55 @@ def pair_tiles(ptr, kb, bits):
   return ptr2.astype(np.int32), (uniq % big).astype(np.int32), bits2
 
 
+def gather_tiles(ptr2, kb2, bits2):
+  """Gathered list derived from a 128-row (paired) list: per block, the distinct columns any of its rows
+  may attend to, ascending, packed into tiles of 32 slots (the last tile padded with its last column,
+  whose padding slots carry no bits). Returns (ptr_g int32[np+1], cols int32[Tg, 32], bits uint32[Tg, 128]);
+  bit j of bits[t, r] allows (row r of the block, column cols[t, j])."""
+  ptr2 = np.asarray(ptr2, np.int64)
+  kb2 = np.asarray(kb2, np.int64)
+  bits2 = np.asarray(bits2, np.uint32)
+  npb = len(ptr2) - 1
+  colmask = np.bitwise_or.reduce(bits2, axis=1) if len(bits2) else np.zeros(0, np.uint32)
+  ptr_g = np.zeros(npb + 1, np.int64)
+  cols_out, bits_out = [], []
+  j = np.arange(32, dtype=np.uint32)
+  for p in range(npb):
+    e0, e1 = ptr2[p], ptr2[p + 1]
+    used = ((colmask[e0:e1, None] >> j) & 1).astype(bool)            # [tiles, 32]
+    keys = (kb2[e0:e1, None] * 32 + j.astype(np.int64))[used]          # ascending
+    slot_of = np.full((e1 - e0, 32), -1, np.int64)
+    slot_of[used] = np.arange(len(keys))
+    ng = -(-len(keys) // 32)
+    cols = np.full(ng * 32, keys[-1] if len(keys) else 0, np.int64)
+    cols[:len(keys)] = keys
+    words = np.zeros((ng, 128), np.uint32)
+    for e in range(e1 - e0):
+      w = bits2[e0 + e]                                                # [128]
+      hit = ((w[:, None] >> j) & 1).astype(bool)                       # [128, 32]
+      rr, jj = np.nonzero(hit)
+      s = slot_of[e, jj]
+      np.bitwise_or.at(words, (s // 32, rr), np.left_shift(np.uint32(1), (s % 32).astype(np.uint32)))
+    cols_out.append(cols.reshape(ng, 32))
+    bits_out.append(words)
+    ptr_g[p + 1] = ptr_g[p] + ng
+  cols = np.concatenate(cols_out) if cols_out else np.zeros((0, 32), np.int64)
+  bits = np.concatenate(bits_out) if bits_out else np.zeros((0, 128), np.uint32)
+  return ptr_g.astype(np.int32), cols.astype(np.int32), bits
+
+
+def gathered_to_dense(ptr_g, cols, bits, n_rows, n_cols, block_q=128):
+  dense = np.zeros((n_rows, n_cols), bool)
+  j = np.arange(32, dtype=np.uint32)
+  for p in range(len(ptr_g) - 1):
+    for t in range(ptr_g[p], ptr_g[p + 1]):
+      hit = ((np.asarray(bits[t], np.uint32)[:, None] >> j) & 1).astype(bool)
+      for r, jj in zip(*np.nonzero(hit)):
+        if p * block_q + r < n_rows:
+          dense[p * block_q + r, cols[t, jj]] = True
+  return dense
+
+
 def tiles_to_dense(ptr, kb, bits, n_rows, n_cols, block_q=BLOCK_Q, block_k=BLOCK_K):
   """Inverse of build_tile_mask: the boolean [n_rows, n_cols] mask the list describes."""
   nqb = len(ptr) - 1

@@ -17,12 +17,12 @@ pytestmark = pytest.mark.gpu
 TOL = {"bf16": 5e-3, "tf32": 5e-3, "tf32x3": 2e-5}
 
 
-def _grads(q, k, v, do, mask, scale, mode, device, tiles=None):
+def _grads(q, k, v, do, mask, scale, mode, device, tiles=None, gather=True):
   from faster_weathernext import _lib
   from faster_weathernext import tiled_attn as ta
   dt = torch.bfloat16 if mode == "bf16" else torch.float32
   if tiles is None:
-    tiles = ta.AttentionTiles.from_mask(mask, device=device)
+    tiles = ta.AttentionTiles.from_mask(mask, device=device, gather=gather)
   m = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[mode]
   tq, tk, tv, tdo = (torch.from_numpy(x).to(device=device, dtype=dt) for x in (q, k, v, do))
   o, lse = ta.attention_forward(tq, tk, tv, tiles, scale, m, with_lse=True)
@@ -36,17 +36,18 @@ def _rounded(mode, arrays):
   return [oa.bf16_round(a) if mode == "bf16" else a for a in arrays]
 
 
+@pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("mode", ["bf16", "tf32"])
 @pytest.mark.parametrize("symmetric", [True, False])
 @pytest.mark.parametrize("batch", [1, 2])
-def test_grads_reference_test_case(golden, cuda, mode, symmetric, batch):
+def test_grads_reference_test_case(golden, cuda, mode, symmetric, batch, gather):
   """tests/test_pallas_kernel.py:72-99: n=300 (padding rows), h=2, d=64, density 0.08, sym / non-sym."""
   q, k, v, do = kernel_inputs(2, (1, 300, 2, 64), 4)
   if batch == 2:
     q2, k2, v2, do2 = kernel_inputs(12, (1, 300, 2, 64), 4)
     q, k, v, do = (np.concatenate([a, b]) for a, b in zip((q, k, v, do), (q2, k2, v2, do2)))
   m = golden_mask(golden["tiles"], "k_sym" if symmetric else "k_nonsym")
-  got = _grads(q, k, v, do, m, 0.125, mode, cuda)
+  got = _grads(q, k, v, do, m, 0.125, mode, cuda, gather=gather)
   ref = oa.sparse_attention_vjp(*_rounded(mode, (q, k, v, do)), m, 0.125)
   for name, a, r in zip(("dq", "dk", "dv"), got, ref):
     assert oa.rel_rms(a, r) < TOL[mode], (name, oa.rel_rms(a, r))
@@ -68,8 +69,8 @@ def test_nonsymmetric_mask_needs_transposed_tiles(golden, cuda):
   q, k, v, do = (pad(x) for x in (q, k, v, do))
   m = golden_mask(golden["tiles"], "k_guard")
   scale = 32 ** -0.5
-  good = ta.AttentionTiles.from_mask(m, device=cuda)
-  wrong = ta.AttentionTiles(good.fwd, good.fwd, 130, True)
+  good = ta.AttentionTiles.from_mask(m, device=cuda, gather=False)
+  wrong = ta.AttentionTiles(good.fwd, good.fwd, 130, True, gather=False)
   ref_dk = golden["attention"]["guard/dk"]
   _, dk_good, _ = _grads(q, k, v, do, m, scale, "tf32", cuda, tiles=good)
   _, dk_bad, _ = _grads(q, k, v, do, m, scale, "tf32", cuda, tiles=wrong)
@@ -95,27 +96,28 @@ def test_grads_config1(golden, cuda, mode):
       assert oa.max_rel(a[0][::int(gold["every"])], gold[f"cfg1/{name}"]) < 3e-2, name
 
 
+@pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("head_dim", [64, 128])
-def test_grads_bf16_odd_sizes_nonsymmetric(cuda, head_dim):
+def test_grads_bf16_odd_sizes_nonsymmetric(cuda, head_dim, gather):
   n = 457
   m = sparse.random(n, n, density=0.05, random_state=11, format="csr").astype(bool)
   m = (m + sparse.identity(n, dtype=bool)).tocsr()
   q, k, v, do = kernel_inputs(6, (2, n, 3, head_dim), 4)
-  got = _grads(q, k, v, do, m, head_dim ** -0.5, "bf16", cuda)
+  got = _grads(q, k, v, do, m, head_dim ** -0.5, "bf16", cuda, gather=gather)
   ref = oa.sparse_attention_vjp(*_rounded("bf16", (q, k, v, do)), m, head_dim ** -0.5)
   for name, a, r in zip(("dq", "dk", "dv"), got, ref):
     assert oa.rel_rms(a, r) < TOL["bf16"], (name, oa.rel_rms(a, r))
 
 
-@pytest.mark.parametrize("mode", ["bf16", "tf32"])
-def test_grads_full_size_config3(cuda, mode):
+@pytest.mark.parametrize("mode,gather", [("bf16", True), ("tf32", True), ("bf16", False)])
+def test_grads_full_size_config3(cuda, mode, gather):
   from faster_weathernext import mesh
   m, _, _ = mesh.config_mask(3)
   n = m.shape[0]
   rng = np.random.default_rng(0)
   q, k, v = (rng.standard_normal((1, n, 8, 64)).astype(np.float32) for _ in range(3))
   do = np.random.default_rng(1).standard_normal((1, n, 8, 64)).astype(np.float32)
-  got = _grads(q, k, v, do, m, 0.125, mode, cuda)
+  got = _grads(q, k, v, do, m, 0.125, mode, cuda, gather=gather)
   ref = oa.sparse_attention_vjp(*_rounded(mode, (q, k, v, do)), m, 0.125)
   for name, a, r in zip(("dq", "dk", "dv"), got, ref):
     assert oa.rel_rms(a, r) < TOL[mode], (name, oa.rel_rms(a, r))

@@ -17,11 +17,11 @@ pytestmark = pytest.mark.gpu
 TOL = {"bf16": 5e-3, "tf32": 5e-3, "tf32x3": 2e-5}
 
 
-def _run(q, k, v, mask, scale, mode, device, with_lse=True):
+def _run(q, k, v, mask, scale, mode, device, with_lse=True, gather=True):
   from faster_weathernext import _lib
   from faster_weathernext import tiled_attn as ta
   dt = torch.bfloat16 if mode == "bf16" else torch.float32
-  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  tiles = ta.AttentionTiles.from_mask(mask, device=device, gather=gather)
   m = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[mode]
   tq, tk, tv = (torch.from_numpy(x).to(device=device, dtype=dt) for x in (q, k, v))
   o, lse = ta.attention_forward(tq, tk, tv, tiles, scale, m, with_lse=with_lse)
@@ -34,14 +34,15 @@ def _inputs_for(mode, arrays):
   return [oa.bf16_round(a) if mode == "bf16" else a for a in arrays]
 
 
+@pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("mode", ["bf16", "tf32"])
 @pytest.mark.parametrize("batch", [1, 2])
-def test_forward_reference_test_case(golden, cuda, mode, batch):
+def test_forward_reference_test_case(golden, cuda, mode, batch, gather):
   """tests/test_pallas_kernel.py:35-55 (n=300, h=2, d=64, density 0.1 + identity) on the GPU."""
   q, k, v = kernel_inputs(0, (2, 300, 2, 64), 3)
   q, k, v = q[:batch], k[:batch], v[:batch]
   m = golden_mask(golden["tiles"], "k_fwd")
-  out, lse = _run(q, k, v, m, 64 ** -0.5, mode, cuda)
+  out, lse = _run(q, k, v, m, 64 ** -0.5, mode, cuda, gather=gather)
   qi, ki, vi = _inputs_for(mode, (q, k, v))
   ref, ref_lse = oa.sparse_attention(qi, ki, vi, m, 64 ** -0.5)
   assert oa.rel_rms(out, ref) < TOL[mode]
@@ -69,15 +70,16 @@ def test_forward_config1(golden, cuda, mode):
     assert oa.max_rel(out[0][::int(a["every"])], a["cfg1/out"]) < 2e-2
 
 
+@pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("head_dim", [64, 128])
-def test_forward_bf16_head_dims_and_odd_sizes(cuda, head_dim):
+def test_forward_bf16_head_dims_and_odd_sizes(cuda, head_dim, gather):
   """n not a multiple of 64/128, H=3, non-symmetric random mask with empty query blocks."""
   from scipy import sparse
   n = 457
   m = sparse.random(n, n, density=0.05, random_state=11, format="csr").astype(bool)
   m = (m + sparse.identity(n, dtype=bool)).tocsr()
   q, k, v = kernel_inputs(5, (2, n, 3, head_dim), 3)
-  out, lse = _run(q, k, v, m, head_dim ** -0.5, "bf16", cuda)
+  out, lse = _run(q, k, v, m, head_dim ** -0.5, "bf16", cuda, gather=gather)
   ref, ref_lse = oa.sparse_attention(*_inputs_for("bf16", (q, k, v)), m, head_dim ** -0.5)
   assert oa.rel_rms(out, ref) < TOL["bf16"]
   np.testing.assert_allclose(lse[:, :, :n], ref_lse, rtol=0, atol=2e-2)
@@ -113,8 +115,9 @@ def test_forward_strided_input_layout(cuda):
   assert oa.rel_rms(o.float().cpu().numpy(), ref) < TOL["bf16"]
 
 
-@pytest.mark.parametrize("cfg,mode", [(2, "bf16"), (3, "bf16"), (3, "tf32")])
-def test_forward_full_size_configs(cuda, cfg, mode):
+@pytest.mark.parametrize("cfg,mode,gather", [(2, "bf16", True), (3, "bf16", True), (3, "tf32", True),
+                                             (3, "bf16", False)])
+def test_forward_full_size_configs(cuda, cfg, mode, gather):
   """Configurations 2 and 3 at full size (oracle on the allowed pairs only)."""
   from faster_weathernext import mesh
   m, _, _ = mesh.config_mask(cfg)
@@ -122,7 +125,21 @@ def test_forward_full_size_configs(cuda, cfg, mode):
   n = m.shape[0]
   rng = np.random.default_rng(0)
   q, k, v = (rng.standard_normal((b, n, h, d)).astype(np.float32) for _ in range(3))
-  out, lse = _run(q, k, v, m, d ** -0.5, mode, cuda)
+  out, lse = _run(q, k, v, m, d ** -0.5, mode, cuda, gather=gather)
   ref, ref_lse = oa.sparse_attention(*_inputs_for(mode, (q, k, v)), m, d ** -0.5)
   assert oa.rel_rms(out, ref) < TOL[mode]
   assert np.abs(lse[:, :, :n] - ref_lse).max() < 5e-2
+
+
+def test_forward_head_major_layout_gathered(cuda):
+  """q, k, v as [B, n, H, D] views of head-major [B, H, n, D] storage: gathered rows use (b, h, node)."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  m, _, _ = mesh.config_mask(1)
+  x = torch.randn(3, 2, 4, 642, 64, device=cuda, dtype=torch.bfloat16)
+  q, k, v = (x[i].transpose(1, 2) for i in range(3))
+  assert ta._gather_layout(q) == 1
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  o = ta.attention(q, k, v, tiles, scale=0.125)
+  ref, _ = oa.sparse_attention(*(t.float().cpu().numpy() for t in (q, k, v)), m, 0.125)
+  assert oa.rel_rms(o.float().cpu().numpy(), ref) < TOL["bf16"]

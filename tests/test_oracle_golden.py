@@ -148,3 +148,17 @@ def test_chunked_vjp_matches_analytic_gradient(golden):
   got = oa.chunked_attention_vjp(q, k, v, do, m, 0.125, chunk=64, dtype=np.float64)
   for nm, x in zip(("dq", "dk", "dv"), got):
     np.testing.assert_allclose(x[0][::ev], a[f"grad_sym/{nm}"], rtol=1e-5, atol=1e-6, err_msg=nm)
+
+
+def test_gathered_lists_cover_the_same_mask(golden):
+  g = golden["tiles"]
+  for name in ("rand257", "k_nonsym", "cfg1"):
+    m = golden_mask(g, name)
+    p2, kb2, b2 = ot.pair_tiles(*ot.build_tile_mask(m))
+    pg, cols, bits = ot.gather_tiles(p2, kb2, b2)
+    np.testing.assert_array_equal(ot.gathered_to_dense(pg, cols, bits, m.shape[0], m.shape[1]), m.toarray())
+    for p in range(len(pg) - 1):
+      c = cols[pg[p]:pg[p + 1]].ravel()
+      assert (np.diff(c) >= 0).all()                      # ascending (padding repeats the last column)
+      rows = np.arange(p * 128, min(m.shape[0], p * 128 + 128))
+      assert len(np.unique(c)) == len(np.unique(m[rows].indices))

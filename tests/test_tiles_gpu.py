@@ -118,3 +118,17 @@ def test_hilbert_order_config_digests(golden, cuda, cfg):
   from faster_weathernext import tiled_attn as ta
   _, lat, lon = mesh.config_mask(cfg)
   assert digest(ta.hilbert_order(lat, lon).astype(np.int64)) == golden["digests"][f"cfg{cfg}/hilbert"]
+
+
+def test_gather_lists_match_oracle(golden, cuda):
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  g = golden["tiles"]
+  cases = [golden_mask(g, nm) for nm in ("rand100", "rand257", "rand1000", "k_nonsym_T", "cfg1")]
+  cases.append(mesh.config_mask(3)[0])
+  for m in cases:
+    t128 = ta.pair_tiles(_build(m, cuda))
+    got = ta.gather_tiles(t128).numpy()
+    ref = ot.gather_tiles(*ot.pair_tiles(*ot.build_tile_mask(m)))
+    for a, b in zip(got, ref):
+      np.testing.assert_array_equal(a, b)
