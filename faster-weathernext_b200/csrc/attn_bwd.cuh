@@ -180,15 +180,29 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (whole warp)
+    // Tile metadata is prefetched two chunks ahead, and the next item's list range one item ahead.
     uint32_t g = 0, qc = 0;
     bool ok = true;
     int pending_r = 0;
     constexpr uint32_t kColBytes = C::SUB * D * C::ES;  // one 32-wide tile of one column operand
-    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+    int it = blockIdx.x;
+    int nt0 = 0, nt1 = 0;
+    if (it < p.n_items) {
+      nt0 = __ldg(p.ptr2 + it % per_bh);
+      nt1 = __ldg(p.ptr2 + it % per_bh + 1);
+    }
+    for (; it < p.n_items && ok; it += gridDim.x) {
       const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int t0 = nt0, n_sub = nt1 - nt0;
+      const int it_next = it + gridDim.x;
+      if (it_next < p.n_items) {
+        nt0 = __ldg(p.ptr2 + it_next % per_bh);
+        nt1 = __ldg(p.ptr2 + it_next % per_bh + 1);
+      }
       const int nch = (n_sub + CH - 1) / CH;
       if (nch == 0) continue;
+      ChunkMeta<CH> m0 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
+      ChunkMeta<CH> m1 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
       if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
       if (lane == 0) {
         mbar_arrive_expect_tx(r_full, 2 * C::R_BYTES);
@@ -200,63 +214,79 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       pending_r = 1;
       const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
       const int row_mul = p.head_major ? 1 : p.heads;
-      for (int c = 0; c < nch; ++c, ++g) {
-        const int st = g % C::NS;
-        if (!(ok = mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
-        const int n_in = min(CH, n_sub - CH * c);
-        // Gathered dK/dV: lse / delta of the gathered queries are stored by the lanes, not copied.
-        const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + ((kDKV && !GATHER) ? 256 : 0);
-        if (lane == 0) mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
-        __syncwarp();
-        const uint32_t sb = stage(st);
-        for (int s = 0; s < n_in; ++s) {
-          const int t = t0 + CH * c + s;
-          if constexpr (GATHER) {
-            const int col = p.cols[static_cast<size_t>(t) * 32 + lane];
-            const int row = col * row_mul + row_base;
-            const int j = lane & 7, which = lane >> 3;  // which: 0 C0, 1 C1, 2 C0 (MN copy), 3 C1 (MN copy)
-            const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
-            const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
-            if (which < 2 + C::NMN) {
-              const void* tm = which == 0 ? static_cast<const void*>(&tm_c0)
-                               : which == 1 ? static_cast<const void*>(&tm_c1)
-                               : which == 2 ? static_cast<const void*>(&tm_c0mn)
-                                            : static_cast<const void*>(&tm_c1mn);
-              const uint32_t dst = sb + which * C::C_BYTES + s * C::SUB * 128 + j * 512;
-              for (int cb = 0; cb < C::CB; ++cb)
-                tma_gather4(dst + cb * C::COLS * 128, tm, cb * C::EPB, r0, r1, r2, r3, c_full(st));
-            }
-            if constexpr (kDKV) {
-              const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col;
-              asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(p.lse[vo])
-                           : "memory");
-              asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + 128 + lane * 4),
-                           "f"(p.delta[vo])
-                           : "memory");
-            }
-          } else if (lane == 0) {
-            const int col0 = p.kb2[t] * C::SUB;
-            for (int cb = 0; cb < C::CB; ++cb) {
-              const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
-              tma_load_4d(sb + off, &tm_c0, cb * C::EPB, h, col0, b, c_full(st));
-              tma_load_4d(sb + C::C_BYTES + off, &tm_c1, cb * C::EPB, h, col0, b, c_full(st));
-              if (C::NMN >= 1) tma_load_4d(sb + 2 * C::C_BYTES + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
-              if (C::NMN >= 2) tma_load_4d(sb + 3 * C::C_BYTES + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
-            }
-            if (kDKV) {
-              const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col0;
-              bulk_load(sb + C::VEC_OFF + s * 256, p.lse + vo, 128, c_full(st));
-              bulk_load(sb + C::VEC_OFF + s * 256 + 128, p.delta + vo, 128, c_full(st));
-            }
-          }
-          if (lane == 0) bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
-        }
-        if constexpr (GATHER && kDKV) {
-          // Second arrival of c_full: publishes the lanes' lse / delta stores.
+      // Chunk c's copies; `meta` was loaded two chunks earlier. The loop below is unrolled by two so that
+      // each prefetched register pair is consumed in place (a register move would wait for the load).
+      auto issue_chunk = [&](int c, const ChunkMeta<CH>& meta) -> bool {
+          const int st = g % C::NS;
+          if (!mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
+          const int n_in = min(CH, n_sub - CH * c);
+          // Gathered dK/dV: lse / delta of the gathered queries are stored by the lanes, not copied.
+          const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + ((kDKV && !GATHER) ? 256 : 0);
+          if (lane == 0) mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
           __syncwarp();
-          if (lane == 0) mbar_arrive(c_full(st));
+          const uint32_t sb = stage(st);
+  #pragma unroll
+          for (int s = 0; s < CH; ++s) {
+            if (s >= n_in) break;
+            const int t = t0 + CH * c + s;
+            if constexpr (GATHER) {
+              const int col = meta.v[s];
+              const int row = col * row_mul + row_base;
+              const int j = lane & 7, which = lane >> 3;  // which: 0 C0, 1 C1, 2 C0 (MN copy), 3 C1 (MN copy)
+              const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
+              const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
+              if (which < 2 + C::NMN) {
+                const void* tm = which == 0 ? static_cast<const void*>(&tm_c0)
+                                 : which == 1 ? static_cast<const void*>(&tm_c1)
+                                 : which == 2 ? static_cast<const void*>(&tm_c0mn)
+                                              : static_cast<const void*>(&tm_c1mn);
+                const uint32_t dst = sb + which * C::C_BYTES + s * C::SUB * 128 + j * 512;
+                for (int cb = 0; cb < C::CB; ++cb)
+                  tma_gather4(dst + cb * C::COLS * 128, tm, cb * C::EPB, r0, r1, r2, r3, c_full(st));
+              }
+              if constexpr (kDKV) {
+                const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col;
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(p.lse[vo])
+                             : "memory");
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + 128 + lane * 4),
+                             "f"(p.delta[vo])
+                             : "memory");
+              }
+            } else if (lane == 0) {
+              const int col0 = meta.v[s] * C::SUB;
+              for (int cb = 0; cb < C::CB; ++cb) {
+                const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
+                tma_load_4d(sb + off, &tm_c0, cb * C::EPB, h, col0, b, c_full(st));
+                tma_load_4d(sb + C::C_BYTES + off, &tm_c1, cb * C::EPB, h, col0, b, c_full(st));
+                if (C::NMN >= 1) tma_load_4d(sb + 2 * C::C_BYTES + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
+                if (C::NMN >= 2) tma_load_4d(sb + 3 * C::C_BYTES + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
+              }
+              if (kDKV) {
+                const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col0;
+                bulk_load(sb + C::VEC_OFF + s * 256, p.lse + vo, 128, c_full(st));
+                bulk_load(sb + C::VEC_OFF + s * 256 + 128, p.delta + vo, 128, c_full(st));
+              }
+            }
+            if (lane == 0) bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
+          }
+          if constexpr (GATHER && kDKV) {
+            // Second arrival of c_full: publishes the lanes' lse / delta stores.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(c_full(st));
+          }
+        return true;
+      };
+      for (int c = 0; c < nch && ok; c += 2) {
+        if (!(ok = issue_chunk(c, m0))) break;
+        ++g;
+        m0 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, c + 2, lane);
+        if (c + 1 < nch) {
+          if (!(ok = issue_chunk(c + 1, m1))) break;
+          ++g;
+          m1 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, c + 3, lane);
         }
       }
+      if (!ok) break;
       ++qc;
     }
     if (!ok && lane == 0) {

@@ -44,6 +44,7 @@ struct FwdParams {
   int64_t o_sb, o_sn, o_sh;
   int batch, heads, n, np, lse_rows, n_items;
   float scale_log2;       // scale * log2(e)
+  unsigned long long* trace;  // FWN_TRACE builds: kTraceCtas x kTraceEvents event records (else unused)
 };
 
 template <int D, bool F32>
@@ -105,7 +106,11 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int trace_count;
+  const long long trace_t0 = clock64();
+#define FWN_TR(code, arg) trace_event(p.trace, &trace_count, trace_t0, (code), (arg))
   if (threadIdx.x == 0) {
+    trace_count = 0;
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
@@ -138,16 +143,32 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
   const int per_bh = p.np;
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (whole warp)
+    // Tile metadata is prefetched two chunks ahead, and the next item's list range one item ahead.
     uint32_t g = 0, qc = 0;
     bool ok = true;
     int pending_q = 0;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+    int it = blockIdx.x;
+    int nt0 = 0, nt1 = 0;
+    if (it < p.n_items) {
+      nt0 = __ldg(p.ptr2 + it % per_bh);
+      nt1 = __ldg(p.ptr2 + it % per_bh + 1);
+    }
+    for (; it < p.n_items && ok; it += gridDim.x) {
       const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int t0 = nt0, n_sub = nt1 - nt0;
+      const int it_next = it + gridDim.x;
+      if (it_next < p.n_items) {
+        nt0 = __ldg(p.ptr2 + it_next % per_bh);
+        nt1 = __ldg(p.ptr2 + it_next % per_bh + 1);
+      }
       const int nch = (n_sub + 1) >> 1;
       if (nch == 0) continue;
+      ChunkMeta<2> m0 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
+      ChunkMeta<2> m1 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
+      if (lane == 0) FWN_TR(1, it);
       if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
       if (lane == 0) {
+        FWN_TR(2, nch);
         mbar_arrive_expect_tx(q_full, C::Q_BYTES);
         for (int cb = 0; cb < C::CB; ++cb)
           tma_load_4d(q_smem + cb * C::ROWS * 128, &tm_q, cb * C::EPB, h, pb * C::ROWS, b, q_full);
@@ -156,38 +177,55 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
       // Gathered mode: row of the 2D view of K / V holding (batch b, node `key`, head h).
       const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
       const int row_mul = p.head_major ? 1 : p.heads;
-      for (int c = 0; c < nch; ++c, ++g) {
-        const int st = g % C::NS;
-        if (!(ok = mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
-        const int n_in = min(2, n_sub - 2 * c);
-        if (lane == 0) mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
-        __syncwarp();
-        for (int s = 0; s < n_in; ++s) {
-          const int t = t0 + 2 * c + s;
-          if constexpr (GATHER) {
-            // Lane i holds slot i's row; lanes 0-7 gather K rows 4j..4j+3, lanes 8-15 V rows.
-            const int row = p.cols[static_cast<size_t>(t) * 32 + lane] * row_mul + row_base;
-            const int j = lane & 7;
-            const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
-            const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
-            if (lane < 16) {
-              const uint32_t dst = (lane < 8 ? stage_k(st) : stage_v(st)) + s * C::SUB * 128 + j * 512;
-              const void* tm = lane < 8 ? static_cast<const void*>(&tm_k) : static_cast<const void*>(&tm_v);
-              for (int cb = 0; cb < C::CB; ++cb)
-                tma_gather4(dst + cb * C::KEYS * 128, tm, cb * C::EPB, r0, r1, r2, r3, kv_full(st));
+      // Chunk c's copies; `meta` was loaded two chunks earlier. The loop below is unrolled by two so that
+      // each prefetched register pair is consumed in place (a register move would wait for the load).
+      auto issue_chunk = [&](int c, const ChunkMeta<2>& meta) -> bool {
+          const int st = g % C::NS;
+          if (!mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
+          const int n_in = min(2, n_sub - 2 * c);
+          if (lane == 0) FWN_TR(3, c);
+          if (lane == 0) mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
+          __syncwarp();
+  #pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            if (s >= n_in) break;
+            const int t = t0 + 2 * c + s;
+            if constexpr (GATHER) {
+              // Lane i holds slot i's row; lanes 0-7 gather K rows 4j..4j+3, lanes 8-15 V rows.
+              const int row = meta.v[s] * row_mul + row_base;
+              const int j = lane & 7;
+              const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
+              const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
+              if (lane < 16) {
+                const uint32_t dst = (lane < 8 ? stage_k(st) : stage_v(st)) + s * C::SUB * 128 + j * 512;
+                const void* tm = lane < 8 ? static_cast<const void*>(&tm_k) : static_cast<const void*>(&tm_v);
+                for (int cb = 0; cb < C::CB; ++cb)
+                  tma_gather4(dst + cb * C::KEYS * 128, tm, cb * C::EPB, r0, r1, r2, r3, kv_full(st));
+              }
+            } else if (lane == 0) {
+              const int key0 = meta.v[s] * C::SUB;
+              for (int cb = 0; cb < C::CB; ++cb) {
+                tma_load_4d(stage_k(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_k, cb * C::EPB, h, key0, b,
+                            kv_full(st));
+                tma_load_4d(stage_v(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_v, cb * C::EPB, h, key0, b,
+                            kv_full(st));
+              }
             }
-          } else if (lane == 0) {
-            const int key0 = p.kb2[t] * C::SUB;
-            for (int cb = 0; cb < C::CB; ++cb) {
-              tma_load_4d(stage_k(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_k, cb * C::EPB, h, key0, b,
-                          kv_full(st));
-              tma_load_4d(stage_v(st) + cb * C::KEYS * 128 + s * C::SUB * 128, &tm_v, cb * C::EPB, h, key0, b,
-                          kv_full(st));
-            }
+            if (lane == 0) bulk_load(stage_bits(st) + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, kv_full(st));
           }
-          if (lane == 0) bulk_load(stage_bits(st) + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, kv_full(st));
+        return true;
+      };
+      for (int c = 0; c < nch && ok; c += 2) {
+        if (!(ok = issue_chunk(c, m0))) break;
+        ++g;
+        m0 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, c + 2, lane);
+        if (c + 1 < nch) {
+          if (!(ok = issue_chunk(c + 1, m1))) break;
+          ++g;
+          m1 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, c + 3, lane);
         }
       }
+      if (!ok) break;
       ++qc;
     }
     if (!ok && lane == 0) {
@@ -217,6 +255,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         const int nch = (n_sub + 1) >> 1;
         if (nch == 0) continue;
         if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+        FWN_TR(10, it);
         const uint32_t g0 = g;
         for (int c = 0; c <= nch && ok; ++c) {
           if (c < nch) {
@@ -235,6 +274,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
               mma_ss<F32>(tmem + sb * 64, a, bdesc, idesc_s, kk > 0 ? 1u : 0u);
             }
             mma_commit(s_full(sb));
+            FWN_TR(11, c);
             if (c == nch - 1) mma_commit(q_empty);
           }
           if (c >= 1) {
@@ -254,6 +294,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
             }
             mma_commit(p_empty(pbuf));
             mma_commit(kv_empty(st));
+            FWN_TR(12, c - 1);
             if (c == nch) mma_commit(o_full);
           }
         }
@@ -285,10 +326,12 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         const int n_in = min(2, n_sub - 2 * c);
         float s[64];
         if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
+        if (warp == 2 && lane == 0) FWN_TR(20, c);
         tc_fence_after();
         tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
         if (n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
         tmem_wait_ld();
+        if (warp == 2 && lane == 0) FWN_TR(24, c);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty(sb));
@@ -299,7 +342,8 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
         // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
         // of the warp may attend to is skipped by the whole warp.
-        float mx = -INFINITY;
+        // Four independent partial maxima / sums keep the dependency chains short.
+        float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           const uint32_t w = g < 4 ? w0 : w1;
@@ -308,10 +352,12 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const int j = 8 * g + i;
-              mx = (w & (1u << (j & 31))) ? fmaxf(mx, s[j]) : mx;
+              mxp[i & 3] = (w & (1u << (j & 31))) ? fmaxf(mxp[i & 3], s[j]) : mxp[i & 3];
             }
           }
         }
+        const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+        if (warp == 2 && lane == 0) FWN_TR(25, c);
         const float m_new = mx * p.scale_log2;
         const float m_old = m_ref;
         const bool grow = m_new > m_ref + 8.0f;
@@ -322,6 +368,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
           l *= corr;
         }
         const float neg_m = -m_ref;
+        float lp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           const uint32_t w = g < 4 ? w0 : w1;
@@ -333,13 +380,15 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
               const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
               const float e = (w & (1u << (j & 31))) ? t : 0.f;
               s[j] = e;
-              l += e;
+              lp[i & 3] += e;
             }
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) s[8 * g + i] = 0.f;
           }
         }
+        l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+        if (warp == 2 && lane == 0) FWN_TR(26, c);
         // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
         if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
         const uint32_t pbase = p_smem(sb);
@@ -363,10 +412,12 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
           }
         }
         fence_proxy_async_smem();
+        if (warp == 2 && lane == 0) FWN_TR(27, c);
         // Rescale O rows whose reference max grew (rows that saw no allowed key yet hold O = 0).
         const bool rescale = grow && m_old != -INFINITY;
         if (__any_sync(0xffffffffu, rescale)) {
           const uint32_t prev = gg - 1;
+          if (warp == 2 && lane == 0) FWN_TR(28, c);
           if (!(ok = mbar_wait(p_empty(prev & 1), (prev >> 1) & 1, abort_flag))) break;
           tc_fence_after();
 #pragma unroll
@@ -383,6 +434,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(sb));
+        if (warp == 2 && lane == 0) FWN_TR(21, c);
       }
       if (!ok) break;
       g = g0 + nch;
@@ -404,6 +456,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         continue;
       }
       if (!(ok = mbar_wait(o_full, qc & 1, abort_flag))) break;
+      if (warp == 2 && lane == 0) FWN_TR(22, it);
       tc_fence_after();
 #pragma unroll
       for (int j = 0; j < D / 32; ++j) {
@@ -428,6 +481,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_empty);
+      if (warp == 2 && lane == 0) FWN_TR(23, it);
       ++qc;
     }
   }
@@ -435,6 +489,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+#undef FWN_TR
 }
 
 }  // namespace fwn

@@ -25,6 +25,52 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 // ---------------------------------------------------------------------------------------------------
+// Event tracing (builds with -DFWN_TRACE only): CTAs < kTraceCtas append (clock64 delta, role event
+// code, argument) records to a caller buffer of kTraceCtas x kTraceEvents words, for per-role timelines.
+
+constexpr int kTraceCtas = 4;
+constexpr int kTraceEvents = 4096;
+
+__device__ __forceinline__ void trace_event(unsigned long long* buf, int* counter, long long t0, int code,
+                                            int arg) {
+#ifdef FWN_TRACE
+  if (buf != nullptr && blockIdx.x < kTraceCtas) {
+    const int i = atomicAdd(counter, 1);
+    if (i < kTraceEvents) {
+      const unsigned long long dt = static_cast<unsigned long long>(clock64() - t0) & 0xFFFFFFFFFFull;
+      buf[blockIdx.x * kTraceEvents + i] = dt | (static_cast<unsigned long long>(code & 0xFF) << 56) |
+                                           (static_cast<unsigned long long>(arg & 0xFFFF) << 40);
+    }
+  }
+#else
+  (void)buf; (void)counter; (void)t0; (void)code; (void)arg;
+#endif
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Tile metadata prefetch for producer warps. The column block (tile mode) or the per-lane column
+// (gathered mode) of each tile is read from global memory a few chunks before its TMA copies are
+// issued, so the dependent load latency is not on the producer's critical path.
+
+template <int CH>
+struct ChunkMeta {
+  int v[CH];
+};
+
+template <int CH, bool GATHER>
+__device__ __forceinline__ ChunkMeta<CH> load_chunk_meta(const int32_t* kb, const int32_t* cols, int t0, int n_sub,
+                                                         int c, int lane) {
+  ChunkMeta<CH> m;
+#pragma unroll
+  for (int s = 0; s < CH; ++s) {
+    const int i = CH * c + s;
+    m.v[s] = 0;
+    if (i < n_sub) m.v[s] = GATHER ? __ldg(cols + static_cast<size_t>(t0 + i) * 32 + lane) : __ldg(kb + t0 + i);
+  }
+  return m;
+}
+
+// ---------------------------------------------------------------------------------------------------
 // mbarrier
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

@@ -141,7 +141,7 @@ fwn_status check_tiles(const fwn_tile_list* t, const fwn_attn_desc* d, const cha
                 name, t->block_rows);
   if (t->n_blocks != (d->n + 127) / 128)
     return fail(FWN_ERR_INVALID_ARGUMENT, "%s: %d blocks for n=%d (expected %d)", name, t->n_blocks, d->n, (d->n + 127) / 128);
-  if (!t->ptr || (t->n_tiles > 0 && (!t->kb || !t->bits)))
+  if (!t->ptr || (t->n_tiles > 0 && ((!t->kb && !t->cols) || !t->bits)))
     return fail(FWN_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (!aligned16(t->bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "%s: bits must be 16-byte aligned", name);
   if (t->cols && t->n_tiles > 0 && !aligned16(t->cols))
@@ -179,6 +179,17 @@ fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, 
   return FWN_OK;
 }
 
+#ifdef FWN_TRACE
+unsigned long long* g_trace = nullptr;
+unsigned long long* trace_buffer_peek() { return g_trace; }
+// Trace builds: one device buffer of kTraceCtas x kTraceEvents records, cleared per launch.
+unsigned long long* trace_buffer() {
+  if (!g_trace) cudaMalloc(&g_trace, sizeof(unsigned long long) * fwn::kTraceCtas * fwn::kTraceEvents);
+  cudaMemset(g_trace, 0, sizeof(unsigned long long) * fwn::kTraceCtas * fwn::kTraceEvents);
+  return g_trace;
+}
+#endif
+
 template <int D, bool F32, bool GATHER>
 fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
                       void* o, float* lse, int layout, cudaStream_t stream) {
@@ -211,6 +222,9 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   p.lse_rows = fwn_lse_rows(d.n);
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale_log2 = d.scale * 1.4426950408889634f;
+#ifdef FWN_TRACE
+  p.trace = trace_buffer();
+#endif
   auto kernel = fwn::attn_fwd_kernel<D, F32, GATHER>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
@@ -522,6 +536,15 @@ fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, const void
                             size_t ws_bytes, void* stream) {
   return bwd_dispatch(desc, q, k, v, nullptr, lse, d_o, nullptr, tiles_t, nullptr, dk, dv, ws, ws_bytes, kDkv, stream);
 }
+
+#ifdef FWN_TRACE
+FWN_API int fwn_trace_dump(unsigned long long* host, int words) {
+  const int n = fwn::kTraceCtas * fwn::kTraceEvents;
+  cudaDeviceSynchronize();
+  cudaMemcpy(host, trace_buffer_peek(), sizeof(unsigned long long) * (words < n ? words : n), cudaMemcpyDeviceToHost);
+  return n;
+}
+#endif
 
 }  // extern "C"
 
