@@ -150,14 +150,11 @@ fwn_status check_tiles(const fwn_tile_list* t, const fwn_attn_desc* d, const cha
   return FWN_OK;
 }
 
+// SMs of the current device (queried per call: a process may drive several devices).
 int num_sms() {
-  static int sms = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  });
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
   return sms;
 }
 
