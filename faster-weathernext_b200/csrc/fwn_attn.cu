@@ -176,6 +176,32 @@ fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, 
   return FWN_OK;
 }
 
+// Delta rows of fwn_attn_bwd_noalloc: a fixed array in every device that loads this library, so that
+// callers without an allocator can run the backward (4 MiB per device, held until the process exits).
+// Host code cannot use the symbol as a pointer; its device address is looked up once per device.
+static __device__ __align__(256) float g_noalloc_delta[FWN_NOALLOC_DELTA_ROWS];
+
+std::mutex g_noalloc_mutex;
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_delta on the current device (looked up on the first call per device).
+fwn_status noalloc_delta(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FWN_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_delta);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(delta scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return FWN_OK;
+}
+
 #ifdef FWN_TRACE
 unsigned long long* g_trace = nullptr;
 unsigned long long* trace_buffer_peek() { return g_trace; }
@@ -532,6 +558,23 @@ fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, const void
                             const void* d_o, const fwn_tile_list* tiles_t, void* dk, void* dv, const void* ws,
                             size_t ws_bytes, void* stream) {
   return bwd_dispatch(desc, q, k, v, nullptr, lse, d_o, nullptr, tiles_t, nullptr, dk, dv, ws, ws_bytes, kDkv, stream);
+}
+
+fwn_status fwn_attn_bwd_noalloc(const fwn_attn_desc* desc, const void* q, const void* k, const void* v, const void* o,
+                                const float* lse, const void* d_o, const fwn_tile_list* tiles,
+                                const fwn_tile_list* tiles_t, void* dq, void* dk, void* dv, void* stream) {
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  const long long rows = static_cast<long long>(desc->batch) * desc->heads * fwn_lse_rows(desc->n);
+  if (rows > FWN_NOALLOC_DELTA_ROWS)
+    return fail(FWN_ERR_WORKSPACE,
+                "fwn_attn_bwd_noalloc: batch * heads * lse_rows = %lld exceeds its fixed capacity of %d rows; "
+                "use fwn_attn_bwd with a workspace",
+                rows, FWN_NOALLOC_DELTA_ROWS);
+  float* delta = nullptr;
+  if ((s = noalloc_delta(&delta)) != FWN_OK) return s;
+  return bwd_dispatch(desc, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta,
+                      static_cast<size_t>(FWN_NOALLOC_DELTA_ROWS) * sizeof(float), kAll, stream);
 }
 
 #ifdef FWN_TRACE

@@ -27,7 +27,7 @@ MODE_TF32X3 = 2
 SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_rows",
            "fwn_tiles_workspace_size", "fwn_tiles_count", "fwn_tiles_fill", "fwn_tiles_pair_count",
            "fwn_tiles_pair_fill", "fwn_tiles_gather_count", "fwn_tiles_gather_fill", "fwn_hilbert_codes", "fwn_attn_fwd", "fwn_attn_bwd_workspace_size", "fwn_attn_bwd",
-           "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv")
+           "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv", "fwn_attn_bwd_noalloc")
 
 
 class AttnDesc(ctypes.Structure):
@@ -74,6 +74,8 @@ def _declare(lib):
       "fwn_attn_bwd_workspace_size": [ctypes.POINTER(AttnDesc), ctypes.POINTER(_SZ)],
       "fwn_attn_bwd": [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, ctypes.POINTER(TileList),
                        ctypes.POINTER(TileList), _P, _P, _P, _P, _SZ, _P],
+      "fwn_attn_bwd_noalloc": [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, ctypes.POINTER(TileList),
+                               ctypes.POINTER(TileList), _P, _P, _P, _P],
       "fwn_attn_bwd_delta": [ctypes.POINTER(AttnDesc), _P, _P, _P, _SZ, _P],
       "fwn_attn_bwd_dq": [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, ctypes.POINTER(TileList), _P, _P, _SZ, _P],
       "fwn_attn_bwd_dkv": [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, ctypes.POINTER(TileList), _P, _P, _P, _SZ,

@@ -177,6 +177,26 @@ FWN_API fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, co
                                     const float* lse, const void* d_o, const fwn_tile_list* tiles_t, void* dk,
                                     void* dv, const void* ws, size_t ws_bytes, void* stream);
 
+/* ---- backward without a caller workspace ---------------------------------------------------------------
+ * No counterpart in the reference. fwn_attn_bwd needs a workspace for the per-row delta = rowsum(o * d_o);
+ * this variant keeps delta in a fixed device array inside the library instead, for callers that cannot
+ * allocate device memory at the point of the call: an XLA / jax.ffi custom-call handler whose buffers are
+ * all owned by XLA, code that runs while another component holds the allocator, or a loop that must not
+ * take cudaMalloc's implicit device synchronisation. The caller still passes every input and output.
+ *   - Capacity: batch * heads * fwn_lse_rows(n) <= FWN_NOALLOC_DELTA_ROWS (4 MiB of float32); larger
+ *     problems are rejected with FWN_ERR_WORKSPACE.
+ *   - The first call on each device looks up the array's device address (with that device current);
+ *     make that first call before any stream capture.
+ *   - The array is shared by every call on a device and keeps the last call's contents; each call
+ *     rewrites all of the rows it reads. Calls that overlap on the GPU (different streams, no ordering)
+ *     race on it: order them, or use fwn_attn_bwd with separate workspaces.
+ *   - Nothing is allocated, freed or synchronised. */
+#define FWN_NOALLOC_DELTA_ROWS (1 << 20)
+FWN_API fwn_status fwn_attn_bwd_noalloc(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                                        const void* o, const float* lse, const void* d_o,
+                                        const fwn_tile_list* tiles, const fwn_tile_list* tiles_t, void* dq,
+                                        void* dk, void* dv, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
