@@ -2,6 +2,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -158,20 +159,31 @@ int num_sms() {
   return sms;
 }
 
+// Resident CTAs per SM from the device limits: shared memory (plus the per-block reservation), registers
+// (allocated per warp in units of 256), threads, and tensor memory (512 columns per SM; an allocation that
+// cannot be satisfied waits for a resident CTA to free its columns). The runtime occupancy query reports
+// one CTA per SM for these kernels where two fit by all of these limits, so it is not used.
 template <typename Kernel>
 fwn_status persistent_grid(Kernel kernel, int threads, int smem, int tmem_cols, int items, int* grid) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-  // Ask for the full shared-memory carveout so that the occupancy below is the one the launch gets.
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  cudaFuncAttributes fa;
+  if ((e = cudaFuncGetAttributes(&fa, kernel)) != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+  int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, threads_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+  const int warps = (threads + 31) / 32;
+  const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
+  int per_sm = smem_sm / (smem + static_cast<int>(fa.sharedSizeBytes) + reserved);
+  per_sm = std::min(per_sm, regs_sm / std::max(1, regs_warp * warps));
+  per_sm = std::min(per_sm, threads_sm / threads);
+  per_sm = std::min(per_sm, 512 / tmem_cols);
   if (per_sm < 1) return fail(FWN_ERR_LAUNCH, "kernel does not fit on an SM");
-  // Resident CTAs must never ask for more tensor memory than an SM has (512 columns): an allocation
-  // that cannot be satisfied would wait for a CTA that never exits.
-  if (per_sm * tmem_cols > 512) per_sm = 512 / tmem_cols;
   *grid = items < per_sm * num_sms() ? items : per_sm * num_sms();
   return FWN_OK;
 }
