@@ -37,9 +37,8 @@ CFG = 3
 # Kernel FLOP counts per allowed (query, key) pair per head and head_dim element: forward S and P V (4);
 # dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
 USEFUL_PER_PAIR = 14
-# DRAM bytes per launch of the dominant kernel at this workload from one ncu capture
-# (profiles/ncu_cfg3_bf16.md); None until captured for the current build.
-NCU_TRAFFIC = {}
+# DRAM bytes (read + write) per launch at this workload from one ncu capture (profiles/ncu_cfg3_bf16.md).
+NCU_TRAFFIC = {"attn_fwd": 152_893_952, "attn_bwd_dq": 201_407_296, "attn_bwd_dkv": 229_749_760}
 
 
 def peaks():

@@ -83,38 +83,42 @@ struct BwdCfg {
 };
 
 // delta[b, h, r] = sum_d O[b, r, h, d] * dO[b, r, h, d] (fp32); rows r in [n, lse_rows) get 0.
+// HBM-bound: each lane loads 16 bytes of O and of dO, a row is LPR consecutive lanes (a 128- or
+// 256-byte row), so one warp reads 32 x 16 bytes of each tensor per step, fully coalesced.
 template <bool F32, int D>
 __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ o, const void* __restrict__ d_o,
                                                     float* __restrict__ delta, int heads, int n, int lse_rows,
                                                     int64_t sb, int64_t sn, int64_t sh, int total_rows) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= total_rows) return;
-  const int r = warp % lse_rows, bh = warp / lse_rows, h = bh % heads, b = bh / heads;
+  constexpr int ES = F32 ? 4 : 2;
+  constexpr int LPR = D * ES / 16;          // lanes per row
+  constexpr int RPW = 32 / LPR;             // rows per warp
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int row_id = gwarp * RPW + lane / LPR, part = lane % LPR;
   float acc = 0.f;
-  if (r < n) {
-    const int64_t off = static_cast<int64_t>(b) * sb + static_cast<int64_t>(r) * sn + static_cast<int64_t>(h) * sh;
-    if constexpr (F32) {
-      const float* po = static_cast<const float*>(o) + off;
-      const float* pd = static_cast<const float*>(d_o) + off;
+  if (row_id < total_rows) {
+    const int r = row_id % lse_rows, bh = row_id / lse_rows, h = bh % heads, b = bh / heads;
+    if (r < n) {
+      const int64_t off = (static_cast<int64_t>(b) * sb + static_cast<int64_t>(r) * sn + static_cast<int64_t>(h) * sh) * ES +
+                          part * 16;
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(o) + off));
+      const uint4 c = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(d_o) + off));
+      if constexpr (F32) {
+        acc = __uint_as_float(a.x) * __uint_as_float(c.x) + __uint_as_float(a.y) * __uint_as_float(c.y) +
+              __uint_as_float(a.z) * __uint_as_float(c.z) + __uint_as_float(a.w) * __uint_as_float(c.w);
+      } else {
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-      for (int i = lane * 2; i < D; i += 64) {
-        const float2 a = *reinterpret_cast<const float2*>(po + i), c = *reinterpret_cast<const float2*>(pd + i);
-        acc += a.x * c.x + a.y * c.y;
-      }
-    } else {
-      const __nv_bfloat16* po = static_cast<const __nv_bfloat16*>(o) + off;
-      const __nv_bfloat16* pd = static_cast<const __nv_bfloat16*>(d_o) + off;
-#pragma unroll
-      for (int i = lane * 2; i < D; i += 64) {
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + i));
-        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + i));
-        acc += a.x * c.x + a.y * c.y;
+        for (int i = 0; i < 4; ++i) {
+          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&av[i]));
+          const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&cv[i]));
+          acc += x.x * y.x + x.y * y.y;
+        }
       }
     }
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
   }
-  if (lane == 0) delta[warp] = acc;
+#pragma unroll
+  for (int d = LPR / 2; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+  if (part == 0 && row_id < total_rows) delta[row_id] = acc;
 }
 
 template <bool kDKV, int D, bool F32, int CH, bool GATHER>

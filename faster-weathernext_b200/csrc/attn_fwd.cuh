@@ -341,80 +341,137 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
         const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
         // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
-        // of the warp may attend to is skipped by the whole warp.
-        // Four independent partial maxima / sums keep the dependency chains short.
-        float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const uint32_t w = g < 4 ? w0 : w1;
-          const uint32_t any = g < 4 ? any0 : any1;
-          if ((any >> (8 * (g & 3))) & 0xFFu) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int j = 8 * g + i;
-              mxp[i & 3] = (w & (1u << (j & 31))) ? fmaxf(mxp[i & 3], s[j]) : mxp[i & 3];
-            }
-          }
-        }
-        const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-        if (warp == 2 && lane == 0) FWN_TR(25, c);
-        const float m_new = mx * p.scale_log2;
+        // of the warp may attend to is skipped by the whole warp. Four independent partial maxima / sums
+        // keep the dependency chains short.
         const float m_old = m_ref;
-        const bool grow = m_new > m_ref + 8.0f;
+        bool grow = false;
         float corr = 1.f;
-        if (grow) {
-          corr = ex2(m_old - m_new);
-          m_ref = m_new;
-          l *= corr;
-        }
-        const float neg_m = -m_ref;
-        float lp[4] = {0.f, 0.f, 0.f, 0.f};
+        // Exact two-pass update: masked row max, lazy rescale of the reference, then p = 2^(s - m).
+        auto two_pass = [&](float (&e)[64]) {
+          float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const uint32_t w = g < 4 ? w0 : w1;
-          const uint32_t any = g < 4 ? any0 : any1;
-          if ((any >> (8 * (g & 3))) & 0xFFu) {
+          for (int g = 0; g < 8; ++g) {
+            const uint32_t w = g < 4 ? w0 : w1;
+            const uint32_t any = g < 4 ? any0 : any1;
+            if ((any >> (8 * (g & 3))) & 0xFFu) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int j = 8 * g + i;
-              const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
-              const float e = (w & (1u << (j & 31))) ? t : 0.f;
-              s[j] = e;
-              lp[i & 3] += e;
+              for (int i = 0; i < 8; ++i) {
+                const int j = 8 * g + i;
+                mxp[i & 3] = (w & (1u << (j & 31))) ? fmaxf(mxp[i & 3], s[j]) : mxp[i & 3];
+              }
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) s[8 * g + i] = 0.f;
           }
-        }
-        l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
-        if (warp == 2 && lane == 0) FWN_TR(26, c);
-        // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
-        if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-        const uint32_t pbase = p_smem(sb);
+          const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+          const float m_new = mx * p.scale_log2;
+          if (l == 0.f) {
+            m_ref = m_new;  // nothing accumulated yet (O row is 0): any reference will do
+          } else if (m_new > m_ref + 8.0f) {
+            grow = true;
+            corr = ex2(m_old - m_new);
+            m_ref = m_new;
+            l *= corr;
+          }
+          const float neg_m = -m_ref;
+          float lp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const uint32_t w = g < 4 ? w0 : w1;
+            const uint32_t any = g < 4 ? any0 : any1;
+            if ((any >> (8 * (g & 3))) & 0xFFu) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int j = 8 * g + i;
+                const float t = ex2(fmaf(s[j], p.scale_log2, neg_m));
+                e[j] = (w & (1u << (j & 31))) ? t : 0.f;
+                lp[i & 3] += e[j];
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) e[8 * g + i] = 0.f;
+            }
+          }
+          l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+        };
         if constexpr (!F32) {
+          // One pass against the current reference, exact as long as no allowed p exceeds 2^8 (the lazy
+          // rescale threshold). Rows with nothing accumulated yet take this chunk's unmasked row max as
+          // their reference (an upper bound of the allowed logits); they are accepted only if their
+          // largest allowed p is at least 2^-60, so whatever underflowed is negligible. Otherwise the whole
+          // warp redoes the chunk with the exact two-pass update.
+          uint32_t pk[32];
+          float lp[4] = {0.f, 0.f, 0.f, 0.f};
+          float top = 0.f;
+          const bool fresh = l == 0.f;
+          float m_use = m_ref;
+          if (__any_sync(0xffffffffu, fresh)) {
+            float up[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (j < 32 * n_in) up[j & 3] = fmaxf(up[j & 3], s[j]);
+            const float umax = fmaxf(fmaxf(up[0], up[1]), fmaxf(up[2], up[3])) * p.scale_log2;
+            if (fresh) m_use = umax;
+          }
+          const float neg_m = -m_use;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const uint32_t w = g < 4 ? w0 : w1;
+            const uint32_t any = g < 4 ? any0 : any1;
+            if ((any >> (8 * (g & 3))) & 0xFFu) {
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const int j = 8 * g + i;
+                const float t0 = ex2(fmaf(s[j], p.scale_log2, neg_m));
+                const float t1 = ex2(fmaf(s[j + 1], p.scale_log2, neg_m));
+                const float e0 = (w & (1u << (j & 31))) ? t0 : 0.f;
+                const float e1 = (w & (1u << ((j + 1) & 31))) ? t1 : 0.f;
+                lp[i & 3] += e0;
+                lp[(i + 1) & 3] += e1;
+                top = fmaxf(top, fmaxf(e0, e1));
+                pk[j >> 1] = pack_bf16(e0, e1);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) pk[4 * g + i] = 0u;
+            }
+          }
+          const bool bad = !(top <= 256.f) || (fresh && (w0 | w1) != 0u && !(top >= 8.673617e-19f));  // 2^-60
+          if (__any_sync(0xffffffffu, bad)) {
+            float e[64];
+            two_pass(e);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(e[2 * j], e[2 * j + 1]);
+          } else {
+            m_ref = m_use;
+            l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+          }
+          if (warp == 2 && lane == 0) FWN_TR(26, c);
+          // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
+          if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          const uint32_t pbase = p_smem(sb);
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
             if (cc < 4 * n_in)
-              st_shared_v4(pbase + sw128_offset(row, cc), pack_bf16(s[8 * cc], s[8 * cc + 1]),
-                           pack_bf16(s[8 * cc + 2], s[8 * cc + 3]), pack_bf16(s[8 * cc + 4], s[8 * cc + 5]),
-                           pack_bf16(s[8 * cc + 6], s[8 * cc + 7]));
+              st_shared_v4(pbase + sw128_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
           }
         } else {
+          float e[64];
+          two_pass(e);
+          if (warp == 2 && lane == 0) FWN_TR(26, c);
+          if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          const uint32_t pbase = p_smem(sb);
 #pragma unroll
           for (int cc = 0; cc < 16; ++cc) {
             if (cc < 8 * n_in) {
               const int blk = cc >> 3, ch = cc & 7;
-              st_shared_v4(pbase + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(s[4 * cc]),
-                           __float_as_uint(s[4 * cc + 1]), __float_as_uint(s[4 * cc + 2]),
-                           __float_as_uint(s[4 * cc + 3]));
+              st_shared_v4(pbase + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(e[4 * cc]),
+                           __float_as_uint(e[4 * cc + 1]), __float_as_uint(e[4 * cc + 2]), __float_as_uint(e[4 * cc + 3]));
             }
           }
         }
         fence_proxy_async_smem();
         if (warp == 2 && lane == 0) FWN_TR(27, c);
-        // Rescale O rows whose reference max grew (rows that saw no allowed key yet hold O = 0).
-        const bool rescale = grow && m_old != -INFINITY;
+        // Rescale O rows whose reference max grew (only rows that accumulated something: grow needs l > 0).
+        const bool rescale = grow;
         if (__any_sync(0xffffffffu, rescale)) {
           const uint32_t prev = gg - 1;
           if (warp == 2 && lane == 0) FWN_TR(28, c);

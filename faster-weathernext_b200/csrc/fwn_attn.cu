@@ -355,7 +355,9 @@ template <int D, bool F32>
 fwn_status launch_delta(const fwn_attn_desc& d, const void* o, const void* d_o, float* delta, cudaStream_t stream) {
   const int lse_rows = fwn_lse_rows(d.n);
   const int total = d.batch * d.heads * lse_rows;
-  fwn::delta_kernel<F32, D><<<(total * 32 + 255) / 256, 256, 0, stream>>>(
+  constexpr int rows_per_warp = 32 / (D * (F32 ? 4 : 2) / 16);
+  const int warps = (total + rows_per_warp - 1) / rows_per_warp;
+  fwn::delta_kernel<F32, D><<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
       o, d_o, delta, d.heads, d.n, lse_rows, d.out_stride_b, d.out_stride_n, d.out_stride_h, total);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "delta launch");
