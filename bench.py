@@ -321,6 +321,105 @@ def run_ours(args):
     dist.destroy_process_group()
 
 
+def run_model_workload(args):
+  """Configurations 4 (processor: 8 members x 2 noise samples = 16 forwards, split over the ranks, no
+  communication) and 5 (fine-tune: 8 members split over the ranks, forward + backward through the
+  custom-VJP attention, one NCCL all-reduce of the float32 gradients, Adam). Metric: ms per step (max over
+  ranks); GEMM FLOPs against the bf16 tensor-core peak as the roofline."""
+  import torch
+  import torch.distributed as dist
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.finetune import DataParallelStep
+  from faster_weathernext.processor import Processor, ProcessorConfig
+
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  torch.cuda.set_device(local)
+  device = torch.device("cuda", local)
+  if world > 1:
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+  mask, _, _ = mesh.config_mask(CFG)
+  n = mask.shape[0]
+  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  cfg = ProcessorConfig()
+  model = Processor(cfg, seed=0, device=device)
+  finetune = args.workload == "finetune"
+  members = 8 if finetune else 16
+  if members % world:
+    raise SystemExit(f"{members} members do not split over {world} GPUs")
+  local_m = members // world
+  g = torch.Generator(device=device).manual_seed(100 + rank)
+  if finetune:
+    xs = [torch.randn(1, n, cfg.d_model, device=device, generator=g) for _ in range(local_m)]
+    cs = [torch.randn(1, cfg.cond_dim, device=device, generator=g) for _ in range(local_m)]
+    ts = [torch.randn(1, n, cfg.d_model, device=device, generator=g) for _ in range(local_m)]
+    trainer = DataParallelStep(model, members, lr=1e-5)
+
+    def step():
+      return trainer.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles))
+  else:
+    x = torch.randn(local_m, n, cfg.d_model, device=device, generator=g)
+    c = torch.randn(local_m, cfg.cond_dim, device=device, generator=g)
+
+    def step():
+      with torch.no_grad():
+        return model(x, c, tiles)
+
+  def barrier():
+    torch.cuda.synchronize()
+    if world > 1:
+      dist.barrier()
+
+  clocks = ClockSampler(local)
+  clocks.start()
+  for _ in range(args.warmup):
+    step()
+  barrier()
+  stream = torch.cuda.current_stream()
+  a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  clocks.mark("t0")
+  a.record(stream)
+  for _ in range(args.steps):
+    step()
+  b.record(stream)
+  barrier()
+  clocks.mark("t1")
+  clocks.stop()
+  ms = a.elapsed_time(b)
+  if world > 1:
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+  ms /= args.steps
+  gemm = model.gemm_flops_per_forward(n) * local_m * (3 if finetune else 1)
+  attn = (USEFUL_PER_PAIR if finetune else 4) * cfg.heads * mask.nnz * cfg.head_dim * cfg.layers * local_m
+  hbm, tc, peak_kind = peaks()
+  achieved = gemm / (ms * 1e-3) / 1e12
+  if world > 1:
+    dist.barrier()
+  if rank == 0:
+    name = "fine-tune step ms (cfg5)" if finetune else "processor step ms (cfg4)"
+    print(json.dumps({
+        "metric": name, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic: latents / targets ~ N(0,1), Glorot-uniform weights",
+        "config": {"workload": ("cfg5: 8 members, MSE, fwd + bwd + NCCL all-reduce + Adam" if finetune else
+                                "cfg4: 24 pre-LN blocks d512 8x64 MLP2048 GELU, 16 forwards") +
+                               f", level-6 mesh 0.06 rad", "members": members, "members_per_gpu": local_m,
+                   "parallelism": f"{'dp' if finetune else 'replicas'}{world}"},
+        "roofline": {"bound": "tensor", "kernel": "processor GEMMs (cuBLAS bf16) per GPU", "achieved": round(achieved, 1),
+                     "peak": tc, "unit": "TFLOP/s", "frac": round(achieved / tc, 4), "peak_source": peak_kind,
+                     "traffic": None},
+        "attention_useful_gflop_per_gpu": round(attn / 1e9, 1), "gemm_gflop_per_gpu": round(gemm / 1e9, 1),
+        "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
+        "gpu_launches": None,
+    }), flush=True)
+  if world > 1:
+    dist.destroy_process_group()
+
+
 def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None):
   """The reference's CPU path (XLA chunked attention fwd + autodiff bwd, float32, NumPy/BLAS on all
   host cores) timed on a bounded sample of query chunks; returned in useful TFLOP/s."""
@@ -421,6 +520,8 @@ def main():
   ap.add_argument("--warmup", type=int, default=20)
   ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
   ap.add_argument("--mode", choices=["bf16", "tf32"], default="bf16")
+  ap.add_argument("--workload", choices=["attention", "processor", "finetune"], default="attention",
+                  help="attention: configuration 3 (the headline); processor / finetune: configurations 4 / 5")
   ap.add_argument("--lists", choices=["gathered", "paired"], default="gathered",
                   help="tile lists the kernels walk: gathered (distinct keys per block) or paired 32-key tiles")
   ap.add_argument("--no-e2e", action="store_true")
@@ -430,9 +531,15 @@ def main():
   if args.warmup < 3:
     ap.error("--warmup must be >= 3")
   if args.impl == "reference":
+    if args.workload != "attention":
+      print(json.dumps({"impl": "reference", "unavailable": "the reference's processor runs in JAX, which is not "
+                        "installed on this image"}))
+      return
     run_reference(args)
-  else:
+  elif args.workload == "attention":
     run_ours(args)
+  else:
+    run_model_workload(args)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,102 @@
+"""Mesh-transformer processor around the B200 attention op (configurations 4 and 5).
+
+Structure of the reference's patched processor (src/faster_weathernext/patch.py:229-293): pre-LN blocks
+
+    h = cond(LN(x));  x = x + mha_final(attention(q(h), k(h), v(h)))      (patch.py:238-246, tiled_mha :165-177)
+    x = x + ffw(cond(LN(x)))                                               (patch.py:250-252)
+
+with LayerNorm without scale / offset, a norm conditioning (per-sample scale and offset from the
+conditioning vector, as the official LinearNormConditioning), a final LN + conditioning (patch.py:288-290),
+q/k/v/out projections and a GELU MLP. The official modules (`weathernext.utils.sparse_transformer`,
+`dense.LinearNormConditioning`) are third-party and not available here, so this is a synthetic processor of
+the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU; Glorot-uniform weights from a
+seed), not a numerical copy of the official one. The projections run as cuBLAS GEMMs; the attention is
+faster_weathernext's kernel (q, k, v are strided views of one fused projection, no copies).
+"""
+
+import dataclasses
+import math
+
+import torch
+import torch.nn.functional as F
+
+from faster_weathernext import tiled_attn
+
+
+@dataclasses.dataclass
+class ProcessorConfig:
+  layers: int = 24
+  d_model: int = 512
+  heads: int = 8
+  head_dim: int = 64
+  mlp_hidden: int = 2048
+  cond_dim: int = 32
+
+
+def _glorot(gen, fan_in, fan_out, device):
+  bound = math.sqrt(6.0 / (fan_in + fan_out))
+  w = torch.empty(fan_in, fan_out, device=device)
+  w.uniform_(-bound, bound, generator=gen)
+  return torch.nn.Parameter(w)
+
+
+class Processor(torch.nn.Module):
+  """Random-init processor; parameters float32, compute in `dtype` (bf16 by default)."""
+
+  def __init__(self, cfg: ProcessorConfig = ProcessorConfig(), seed: int = 0, device=None):
+    super().__init__()
+    self.cfg = cfg
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    d, hd = cfg.d_model, cfg.heads * cfg.head_dim
+    self.blocks = torch.nn.ModuleList()
+    for _ in range(cfg.layers):
+      blk = torch.nn.Module()
+      # Fused q/k/v projection; output columns ordered [head, (q, k, v), head_dim] so that q, k, v are
+      # strided [B, n, H, D] views of one tensor.
+      blk.w_qkv = _glorot(gen, d, 3 * hd, dev)
+      blk.w_out = _glorot(gen, hd, d, dev)
+      blk.w1 = _glorot(gen, d, cfg.mlp_hidden, dev)
+      blk.b1 = torch.nn.Parameter(torch.zeros(cfg.mlp_hidden, device=dev))
+      blk.w2 = _glorot(gen, cfg.mlp_hidden, d, dev)
+      blk.b2 = torch.nn.Parameter(torch.zeros(d, device=dev))
+      blk.cond1 = _glorot(gen, cfg.cond_dim, 2 * d, dev)
+      blk.cond2 = _glorot(gen, cfg.cond_dim, 2 * d, dev)
+      self.blocks.append(blk)
+    self.cond_final = _glorot(gen, cfg.cond_dim, 2 * d, dev)
+
+  def _attend(self, q, k, v, tiles, scale):
+    return tiled_attn.attention(q, k, v, tiles, scale=scale)
+
+  @staticmethod
+  def _cond_norm(x, cond, w):
+    """LayerNorm without scale / offset, then x * (1 + scale) + offset from the conditioning vector."""
+    y = F.layer_norm(x, x.shape[-1:])
+    so = (cond @ w.to(cond.dtype)).unsqueeze(1)          # [B, 1, 2d]
+    scale, offset = so.chunk(2, dim=-1)
+    return y * (1 + scale) + offset
+
+  def forward(self, x: torch.Tensor, cond: torch.Tensor, tiles: "tiled_attn.AttentionTiles",
+              dtype=torch.bfloat16) -> torch.Tensor:
+    """x [B, n, d_model] (float32 residual stream), cond [B, cond_dim] -> [B, n, d_model]."""
+    cfg = self.cfg
+    b, n, d = x.shape
+    scale = cfg.head_dim ** -0.5
+    c = cond.to(dtype)
+    for blk in self.blocks:
+      h = self._cond_norm(x, c, blk.cond1).to(dtype)
+      qkv = (h @ blk.w_qkv.to(dtype)).view(b, n, cfg.heads, 3, cfg.head_dim)
+      q, k, v = qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2]
+      o = self._attend(q, k, v, tiles, scale)
+      x = x + (o.reshape(b, n, cfg.heads * cfg.head_dim) @ blk.w_out.to(dtype)).to(x.dtype)
+      h = self._cond_norm(x, c, blk.cond2).to(dtype)
+      m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype))
+      x = x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
+    return self._cond_norm(x, c, self.cond_final).to(x.dtype)
+
+  def gemm_flops_per_forward(self, n: int) -> float:
+    """Projection + MLP GEMM FLOPs of one member's forward (2 n (4 d^2 + 2 d m) per block)."""
+    cfg = self.cfg
+    hd = cfg.heads * cfg.head_dim
+    per = 2 * n * (cfg.d_model * 3 * hd + hd * cfg.d_model + 2 * cfg.d_model * cfg.mlp_hidden)
+    return float(cfg.layers * per)

@@ -1,0 +1,31 @@
+"""CPU: the drop-in API (enable / disable / options, Options fields) behaves as the reference's."""
+import dataclasses
+
+import pytest
+
+
+def test_enable_rejects_unknown_options_and_keeps_reference_fields():
+  import faster_weathernext
+  from faster_weathernext import patch
+  names = {f.name for f in dataclasses.fields(patch.Options)}
+  # The reference's Options fields (src/faster_weathernext/patch.py:50-82).
+  assert names == {"attention", "replace_attention", "reorder", "strict_fp32", "attn_chunk", "grid_chunk",
+                   "edge_chunk", "layer_loop", "remat", "sequential_samples"}
+  with pytest.raises(TypeError):
+    faster_weathernext.enable(not_an_option=1)
+  opts = faster_weathernext.enable(force=True, reorder=False, attn_chunk=256)
+  assert opts is faster_weathernext.options() and opts.reorder is False and opts.attn_chunk == 256
+  assert patch.is_enabled()
+  faster_weathernext.disable()
+  assert not patch.is_enabled()
+  patch.OPTIONS.reorder, patch.OPTIONS.attn_chunk = True, 512
+
+
+def test_attention_impl_refuses_other_backends():
+  from faster_weathernext import patch
+  patch.OPTIONS.attention = "xla"
+  try:
+    with pytest.raises(ValueError):
+      patch.attention_impl()
+  finally:
+    patch.OPTIONS.attention = "auto"

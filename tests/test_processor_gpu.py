@@ -1,0 +1,74 @@
+"""GPU: the processor (configurations 4-5 structure) and the fine-tune step with the B200 attention, against
+the same processor whose attention is a dense float32 masked softmax in torch (test-only subclass).
+Tolerances: the processor computes in bf16 (projections, attention), so rel RMS <= 2e-2 for outputs and
+<= 5e-2 for the global relative L2 error of all parameter gradients."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _small():
+  from faster_weathernext.processor import ProcessorConfig
+  return ProcessorConfig(layers=2, d_model=128, heads=2, head_dim=64, mlp_hidden=256, cond_dim=8)
+
+
+def _dense_processor_class(mask_dense):
+  from faster_weathernext.processor import Processor
+
+  class DenseProcessor(Processor):
+    def _attend(self, q, k, v, tiles, scale):
+      qf, kf, vf = (x.float().permute(0, 2, 1, 3) for x in (q, k, v))        # [B, H, n, D]
+      s = (qf @ kf.transpose(-1, -2)) * scale
+      s = s.masked_fill(~mask_dense, float("-inf"))
+      return (torch.softmax(s, -1) @ vf).permute(0, 2, 1, 3).to(q.dtype)
+  return DenseProcessor
+
+
+def _rel(a, b):
+  a, b = a.double(), b.double()
+  return float(torch.sqrt(torch.mean((a - b) ** 2)) / b.std())
+
+
+def test_processor_forward_and_gradients_match_dense_reference(cuda):
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  mask_dense = torch.from_numpy(m.toarray()).to(cuda)
+  cfg = _small()
+  ours = Processor(cfg, seed=3, device=cuda)
+  ref = _dense_processor_class(mask_dense)(cfg, seed=3, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(5)
+  x = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(2, cfg.cond_dim, device=cuda, generator=g)
+  t = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  ya, yb = ours(x, c, tiles), ref(x, c, tiles)
+  assert _rel(ya, yb) < 2e-2
+  torch.nn.functional.mse_loss(ya, t).backward()
+  torch.nn.functional.mse_loss(yb, t).backward()
+  ga = torch.cat([p.grad.reshape(-1) for p in ours.parameters()])
+  gb = torch.cat([p.grad.reshape(-1) for p in ref.parameters()])
+  assert float((ga - gb).norm() / gb.norm()) < 5e-2
+
+
+def test_finetune_step_runs_and_lowers_the_loss(cuda):
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.finetune import DataParallelStep
+  from faster_weathernext.processor import Processor
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = _small()
+  model = Processor(cfg, seed=0, device=cuda)
+  step = DataParallelStep(model, members=2, lr=1e-3)
+  g = torch.Generator(device=cuda).manual_seed(1)
+  xs = [torch.randn(1, n, cfg.d_model, device=cuda, generator=g) for _ in range(2)]
+  cs = [torch.randn(1, cfg.cond_dim, device=cuda, generator=g) for _ in range(2)]
+  ts = [torch.randn(1, n, cfg.d_model, device=cuda, generator=g) for _ in range(2)]
+  losses = [float(step.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles))) for _ in range(4)]
+  assert all(np.isfinite(losses)) and losses[-1] < losses[0]
