@@ -47,51 +47,76 @@ struct FwdParams {
   unsigned long long* trace;  // FWN_TRACE builds: kTraceCtas x kTraceEvents event records (else unused)
 };
 
-template <int D, bool F32>
+template <int D, bool F32, bool X3 = false>
 struct FwdCfg {
   static constexpr int ES = F32 ? 4 : 2;
   static constexpr int EPB = 128 / ES;        // elements per 128-byte column block
   static constexpr int CB = D / EPB;          // column blocks of a head_dim row
   static constexpr int ROWS = 128;            // query rows per item
   static constexpr int SUB = 32;              // keys per tile
-  static constexpr int KEYS = 64;             // keys per chunk (two tiles)
+  static constexpr int CH = X3 ? 1 : 2;       // tiles per chunk
+  static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
-  static constexpr int NS = 3;                // K/V pipeline stages
+  static constexpr int NS = X3 ? 2 : 3;       // K/V pipeline stages
   static constexpr int Q_BYTES = CB * ROWS * 128;
   static constexpr int KV_BYTES = CB * KEYS * 128;
-  static constexpr int BITS_BYTES = 2 * 128 * 4;
-  static constexpr int STAGE_BYTES = 2 * KV_BYTES + BITS_BYTES;
+  // Stage: K, V, (3xTF32: K_lo, V_lo), mask words.
+  static constexpr int BITS_OFF = (X3 ? 4 : 2) * KV_BYTES;
+  static constexpr int STAGE_BYTES = (BITS_OFF + CH * 512 + 1023) / 1024 * 1024;
   static constexpr int PCB = KEYS * ES / 128;  // column blocks of a P row
   static constexpr int P_BYTES = PCB * ROWS * 128;
-  static constexpr int OFF_STAGE = Q_BYTES;
+  static constexpr int PBUF_BYTES = P_BYTES * (X3 ? 2 : 1);  // P (3xTF32: P_hi, P_lo)
+  static constexpr int OFF_STAGE = Q_BYTES * (X3 ? 2 : 1);    // Q (3xTF32: Q_hi in place, Q_lo)
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1;
+  static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
+  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment
   static constexpr int TMEM_COLS = 256;
   static constexpr int O_COL = 128;
-  static constexpr int THREADS = 192;
+  static constexpr int THREADS = X3 ? 320 : 192;  // 3xTF32: + a warpgroup splitting tiles into hi / lo
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
   // 192-thread CTAs share an SM's 65,536.
-  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 255;
+  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 200;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(!X3 || F32, "3xTF32 takes float32 operands");
 };
 
-template <int D, bool F32, bool GATHER>
-__global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
+// 3xTF32 operand split of a shared-memory tile, byte position by byte position (so any swizzle is kept):
+// hi = x with the 13 low mantissa bits cleared (exact in tf32) in place, lo = x - hi (exact in fp32).
+__device__ __forceinline__ void split_tf32(uint32_t base, uint32_t lo_base, int bytes, int tid, int nthreads) {
+  for (int i = tid * 16; i < bytes; i += nthreads * 16) {
+    uint32_t a, b, c, d;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(base + i));
+    const uint32_t ha = a & 0xFFFFE000u, hb = b & 0xFFFFE000u, hc = c & 0xFFFFE000u, hd = d & 0xFFFFE000u;
+    st_shared_v4(base + i, ha, hb, hc, hd);
+    st_shared_v4(lo_base + i, __float_as_uint(__uint_as_float(a) - __uint_as_float(ha)),
+                 __float_as_uint(__uint_as_float(b) - __uint_as_float(hb)),
+                 __float_as_uint(__uint_as_float(c) - __uint_as_float(hc)),
+                 __float_as_uint(__uint_as_float(d) - __uint_as_float(hd)));
+  }
+}
+
+template <int D, bool F32, bool GATHER, bool X3 = false>
+__global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdCfg<D, F32, X3>::MAX_REGS))
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using C = FwdCfg<D, F32>;
+  using C = FwdCfg<D, F32, X3>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t q_smem = sbase;
   auto stage_k = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES; };
   auto stage_v = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + C::KV_BYTES; };
-  auto stage_bits = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + 2 * C::KV_BYTES; };
-  auto p_smem = [&](int b) { return sbase + C::OFF_P + b * C::P_BYTES; };
+  auto stage_bits = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + C::BITS_OFF; };
+  auto p_smem = [&](int b) { return sbase + C::OFF_P + b * C::PBUF_BYTES; };
+  // 3xTF32 lo copies (same byte layout as their hi tiles).
+  const uint32_t q_lo = sbase + C::Q_BYTES;
+  auto stage_klo = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + 2 * C::KV_BYTES; };
+  auto stage_vlo = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + 3 * C::KV_BYTES; };
+  auto p_lo = [&](int b) { return sbase + C::OFF_P + b * C::PBUF_BYTES + C::P_BYTES; };
   const uint32_t bar0 = sbase + C::OFF_BAR;
   const uint32_t q_full = bar0, q_empty = bar0 + 8;
   auto kv_full = [&](int s) { return bar0 + 16 + 8 * s; };
@@ -102,6 +127,9 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
   auto p_full = [&](int b) { return bar1 + 32 + 8 * b; };
   auto p_empty = [&](int b) { return bar1 + 48 + 8 * b; };
   const uint32_t o_full = bar1 + 64, o_empty = bar1 + 72, drain = bar1 + 80;
+  // 3xTF32: the converter's "split done" barriers; the MMA waits on these instead of the TMA ones.
+  const uint32_t q_ready = bar1 + 88;
+  auto kv_ready = [&](int s) { return bar1 + 96 + 8 * s; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
@@ -126,6 +154,8 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
     mbar_init(o_full, 1);
     mbar_init(o_empty, 4);
     mbar_init(drain, 1);
+    mbar_init(q_ready, 4);
+    for (int st = 0; st < C::NS; ++st) mbar_init(kv_ready(st), 4);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -161,10 +191,10 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
         nt0 = __ldg(p.ptr2 + it_next % per_bh);
         nt1 = __ldg(p.ptr2 + it_next % per_bh + 1);
       }
-      const int nch = (n_sub + 1) >> 1;
+      const int nch = (n_sub + C::CH - 1) / C::CH;
       if (nch == 0) continue;
-      ChunkMeta<2> m0 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
-      ChunkMeta<2> m1 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
+      ChunkMeta<C::CH> m0 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
+      ChunkMeta<C::CH> m1 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
       if (lane == 0) FWN_TR(1, it);
       if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
       if (lane == 0) {
@@ -179,17 +209,17 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
       const int row_mul = p.head_major ? 1 : p.heads;
       // Chunk c's copies; `meta` was loaded two chunks earlier. The loop below is unrolled by two so that
       // each prefetched register pair is consumed in place (a register move would wait for the load).
-      auto issue_chunk = [&](int c, const ChunkMeta<2>& meta) -> bool {
+      auto issue_chunk = [&](int c, const ChunkMeta<C::CH>& meta) -> bool {
           const int st = g % C::NS;
           if (!mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
-          const int n_in = min(2, n_sub - 2 * c);
+          const int n_in = min(C::CH, n_sub - C::CH * c);
           if (lane == 0) FWN_TR(3, c);
           if (lane == 0) mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
           __syncwarp();
   #pragma unroll
-          for (int s = 0; s < 2; ++s) {
+          for (int s = 0; s < C::CH; ++s) {
             if (s >= n_in) break;
-            const int t = t0 + 2 * c + s;
+            const int t = t0 + C::CH * c + s;
             if constexpr (GATHER) {
               // Lane i holds slot i's row; lanes 0-7 gather K rows 4j..4j+3, lanes 8-15 V rows.
               const int row = meta.v[s] * row_mul + row_base;
@@ -218,11 +248,11 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
       for (int c = 0; c < nch && ok; c += 2) {
         if (!(ok = issue_chunk(c, m0))) break;
         ++g;
-        m0 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, c + 2, lane);
+        m0 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, c + 2, lane);
         if (c + 1 < nch) {
           if (!(ok = issue_chunk(c + 1, m1))) break;
           ++g;
-          m1 = load_chunk_meta<2, GATHER>(p.kb2, p.cols, t0, n_sub, c + 3, lane);
+          m1 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, c + 3, lane);
         }
       }
       if (!ok) break;
@@ -239,39 +269,45 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdescPV = instr_desc(F32, 128, D, false, true);
+      // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
+      constexpr int kPasses = X3 ? 3 : 1;
       uint32_t g = 0, qc = 0;
       bool ok = true;
       auto issue_pv = [&](uint32_t gg, bool first) -> bool {
-        const int pbuf = gg & 1, st = gg % C::NS;
+        const int pbuf = gg & 1;
         if (!mbar_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag)) return false;
         if (first && !mbar_wait(o_empty, (qc & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
         return true;
-        (void)st;
       };
       for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
         const int pb = it % per_bh;
         const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-        const int nch = (n_sub + 1) >> 1;
+        const int nch = (n_sub + C::CH - 1) / C::CH;
         if (nch == 0) continue;
-        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(X3 ? q_ready : q_full, qc & 1, abort_flag))) break;
         FWN_TR(10, it);
         const uint32_t g0 = g;
         for (int c = 0; c <= nch && ok; ++c) {
           if (c < nch) {
             const uint32_t gg = g0 + c;
             const int st = gg % C::NS, sb = gg & 1;
-            const int n_in = min(2, n_sub - 2 * c);
-            if (!(ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
+            const int n_in = min(C::CH, n_sub - C::CH * c);
+            if (!(ok = mbar_wait(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
             if (!(ok = mbar_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
             tc_fence_after();
             const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
 #pragma unroll
-            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint64_t a = smem_desc(q_smem + cb * C::ROWS * 128 + within, 16, 1024);
-              const uint64_t bdesc = smem_desc(stage_k(st) + cb * C::KEYS * 128 + within, 16, 1024);
-              mma_ss<F32>(tmem + sb * 64, a, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const uint32_t qa = pass == 2 ? q_lo : q_smem;
+              const uint32_t kb = pass == 1 ? stage_klo(st) : stage_k(st);
+#pragma unroll
+              for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = smem_desc(qa + cb * C::ROWS * 128 + within, 16, 1024);
+                const uint64_t bdesc = smem_desc(kb + cb * C::KEYS * 128 + within, 16, 1024);
+                mma_ss<F32>(tmem + sb * 64, a, bdesc, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u);
+              }
             }
             mma_commit(s_full(sb));
             FWN_TR(11, c);
@@ -280,17 +316,20 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
           if (c >= 1) {
             const uint32_t gg = g0 + c - 1;
             const int st = gg % C::NS, pbuf = gg & 1;
-            const int n_in = min(2, n_sub - 2 * (c - 1));
+            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
             if (!(ok = issue_pv(gg, c == 1))) break;
             const int ksteps = n_in * C::SUB / C::KSTEP;
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint64_t a = smem_desc(p_smem(pbuf) + cb * C::ROWS * 128 + within, 16, 1024);
-              // V is the MN-major B operand: 128-byte swizzle for bf16, the 32-byte-atom variant for tf32.
-              const uint64_t bdesc = F32 ? smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 512,
-                                                     kLayoutSW128Base32B)
-                                         : smem_desc(stage_v(st) + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
-              mma_ss<F32>(tmem + C::O_COL, a, bdesc, kIdescPV, (c == 1 && kk == 0) ? 0u : 1u);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const uint32_t pa = pass == 2 ? p_lo(pbuf) : p_smem(pbuf);
+              const uint32_t vb = pass == 1 ? stage_vlo(st) : stage_v(st);
+              for (int kk = 0; kk < ksteps; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = smem_desc(pa + cb * C::ROWS * 128 + within, 16, 1024);
+                // V is the MN-major B operand: 128-byte swizzle for bf16, the 32-byte-atom variant for tf32.
+                const uint64_t bdesc = F32 ? smem_desc(vb + kk * C::KSTEP * 128, C::KEYS * 128, 512, kLayoutSW128Base32B)
+                                           : smem_desc(vb + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
+                mma_ss<F32>(tmem + C::O_COL, a, bdesc, kIdescPV, (c == 1 && pass == 0 && kk == 0) ? 0u : 1u);
+              }
             }
             mma_commit(p_empty(pbuf));
             mma_commit(kv_empty(st));
@@ -306,6 +345,32 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
       volatile int never = 0;
       mbar_wait(drain, 0, &never);
     }
+  } else if (X3 && warp >= 6) {
+    // ------------------------------------------------------------------ 3xTF32 converter (warps 6-9)
+    const int ctid = threadIdx.x - 192;
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh;
+      const int n_sub = p.ptr2[pb + 1] - p.ptr2[pb];
+      const int nch = (n_sub + C::CH - 1) / C::CH;
+      if (nch == 0) continue;
+      if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+      split_tf32(q_smem, q_lo, C::Q_BYTES, ctid, 128);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = mbar_wait(kv_full(st), (g / C::NS) & 1, abort_flag))) break;
+        split_tf32(stage_k(st), stage_klo(st), C::KV_BYTES, ctid, 128);
+        split_tf32(stage_v(st), stage_vlo(st), C::KV_BYTES, ctid, 128);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(kv_ready(st));
+      }
+      ++qc;
+    }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
@@ -316,14 +381,14 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
       const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
       const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-      const int nch = (n_sub + 1) >> 1;
+      const int nch = (n_sub + C::CH - 1) / C::CH;
       const int qrow = pb * C::ROWS + row;
       float m_ref = -INFINITY, l = 0.f;
       const uint32_t g0 = g;
       for (int c = 0; c < nch; ++c) {
         const uint32_t gg = g0 + c;
         const int sb = gg & 1, st = gg % C::NS;
-        const int n_in = min(2, n_sub - 2 * c);
+        const int n_in = min(C::CH, n_sub - C::CH * c);
         float s[64];
         if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
         if (warp == 2 && lane == 0) FWN_TR(20, c);
@@ -463,8 +528,20 @@ __global__ void __launch_bounds__(192) __maxnreg__((FwdCfg<D, F32>::MAX_REGS))
           for (int cc = 0; cc < 16; ++cc) {
             if (cc < 8 * n_in) {
               const int blk = cc >> 3, ch = cc & 7;
-              st_shared_v4(pbase + blk * C::ROWS * 128 + sw128_offset(row, ch), __float_as_uint(e[4 * cc]),
-                           __float_as_uint(e[4 * cc + 1]), __float_as_uint(e[4 * cc + 2]), __float_as_uint(e[4 * cc + 3]));
+              const uint32_t off = blk * C::ROWS * 128 + sw128_offset(row, ch);
+              if constexpr (X3) {
+                uint32_t h[4], lo[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  h[i] = __float_as_uint(e[4 * cc + i]) & 0xFFFFE000u;
+                  lo[i] = __float_as_uint(e[4 * cc + i] - __uint_as_float(h[i]));
+                }
+                st_shared_v4(pbase + off, h[0], h[1], h[2], h[3]);
+                st_shared_v4(p_lo(sb) + off, lo[0], lo[1], lo[2], lo[3]);
+              } else {
+                st_shared_v4(pbase + off, __float_as_uint(e[4 * cc]), __float_as_uint(e[4 * cc + 1]),
+                             __float_as_uint(e[4 * cc + 2]), __float_as_uint(e[4 * cc + 3]));
+              }
             }
           }
         }

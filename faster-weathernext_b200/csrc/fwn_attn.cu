@@ -225,10 +225,10 @@ unsigned long long* trace_buffer() {
 }
 #endif
 
-template <int D, bool F32, bool GATHER>
+template <int D, bool F32, bool GATHER, bool X3 = false>
 fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
                       void* o, float* lse, int layout, cudaStream_t stream) {
-  using C = fwn::FwdCfg<D, F32>;
+  using C = fwn::FwdCfg<D, F32, X3>;
   CUtensorMap tq, tk, tv;
   fwn_status s;
   if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
@@ -260,7 +260,7 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
 #ifdef FWN_TRACE
   p.trace = trace_buffer();
 #endif
-  auto kernel = fwn::attn_fwd_kernel<D, F32, GATHER>;
+  auto kernel = fwn::attn_fwd_kernel<D, F32, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
@@ -539,6 +539,9 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
   if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
     return g ? launch_fwd<64, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
              : launch_fwd<64, true, false>(d, q, k, v, *tiles, o, lse, layout, st);
+  if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
+    return g ? launch_fwd<64, true, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
+             : launch_fwd<64, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
   return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
 }
 

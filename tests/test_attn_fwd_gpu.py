@@ -143,3 +143,33 @@ def test_forward_head_major_layout_gathered(cuda):
   o = ta.attention(q, k, v, tiles, scale=0.125)
   ref, _ = oa.sparse_attention(*(t.float().cpu().numpy() for t in (q, k, v)), m, 0.125)
   assert oa.rel_rms(o.float().cpu().numpy(), ref) < TOL["bf16"]
+
+
+@pytest.mark.parametrize("gather", [True, False])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_forward_tf32x3_reference_test_case(golden, cuda, batch, gather):
+  """The fp32-equivalent mode (3xTF32, the reference's `highest`): rel RMS <= 2e-5 and the reference test's
+  max|err| / max|ref| < 1e-5 (tests/test_pallas_kernel.py:36) against the float64 reference."""
+  q, k, v = kernel_inputs(0, (2, 300, 2, 64), 3)
+  q, k, v = q[:batch], k[:batch], v[:batch]
+  m = golden_mask(golden["tiles"], "k_fwd")
+  out, lse = _run(q, k, v, m, 64 ** -0.5, "tf32x3", cuda, gather=gather)
+  ref, ref_lse = oa.sparse_attention(q, k, v, m, 64 ** -0.5)
+  assert oa.rel_rms(out, ref) < TOL["tf32x3"]
+  assert oa.max_rel(out, ref) < 1e-5
+  np.testing.assert_allclose(lse[:, :, :300], ref_lse, rtol=0, atol=1e-5)
+  gold = golden["attention"]
+  for b in range(batch):
+    assert oa.max_rel(out[b][::int(gold["every"])], gold[f"fwd/b{b}/out"]) < 1e-5
+
+
+@pytest.mark.parametrize("cfg", [1, 3])
+def test_forward_tf32x3_configs(cuda, cfg):
+  from faster_weathernext import mesh
+  m, _, _ = mesh.config_mask(cfg)
+  _, _, b, h, d = mesh.CONFIGS[cfg]
+  rng = np.random.default_rng(0)
+  q, k, v = (rng.standard_normal((b, m.shape[0], h, d)).astype(np.float32) for _ in range(3))
+  out, _ = _run(q, k, v, m, d ** -0.5, "tf32x3", cuda)
+  ref, _ = oa.sparse_attention(q, k, v, m, d ** -0.5)
+  assert oa.rel_rms(out, ref) < TOL["tf32x3"]
