@@ -3,23 +3,27 @@
 // Replaces _attention_bwd with _bwd_dq_kernel / _bwd_dkv_kernel (src/faster_weathernext/pallas_attn.py:
 // 161-215, 274-311). Same algorithm: delta = rowsum(O * dO) first; then P is recomputed tile by tile
 // from the forward's log-sum-exp, P = where(valid, exp(S - lse), 0), dS = P * (dP - delta), and
-//   dQ  = scale * sum dS K        per query block over the forward list      (kDKV = false)
+//   dQ  = scale * sum dS K        per query block over the forward list
 //   dK  = scale * sum dS^T Q,  dV = sum P^T dO
-//                                 per key block over the transposed list     (kDKV = true)
+//                                 per key block over the transposed list
 // so every output row is owned by one CTA: no atomics, deterministic (as pallas_attn.py:297-311).
 //
-// One kernel template serves both: "rows" are the 128 rows of the work item (queries for dQ, keys for
-// dK/dV) held in shared memory for the whole item (R0, R1), "columns" are walked in chunks of CH
-// 32-wide tiles (C0, C1):
-//               dQ kernel           dK/dV kernel
-//   R0, R1      Q, dO               K, V
-//   C0, C1      K, V                Q, dO
-//   S  = R0 C0^T (TMEM)             dP = R1 C1^T (TMEM)
-//   acc0 += dS C0 (MN-major B)      acc1 += P C1 (dK/dV only)
-// Roles (192 threads): warp 0 TMA producer; warp 1 TMEM allocation + single-thread MMA issue; warps
-// 2-5 the elementwise stage (thread = row = TMEM lane) and the epilogue. S / dP of chunk c+1 are
-// issued before the accumulating MMAs of chunk c. tf32 operands read MN-major use a second copy of
-// the column tile with the 32-byte-atom swizzle (SWIZZLE_128B_BASE32B).
+// One kernel template serves every pass ("kind"): "rows" are the 128 rows of the work item (queries for
+// dQ, keys otherwise) held in shared memory for the whole item (R0, R1), "columns" are walked in chunks of
+// CH 32-wide tiles (C0, C1):
+//               dQ          dK/dV        dV only      dK only
+//   R0, R1      Q, dO       K, V         K            K, V
+//   C0, C1      K, V        Q, dO        Q, dO        Q, dO
+//   S  = R0 C0^T            always
+//   dP = R1 C1^T            dQ, dK/dV, dK only
+//   acc0 += dS C0           dQ, dK/dV, dK only   (MN-major B)
+//   acc1 += P  C1           dK/dV, dV only       (MN-major B)
+// dV only + dK only are the 3xTF32 replacement of the dK/dV pass, whose hi / lo operand copies do not fit
+// one CTA's shared memory. Roles: warp 0 TMA producer; warp 1 TMEM allocation + single-thread MMA issue;
+// warps 2-5 the elementwise stage (thread = row = TMEM lane) and the epilogue; in 3xTF32 warps 6-9 split
+// every landed tile into hi (in place) and lo copies. S / dP of chunk c+1 are issued before the
+// accumulating MMAs of chunk c. tf32 operands read MN-major use a second copy of the column tile with
+// the 32-byte-atom swizzle (SWIZZLE_128B_BASE32B).
 #pragma once
 
 #include <cuda.h>
@@ -27,6 +31,8 @@
 #include "common.cuh"
 
 namespace fwn {
+
+enum BwdKind : int { kBwdDQ = 0, kBwdDKV = 1, kBwdDV = 2, kBwdDK = 3 };
 
 struct BwdParams {
   const int32_t* ptr2;
@@ -36,16 +42,20 @@ struct BwdParams {
   int head_major;         // gathered mode: rows of the 2D column-operand views are (b, h, node)
   const float* lse;    // [B, H, lse_rows] natural log
   const float* delta;  // [B, H, lse_rows]
-  void* out0;          // dQ (dq kernel) or dK (dkv kernel)
-  void* out1;          // dV (dkv kernel)
+  void* out0;          // dQ or dK (kinds with acc0)
+  void* out1;          // dV (kinds with acc1)
   int64_t o_sb, o_sn, o_sh;
   int heads, n, np, lse_rows, n_items;
   float scale;         // softmax scale (applied to acc0)
   float scale_log2;    // scale * log2(e)
 };
 
-template <bool kDKV, int D, bool F32, int CH>
+template <int KIND, int D, bool F32, int CH, bool X3>
 struct BwdCfg {
+  static constexpr bool ROWS_ARE_KEYS = KIND != kBwdDQ;
+  static constexpr bool NEED_DP = KIND != kBwdDV;
+  static constexpr bool ACC_DS = KIND != kBwdDV;
+  static constexpr bool ACC_P = KIND == kBwdDKV || KIND == kBwdDV;
   static constexpr int ES = F32 ? 4 : 2;
   static constexpr int EPB = 128 / ES;
   static constexpr int CB = D / EPB;
@@ -53,33 +63,47 @@ struct BwdCfg {
   static constexpr int SUB = 32;
   static constexpr int COLS = 32 * CH;       // columns per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;
-  static constexpr int NS = 2;
-  static constexpr int NMN = F32 ? (kDKV ? 2 : 1) : 0;  // extra MN-major copies of column tiles (tf32)
+  static constexpr int XL = X3 ? 2 : 1;      // copies of an operand: hi (in place) and lo
+  // Row operands: R0, R1 (dP needs R1).
+  static constexpr int NR = NEED_DP ? 2 : 1;
+  // Column tiles per stage: C0 (K-major), C1 (K-major for dP; bf16 also serves as dV's MN-major B),
+  // C0 MN-major copy (tf32, for acc0), C1 MN-major copy (tf32, for acc1); then lo copies (3xTF32).
+  static constexpr bool LOAD_C1 = NEED_DP || (ACC_P && !F32);
+  static constexpr bool LOAD_C0MN = F32 && ACC_DS;
+  static constexpr bool LOAD_C1MN = F32 && ACC_P;
+  static constexpr int SLOT_C1 = 1;
+  static constexpr int SLOT_C0MN = 1 + (LOAD_C1 ? 1 : 0);
+  static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
+  static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
+  static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1) : 2;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
-  static constexpr int BITS_OFF = (2 + NMN) * C_BYTES;
-  static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (dK/dV)
-  static constexpr int STAGE_RAW = VEC_OFF + (kDKV ? CH * 256 : 0);
+  static constexpr int BITS_OFF = NC * XL * C_BYTES;
+  static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (rows are keys)
+  static constexpr int STAGE_RAW = VEC_OFF + (ROWS_ARE_KEYS ? CH * 256 : 0);
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int PCB = COLS * ES / 128 > 0 ? COLS * ES / 128 : 1;  // 128-byte column blocks of dS / P
   static constexpr int G_BYTES = ((COLS * ES + 127) / 128) * ROWS * 128; // one dS (or P) tile
-  static constexpr int NG = kDKV ? 2 : 1;              // tiles per buffer (dS; dS and P)
-  // dS / P buffers: one for the bf16 dK/dV kernel at head_dim 64 (keeps two CTAs per SM), else two.
-  static constexpr int NB = (kDKV && !F32 && D == 64) ? 1 : 2;
-  static constexpr int OFF_C = 2 * R_BYTES;
+  static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
+  // dS / P buffers: one for the bf16 dK/dV pass at head_dim 64 (keeps two CTAs per SM) and in 3xTF32
+  // (except dV only), else two.
+  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (X3 && KIND != kBwdDV)) ? 1 : 2;
+  static constexpr int OFF_C = NR * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
-  static constexpr int OFF_BAR = OFF_G + NB * NG * G_BYTES;
-  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 * NB + 2 + 1;
+  static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
+  // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
+  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 * NB + 2 + 1 + (X3 ? 1 + NS : 0);
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
   static constexpr int ACC0 = 128;
-  static constexpr int ACC1 = 128 + D;
-  static constexpr int TMEM_NEED = kDKV ? 128 + 2 * D : 128 + D;
+  static constexpr int ACC1 = 128 + (ACC_DS ? D : 0);
+  static constexpr int TMEM_NEED = 128 + (ACC_DS ? D : 0) + (ACC_P ? D : 0);
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
-  static constexpr int THREADS = 192;
-  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256) ? 2 : 1;
-  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 255;
+  static constexpr int THREADS = X3 ? 320 : 192;
+  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
+  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : (X3 ? 200 : 255);
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(COLS * ES % 128 == 0, "dS rows must fill 128-byte column blocks");
+  static_assert(!X3 || F32, "3xTF32 takes float32 operands");
+  static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
 };
 
 // delta[b, h, r] = sum_d O[b, r, h, d] * dO[b, r, h, d] (fp32); rows r in [n, lse_rows) get 0.
@@ -121,19 +145,24 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ o, 
   if (part == 0 && row_id < total_rows) delta[row_id] = acc;
 }
 
-template <bool kDKV, int D, bool F32, int CH, bool GATHER>
-__global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MAX_REGS))
+template <int KIND, int D, bool F32, int CH, bool GATHER, bool X3>
+__global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnreg__((BwdCfg<KIND, D, F32, CH, X3>::MAX_REGS))
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
                     const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
                     const __grid_constant__ CUtensorMap tm_c0mn, const __grid_constant__ CUtensorMap tm_c1mn,
                     const BwdParams p) {
-  using C = BwdCfg<kDKV, D, F32, CH>;
+  using C = BwdCfg<KIND, D, F32, CH, X3>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t r0_smem = sbase, r1_smem = sbase + C::R_BYTES;
+  // Row operand i (hi, or the operand itself), its lo copy at +NR; column slot s of a stage, lo copy at +NC.
+  auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR + i) * C::R_BYTES; };
   auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };
-  auto g_tile = [&](int b, int which) { return sbase + C::OFF_G + (b * C::NG + which) * C::G_BYTES; };
+  auto slot = [&](uint32_t sb, int s, int lo) { return sb + (lo * C::NC + s) * C::C_BYTES; };
+  auto g_tile = [&](int b, int which, int lo) {
+    return sbase + C::OFF_G + ((b * C::NG + which) * C::XL + lo) * C::G_BYTES;
+  };
+  constexpr int G_DS = 0, G_P = C::ACC_DS ? 1 : 0;  // dS / P tile index within a buffer
   const uint32_t bar0 = sbase + C::OFF_BAR;
   const uint32_t r_full = bar0, r_empty = bar0 + 8;
   auto c_full = [&](int s) { return bar0 + 16 + 8 * s; };
@@ -144,6 +173,9 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
   auto g_empty = [&](int b) { return bar1 + 16 + 8 * (C::NB + b); };
   const uint32_t bar2 = bar1 + 16 + 16 * C::NB;
   const uint32_t acc_full = bar2, acc_empty = bar2 + 8, drain = bar2 + 16;
+  // 3xTF32: the converter's "split done" barriers; the MMA waits on these instead of the TMA ones.
+  const uint32_t r_ready = bar2 + 24;
+  auto c_ready = [&](int s) { return bar2 + 32 + 8 * s; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
@@ -152,7 +184,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
-      mbar_init(c_full(s), (GATHER && kDKV) ? 2 : 1);
+      mbar_init(c_full(s), (GATHER && C::ROWS_ARE_KEYS) ? 2 : 1);
       mbar_init(c_empty(s), 1);
     }
     mbar_init(sd_full, 1);
@@ -164,16 +196,20 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
     mbar_init(drain, 1);
+    if constexpr (X3) {
+      mbar_init(r_ready, 4);
+      for (int s = 0; s < C::NS; ++s) mbar_init(c_ready(s), 4);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_r0);
-    tma_prefetch_desc(&tm_r1);
+    if (C::NR == 2) tma_prefetch_desc(&tm_r1);
     tma_prefetch_desc(&tm_c0);
-    tma_prefetch_desc(&tm_c1);
-    if (C::NMN >= 1) tma_prefetch_desc(&tm_c0mn);
-    if (C::NMN >= 2) tma_prefetch_desc(&tm_c1mn);
+    if (C::LOAD_C1) tma_prefetch_desc(&tm_c1);
+    if (C::LOAD_C0MN) tma_prefetch_desc(&tm_c0mn);
+    if (C::LOAD_C1MN) tma_prefetch_desc(&tm_c1mn);
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
   tc_fence_before();
@@ -209,10 +245,11 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       ChunkMeta<CH> m1 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
       if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(r_full, 2 * C::R_BYTES);
+        mbar_arrive_expect_tx(r_full, C::NR * C::R_BYTES);
         for (int cb = 0; cb < C::CB; ++cb) {
-          tma_load_4d(r0_smem + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
-          tma_load_4d(r1_smem + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+          tma_load_4d(r_op(0, 0) + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+          if (C::NR == 2)
+            tma_load_4d(r_op(1, 0) + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
         }
       }
       pending_r = 1;
@@ -224,8 +261,8 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
           const int st = g % C::NS;
           if (!mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
           const int n_in = min(CH, n_sub - CH * c);
-          // Gathered dK/dV: lse / delta of the gathered queries are stored by the lanes, not copied.
-          const uint32_t per_tile = (2 + C::NMN) * kColBytes + 512 + ((kDKV && !GATHER) ? 256 : 0);
+          // Gathered key rows: lse / delta of the gathered queries are stored by the lanes, not copied.
+          const uint32_t per_tile = C::NC * kColBytes + 512 + ((C::ROWS_ARE_KEYS && !GATHER) ? 256 : 0);
           if (lane == 0) mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
           __syncwarp();
           const uint32_t sb = stage(st);
@@ -236,19 +273,19 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
             if constexpr (GATHER) {
               const int col = meta.v[s];
               const int row = col * row_mul + row_base;
-              const int j = lane & 7, which = lane >> 3;  // which: 0 C0, 1 C1, 2 C0 (MN copy), 3 C1 (MN copy)
+              const int j = lane & 7, which = lane >> 3;  // which: the column slot this lane octet loads
               const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
               const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
-              if (which < 2 + C::NMN) {
-                const void* tm = which == 0 ? static_cast<const void*>(&tm_c0)
-                                 : which == 1 ? static_cast<const void*>(&tm_c1)
-                                 : which == 2 ? static_cast<const void*>(&tm_c0mn)
-                                              : static_cast<const void*>(&tm_c1mn);
-                const uint32_t dst = sb + which * C::C_BYTES + s * C::SUB * 128 + j * 512;
+              if (which < C::NC) {
+                const void* tm = which == 0                                  ? static_cast<const void*>(&tm_c0)
+                                 : (C::LOAD_C1 && which == C::SLOT_C1)       ? static_cast<const void*>(&tm_c1)
+                                 : (C::LOAD_C0MN && which == C::SLOT_C0MN)   ? static_cast<const void*>(&tm_c0mn)
+                                                                             : static_cast<const void*>(&tm_c1mn);
+                const uint32_t dst = slot(sb, which, 0) + s * C::SUB * 128 + j * 512;
                 for (int cb = 0; cb < C::CB; ++cb)
                   tma_gather4(dst + cb * C::COLS * 128, tm, cb * C::EPB, r0, r1, r2, r3, c_full(st));
               }
-              if constexpr (kDKV) {
+              if constexpr (C::ROWS_ARE_KEYS) {
                 const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col;
                 asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(p.lse[vo])
                              : "memory");
@@ -260,12 +297,14 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
               const int col0 = meta.v[s] * C::SUB;
               for (int cb = 0; cb < C::CB; ++cb) {
                 const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
-                tma_load_4d(sb + off, &tm_c0, cb * C::EPB, h, col0, b, c_full(st));
-                tma_load_4d(sb + C::C_BYTES + off, &tm_c1, cb * C::EPB, h, col0, b, c_full(st));
-                if (C::NMN >= 1) tma_load_4d(sb + 2 * C::C_BYTES + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
-                if (C::NMN >= 2) tma_load_4d(sb + 3 * C::C_BYTES + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
+                tma_load_4d(slot(sb, 0, 0) + off, &tm_c0, cb * C::EPB, h, col0, b, c_full(st));
+                if (C::LOAD_C1) tma_load_4d(slot(sb, C::SLOT_C1, 0) + off, &tm_c1, cb * C::EPB, h, col0, b, c_full(st));
+                if (C::LOAD_C0MN)
+                  tma_load_4d(slot(sb, C::SLOT_C0MN, 0) + off, &tm_c0mn, cb * C::EPB, h, col0, b, c_full(st));
+                if (C::LOAD_C1MN)
+                  tma_load_4d(slot(sb, C::SLOT_C1MN, 0) + off, &tm_c1mn, cb * C::EPB, h, col0, b, c_full(st));
               }
-              if (kDKV) {
+              if (C::ROWS_ARE_KEYS) {
                 const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col0;
                 bulk_load(sb + C::VEC_OFF + s * 256, p.lse + vo, 128, c_full(st));
                 bulk_load(sb + C::VEC_OFF + s * 256 + 128, p.delta + vo, 128, c_full(st));
@@ -273,7 +312,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
             }
             if (lane == 0) bulk_load(sb + C::BITS_OFF + s * 512, p.bits2 + static_cast<size_t>(t) * 128, 512, c_full(st));
           }
-          if constexpr (GATHER && kDKV) {
+          if constexpr (GATHER && C::ROWS_ARE_KEYS) {
             // Second arrival of c_full: publishes the lanes' lse / delta stores.
             __syncwarp();
             if (lane == 0) mbar_arrive(c_full(st));
@@ -303,6 +342,8 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdescAcc = instr_desc(F32, 128, D, false, true);
+      // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
+      constexpr int kPasses = X3 ? 3 : 1;
       uint32_t g = 0, qc = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
@@ -310,65 +351,84 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
         const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
         const int nch = (n_sub + CH - 1) / CH;
         if (nch == 0) continue;
-        if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(X3 ? r_ready : r_full, qc & 1, abort_flag))) break;
         const uint32_t g0 = g;
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch) {
-            const uint32_t gg = g0 + c;
-            const int st = gg % C::NS;
-            const int n_in = min(CH, n_sub - CH * c);
-            if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
-            if (!(ok = mbar_wait(sd_empty, (gg & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
-            const uint32_t sb = stage(st);
+        // S (and dP) of chunk c: S = R0 C0^T at TMEM column 0, dP = R1 C1^T at column 64 (both K-major).
+        auto issue_sd = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS;
+          const int n_in = min(CH, n_sub - CH * c);
+          if (!mbar_wait(X3 ? c_ready(st) : c_full(st), (gg / C::NS) & 1, abort_flag)) return false;
+          if (!mbar_wait(sd_empty, (gg & 1) ^ 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
+          const uint32_t sb = stage(st);
 #pragma unroll
-            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<F32>(tmem, smem_desc(r0_smem + cb * C::ROWS * 128 + within, 16, 1024),
-                          smem_desc(sb + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
-            }
+          for (int op = 0; op < C::NR; ++op) {
+            const int cs = op == 0 ? 0 : C::SLOT_C1;
 #pragma unroll
-            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<F32>(tmem + 64, smem_desc(r1_smem + cb * C::ROWS * 128 + within, 16, 1024),
-                          smem_desc(sb + C::C_BYTES + cb * C::COLS * 128 + within, 16, 1024), idesc,
-                          kk > 0 ? 1u : 0u);
-            }
-            mma_commit(sd_full);
-            if (c == nch - 1) mma_commit(r_empty);
-          }
-          if (c >= 1) {
-            const uint32_t gg = g0 + c - 1;
-            const int st = gg % C::NS, gb = gg % C::NB;
-            const int n_in = min(CH, n_sub - CH * (c - 1));
-            if (!(ok = mbar_wait(g_full(gb), (gg / C::NB) & 1, abort_flag))) break;
-            if (c == 1 && !(ok = mbar_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t sb = stage(st);
-            // MN-major B operands: the K-major tile itself (bf16) or its 32-byte-atom copy (tf32).
-            const uint32_t b0 = F32 ? sb + 2 * C::C_BYTES : sb;
-            const uint32_t b1 = F32 ? sb + 3 * C::C_BYTES : sb + C::C_BYTES;
-            const int ksteps = n_in * C::SUB / C::KSTEP;
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint64_t a = smem_desc(g_tile(gb, 0) + cb * C::ROWS * 128 + within, 16, 1024);
-              const uint64_t bd = F32 ? smem_desc(b0 + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
-                                      : smem_desc(b0 + kk * C::KSTEP * 128, C::COLS * 128, 1024);
-              mma_ss<F32>(tmem + C::ACC0, a, bd, kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
-            }
-            if constexpr (kDKV) {
-              for (int kk = 0; kk < ksteps; ++kk) {
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const uint32_t ra = r_op(op, pass == 2 ? 1 : 0);
+              const uint32_t cbase = slot(sb, cs, pass == 1 ? 1 : 0);
+#pragma unroll
+              for (int kk = 0; kk < D / C::KSTEP; ++kk) {
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                const uint64_t a = smem_desc(g_tile(gb, 1) + cb * C::ROWS * 128 + within, 16, 1024);
-                const uint64_t bd = F32 ? smem_desc(b1 + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
-                                        : smem_desc(b1 + kk * C::KSTEP * 128, C::COLS * 128, 1024);
-                mma_ss<F32>(tmem + C::ACC1, a, bd, kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
+                mma_ss<F32>(tmem + 64 * op, smem_desc(ra + cb * C::ROWS * 128 + within, 16, 1024),
+                            smem_desc(cbase + cb * C::COLS * 128 + within, 16, 1024), idesc,
+                            (pass > 0 || kk > 0) ? 1u : 0u);
               }
             }
-            mma_commit(g_empty(gb));
-            mma_commit(c_empty(st));
-            if (c == nch) mma_commit(acc_full);
+          }
+          mma_commit(sd_full);
+          if (c == nch - 1) mma_commit(r_empty);
+          return true;
+        };
+        // acc0 += dS C0 and / or acc1 += P C1 of chunk c (C0 / C1 as MN-major B operands: the K-major tile
+        // itself for bf16, the 32-byte-atom copy for tf32).
+        auto issue_acc = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS, gb = gg % C::NB;
+          const int n_in = min(CH, n_sub - CH * c);
+          if (!mbar_wait(g_full(gb), (gg / C::NB) & 1, abort_flag)) return false;
+          if (c == 0 && !mbar_wait(acc_empty, (qc & 1) ^ 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t sb = stage(st);
+          const int ksteps = n_in * C::SUB / C::KSTEP;
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            if (which == 0 && !C::ACC_DS) continue;
+            if (which == 1 && !C::ACC_P) continue;
+            const int bs = which == 0 ? (F32 ? C::SLOT_C0MN : 0) : (F32 ? C::SLOT_C1MN : C::SLOT_C1);
+            const int gi = which == 0 ? G_DS : G_P;
+            const uint32_t acc = tmem + (which == 0 ? C::ACC0 : C::ACC1);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const uint32_t ga = g_tile(gb, gi, pass == 2 ? 1 : 0);
+              const uint32_t bbase = slot(sb, bs, pass == 1 ? 1 : 0);
+              for (int kk = 0; kk < ksteps; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = smem_desc(ga + cb * C::ROWS * 128 + within, 16, 1024);
+                const uint64_t bd = F32 ? smem_desc(bbase + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
+                                        : smem_desc(bbase + kk * C::KSTEP * 128, C::COLS * 128, 1024);
+                mma_ss<F32>(acc, a, bd, kIdescAcc, (c == 0 && pass == 0 && kk == 0) ? 0u : 1u);
+              }
+            }
+          }
+          mma_commit(g_empty(gb));
+          mma_commit(c_empty(st));
+          if (c == nch - 1) mma_commit(acc_full);
+          return true;
+        };
+        if constexpr (C::NS >= 2) {
+          // S / dP of chunk c+1 go ahead of the accumulating MMAs of chunk c (two stages in flight).
+          for (int c = 0; c <= nch && ok; ++c) {
+            if (c < nch && !(ok = issue_sd(c))) break;
+            if (c >= 1 && !(ok = issue_acc(c - 1))) break;
+          }
+        } else {
+          // One stage: the accumulating MMAs of chunk c free it before chunk c+1 can land.
+          for (int c = 0; c < nch && ok; ++c) {
+            if (!(ok = issue_sd(c))) break;
+            if (!(ok = issue_acc(c))) break;
           }
         }
         g = g0 + nch;
@@ -377,6 +437,32 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       mma_commit(drain);
       volatile int never = 0;
       mbar_wait(drain, 0, &never);
+    }
+  } else if (X3 && warp >= 6) {
+    // ------------------------------------------------------------------ 3xTF32 converter (warps 6-9)
+    const int ctid = threadIdx.x - 192;
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh;
+      const int n_sub = p.ptr2[pb + 1] - p.ptr2[pb];
+      const int nch = (n_sub + CH - 1) / CH;
+      if (nch == 0) continue;
+      if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
+      for (int op = 0; op < C::NR; ++op) split_tf32(r_op(op, 0), r_op(op, 1), C::R_BYTES, ctid, 128);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(r_ready);
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = mbar_wait(c_full(st), (g / C::NS) & 1, abort_flag))) break;
+        const uint32_t sb = stage(st);
+        for (int s = 0; s < C::NC; ++s) split_tf32(slot(sb, s, 0), slot(sb, s, 1), C::C_BYTES, ctid, 128);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c_ready(st));
+      }
+      ++qc;
     }
   } else {
     // ------------------------------------------------------------------ elementwise + epilogue
@@ -392,7 +478,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       const int nch = (n_sub + CH - 1) / CH;
       const int grow = pb * C::ROWS + row;
       float lse2_row = 0.f, delta_row = 0.f;
-      if (!kDKV) {
+      if (!C::ROWS_ARE_KEYS) {
         lse2_row = p.lse[static_cast<size_t>(bh) * p.lse_rows + grow] * kLog2e;
         delta_row = p.delta[static_cast<size_t>(bh) * p.lse_rows + grow];
       }
@@ -413,7 +499,7 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
           if (j < n_in) {
             float s[32], dp[32];
             tmem_ld32(trow + 32 * j, s);
-            tmem_ld32(trow + 64 + 32 * j, dp);
+            if constexpr (C::NEED_DP) tmem_ld32(trow + 64 + 32 * j, dp);
             tmem_wait_ld();
             if (j == n_in - 1) {
               tc_fence_before();
@@ -430,9 +516,9 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
                 for (int ii = 0; ii < 8; ++ii) {
                   const int i = 8 * g + ii;
                   float l2, dl;
-                  if constexpr (kDKV) {
+                  if constexpr (C::ROWS_ARE_KEYS) {
                     l2 = ld_shared_f32(sb + C::VEC_OFF + j * 256 + i * 4) * kLog2e;
-                    dl = ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4);
+                    dl = C::NEED_DP ? ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4) : 0.f;
                   } else {
                     l2 = lse2_row;
                     dl = delta_row;
@@ -440,20 +526,22 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
                   const float e = ex2(fmaf(s[i], p.scale_log2, -l2));
                   const float pv = (w & (1u << i)) ? e : 0.f;
                   s[i] = pv;
-                  dp[i] = pv * (dp[i] - dl);
+                  if constexpr (C::NEED_DP) dp[i] = pv * (dp[i] - dl);
                 }
               } else {
 #pragma unroll
                 for (int ii = 0; ii < 8; ++ii) {
                   s[8 * g + ii] = 0.f;
-                  dp[8 * g + ii] = 0.f;
+                  if constexpr (C::NEED_DP) dp[8 * g + ii] = 0.f;
                 }
               }
             }
 #pragma unroll
-            for (int which = 0; which < C::NG; ++which) {
+            for (int which = 0; which < 2; ++which) {
+              if (which == 0 && !C::ACC_DS) continue;
+              if (which == 1 && !C::ACC_P) continue;
               const float* src = which == 0 ? dp : s;
-              const uint32_t base = g_tile(gb, which);
+              const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
               if constexpr (!F32) {
                 // 32 bf16 columns = chunks 4j .. 4j+3 of the 128-byte row.
 #pragma unroll
@@ -461,6 +549,21 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
                   st_shared_v4(base + sw128_offset(row, 4 * j + cc), pack_bf16(src[8 * cc], src[8 * cc + 1]),
                                pack_bf16(src[8 * cc + 2], src[8 * cc + 3]), pack_bf16(src[8 * cc + 4], src[8 * cc + 5]),
                                pack_bf16(src[8 * cc + 6], src[8 * cc + 7]));
+              } else if constexpr (X3) {
+                // hi (13 low mantissa bits cleared) and lo = x - hi tiles.
+                const uint32_t lo_base = g_tile(gb, which == 0 ? G_DS : G_P, 1);
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                  uint32_t hv[4], lv[4];
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    hv[i] = __float_as_uint(src[4 * cc + i]) & 0xFFFFE000u;
+                    lv[i] = __float_as_uint(src[4 * cc + i] - __uint_as_float(hv[i]));
+                  }
+                  const uint32_t off = j * C::ROWS * 128 + sw128_offset(row, cc);
+                  st_shared_v4(base + off, hv[0], hv[1], hv[2], hv[3]);
+                  st_shared_v4(lo_base + off, lv[0], lv[1], lv[2], lv[3]);
+                }
               } else {
                 // 32 fp32 columns = one whole 128-byte column block.
 #pragma unroll
@@ -483,12 +586,13 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       const bool store = grow < p.n;
       const int64_t roff = (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sn +
                             static_cast<int64_t>(h) * p.o_sh) * C::ES;
-      uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.out0) + roff;
-      uint8_t* dst1 = kDKV ? reinterpret_cast<uint8_t*>(p.out1) + roff : nullptr;
+      uint8_t* dst0 = C::ACC_DS ? reinterpret_cast<uint8_t*>(p.out0) + roff : nullptr;
+      uint8_t* dst1 = C::ACC_P ? reinterpret_cast<uint8_t*>(p.out1) + roff : nullptr;
       if (nch == 0) {
         if (store) {
-          for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst0)[i] = make_uint4(0, 0, 0, 0);
-          if (kDKV)
+          if (C::ACC_DS)
+            for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst0)[i] = make_uint4(0, 0, 0, 0);
+          if (C::ACC_P)
             for (int i = 0; i < D * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst1)[i] = make_uint4(0, 0, 0, 0);
         }
         continue;
@@ -496,7 +600,9 @@ __global__ void __launch_bounds__(192) __maxnreg__((BwdCfg<kDKV, D, F32, CH>::MA
       if (!(ok = mbar_wait(acc_full, qc & 1, abort_flag))) break;
       tc_fence_after();
 #pragma unroll
-      for (int which = 0; which < (kDKV ? 2 : 1); ++which) {
+      for (int which = 0; which < 2; ++which) {
+        if (which == 0 && !C::ACC_DS) continue;
+        if (which == 1 && !C::ACC_P) continue;
         uint8_t* dst = which == 0 ? dst0 : dst1;
         const float mul = which == 0 ? p.scale : 1.f;
         const uint32_t col = which == 0 ? C::ACC0 : C::ACC1;

@@ -84,21 +84,6 @@ struct FwdCfg {
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
 };
 
-// 3xTF32 operand split of a shared-memory tile, byte position by byte position (so any swizzle is kept):
-// hi = x with the 13 low mantissa bits cleared (exact in tf32) in place, lo = x - hi (exact in fp32).
-__device__ __forceinline__ void split_tf32(uint32_t base, uint32_t lo_base, int bytes, int tid, int nthreads) {
-  for (int i = tid * 16; i < bytes; i += nthreads * 16) {
-    uint32_t a, b, c, d;
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(base + i));
-    const uint32_t ha = a & 0xFFFFE000u, hb = b & 0xFFFFE000u, hc = c & 0xFFFFE000u, hd = d & 0xFFFFE000u;
-    st_shared_v4(base + i, ha, hb, hc, hd);
-    st_shared_v4(lo_base + i, __float_as_uint(__uint_as_float(a) - __uint_as_float(ha)),
-                 __float_as_uint(__uint_as_float(b) - __uint_as_float(hb)),
-                 __float_as_uint(__uint_as_float(c) - __uint_as_float(hc)),
-                 __float_as_uint(__uint_as_float(d) - __uint_as_float(hd)));
-  }
-}
-
 template <int D, bool F32, bool GATHER, bool X3 = false>
 __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdCfg<D, F32, X3>::MAX_REGS))
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,

@@ -269,19 +269,20 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   return ok();
 }
 
-template <bool kDKV, int D, bool F32, int CH, bool GATHER>
+template <int KIND, int D, bool F32, int CH, bool GATHER, bool X3>
 fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
                            const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
                            int layout, cudaStream_t stream) {
-  using C = fwn::BwdCfg<kDKV, D, F32, CH>;
+  using C = fwn::BwdCfg<KIND, D, F32, CH, X3>;
+  constexpr bool kKeys = KIND != fwn::kBwdDQ;
   CUtensorMap r0, r1, c0, c1, c0mn, c1mn;
   fwn_status s;
-  // dq kernel: rows Q, dO; columns K, V.   dkv kernel: rows K, V; columns Q, dO.
-  const void* rp0 = kDKV ? k : q;
-  const void* rp1 = kDKV ? v : d_o;
-  const void* cp0 = kDKV ? q : k;
-  const void* cp1 = kDKV ? d_o : v;
-  const bool r1_out = !kDKV, c1_out = kDKV;
+  // dQ pass: rows Q, dO; columns K, V.   dK / dV passes: rows K, V; columns Q, dO.
+  const void* rp0 = kKeys ? k : q;
+  const void* rp1 = kKeys ? v : d_o;
+  const void* cp0 = kKeys ? q : k;
+  const void* cp1 = kKeys ? d_o : v;
+  const bool r1_out = !kKeys, c1_out = kKeys;
   if ((s = make_map(&r0, rp0, d, C::ROWS)) != FWN_OK) return s;
   if ((s = make_map(&r1, rp1, d, C::ROWS, false, r1_out)) != FWN_OK) return s;
   if (GATHER) {
@@ -322,33 +323,35 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale = d.scale;
   p.scale_log2 = d.scale * 1.4426950408889634f;
-  auto kernel = fwn::attn_bwd_kernel<kDKV, D, F32, CH, GATHER>;
+  auto kernel = fwn::attn_bwd_kernel<KIND, D, F32, CH, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, p);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, kDKV ? "attn_bwd dkv launch" : "attn_bwd dq launch");
+  static const char* const kNames[] = {"attn_bwd dq launch", "attn_bwd dkv launch", "attn_bwd dv launch",
+                                       "attn_bwd dk launch"};
+  if (e != cudaSuccess) return cuda_fail(e, kNames[KIND]);
   return FWN_OK;
 }
 
 // Gathered-mode layout for the column operands of one pass (-1: not gatherable).
-int pass_layout(const fwn_attn_desc& d, bool dkv) {
+int pass_layout(const fwn_attn_desc& d, bool keys) {
   const int a = gather_layout(d, false);
-  if (!dkv) return a;                    // columns K, V (input strides)
+  if (!keys) return a;                   // columns K, V (input strides)
   const int b = gather_layout(d, true);  // columns Q (input) and dO (output strides)
   return (a >= 0 && a == b) ? a : -1;
 }
 
-template <bool kDKV, int D, bool F32, int CH>
+template <int KIND, int D, bool F32, int CH, bool X3 = false>
 fwn_status launch_bwd_pass_any(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
                                const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
                                cudaStream_t stream) {
   if (t.cols) {
-    const int layout = pass_layout(d, kDKV);
+    const int layout = pass_layout(d, KIND != fwn::kBwdDQ);
     if (layout < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "gathered lists need a node-major or head-major packed layout");
-    return launch_bwd_pass<kDKV, D, F32, CH, true>(d, q, k, v, d_o, lse, delta, t, out0, out1, layout, stream);
+    return launch_bwd_pass<KIND, D, F32, CH, true, X3>(d, q, k, v, d_o, lse, delta, t, out0, out1, layout, stream);
   }
-  return launch_bwd_pass<kDKV, D, F32, CH, false>(d, q, k, v, d_o, lse, delta, t, out0, out1, 0, stream);
+  return launch_bwd_pass<KIND, D, F32, CH, false, X3>(d, q, k, v, d_o, lse, delta, t, out0, out1, 0, stream);
 }
 
 template <int D, bool F32>
@@ -367,17 +370,30 @@ fwn_status launch_delta(const fwn_attn_desc& d, const void* o, const void* d_o, 
 // Which backward launches to issue.
 enum BwdParts { kDelta = 1, kDq = 2, kDkv = 4, kAll = 7 };
 
-template <int D, bool F32>
+template <int D, bool F32, bool X3 = false>
 fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
                       const float* lse, const void* d_o, const fwn_tile_list* t, const fwn_tile_list* tt, void* dq,
                       void* dk, void* dv, float* delta, int parts, cudaStream_t stream) {
   constexpr int CH = F32 ? 1 : 2;
   fwn_status s;
   if ((parts & kDelta) && (s = launch_delta<D, F32>(d, o, d_o, delta, stream)) != FWN_OK) return s;
-  if ((parts & kDq) && (s = launch_bwd_pass_any<false, D, F32, CH>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
+  if ((parts & kDq) &&
+      (s = launch_bwd_pass_any<fwn::kBwdDQ, D, F32, CH, X3>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
     return s;
-  if ((parts & kDkv) && (s = launch_bwd_pass_any<true, D, F32, CH>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) != FWN_OK)
-    return s;
+  if (parts & kDkv) {
+    if constexpr (X3) {
+      // 3xTF32: the hi / lo copies of both passes' operands do not fit one CTA; dV and dK run separately.
+      if ((s = launch_bwd_pass_any<fwn::kBwdDV, D, F32, CH, X3>(d, q, k, v, d_o, lse, delta, *tt, nullptr, dv, stream)) !=
+          FWN_OK)
+        return s;
+      if ((s = launch_bwd_pass_any<fwn::kBwdDK, D, F32, CH, X3>(d, q, k, v, d_o, lse, delta, *tt, dk, nullptr, stream)) !=
+          FWN_OK)
+        return s;
+    } else if ((s = launch_bwd_pass_any<fwn::kBwdDKV, D, F32, CH>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) !=
+               FWN_OK) {
+      return s;
+    }
+  }
   return ok();
 }
 
@@ -635,6 +651,8 @@ fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k,
   }
   if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
     return launch_bwd<64, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
+  if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
+    return launch_bwd<64, true, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
   return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
 }
 

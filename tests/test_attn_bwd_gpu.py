@@ -137,3 +137,41 @@ def test_autograd_matches_explicit_backward(cuda):
   ref = oa.sparse_attention_vjp(*(x.float().cpu().numpy() for x in (q, k, v, do)), m, 0.125)
   for t, r in zip((qq.grad, kk.grad, vv.grad), ref):
     assert oa.rel_rms(t.float().cpu().numpy(), r) < TOL["bf16"]
+
+
+@pytest.mark.parametrize("gather", [True, False])
+@pytest.mark.parametrize("symmetric", [True, False])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_grads_tf32x3_reference_test_case(golden, cuda, symmetric, batch, gather):
+  """fp32-equivalent backward (3xTF32: delta, dQ, then dV and dK as separate passes): rel RMS <= 2e-5 against
+  the float64 VJP on the reference test's case (tests/test_pallas_kernel.py:72-99), max|err| / max|ref| < 1e-4."""
+  q, k, v, do = kernel_inputs(2, (1, 300, 2, 64), 4)
+  if batch == 2:
+    q2, k2, v2, do2 = kernel_inputs(12, (1, 300, 2, 64), 4)
+    q, k, v, do = (np.concatenate([a, b]) for a, b in zip((q, k, v, do), (q2, k2, v2, do2)))
+  m = golden_mask(golden["tiles"], "k_sym" if symmetric else "k_nonsym")
+  got = _grads(q, k, v, do, m, 0.125, "tf32x3", cuda, gather=gather)
+  ref = oa.sparse_attention_vjp(q, k, v, do, m, 0.125)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL["tf32x3"], (name, oa.rel_rms(a, r))
+    assert oa.max_rel(a, r) < 1e-4, (name, oa.max_rel(a, r))
+  gold = golden["attention"]
+  tag = "sym" if symmetric else "nonsym"
+  for name, a in zip(("dq", "dk", "dv"), got):
+    assert oa.max_rel(a[0][::int(gold["every"])], gold[f"grad_{tag}/{name}"]) < 1e-4, name
+
+
+@pytest.mark.parametrize("cfg", [1, 3])
+def test_grads_tf32x3_configs(cuda, cfg):
+  """Configurations 1 and 3 (full size) in the fp32-equivalent mode: rel RMS <= 2e-5 per gradient."""
+  from faster_weathernext import mesh
+  m, _, _ = mesh.config_mask(cfg)
+  _, _, b, h, d = mesh.CONFIGS[cfg]
+  n = m.shape[0]
+  rng = np.random.default_rng(0)
+  q, k, v = (rng.standard_normal((b, n, h, d)).astype(np.float32) for _ in range(3))
+  do = np.random.default_rng(1).standard_normal((b, n, h, d)).astype(np.float32)
+  got = _grads(q, k, v, do, m, d ** -0.5, "tf32x3", cuda)
+  ref = oa.sparse_attention_vjp(q, k, v, do, m, d ** -0.5)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL["tf32x3"], (name, oa.rel_rms(a, r))
