@@ -38,7 +38,8 @@ CFG = 3
 # dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
 USEFUL_PER_PAIR = 14
 # DRAM bytes (read + write) per launch at this workload from one ncu capture (profiles/ncu_cfg3_bf16.md).
-NCU_TRAFFIC = {"attn_fwd": 152_893_952, "attn_bwd_dq": 201_407_296, "attn_bwd_dkv": 229_749_760}
+NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 152_893_952, "attn_bwd_dq": 201_407_296,
+                                                   "attn_bwd_dkv": 229_749_760}}
 
 
 def peaks():
@@ -107,19 +108,45 @@ class ClockSampler:
             "reasons": reasons, "samples": len(inside)}
 
 
-def workload(device, seed, mode):
+class MaskInfo:
+  """n, nnz and (on demand) the host CSR of a workload's mask."""
+
+  def __init__(self, n, nnz, host=None, device_csr=None):
+    self.n, self.nnz, self._host, self._dev = n, nnz, host, device_csr
+
+  def host(self):
+    if self._host is None:
+      from scipy import sparse
+      ip, ix = (x.cpu().numpy() for x in self._dev)
+      self._host = sparse.csr_matrix((np.ones(ix.size, bool), ix, ip), shape=(self.n, self.n))
+    return self._host
+
+
+def workload(device, seed, mode, name="attention"):
+  """(mask info, device tile lists, 3 input sets of [1, n, H, D] q/k/v/dO, heads, head_dim)."""
   import torch
   from faster_weathernext import mesh
   from faster_weathernext import tiled_attn as ta
-  mask, _, _ = mesh.config_mask(CFG)
-  _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
-  n = mask.shape[0]
-  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  if name == "wn2":
+    # The real WeatherNext 2 shape: level-6 mesh in Hilbert order, 32-hop mask built on the device.
+    adj, _, _ = mesh.wn2_adjacency("hilbert")
+    n = adj.shape[0]
+    indptr, indices = ta.khop_csr_device(adj, mesh.WN2["hops"], device)
+    fwd = ta.pair_tiles(ta.build_tiles_device(indptr, indices, n, n))
+    tiles = ta.AttentionTiles(fwd, fwd, n, True)
+    info = MaskInfo(n, int(indices.numel()), device_csr=(indptr, indices))
+    heads, head_dim = mesh.WN2["heads"], mesh.WN2["head_dim"]
+  else:
+    mask, _, _ = mesh.config_mask(CFG)
+    _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
+    n = mask.shape[0]
+    tiles = ta.AttentionTiles.from_mask(mask, device=device)
+    info = MaskInfo(n, mask.nnz, host=mask)
   dt = torch.bfloat16 if mode == "bf16" else torch.float32
   g = torch.Generator(device=device).manual_seed(seed)
   sets = [[torch.randn(1, n, heads, head_dim, device=device, dtype=dt, generator=g) for _ in range(4)]
           for _ in range(3)]
-  return mask, tiles, sets, heads, head_dim
+  return info, tiles, sets, heads, head_dim
 
 
 def kernel_costs(nnz, n, heads, head_dim, es, lf, lb):
@@ -150,9 +177,9 @@ def run_ours(args):
   device = torch.device("cuda", local)
   if world > 1:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-  mode = _lib.MODE_BF16 if args.mode == "bf16" else _lib.MODE_TF32
-  mask, tiles, sets, heads, head_dim = workload(device, 1000 + rank, args.mode)
-  n, nnz = mask.shape[0], mask.nnz
+  mode = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[args.mode]
+  mask, tiles, sets, heads, head_dim = workload(device, 1000 + rank, args.mode, args.workload)
+  n, nnz = mask.n, mask.nnz
   scale = head_dim ** -0.5
   es = 2 if args.mode == "bf16" else 4
   useful = USEFUL_PER_PAIR * heads * nnz * head_dim
@@ -249,20 +276,22 @@ def run_ours(args):
                   "algorithmic_gbs": round(nbytes / (ms_k * 1e-3) / 1e9, 1),
                   "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm"}
   dom = max(kernel_ms, key=kernel_ms.get)
+  traffic = NCU_TRAFFIC.get((args.workload, args.mode, args.lists), {})
   flops, nbytes = costs[dom]
   bound = kernels[dom]["bound"]
   if bound == "hbm":
     achieved = nbytes / (kernel_ms[dom] * 1e-3) / 1e9
     roof = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
             "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
-            "algorithmic_bytes": nbytes, "traffic": NCU_TRAFFIC.get(dom)}
+            "algorithmic_bytes": nbytes, "traffic": traffic.get(dom)}
   else:
     achieved = flops / (kernel_ms[dom] * 1e-3) / 1e12
     roof = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 2), "peak": tc, "unit": "TFLOP/s",
             "frac": round(achieved / tc, 4), "peak_source": peak_kind,
-            "algorithmic_flops": flops, "traffic": NCU_TRAFFIC.get(dom)}
+            "algorithmic_flops": flops, "traffic": traffic.get(dom)}
   # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile.
-  issued = 2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + 4 * lb.n_tiles)
+  # 3xTF32 issues three products per MMA.
+  issued = 2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + 4 * lb.n_tiles) * (3 if args.mode == "tf32x3" else 1)
 
   # End to end through the public API with host buffers: pinned H2D of q, k, v, dO, forward + backward
   # through torch.autograd, D2H of o, dq, dk, dv, every step.
@@ -277,7 +306,7 @@ def run_ours(args):
       hq, hk, hv, hdo = host_in[i % 2]
       q, k, v = (x.to(device, non_blocking=True).requires_grad_(True) for x in (hq, hk, hv))
       do = hdo.to(device, non_blocking=True)
-      o = ta.attention(q, k, v, tiles, scale=scale, precision=None)
+      o = ta.attention(q, k, v, tiles, scale=scale, precision="highest" if args.mode == "tf32x3" else None)
       dq, dk, dv = torch.autograd.grad(o, (q, k, v), do)
       for dst, src in zip(host_out, (o, dq, dk, dv)):
         dst.copy_(src.detach(), non_blocking=True)
@@ -298,20 +327,28 @@ def run_ours(args):
 
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu:
-    cpu = cpu_baseline(mask, heads, head_dim, seconds=args.cpu_seconds)
+    cpu = cpu_baseline(mask.host(), heads, head_dim, seconds=args.cpu_seconds, name=args.workload)
 
   if world > 1:
     dist.barrier()
   if rank == 0:
+    if args.workload == "wn2":
+      desc_w = (f"WN2 real shape fwd+bwd: 40,962 nodes (level-6 mesh, Hilbert order), 32-hop mask ({nnz} pairs, "
+                f"built on the device), B1 H{heads} D{head_dim} per GPU")
+      data = "synthetic: Q/K/V/dO ~ N(0,1) seeded per rank; icosphere level-6 32-hop mask built on the GPU"
+    else:
+      desc_w = (f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({nnz} pairs), "
+                f"B1 H{heads} D{head_dim} per GPU")
+      data = "synthetic: Q/K/V/dO ~ N(0,1) seeded per rank; icosphere level-6 great-circle mask built on the host"
+    set_mb = 4 * sets[0][0].numel() * sets[0][0].element_size() / 1e6
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": args.mode, "data": "synthetic: Q/K/V/dO ~ N(0,1) seeded per rank; "
-        "icosphere level-6 great-circle mask built on the host",
-        "config": {"workload": f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({nnz} pairs), "
-                               f"B1 H{heads} D{head_dim} per GPU", "global_batch": world, "nodes": n,
+        "vs_baseline": published_ratio(args, value, nnz, heads, head_dim),
+        "dtype": {"bf16": "bf16", "tf32": "tf32", "tf32x3": "3xtf32"}[args.mode], "data": data,
+        "config": {"workload": desc_w, "global_batch": world, "nodes": n,
                    "heads": heads, "head_dim": head_dim, "parallelism": f"replicas x{world} (no communication)",
-                   "l2": "inputs larger than L2: 3 rotating input sets of 168 MB", "tile_lists": args.lists},
+                   "l2": f"inputs larger than L2: 3 rotating input sets of {set_mb:.0f} MB", "tile_lists": args.lists},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
         "clocks": clocks.summary(), "kernels": kernels,
         "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2),
@@ -319,6 +356,21 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
   if world > 1:
     dist.destroy_process_group()
+
+
+# The reference's published fwd+bwd times at the WN2 shape (RTX 5090, one layer, 6 x 128 heads, 32-hop mask,
+# 3,101 keys per query): TF32 42.2 ms, 3xTF32 115.4 ms (docs/results/attn_bwd/attn_bwd_{default,highest}_rtx5090.txt:6).
+PUBLISHED_WN2_MS = {"tf32": 42.2, "tf32x3": 115.4}
+PUBLISHED_WN2_NNZ = 40_962 * 3_101
+
+
+def published_ratio(args, value, nnz, heads, head_dim):
+  """value / the reference's published useful TFLOP/s for the same metric, shape and precision (else None)."""
+  ms = PUBLISHED_WN2_MS.get(args.mode) if args.workload == "wn2" else None
+  if ms is None:
+    return None
+  ref = USEFUL_PER_PAIR * heads * PUBLISHED_WN2_NNZ * head_dim / (ms * 1e-3) / 1e12
+  return round(value / ref, 3)
 
 
 def run_model_workload(args):
@@ -420,7 +472,7 @@ def run_model_workload(args):
     dist.destroy_process_group()
 
 
-def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None):
+def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None, name="attention"):
   """The reference's CPU path (XLA chunked attention fwd + autodiff bwd, float32, NumPy/BLAS on all
   host cores) timed on a bounded sample of query chunks; returned in useful TFLOP/s."""
   from oracle import attention as oa
@@ -450,7 +502,8 @@ def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None):
     if (steps is None and el > seconds) or (steps is not None and done >= steps):
       break
   return {"value": round(flops / el / 1e12, 6), "unit": UNIT, "cores": cores, "kind": "port",
-          "sample": f"{done} of {path.n_chunks} query chunks (512 queries, key window {path.window}) of cfg3, "
+          "sample": f"{done} of {path.n_chunks} query chunks (512 queries, key window {path.window}) of "
+                    f"{'the WN2 shape' if name == 'wn2' else 'cfg3'}, "
                     f"fwd + bwd, float32, {el:.1f} s"}
 
 
@@ -519,9 +572,11 @@ def main():
   ap.add_argument("--steps", type=int, default=2000)
   ap.add_argument("--warmup", type=int, default=20)
   ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-  ap.add_argument("--mode", choices=["bf16", "tf32"], default="bf16")
-  ap.add_argument("--workload", choices=["attention", "processor", "finetune"], default="attention",
-                  help="attention: configuration 3 (the headline); processor / finetune: configurations 4 / 5")
+  ap.add_argument("--mode", choices=["bf16", "tf32", "tf32x3"], default="bf16",
+                  help="bf16 MMAs, TF32 (the reference's default precision) or 3xTF32 (its `highest`)")
+  ap.add_argument("--workload", choices=["attention", "wn2", "processor", "finetune"], default="attention",
+                  help="attention: configuration 3 (the headline); wn2: the real WeatherNext 2 shape (32-hop mask, "
+                       "6 x 128 heads); processor / finetune: configurations 4 / 5")
   ap.add_argument("--lists", choices=["gathered", "paired"], default="gathered",
                   help="tile lists the kernels walk: gathered (distinct keys per block) or paired 32-key tiles")
   ap.add_argument("--no-e2e", action="store_true")
@@ -531,12 +586,12 @@ def main():
   if args.warmup < 3:
     ap.error("--warmup must be >= 3")
   if args.impl == "reference":
-    if args.workload != "attention":
+    if args.workload not in ("attention",):
       print(json.dumps({"impl": "reference", "unavailable": "the reference's processor runs in JAX, which is not "
                         "installed on this image"}))
       return
     run_reference(args)
-  elif args.workload == "attention":
+  elif args.workload in ("attention", "wn2"):
     run_ours(args)
   else:
     run_model_workload(args)

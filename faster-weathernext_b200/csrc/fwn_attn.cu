@@ -529,6 +529,42 @@ fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32
   return ok();
 }
 
+int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }
+
+fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops, uint32_t* reach,
+                           uint32_t* scratch, void* stream) {
+  if (n < 0 || hops < 0 || hops > 4096) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n=%d or hops=%d", n, hops);
+  if (n > 0 && (!indptr || !reach || !scratch)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n > 0 && (!aligned16(reach) || !aligned16(scratch)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "reach and scratch must be 16-byte aligned");
+  cudaError_t e = fwn::launch_khop(indptr, indices, n, hops, reach, scratch, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "khop");
+  return ok();
+}
+
+fwn_status fwn_bitset_csr_count(const uint32_t* bits, int32_t n_rows, int32_t n_cols, int32_t* indptr, void* ws,
+                                size_t ws_bytes, void* stream) {
+  if (n_rows < 0 || n_cols < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape %d x %d", n_rows, n_cols);
+  if (static_cast<int64_t>(n_rows) * n_cols >= (int64_t(1) << 31))
+    return fail(FWN_ERR_UNSUPPORTED, "%d x %d mask: nnz may not fit int32", n_rows, n_cols);
+  if (!indptr || (n_rows > 0 && !bits)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  const size_t need = static_cast<size_t>(n_rows) * 4;
+  if (n_rows > 0 && (!ws || ws_bytes < need)) return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaError_t e = fwn::launch_bitset_csr_count(bits, n_rows, n_cols, indptr, static_cast<int32_t*>(ws),
+                                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bitset_csr_count");
+  return ok();
+}
+
+fwn_status fwn_bitset_csr_fill(const uint32_t* bits, int32_t n_rows, int32_t n_cols, const int32_t* indptr,
+                               int32_t* indices, void* stream) {
+  if (n_rows < 0 || n_cols < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape %d x %d", n_rows, n_cols);
+  if (n_rows > 0 && (!bits || !indptr)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaError_t e = fwn::launch_bitset_csr_fill(bits, n_rows, n_cols, indptr, indices, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bitset_csr_fill");
+  return ok();
+}
+
 fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
                         const fwn_tile_list* tiles, void* o, float* lse, void* stream) {
   fwn_status s = check_desc(desc);

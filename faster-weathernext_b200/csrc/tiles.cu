@@ -430,6 +430,11 @@ cudaError_t launch_hilbert_codes(const double* lat_deg, const double* lon_deg, i
 
 int tiles_bitmap_words(int n_cols) { return ((n_cols + 31) / 32 + 31) / 32; }
 
+cudaError_t launch_exclusive_scan(const int32_t* counts, int n, int32_t* ptr, cudaStream_t stream) {
+  exclusive_scan_kernel<<<1, 1024, 0, stream>>>(counts, n, ptr);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gather_count(const int32_t* ptr2, const uint32_t* bits2, int n_blocks, int32_t* ptr_g,
                                 int32_t* counts, cudaStream_t stream) {
   if (n_blocks > 0) gather_count_kernel<<<n_blocks, kThreads, 0, stream>>>(ptr2, bits2, counts);

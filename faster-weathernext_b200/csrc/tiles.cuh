@@ -1,6 +1,7 @@
 // Host launchers of the tile-list builder kernels (tiles.cu).
 #pragma once
 
+#include <algorithm>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -33,5 +34,22 @@ cudaError_t launch_gather_fill(const int32_t* ptr2, const int32_t* kb2, const ui
 // Hilbert-curve codes of (lat, lon) points in degrees (bits per axis <= 20); INT64_MAX for non-finite.
 cudaError_t launch_hilbert_codes(const double* lat_deg, const double* lon_deg, int n, int bits, long long* codes,
                                  cudaStream_t stream);
+
+// ptr[0] = 0, ptr[i + 1] = ptr[i] + counts[i] for i < n (one CTA).
+cudaError_t launch_exclusive_scan(const int32_t* counts, int n, int32_t* ptr, cudaStream_t stream);
+
+// k-hop reach (khop.cu): uint32 words per bitset row of n_cols columns (a multiple of 4).
+int bitset_words(int n_cols);
+
+// reach[n, bitset_words(n)] = nodes within `hops` edges of each node (self included); scratch is the same
+// size. indptr / indices: CSR of the graph (any column order, duplicates allowed).
+cudaError_t launch_khop(const int32_t* indptr, const int32_t* indices, int n, int hops, uint32_t* reach,
+                        uint32_t* scratch, cudaStream_t stream);
+
+// CSR of a bitset matrix: indptr[n_rows + 1] (counts: n_rows ints of workspace), then ascending indices.
+cudaError_t launch_bitset_csr_count(const uint32_t* bits, int n_rows, int n_cols, int32_t* indptr, int32_t* counts,
+                                    cudaStream_t stream);
+cudaError_t launch_bitset_csr_fill(const uint32_t* bits, int n_rows, int n_cols, const int32_t* indptr,
+                                   int32_t* indices, cudaStream_t stream);
 
 }  // namespace fwn

@@ -27,7 +27,8 @@ MODE_TF32X3 = 2
 SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_rows",
            "fwn_tiles_workspace_size", "fwn_tiles_count", "fwn_tiles_fill", "fwn_tiles_pair_count",
            "fwn_tiles_pair_fill", "fwn_tiles_gather_count", "fwn_tiles_gather_fill", "fwn_hilbert_codes", "fwn_attn_fwd", "fwn_attn_bwd_workspace_size", "fwn_attn_bwd",
-           "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv", "fwn_attn_bwd_noalloc")
+           "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv", "fwn_attn_bwd_noalloc",
+           "fwn_bitset_words", "fwn_khop_bitset", "fwn_bitset_csr_count", "fwn_bitset_csr_fill")
 
 
 class AttnDesc(ctypes.Structure):
@@ -60,6 +61,8 @@ def _declare(lib):
   lib.fwn_last_error_string.restype = ctypes.c_char_p
   lib.fwn_lse_rows.argtypes = [_I]
   lib.fwn_lse_rows.restype = _I
+  lib.fwn_bitset_words.argtypes = [_I]
+  lib.fwn_bitset_words.restype = _I
   sigs = {
       "fwn_device_error": [_P, ctypes.POINTER(_I)],
       "fwn_tiles_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
@@ -70,6 +73,9 @@ def _declare(lib):
       "fwn_tiles_gather_count": [ctypes.POINTER(TileList), _P, _P, _SZ, _P],
       "fwn_tiles_gather_fill": [ctypes.POINTER(TileList), _I, _P, _P, _P, _P],
       "fwn_hilbert_codes": [_P, _P, _I, _I, _P, _P],
+      "fwn_khop_bitset": [_P, _P, _I, _I, _P, _P, _P],
+      "fwn_bitset_csr_count": [_P, _I, _I, _P, _P, _SZ, _P],
+      "fwn_bitset_csr_fill": [_P, _I, _I, _P, _P, _P],
       "fwn_attn_fwd": [ctypes.POINTER(AttnDesc), _P, _P, _P, ctypes.POINTER(TileList), _P, _P, _P],
       "fwn_attn_bwd_workspace_size": [ctypes.POINTER(AttnDesc), ctypes.POINTER(_SZ)],
       "fwn_attn_bwd": [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, ctypes.POINTER(TileList),

@@ -164,6 +164,25 @@ def config_mask(cfg: int):
   return permute(mask, perm), lat[perm], lon[perm]
 
 
+# The real WeatherNext 2 attention shape: finest mesh (level 6), 32-hop neighbourhood, batch 1, 6 heads x 128.
+WN2 = {"level": 6, "hops": 32, "batch": 1, "heads": 6, "head_dim": 128}
+
+
+def wn2_adjacency(order: str = "hilbert"):
+  """(adjacency CSR with self edges, lat, lon) of the level-6 mesh in Hilbert (GPU codes) or Morton order;
+  its WN2["hops"]-hop mask is the attention mask (AttentionTiles.from_khop builds it on the device)."""
+  xyz, faces = icosphere(WN2["level"])
+  lat, lon = latlon(xyz)
+  if order == "hilbert":
+    from faster_weathernext import _hilbert
+    perm = _hilbert.hilbert_order(lat, lon)
+  elif order == "morton":
+    perm = morton_order(lat, lon)
+  else:
+    raise ValueError(f"unknown order {order!r}")
+  return permute(adjacency(faces, xyz.shape[0]), perm), lat[perm], lon[perm]
+
+
 def csr_digest(m: sparse.csr_matrix) -> str:
   """sha256 over (shape, indptr int64, indices int64) of a CSR with sorted indices."""
   m = m.tocsr()

@@ -132,6 +132,33 @@ def build_tiles_device(indptr: torch.Tensor, indices: torch.Tensor, n_rows: int,
   return TileList64(ptr, kb, bits.view(n_tiles, block_q), n_rows, n_cols)
 
 
+def khop_csr_device(adj, hops: int, device=None):
+  """Device CSR (int32 indptr [n+1], indices [nnz], ascending) of every node within `hops` edges of each
+  node, self included: the pattern of (adj + I) ** hops, built on the GPU (bitset k-hop kernels). Stands in
+  for the host `adj_mat ** attention_k_hop` of the reference (patch.py:209)."""
+  lib = _lib.lib()
+  dev = _device(device)
+  a = sparse.csr_matrix(adj).astype(bool)
+  a.eliminate_zeros()
+  n = a.shape[0]
+  assert a.shape == (n, n), "adjacency must be square"
+  ip, ix, _ = _csr_to_device(a, dev)
+  words = lib.fwn_bitset_words(n)
+  reach = torch.empty(n * words, dtype=torch.int32, device=dev)
+  scratch = torch.empty(n * words, dtype=torch.int32, device=dev)
+  s = _stream()
+  _lib.check(lib.fwn_khop_bitset(ip.data_ptr(), ix.data_ptr() if ix.numel() else 0, n, hops, reach.data_ptr(),
+                                 scratch.data_ptr(), s))
+  del scratch
+  indptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
+  ws = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+  _lib.check(lib.fwn_bitset_csr_count(reach.data_ptr(), n, n, indptr.data_ptr(), ws.data_ptr(), ws.numel() * 4, s))
+  nnz = _read_last(indptr)
+  indices = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)[:nnz]
+  _lib.check(lib.fwn_bitset_csr_fill(reach.data_ptr(), n, n, indptr.data_ptr(), indices.data_ptr(), s))
+  return indptr, indices
+
+
 def pair_tiles(t: TileList64) -> TileList128:
   """128-row list derived from a 64-row list (union of the two blocks' key tiles)."""
   lib = _lib.lib()
@@ -227,6 +254,18 @@ class AttentionTiles:
       ip, ix, _ = _csr_to_device(mt, dev)
       bwd = pair_tiles(build_tiles_device(ip, ix, n, n))
     return cls(fwd, bwd, n, symmetric, gather)
+
+  @classmethod
+  def from_khop(cls, adj, hops: int, device=None, gather: bool = True) -> "AttentionTiles":
+    """Lists of the k-hop mask of a symmetric adjacency, built entirely on the device (mask, CSR, lists);
+    permute the adjacency first for a node order (the k-hop mask of a permuted graph is the permuted mask)."""
+    dev = _device(device)
+    a = sparse.csr_matrix(adj).astype(bool)
+    assert (a != a.T).nnz == 0, "from_khop takes a symmetric adjacency"
+    n = a.shape[0]
+    indptr, indices = khop_csr_device(a, hops, dev)
+    fwd = pair_tiles(build_tiles_device(indptr, indices, n, n))
+    return cls(fwd, fwd, n, True, gather)
 
   @classmethod
   def from_lists(cls, tile_ptr, tile_kb, tile_bits, n: int, tiles_t=None, device=None,

@@ -146,6 +146,29 @@ FWN_API fwn_status fwn_tiles_gather_fill(const fwn_tile_list* tiles128, int32_t 
 FWN_API fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32_t n, int32_t bits,
                                      int64_t* codes, void* stream);
 
+/* ---- neighbourhood masks on the device ------------------------------------------------------------- */
+
+/* uint32 words per row of a bitset matrix with n_cols columns (bit c of word w = column 32 w + c); a
+ * multiple of 4, so every row starts on a 16-byte boundary. */
+FWN_API int32_t fwn_bitset_words(int32_t n_cols);
+
+/* k-hop neighbourhood: reach[n * fwn_bitset_words(n)] row i = every node within `hops` edges of node i,
+ * self included, i.e. the nonzero pattern of (adj + I) ** hops. Replaces the host sparse matrix power
+ * `adj_mat ** attention_k_hop` (src/faster_weathernext/patch.py:209); for a mesh adjacency (which has
+ * triangles) and hops >= 2 the two patterns are equal. indptr[n + 1] / indices: CSR of adj (any column
+ * order, duplicates allowed). scratch has reach's size. 0 <= hops <= 4096. */
+FWN_API fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops,
+                                   uint32_t* reach, uint32_t* scratch, void* stream);
+
+/* CSR of a bitset matrix [n_rows, fwn_bitset_words(n_cols)] (columns >= n_cols ignored), in two passes as
+ * the tile builder: pass 1 writes indptr[n_rows + 1] (ws: n_rows int32; nnz = indptr[n_rows]); pass 2
+ * writes indices[nnz], ascending per row. n_rows * n_cols must be below 2^31. The result feeds
+ * fwn_tiles_count / fwn_tiles_fill directly. */
+FWN_API fwn_status fwn_bitset_csr_count(const uint32_t* bits, int32_t n_rows, int32_t n_cols, int32_t* indptr,
+                                        void* ws, size_t ws_bytes, void* stream);
+FWN_API fwn_status fwn_bitset_csr_fill(const uint32_t* bits, int32_t n_rows, int32_t n_cols, const int32_t* indptr,
+                                       int32_t* indices, void* stream);
+
 /* ---- attention --------------------------------------------------------------------------------------- */
 
 /* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)
