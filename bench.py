@@ -195,7 +195,11 @@ def run_ours(args):
   ws_bytes = heads * lse_rows * 4
   ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
   import ctypes
-  lf, lb = (tiles.fwd_g, tiles.bwd_g) if args.lists == "gathered" else (tiles.fwd, tiles.bwd)
+  if args.lists == "auto":
+    lf, lb = ta._lists(tiles, q0, o_like)   # what the public API walks for this mask and layout
+  else:
+    lf, lb = (tiles.fwd_g, tiles.bwd_g) if args.lists == "gathered" else (tiles.fwd, tiles.bwd)
+  lists_used = "gathered" if lf.cols is not None else "paired"
   sf, sb = lf.struct(), lb.struct()
   dref = ctypes.byref(desc)
 
@@ -276,7 +280,7 @@ def run_ours(args):
                   "algorithmic_gbs": round(nbytes / (ms_k * 1e-3) / 1e9, 1),
                   "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm"}
   dom = max(kernel_ms, key=kernel_ms.get)
-  traffic = NCU_TRAFFIC.get((args.workload, args.mode, args.lists), {})
+  traffic = NCU_TRAFFIC.get((args.workload, args.mode, lists_used), {})
   flops, nbytes = costs[dom]
   bound = kernels[dom]["bound"]
   if bound == "hbm":
@@ -348,7 +352,7 @@ def run_ours(args):
         "dtype": {"bf16": "bf16", "tf32": "tf32", "tf32x3": "3xtf32"}[args.mode], "data": data,
         "config": {"workload": desc_w, "global_batch": world, "nodes": n,
                    "heads": heads, "head_dim": head_dim, "parallelism": f"replicas x{world} (no communication)",
-                   "l2": f"inputs larger than L2: 3 rotating input sets of {set_mb:.0f} MB", "tile_lists": args.lists},
+                   "l2": f"inputs larger than L2: 3 rotating input sets of {set_mb:.0f} MB", "tile_lists": lists_used},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
         "clocks": clocks.summary(), "kernels": kernels,
         "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2),
@@ -577,8 +581,9 @@ def main():
   ap.add_argument("--workload", choices=["attention", "wn2", "processor", "finetune"], default="attention",
                   help="attention: configuration 3 (the headline); wn2: the real WeatherNext 2 shape (32-hop mask, "
                        "6 x 128 heads); processor / finetune: configurations 4 / 5")
-  ap.add_argument("--lists", choices=["gathered", "paired"], default="gathered",
-                  help="tile lists the kernels walk: gathered (distinct keys per block) or paired 32-key tiles")
+  ap.add_argument("--lists", choices=["auto", "gathered", "paired"], default="auto",
+                  help="tile lists the kernels walk: gathered (distinct keys per block), paired 32-key tiles, or "
+                       "auto (the public API's choice: gathered for sparse masks, paired for dense ones / D 128)")
   ap.add_argument("--no-e2e", action="store_true")
   ap.add_argument("--no-cpu", action="store_true")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)

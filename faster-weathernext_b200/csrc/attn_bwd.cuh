@@ -48,6 +48,7 @@ struct BwdParams {
   int heads, n, np, lse_rows, n_items;
   float scale;         // softmax scale (applied to acc0)
   float scale_log2;    // scale * log2(e)
+  unsigned long long* trace;  // FWN_TRACE builds: event records (else unused)
 };
 
 template <int KIND, int D, bool F32, int CH, bool X3>
@@ -76,17 +77,20 @@ struct BwdCfg {
   static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
   static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
   static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1) : 2;
+  // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
+  static constexpr bool G64 = COLS * ES == 64;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
   static constexpr int BITS_OFF = NC * XL * C_BYTES;
   static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (rows are keys)
   static constexpr int STAGE_RAW = VEC_OFF + (ROWS_ARE_KEYS ? CH * 256 : 0);
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int G_BYTES = ((COLS * ES + 127) / 128) * ROWS * 128; // one dS (or P) tile
+  static constexpr int G_BYTES = G64 ? ROWS * 64 : (COLS * ES / 128) * ROWS * 128;  // one dS (or P) tile
   static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
-  // dS / P buffers: one for the bf16 dK/dV pass at head_dim 64 (keeps two CTAs per SM) and in 3xTF32
-  // (except dV only), else two.
-  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (X3 && KIND != kBwdDV)) ? 1 : 2;
+  // dS / P buffers: one where two would not leave room for a second CTA per SM (bf16 dK/dV at head_dim 64,
+  // bf16 dQ / dK only at head_dim 128) or would not fit at all (3xTF32 except dV only); else two.
+  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (D == 128 && !F32 && KIND != kBwdDV) ||
+                             (X3 && KIND != kBwdDV)) ? 1 : 2;
   static constexpr int OFF_C = NR * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
@@ -99,9 +103,12 @@ struct BwdCfg {
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
-  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : (X3 ? 200 : 255);
+  // Each SM sub-partition has 16,384 registers and takes a quarter of the resident warps (rounded up):
+  // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
+  static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 255;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(COLS * ES % 128 == 0, "dS rows must fill 128-byte column blocks");
+  static_assert(G64 || COLS * ES % 128 == 0, "dS rows must fill 64-byte or whole 128-byte column blocks");
+  static_assert(!G64 || (!F32 && CH == 1), "64-byte dS rows hold 32 bf16 columns");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
 };
@@ -406,7 +413,8 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               const uint32_t bbase = slot(sb, bs, pass == 1 ? 1 : 0);
               for (int kk = 0; kk < ksteps; ++kk) {
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                const uint64_t a = smem_desc(ga + cb * C::ROWS * 128 + within, 16, 1024);
+                const uint64_t a = C::G64 ? smem_desc(ga + kk * 32, 16, 512, kLayoutSW64)
+                                          : smem_desc(ga + cb * C::ROWS * 128 + within, 16, 1024);
                 const uint64_t bd = F32 ? smem_desc(bbase + kk * C::KSTEP * 128, C::COLS * 128, 512, kLayoutSW128Base32B)
                                         : smem_desc(bbase + kk * C::KSTEP * 128, C::COLS * 128, 1024);
                 mma_ss<F32>(acc, a, bd, kIdescAcc, (c == 0 && pass == 0 && kk == 0) ? 0u : 1u);
@@ -542,7 +550,14 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               if (which == 1 && !C::ACC_P) continue;
               const float* src = which == 0 ? dp : s;
               const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
-              if constexpr (!F32) {
+              if constexpr (C::G64) {
+                // 32 bf16 columns = one 64-byte row.
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                  st_shared_v4(base + sw64_offset(row, cc), pack_bf16(src[8 * cc], src[8 * cc + 1]),
+                               pack_bf16(src[8 * cc + 2], src[8 * cc + 3]), pack_bf16(src[8 * cc + 4], src[8 * cc + 5]),
+                               pack_bf16(src[8 * cc + 6], src[8 * cc + 7]));
+              } else if constexpr (!F32) {
                 // 32 bf16 columns = chunks 4j .. 4j+3 of the 128-byte row.
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)

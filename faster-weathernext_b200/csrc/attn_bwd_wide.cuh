@@ -1,0 +1,505 @@
+// Backward kernels for dense neighbourhoods (bf16, 128-row tile lists): 128-column chunks.
+//
+// Same algorithm as attn_bwd.cuh (_bwd_dq_kernel / _bwd_dkv_kernel, src/faster_weathernext/pallas_attn.py:
+// 161-215): P = where(valid, exp(S - lse), 0), dS = P (dP - delta), dQ = scale dS K, dK = scale dS^T Q,
+// dV = P^T dO; every output row is owned by one CTA (no atomics, deterministic).
+//
+// Why separate kernels: as in the forward, tcgen05.mma instructions with N = 32 or 64 leave most of the
+// tensor core idle on dense masks. Here a chunk is four consecutive tiles of the list (128 columns), so
+// S and dP are N = 128 MMAs and the accumulating MMAs have K = 128. At head_dim 128 the operands of one
+// dK/dV pass do not fit one CTA, so there are three passes ("kinds"), each one CTA per SM:
+//               dQ              dV only         dK only
+//   rows        queries         keys            keys            (128 per work item, held all item long)
+//   R0, R1      Q, dO           K               K, V
+//   C0, C1      K, V            Q, dO           Q, dO           (per chunk, in rings)
+//   S  = R0 C0^T, dP = R1 C1^T  (dV only: no dP)
+//   acc += G C                  G = dS, C = C0 (dQ, dK); G = P, C = C1 (dV); C read MN-major
+// G (bf16, 128 x 128) is written by the elementwise warps into TMEM and is the A operand of the
+// accumulating MMA (two G buffers). A column operand read again by the accumulating MMA lives in a ring of
+// three slots, one read only by S / dP in a ring of two. Rows are keys for dV / dK: their columns' lse and
+// delta come with the chunk (a ring of vectors); for dQ they are per thread.
+//
+// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM allocation and single-thread MMA issue (S and dP
+// of chunk c+1 ahead of the accumulating MMA of chunk c); warps 2-9 elementwise, warps w and w+4 sharing
+// TMEM lane quadrant w % 4 (thread = row) and taking columns 0-63 / 64-127 of each chunk; the mask words
+// are read from global memory one chunk ahead. Epilogue: each warp stores half of the accumulator
+// columns. Every mbarrier wait is bounded (common.cuh).
+#pragma once
+
+#include <cuda.h>
+
+#include "attn_bwd.cuh"
+#include "common.cuh"
+
+namespace fwn {
+
+template <int KIND, int D>
+struct BwdWideCfg {
+  static constexpr bool ROWS_ARE_KEYS = KIND != kBwdDQ;
+  static constexpr bool NEED_DP = KIND != kBwdDV;
+  static constexpr bool ACC_ON_C0 = KIND != kBwdDV;   // dS C0 (dQ, dK) or P C1 (dV)
+  static constexpr int ES = 2;
+  static constexpr int EPB = 64;
+  static constexpr int CB = D / EPB;
+  static constexpr int ROWS = 128;
+  static constexpr int SUB = 32;
+  static constexpr int CH = 4;
+  static constexpr int COLS = SUB * CH;
+  static constexpr int NR = NEED_DP ? 2 : 1;
+  static constexpr int R_BYTES = CB * ROWS * 128;
+  static constexpr int C_BYTES = CB * COLS * 128;
+  static constexpr int N0 = ACC_ON_C0 ? 3 : 2;      // C0 ring
+  static constexpr int N1 = ACC_ON_C0 ? 2 : 3;      // C1 ring
+  static constexpr int NVEC = ROWS_ARE_KEYS ? 2 : 0;  // lse / delta vectors of the chunk's columns (1 KB)
+  static constexpr int NVEC_RING = NVEC > 0 ? NVEC : 1; // ring arithmetic (no vectors for dQ)
+  static constexpr int OFF_C0 = NR * R_BYTES;
+  static constexpr int OFF_C1 = OFF_C0 + N0 * C_BYTES;
+  static constexpr int OFF_VEC = OFF_C1 + N1 * C_BYTES;
+  static constexpr int OFF_BAR = OFF_VEC + NVEC * 1024;
+  static constexpr int NSB = NEED_DP ? 1 : 2;        // S (and dP) buffers
+  static constexpr int N_BAR = 2 + 2 * N0 + 2 * N1 + 2 * NVEC + 2 * NSB + 4 + 3;
+  // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
+  // TMEM: S[NSB] (128 each), dP (128), acc (D), G[2] (64 each).
+  static constexpr int DP_COL = 128 * NSB;
+  static constexpr int ACC_COL = DP_COL + (NEED_DP ? 128 : 0);
+  static constexpr int G_COL = ACC_COL + D;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 320;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(G_COL + 128 <= TMEM_COLS, "TMEM budget");
+};
+
+template <int KIND, int D>
+__global__ void __maxnreg__(168)
+    attn_bwd_wide_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
+                         const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
+                         const __grid_constant__ CUtensorMap tm_c0w, const __grid_constant__ CUtensorMap tm_c1w,
+                         const BwdParams p) {
+  using C = BwdWideCfg<KIND, D>;
+  extern __shared__ __align__(1024) uint8_t smem_bwd_wide[];
+  uint8_t* smem = smem_bwd_wide;
+  const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {
+    // The tile layouts need 1024-byte aligned shared memory; report and leave (uniformly, before any wait).
+    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
+    return;
+  }
+  auto r_op = [&](int i) { return sbase + i * C::R_BYTES; };
+  auto c0_slot = [&](int s) { return sbase + C::OFF_C0 + s * C::C_BYTES; };
+  auto c1_slot = [&](int s) { return sbase + C::OFF_C1 + s * C::C_BYTES; };
+  auto vec_slot = [&](int s) { return sbase + C::OFF_VEC + s * 1024; };
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  const uint32_t r_full = bar0, r_empty = bar0 + 8;
+  auto c0_full = [&](int s) { return bar0 + 16 + 8 * s; };
+  auto c0_empty = [&](int s) { return bar0 + 16 + 8 * (C::N0 + s); };
+  const uint32_t bar1 = bar0 + 16 + 16 * C::N0;
+  auto c1_full = [&](int s) { return bar1 + 8 * s; };
+  auto c1_empty = [&](int s) { return bar1 + 8 * (C::N1 + s); };
+  const uint32_t bar2 = bar1 + 16 * C::N1;
+  auto v_full = [&](int s) { return bar2 + 8 * s; };
+  auto v_empty = [&](int s) { return bar2 + 8 * (C::NVEC + s); };
+  const uint32_t bar3 = bar2 + 16 * C::NVEC;
+  auto s_full = [&](int b) { return bar3 + 8 * b; };
+  auto s_empty = [&](int b) { return bar3 + 8 * (C::NSB + b); };
+  const uint32_t bar4 = bar3 + 16 * C::NSB;
+  auto g_full = [&](int b) { return bar4 + 8 * b; };
+  auto g_empty = [&](int b) { return bar4 + 16 + 8 * b; };
+  const uint32_t acc_full = bar4 + 32, acc_empty = bar4 + 40, drain = bar4 + 48;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
+  int* trace_count = reinterpret_cast<int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 8);
+  const long long trace_t0 = clock64();
+#define FWN_TR(code, arg) trace_event(p.trace, trace_count, trace_t0, (code), (arg))
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    *trace_count = 0;
+    mbar_init(r_full, 1);
+    mbar_init(r_empty, 1);
+    for (int s = 0; s < C::N0; ++s) {
+      mbar_init(c0_full(s), 1);
+      mbar_init(c0_empty(s), 1);
+    }
+    for (int s = 0; s < C::N1; ++s) {
+      mbar_init(c1_full(s), 1);
+      mbar_init(c1_empty(s), 1);
+    }
+    for (int s = 0; s < C::NVEC; ++s) {
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 8);
+    }
+    for (int b = 0; b < C::NSB; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(s_empty(b), 8);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(g_full(b), 8);
+      mbar_init(g_empty(b), 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_r0);
+    if (C::NR == 2) tma_prefetch_desc(&tm_r1);
+    tma_prefetch_desc(&tm_c0);
+    tma_prefetch_desc(&tm_c1);
+    tma_prefetch_desc(&tm_c0w);
+    tma_prefetch_desc(&tm_c1w);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int per_bh = p.np;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (whole warp)
+    uint32_t n0 = 0, n1 = 0, nvec = 0, qc = 0;  // copies issued per ring
+    bool ok = true;
+    int pending_r = 0;
+    int it = blockIdx.x;
+    int nt0 = 0, nt1 = 0;
+    if (it < p.n_items) {
+      nt0 = __ldg(p.ptr2 + it % per_bh);
+      nt1 = __ldg(p.ptr2 + it % per_bh + 1);
+    }
+    for (; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = nt0, n_sub = nt1 - nt0;
+      const int it_next = it + gridDim.x;
+      if (it_next < p.n_items) {
+        nt0 = __ldg(p.ptr2 + it_next % per_bh);
+        nt1 = __ldg(p.ptr2 + it_next % per_bh + 1);
+      }
+      const int nch = (n_sub + C::CH - 1) / C::CH;
+      if (nch == 0) continue;
+      auto meta = [&](int c) { const int i = C::CH * c + (lane & 3); return i < n_sub ? __ldg(p.kb2 + t0 + i) : 0; };
+      if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(r_full, C::NR * C::R_BYTES);
+        for (int cb = 0; cb < C::CB; ++cb) {
+          tma_load_4d(r_op(0) + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+          if (C::NR == 2) tma_load_4d(r_op(1) + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+        }
+      }
+      pending_r = 1;
+      // One column operand of a chunk: one 128-row box per column block for four consecutive tiles, else one
+      // 32-row box per tile and column block (lanes 0 .. n_in * CB - 1).
+      auto load_op = [&](uint32_t dst, const CUtensorMap* t32, const CUtensorMap* t128, int kbl, int n_in,
+                         uint32_t bar) {
+        const int k0 = __shfl_sync(0xffffffffu, kbl, 0), k1 = __shfl_sync(0xffffffffu, kbl, 1);
+        const int k2 = __shfl_sync(0xffffffffu, kbl, 2), k3 = __shfl_sync(0xffffffffu, kbl, 3);
+        const bool run = n_in == 4 && k1 == k0 + 1 && k2 == k0 + 2 && k3 == k0 + 3;
+        if (lane == 0) mbar_arrive_expect_tx(bar, n_in * C::SUB * D * C::ES);
+        __syncwarp();
+        if (run) {
+          if (lane < C::CB) tma_load_4d(dst + lane * C::COLS * 128, t128, lane * C::EPB, h, k0 * C::SUB, b, bar);
+        } else if (lane < n_in * C::CB) {
+          const int s = lane / C::CB, cb = lane % C::CB;
+          const int kb = s == 0 ? k0 : s == 1 ? k1 : s == 2 ? k2 : k3;
+          tma_load_4d(dst + cb * C::COLS * 128 + s * C::SUB * 128, t32, cb * C::EPB, h, kb * C::SUB, b, bar);
+        }
+      };
+      // lse and delta of the chunk's columns (rows are keys): lane s < n_in copies tile s's 32 + 32 floats.
+      auto load_vec = [&](int kbl, int n_in) -> bool {
+        if (!mbar_wait(v_empty(nvec % C::NVEC_RING), ((nvec / C::NVEC_RING) & 1) ^ 1, abort_flag)) return false;
+        const uint32_t dst = vec_slot(nvec % C::NVEC_RING), bar = v_full(nvec % C::NVEC_RING);
+        if (lane == 0) mbar_arrive_expect_tx(bar, n_in * 256);
+        __syncwarp();
+        if (lane < n_in) {
+          const size_t vo = static_cast<size_t>(bh) * p.lse_rows + static_cast<size_t>(kbl) * C::SUB;
+          bulk_load(dst + lane * 128, p.lse + vo, 128, bar);
+          bulk_load(dst + 512 + lane * 128, p.delta + vo, 128, bar);
+        }
+        ++nvec;
+        return true;
+      };
+      int kb_cur = meta(0), kb_prev = 0;
+      for (int c = 0; c <= nch && ok; ++c) {
+        const int kb_next = c + 1 < nch ? meta(c + 1) : 0;
+        if (c < nch) {
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!(ok = mbar_wait(c0_empty(n0 % C::N0), ((n0 / C::N0) & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(3, c);
+          load_op(c0_slot(n0 % C::N0), &tm_c0, &tm_c0w, kb_cur, n_in, c0_full(n0 % C::N0));
+          ++n0;
+          if constexpr (C::NEED_DP) {
+            if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
+            load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_cur, n_in, c1_full(n1 % C::N1));
+            ++n1;
+          }
+          if constexpr (C::ROWS_ARE_KEYS) {
+            if (!(ok = load_vec(kb_cur, n_in))) break;
+          }
+        }
+        if constexpr (!C::NEED_DP) {
+          // dV only: dO (C1) is read by the accumulating MMA, one chunk after Q.
+          if (c >= 1) {
+            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+            if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
+            load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_prev, n_in, c1_full(n1 % C::N1));
+            ++n1;
+          }
+        }
+        kb_prev = kb_cur;
+        kb_cur = kb_next;
+      }
+      if (!ok) break;
+      ++qc;
+    }
+    if (!ok && lane == 0) {
+      volatile int never = 0;
+      for (uint32_t k = (n0 >= C::N0 ? n0 - C::N0 : 0); k < n0; ++k) mbar_wait(c0_full(k % C::N0), (k / C::N0) & 1, &never);
+      for (uint32_t k = (n1 >= C::N1 ? n1 - C::N1 : 0); k < n1; ++k) mbar_wait(c1_full(k % C::N1), (k / C::N1) & 1, &never);
+      if (C::NVEC)
+        for (uint32_t k = (nvec >= C::NVEC_RING ? nvec - C::NVEC_RING : 0); k < nvec; ++k)
+          mbar_wait(v_full(k % C::NVEC_RING), (k / C::NVEC_RING) & 1, &never);
+      if (pending_r) mbar_wait(r_full, qc & 1, &never);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescAcc = instr_desc(false, 128, D, false, true);
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + C::CH - 1) / C::CH;
+        if (nch == 0) continue;
+        if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
+        const uint32_t g0 = g;
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {
+            const uint32_t gg = g0 + c;
+            const int sb = gg % C::NSB;
+            const int n_in = min(C::CH, n_sub - C::CH * c);
+            if (!(ok = mbar_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
+            if (C::NEED_DP && !(ok = mbar_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+            if (!(ok = mbar_wait(s_empty(sb), ((gg / C::NSB) & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
+            const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
+            const uint32_t c0t = c0_slot(gg % C::N0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<false>(tmem + 128 * sb, smem_desc(r_op(0) + cb * C::ROWS * 128 + within, 16, 1024),
+                            smem_desc(c0t + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            }
+            if constexpr (C::NEED_DP) {
+              const uint32_t c1t = c1_slot(gg % C::N1);
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                mma_ss<false>(tmem + C::DP_COL, smem_desc(r_op(1) + cb * C::ROWS * 128 + within, 16, 1024),
+                              smem_desc(c1t + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+              }
+              mma_commit(c1_empty(gg % C::N1));  // C1 is read only by dP here
+            } else {
+              mma_commit(c0_empty(gg % C::N0));  // dV only: C0 (Q) is read only by S
+            }
+            mma_commit(s_full(sb));
+            FWN_TR(11, c);
+            if (c == nch - 1) mma_commit(r_empty);
+          }
+          if (c >= 1) {
+            const uint32_t gg = g0 + c - 1;
+            const int gb = gg & 1;
+            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+            if (!(ok = mbar_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
+            if (!C::NEED_DP && !(ok = mbar_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+            if (c == 1 && !(ok = mbar_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
+            const uint32_t bt = C::ACC_ON_C0 ? c0_slot(gg % C::N0) : c1_slot(gg % C::N1);
+            const int ksteps = 2 * n_in;
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_ts(tmem + C::ACC_COL, tmem + C::G_COL + 64 * gb + 8 * kk,
+                     smem_desc(bt + kk * 16 * 128, C::COLS * 128, 1024), kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
+            mma_commit(g_empty(gb));
+            if (C::ACC_ON_C0) mma_commit(c0_empty(gg % C::N0));
+            else mma_commit(c1_empty(gg % C::N1));
+            FWN_TR(12, c - 1);
+            if (c == nch) mma_commit(acc_full);
+          }
+        }
+        g = g0 + nch;
+        ++qc;
+      }
+      mma_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // ------------------------------------------------------------------ elementwise + epilogue (warps 2-9)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float c2 = p.scale_log2;
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + C::CH - 1) / C::CH;
+      const int grow = pb * C::ROWS + row;
+      float nl2_row = 0.f, delta_row = 0.f;
+      if (!C::ROWS_ARE_KEYS) {
+        nl2_row = -p.lse[static_cast<size_t>(bh) * p.lse_rows + grow] * kLog2e;
+        delta_row = p.delta[static_cast<size_t>(bh) * p.lse_rows + grow];
+      }
+      // Mask words of this half's two tiles of chunk c (global memory, read one chunk ahead).
+      auto words = [&](int c, uint32_t& w0, uint32_t& w1) {
+        const int i = C::CH * c + 2 * half;
+        w0 = i < n_sub ? __ldg(p.bits2 + static_cast<size_t>(t0 + i) * 128 + row) : 0u;
+        w1 = i + 1 < n_sub ? __ldg(p.bits2 + static_cast<size_t>(t0 + i + 1) * 128 + row) : 0u;
+      };
+      uint32_t nw0 = 0, nw1 = 0;
+      if (nch > 0) words(0, nw0, nw1);
+      const uint32_t g0 = g;
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t gg = g0 + c;
+        const int sb = gg % C::NSB, gb = gg & 1;
+        const int n_in = min(C::CH, n_sub - C::CH * c);
+        const int j0 = 2 * half;
+        const uint32_t w0 = nw0, w1 = nw1;
+        if (c + 1 < nch) words(c + 1, nw0, nw1);
+        const uint32_t a0 = __reduce_or_sync(0xffffffffu, w0), a1 = __reduce_or_sync(0xffffffffu, w1);
+        if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
+        if (warp == 2 && lane == 0) FWN_TR(20, c);
+        tc_fence_after();
+        // Column lse (as -lse * log2 e) and delta of this half (rows are keys).
+        uint32_t vslot = 0;
+        if constexpr (C::ROWS_ARE_KEYS) {
+          const uint32_t vs = gg % C::NVEC_RING;
+          if (!(ok = mbar_wait(v_full(vs), (gg / C::NVEC_RING) & 1, abort_flag))) break;
+          vslot = vec_slot(vs) + 64 * half * 4;
+        }
+        // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs, one 32-column sub-tile at a time;
+        // the S / dP buffer is released once the second sub-tile is in registers.
+        uint32_t pk[32];
+        const float2 cc = make_float2(c2, c2);
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          float s[32], dp[32];
+          if (j0 + jj < n_in) {
+            tmem_ld32(trow + 128 * sb + 64 * half + 32 * jj, s);
+            if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 64 * half + 32 * jj, dp);
+          }
+          tmem_wait_ld();
+          if (jj == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_empty(sb));
+          }
+          const uint32_t w = jj ? w1 : w0;
+          const uint32_t a = jj ? a1 : a0;
+#pragma unroll
+          for (int gi = 0; gi < 4; ++gi) {
+            if ((a >> (8 * gi)) & 0xFFu) {
+              float lv[8], dv[8];
+              if constexpr (C::ROWS_ARE_KEYS) {
+                const uint32_t va = vslot + 32 * (4 * jj + gi);
+                const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
+                lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
+                if constexpr (C::NEED_DP) {
+                  const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
+                  dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  lv[i] = nl2_row;
+                  dv[i] = delta_row;
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const int k = 8 * gi + i;
+                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
+                float2 e;
+                if (i < 2) {
+                  e = exp2_poly2(x);
+                } else {
+                  e.x = ex2(x.x);
+                  e.y = ex2(x.y);
+                }
+                e.x = (w >> k) & 1u ? e.x : 0.f;
+                e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
+                if constexpr (C::NEED_DP) {
+                  const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
+                  pk[16 * jj + (k >> 1)] = pack_bf16(ds.x, ds.y);
+                } else {
+                  pk[16 * jj + (k >> 1)] = pack_bf16(e.x, e.y);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) pk[16 * jj + 4 * gi + i] = 0u;
+            }
+          }
+        }
+        if constexpr (C::ROWS_ARE_KEYS) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(v_empty(gg % C::NVEC_RING));
+        }
+        if (warp == 2 && lane == 0) FWN_TR(26, c);
+        // G buffer free once the accumulating MMA of chunk gg-2 is complete.
+        if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+        if (j0 < n_in) tmem_st32(trow + C::G_COL + 64 * gb + 32 * half, *reinterpret_cast<const float(*)[32]>(pk));
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(g_full(gb));
+        if (warp == 2 && lane == 0) FWN_TR(21, c);
+      }
+      if (!ok) break;
+      g = g0 + nch;
+      // ---------------------------------------------------------------- epilogue: this half's D / 2 columns
+      const bool store = grow < p.n;
+      const int64_t roff = (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sn +
+                            static_cast<int64_t>(h) * p.o_sh) * C::ES + (D / 2) * C::ES * half;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(C::ACC_ON_C0 ? p.out0 : p.out1) + roff;
+      const float mul = C::ACC_ON_C0 ? p.scale : 1.f;
+      if (nch == 0) {
+        if (store)
+          for (int i = 0; i < D * C::ES / 32; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      if (!(ok = mbar_wait(acc_full, qc & 1, abort_flag))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int j = 0; j < D / 64; ++j) {
+        float o[32];
+        tmem_ld32(trow + C::ACC_COL + (D / 2) * half + 32 * j, o);
+        tmem_wait_ld();
+        if (store) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(dst + j * 64)[i] =
+                make_uint4(pack_bf16(o[8 * i] * mul, o[8 * i + 1] * mul), pack_bf16(o[8 * i + 2] * mul, o[8 * i + 3] * mul),
+                           pack_bf16(o[8 * i + 4] * mul, o[8 * i + 5] * mul), pack_bf16(o[8 * i + 6] * mul, o[8 * i + 7] * mul));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      ++qc;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+#undef FWN_TR
+}
+
+}  // namespace fwn

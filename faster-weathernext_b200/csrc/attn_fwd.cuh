@@ -54,7 +54,9 @@ struct FwdCfg {
   static constexpr int CB = D / EPB;          // column blocks of a head_dim row
   static constexpr int ROWS = 128;            // query rows per item
   static constexpr int SUB = 32;              // keys per tile
-  static constexpr int CH = X3 ? 1 : 2;       // tiles per chunk
+  // Tiles per chunk: one at head_dim 128 in bf16 (keeps two CTAs per SM, so that one CTA's softmax overlaps
+  // the other's MMAs), and in 3xTF32; else two.
+  static constexpr int CH = (X3 || (D == 128 && !F32)) ? 1 : 2;
   static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
   static constexpr int NS = X3 ? 2 : 3;       // K/V pipeline stages
@@ -63,8 +65,9 @@ struct FwdCfg {
   // Stage: K, V, (3xTF32: K_lo, V_lo), mask words.
   static constexpr int BITS_OFF = (X3 ? 4 : 2) * KV_BYTES;
   static constexpr int STAGE_BYTES = (BITS_OFF + CH * 512 + 1023) / 1024 * 1024;
-  static constexpr int PCB = KEYS * ES / 128;  // column blocks of a P row
-  static constexpr int P_BYTES = PCB * ROWS * 128;
+  static constexpr int PCB = KEYS * ES / 128;  // 128-byte column blocks of a P row (0: one 64-byte row)
+  static constexpr bool P64 = PCB == 0;         // 32 bf16 keys: P rows of 64 bytes, 64-byte swizzle
+  static constexpr int P_BYTES = P64 ? ROWS * 64 : PCB * ROWS * 128;
   static constexpr int PBUF_BYTES = P_BYTES * (X3 ? 2 : 1);  // P (3xTF32: P_hi, P_lo)
   static constexpr int OFF_STAGE = Q_BYTES * (X3 ? 2 : 1);    // Q (3xTF32: Q_hi in place, Q_lo)
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
@@ -77,8 +80,11 @@ struct FwdCfg {
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
   // 192-thread CTAs share an SM's 65,536.
-  static constexpr int MAX_REGS = MIN_BLOCKS == 2 ? 168 : 200;
+  // Each SM sub-partition has 16,384 registers and takes a quarter of the resident warps (rounded up):
+  // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
+  static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 200;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
+  static_assert(!P64 || (!F32 && CH == 1), "64-byte P rows hold 32 bf16 keys");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
@@ -309,7 +315,8 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
               const uint32_t vb = pass == 1 ? stage_vlo(st) : stage_v(st);
               for (int kk = 0; kk < ksteps; ++kk) {
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                const uint64_t a = smem_desc(pa + cb * C::ROWS * 128 + within, 16, 1024);
+                const uint64_t a = C::P64 ? smem_desc(pa + kk * 32, 16, 512, kLayoutSW64)
+                                          : smem_desc(pa + cb * C::ROWS * 128 + within, 16, 1024);
                 // V is the MN-major B operand: 128-byte swizzle for bf16, the 32-byte-atom variant for tf32.
                 const uint64_t bdesc = F32 ? smem_desc(vb + kk * C::KSTEP * 128, C::KEYS * 128, 512, kLayoutSW128Base32B)
                                            : smem_desc(vb + kk * C::KSTEP * 128, C::KEYS * 128, 1024);
@@ -379,15 +386,16 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         if (warp == 2 && lane == 0) FWN_TR(20, c);
         tc_fence_after();
         tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
-        if (n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        if (C::CH == 2 && n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
         tmem_wait_ld();
         if (warp == 2 && lane == 0) FWN_TR(24, c);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty(sb));
         if (!(ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
+        if (warp == 2 && lane == 0) FWN_TR(25, c);
         const uint32_t w0 = ld_shared_u32(stage_bits(st) + row * 4);
-        const uint32_t w1 = n_in == 2 ? ld_shared_u32(stage_bits(st) + 512 + row * 4) : 0u;
+        const uint32_t w1 = (C::CH == 2 && n_in == 2) ? ld_shared_u32(stage_bits(st) + 512 + row * 4) : 0u;
         const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
         const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
         // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
@@ -497,11 +505,18 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           if (warp == 2 && lane == 0) FWN_TR(26, c);
           // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
           if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          if (warp == 2 && lane == 0) FWN_TR(29, c);
           const uint32_t pbase = p_smem(sb);
+          if constexpr (C::P64) {
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            if (cc < 4 * n_in)
-              st_shared_v4(pbase + sw128_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+            for (int cc = 0; cc < 4; ++cc)
+              st_shared_v4(pbase + sw64_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              if (cc < 4 * n_in)
+                st_shared_v4(pbase + sw128_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+            }
           }
         } else {
           float e[64];

@@ -201,6 +201,17 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 }
 
 // Arrive (once) on `bar` when every MMA this thread issued before has completed.
+// D (+)= A B with A read from tensor memory (M = 128 lanes, K along columns, two bf16 per 32-bit column)
+// and B from shared memory (kind::f16).
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -251,7 +262,7 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // atoms of 8 K-rows x 128 bytes of MN, stacked along K at SBO and along MN at LBO.
 // 32-bit MN-major operands (tf32) use SWIZZLE_128B_BASE32B: 32-byte chunks of a 128-byte row XOR
 // (row & 3), atoms of 4 K-rows (TMA: CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
-enum : uint32_t { kLayoutSW128 = 2, kLayoutSW128Base32B = 1 };
+enum : uint32_t { kLayoutSW128 = 2, kLayoutSW128Base32B = 1, kLayoutSW64 = 4 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
                                               uint32_t layout = kLayoutSW128) {
@@ -280,6 +291,12 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
   return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
 }
 
+// Byte offset of 16-byte chunk c (0..3) of row r in a K-major tile of 64-byte rows with the 64-byte
+// swizzle (8-row atoms of 512 bytes; chunk index XOR bits 1-2 of the row).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
+  return (r >> 3) * 512u + (r & 7u) * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -302,6 +319,68 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// Paired fp32 arithmetic (one instruction for two lanes of a 64-bit register pair).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair of x <= ~8 on the FMA pipe (relieves the MUFU unit, which computes the other exponentials):
+// x = j + f with j = round(x) (added to and subtracted from 1.5 * 2^23) and f in [-1/2, 1/2]; 2^f by a cubic
+// fitted here for least maximum relative error on [-1/2, 1/2] (Lawson's iteratively reweighted least
+// squares; max relative error 9.1e-5 in float32, far below bf16's 2^-9); then j is added to the exponent
+// field. x is clamped at -126 so that the result stays a positive (possibly subnormal) float.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.99992810936f, kC1 = 0.69326098561f, kC2 = 0.24261054228f, kC3 = 0.05517132143f;
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 f = fsub2(x, fsub2(t, make_float2(kRound, kRound)));
+  float2 q = ffma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  q = ffma2(q, f, make_float2(kC1, kC1));
+  q = ffma2(q, f, make_float2(kC0, kC0));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // 3xTF32 operand split of a shared-memory tile, byte position by byte position (so any swizzle is kept):
 // hi = x with the 13 low mantissa bits cleared (exact in tf32) in place, lo = x - hi (exact in fp32).
 __device__ __forceinline__ void split_tf32(uint32_t base, uint32_t lo_base, int bytes, int tid, int nthreads) {
@@ -317,6 +396,12 @@ __device__ __forceinline__ void split_tf32(uint32_t base, uint32_t lo_base, int 
   }
 }
 
+__device__ __forceinline__ float4 ld_shared_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");

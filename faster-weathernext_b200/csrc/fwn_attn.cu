@@ -13,6 +13,8 @@
 
 #include "attn_bwd.cuh"
 #include "attn_fwd.cuh"
+#include "attn_fwd_wide.cuh"
+#include "attn_bwd_wide.cuh"
 #include "tiles.cuh"
 
 namespace {
@@ -269,6 +271,53 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   return ok();
 }
 
+// Wide-chunk forward (bf16, 128-row tile lists): 32- and 128-row K / V boxes, one CTA per SM.
+template <int D>
+fwn_status launch_fwd_wide(const fwn_attn_desc& d, const void* q, const void* k, const void* v,
+                           const fwn_tile_list& t, void* o, float* lse, cudaStream_t stream) {
+  using C = fwn::WideCfg<D>;
+  CUtensorMap tq, tk, tv, tk4, tv4;
+  fwn_status s;
+  if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
+  if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&tv, v, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&tk4, k, d, C::KEYS)) != FWN_OK) return s;
+  if ((s = make_map(&tv4, v, d, C::KEYS)) != FWN_OK) return s;
+  fwn::FwdParams p{};
+  p.ptr2 = t.ptr;
+  p.kb2 = t.kb;
+  p.bits2 = t.bits;
+  p.o = o;
+  p.lse = lse;
+  p.o_sb = d.out_stride_b;
+  p.o_sn = d.out_stride_n;
+  p.o_sh = d.out_stride_h;
+  p.batch = d.batch;
+  p.heads = d.heads;
+  p.n = d.n;
+  p.np = t.n_blocks;
+  p.lse_rows = fwn_lse_rows(d.n);
+  p.n_items = d.batch * d.heads * t.n_blocks;
+  p.scale_log2 = d.scale * 1.4426950408889634f;
+#ifdef FWN_TRACE
+  p.trace = trace_buffer();
+#endif
+  auto kernel = fwn::attn_fwd_wide_kernel<D>;
+  int grid = 0;
+  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, tk4, tv4, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_wide launch");
+  return ok();
+}
+
+// Dense lists (on average at least 16 tiles of 32 keys per 128-row block) and head_dim 128 take the
+// wide-chunk forward in bf16 with 32-key tile lists.
+bool use_wide(const fwn_attn_desc& d, const fwn_tile_list& t) {
+  if (d.mode != FWN_MODE_BF16 || t.cols) return false;
+  return d.head_dim == 128 || static_cast<int64_t>(t.n_tiles) >= 16 * static_cast<int64_t>(t.n_blocks);
+}
+
 template <int KIND, int D, bool F32, int CH, bool GATHER, bool X3>
 fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
                            const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
@@ -334,6 +383,58 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   return FWN_OK;
 }
 
+// Wide-chunk backward pass (bf16, 128-row tile lists): rows 128-row boxes, columns 32- and 128-row boxes.
+template <int KIND, int D>
+fwn_status launch_bwd_wide(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* d_o,
+                           const float* lse, const float* delta, const fwn_tile_list& t, void* out0, void* out1,
+                           cudaStream_t stream) {
+  using C = fwn::BwdWideCfg<KIND, D>;
+  constexpr bool kKeys = KIND != fwn::kBwdDQ;
+  CUtensorMap r0, r1, c0, c1, c0w, c1w;
+  fwn_status s;
+  const void* rp0 = kKeys ? k : q;
+  const void* rp1 = kKeys ? v : d_o;
+  const void* cp0 = kKeys ? q : k;
+  const void* cp1 = kKeys ? d_o : v;
+  const bool r1_out = !kKeys, c1_out = kKeys;
+  if ((s = make_map(&r0, rp0, d, C::ROWS)) != FWN_OK) return s;
+  if ((s = make_map(&r1, rp1, d, C::ROWS, false, r1_out)) != FWN_OK) return s;
+  if ((s = make_map(&c0, cp0, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&c1, cp1, d, C::SUB, false, c1_out)) != FWN_OK) return s;
+  if ((s = make_map(&c0w, cp0, d, C::COLS)) != FWN_OK) return s;
+  if ((s = make_map(&c1w, cp1, d, C::COLS, false, c1_out)) != FWN_OK) return s;
+  fwn::BwdParams p{};
+  p.ptr2 = t.ptr;
+  p.kb2 = t.kb;
+  p.bits2 = t.bits;
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = out0;
+  p.out1 = out1;
+  p.o_sb = d.out_stride_b;
+  p.o_sn = d.out_stride_n;
+  p.o_sh = d.out_stride_h;
+  p.heads = d.heads;
+  p.n = d.n;
+  p.np = t.n_blocks;
+  p.lse_rows = fwn_lse_rows(d.n);
+  p.n_items = d.batch * d.heads * t.n_blocks;
+  p.scale = d.scale;
+  p.scale_log2 = d.scale * 1.4426950408889634f;
+#ifdef FWN_TRACE
+  p.trace = trace_buffer();
+#endif
+  auto kernel = fwn::attn_bwd_wide_kernel<KIND, D>;
+  int grid = 0;
+  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0w, c1w, p);
+  cudaError_t e = cudaGetLastError();
+  static const char* const kNames[] = {"attn_bwd_wide dq launch", "", "attn_bwd_wide dv launch",
+                                       "attn_bwd_wide dk launch"};
+  if (e != cudaSuccess) return cuda_fail(e, kNames[KIND]);
+  return FWN_OK;
+}
+
 // Gathered-mode layout for the column operands of one pass (-1: not gatherable).
 int pass_layout(const fwn_attn_desc& d, bool keys) {
   const int a = gather_layout(d, false);
@@ -374,15 +475,31 @@ template <int D, bool F32, bool X3 = false>
 fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
                       const float* lse, const void* d_o, const fwn_tile_list* t, const fwn_tile_list* tt, void* dq,
                       void* dk, void* dv, float* delta, int parts, cudaStream_t stream) {
-  constexpr int CH = F32 ? 1 : 2;
+  // 32-column chunks for tf32 and at head_dim 128 (two CTAs per SM in bf16), else 64.
+  constexpr int CH = (F32 || D == 128) ? 1 : 2;
+  // dV and dK as separate passes where one dK/dV pass does not fit: 3xTF32 (shared memory) and bf16 at
+  // head_dim 128 (dK and dV accumulators plus S and dP exceed the 256 TMEM columns of a CTA that shares
+  // its SM).
+  constexpr bool kSplit = X3 || (D == 128 && !F32);
   fwn_status s;
   if ((parts & kDelta) && (s = launch_delta<D, F32>(d, o, d_o, delta, stream)) != FWN_OK) return s;
+  if constexpr (!F32) {
+    // Dense lists and head_dim 128 (32-key tile lists): the wide-chunk passes.
+    if ((parts & kDq) && use_wide(d, *t)) {
+      if ((s = launch_bwd_wide<fwn::kBwdDQ, D>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK) return s;
+      parts &= ~kDq;
+    }
+    if ((parts & kDkv) && use_wide(d, *tt)) {
+      if ((s = launch_bwd_wide<fwn::kBwdDV, D>(d, q, k, v, d_o, lse, delta, *tt, nullptr, dv, stream)) != FWN_OK) return s;
+      if ((s = launch_bwd_wide<fwn::kBwdDK, D>(d, q, k, v, d_o, lse, delta, *tt, dk, nullptr, stream)) != FWN_OK) return s;
+      parts &= ~kDkv;
+    }
+  }
   if ((parts & kDq) &&
       (s = launch_bwd_pass_any<fwn::kBwdDQ, D, F32, CH, X3>(d, q, k, v, d_o, lse, delta, *t, dq, nullptr, stream)) != FWN_OK)
     return s;
   if (parts & kDkv) {
-    if constexpr (X3) {
-      // 3xTF32: the hi / lo copies of both passes' operands do not fit one CTA; dV and dK run separately.
+    if constexpr (kSplit) {
       if ((s = launch_bwd_pass_any<fwn::kBwdDV, D, F32, CH, X3>(d, q, k, v, d_o, lse, delta, *tt, nullptr, dv, stream)) !=
           FWN_OK)
         return s;
@@ -581,6 +698,9 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
     if (layout < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "gathered lists need a node-major or head-major packed layout");
   }
   const bool g = tiles->cols != nullptr;
+  if (use_wide(d, *tiles))
+    return d.head_dim == 64 ? launch_fwd_wide<64>(d, q, k, v, *tiles, o, lse, st)
+                            : launch_fwd_wide<128>(d, q, k, v, *tiles, o, lse, st);
   if (d.mode == FWN_MODE_BF16) {
     if (d.head_dim == 64)
       return g ? launch_fwd<64, false, true>(d, q, k, v, *tiles, o, lse, layout, st)

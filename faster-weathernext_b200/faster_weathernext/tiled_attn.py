@@ -312,7 +312,12 @@ def _gather_layout(t: torch.Tensor) -> int:
 
 
 def _lists(tiles: "AttentionTiles", q: torch.Tensor, o: torch.Tensor):
-  """(forward list, transposed list): gathered when the layouts allow gathered row loads."""
+  """(forward list, transposed list): gathered when the layouts allow gathered row loads and the mask is
+  sparse; the 32-key tile lists for dense masks (at least 16 tiles per 128-row block on average, where
+  gathering saves few tiles and the wide-chunk forward applies) and for bf16 at head_dim 128."""
+  dense = tiles.fwd.n_tiles >= 16 * tiles.fwd.n_blocks
+  if dense or (q.shape[-1] == 128 and q.dtype == torch.bfloat16):
+    return tiles.fwd, tiles.bwd
   if tiles.fwd_g is not None:
     a, c = _gather_layout(q), _gather_layout(o)
     if a >= 0 and a == c:

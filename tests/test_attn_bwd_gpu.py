@@ -175,3 +175,29 @@ def test_grads_tf32x3_configs(cuda, cfg):
   ref = oa.sparse_attention_vjp(q, k, v, do, m, d ** -0.5)
   for name, a, r in zip(("dq", "dk", "dv"), got, ref):
     assert oa.rel_rms(a, r) < TOL["tf32x3"], (name, oa.rel_rms(a, r))
+
+
+def _khop_mask(level, hops):
+  from faster_weathernext import mesh
+  xyz, faces = mesh.icosphere(level)
+  lat, lon = mesh.latlon(xyz)
+  adj = mesh.permute(mesh.adjacency(faces, xyz.shape[0]), mesh.morton_order(lat, lon))
+  return mesh.k_hop_mask(adj, hops)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("mask_kind", ["khop", "random_nonsym"])
+def test_grads_dense_masks_wide_passes(cuda, head_dim, mask_kind):
+  """Dense masks (> 16 tiles per 128-row block): the wide-chunk dQ / dV / dK passes, batch 2, H 3, ragged n."""
+  if mask_kind == "khop":
+    m = _khop_mask(4, 6)
+  else:
+    n = 700
+    m = sparse.random(n, n, density=0.3, random_state=5, format="csr").astype(bool)
+    m = (m + sparse.identity(n, dtype=bool)).tocsr()
+  n = m.shape[0]
+  q, k, v, do = kernel_inputs(31, (2, n, 3, head_dim), 4)
+  got = _grads(q, k, v, do, m, head_dim ** -0.5, "bf16", cuda, gather=False)
+  ref = oa.sparse_attention_vjp(*_rounded("bf16", (q, k, v, do)), m, head_dim ** -0.5)
+  for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+    assert oa.rel_rms(a, r) < TOL["bf16"], (name, oa.rel_rms(a, r))

@@ -173,3 +173,58 @@ def test_forward_tf32x3_configs(cuda, cfg):
   out, _ = _run(q, k, v, m, d ** -0.5, "tf32x3", cuda)
   ref, _ = oa.sparse_attention(q, k, v, m, d ** -0.5)
   assert oa.rel_rms(out, ref) < TOL["tf32x3"]
+
+
+def _khop_mask(level, hops):
+  from faster_weathernext import mesh
+  xyz, faces = mesh.icosphere(level)
+  lat, lon = mesh.latlon(xyz)
+  adj = mesh.permute(mesh.adjacency(faces, xyz.shape[0]), mesh.morton_order(lat, lon))
+  return mesh.k_hop_mask(adj, hops)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("kernel", ["wide", "narrow"])
+def test_forward_dense_mask_both_kernels(cuda, head_dim, kernel):
+  """Dense neighbourhood mask (level-4 mesh, 6 hops: ~127 keys per query, > 16 tiles per block): the
+  wide-chunk kernel (32-key tile lists) and the narrow kernel (gathered lists through the C ABI)."""
+  import ctypes
+  from faster_weathernext import _lib
+  from faster_weathernext import tiled_attn as ta
+  m = _khop_mask(4, 6)
+  n = m.shape[0]
+  q, k, v = kernel_inputs(21, (2, n, 3, head_dim), 3)
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda, gather=True)
+  assert tiles.fwd.n_tiles >= 16 * tiles.fwd.n_blocks
+  tq, tk, tv = (torch.from_numpy(x).to(device=cuda, dtype=torch.bfloat16) for x in (q, k, v))
+  lib = _lib.lib()
+  o = torch.empty_like(tq)
+  lse = torch.empty(2, 3, lib.fwn_lse_rows(n), device=cuda)
+  desc = ta._desc(tq, o, head_dim ** -0.5, _lib.MODE_BF16)
+  st = (tiles.fwd if kernel == "wide" else tiles.fwd_g).struct()
+  _lib.check(lib.fwn_attn_fwd(ctypes.byref(desc), tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), ctypes.byref(st),
+                              o.data_ptr(), lse.data_ptr(), 0))
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  ref, ref_lse = oa.sparse_attention(*_inputs_for("bf16", (q, k, v)), m, head_dim ** -0.5)
+  assert oa.rel_rms(o.float().cpu().numpy(), ref) < TOL["bf16"]
+  np.testing.assert_allclose(lse.cpu().numpy()[:, :, :n], ref_lse, rtol=0, atol=2e-2)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_forward_dense_growing_logits_rescale(cuda, head_dim):
+  """Logits that grow along the key order by several powers of two per chunk: the one-pass softmax must
+  fall back to the exact two-pass update and rescale O in TMEM (wide kernel)."""
+  m = _khop_mask(4, 6)
+  n = m.shape[0]
+  rng = np.random.default_rng(3)
+  u = rng.standard_normal(head_dim).astype(np.float32)
+  u /= np.linalg.norm(u)
+  ramp = (np.arange(n, dtype=np.float32) / n * 4000.0)[:, None]
+  q = np.broadcast_to(u * 3.0, (1, n, 2, head_dim)).copy() + 0.05 * rng.standard_normal((1, n, 2, head_dim)).astype(np.float32)
+  k = (ramp * u)[None, :, None, :].repeat(2, axis=2) * head_dim ** 0.5 / 3.0 / 40.0
+  v = rng.standard_normal((1, n, 2, head_dim)).astype(np.float32)
+  out, lse = _run(q, k.astype(np.float32), v, m, head_dim ** -0.5, "bf16", cuda, gather=False)
+  ref, ref_lse = oa.sparse_attention(*_inputs_for("bf16", (q, k.astype(np.float32), v)), m, head_dim ** -0.5)
+  assert oa.rel_rms(out, ref) < TOL["bf16"]
+  np.testing.assert_allclose(lse[:, :, :n], ref_lse, rtol=2e-3, atol=5e-2)
