@@ -236,6 +236,13 @@ class AttentionTiles:
     self.symmetric = symmetric
     self.fwd_g = gather_tiles(fwd) if gather else None
     self.bwd_g = (self.fwd_g if bwd is fwd else gather_tiles(bwd)) if gather else None
+    # Dense: gathering the distinct keys of each block would save under a quarter of the tiles (the
+    # neighbourhoods fill their 32-key tiles), or, without gathered lists, 16+ tiles per 128-row block. Dense
+    # masks run the wide-chunk kernels on the 32-key tile lists.
+    if self.fwd_g is not None:
+      self.dense = 4 * fwd.n_tiles < 5 * max(self.fwd_g.n_tiles, 1)
+    else:
+      self.dense = fwd.n_tiles >= 16 * fwd.n_blocks
 
   @classmethod
   def from_mask(cls, mask, device=None, gather: bool = True) -> "AttentionTiles":
@@ -313,10 +320,9 @@ def _gather_layout(t: torch.Tensor) -> int:
 
 def _lists(tiles: "AttentionTiles", q: torch.Tensor, o: torch.Tensor):
   """(forward list, transposed list): gathered when the layouts allow gathered row loads and the mask is
-  sparse; the 32-key tile lists for dense masks (at least 16 tiles per 128-row block on average, where
-  gathering saves few tiles and the wide-chunk forward applies) and for bf16 at head_dim 128."""
-  dense = tiles.fwd.n_tiles >= 16 * tiles.fwd.n_blocks
-  if dense or (q.shape[-1] == 128 and q.dtype == torch.bfloat16):
+  sparse; the 32-key tile lists for dense masks (where gathering saves few tiles and the wide-chunk kernels
+  apply) and for bf16 at head_dim 128."""
+  if tiles.dense or (q.shape[-1] == 128 and q.dtype == torch.bfloat16):
     return tiles.fwd, tiles.bwd
   if tiles.fwd_g is not None:
     a, c = _gather_layout(q), _gather_layout(o)
