@@ -76,7 +76,9 @@ struct BwdCfg {
   static constexpr int SLOT_C0MN = 1 + (LOAD_C1 ? 1 : 0);
   static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
   static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
-  static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1) : 2;
+  // One stage where the hi / lo (3xTF32) or fp32 head_dim-128 operands leave room for no second one.
+  static constexpr bool BIG = X3 || (F32 && D == 128);
+  static constexpr int NS = BIG ? (KIND == kBwdDV ? 2 : 1) : 2;
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
   static constexpr bool G64 = COLS * ES == 64;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
@@ -89,7 +91,7 @@ struct BwdCfg {
   static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
   // dS / P buffers: one where two would not leave room for a second CTA per SM (bf16 dK/dV at head_dim 64,
   // bf16 dQ / dK only at head_dim 128) or would not fit at all (3xTF32 except dV only); else two.
-  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (D == 128 && !F32 && KIND != kBwdDV) ||
+  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (D == 128 && KIND != kBwdDV) ||
                              (X3 && KIND != kBwdDV)) ? 1 : 2;
   static constexpr int OFF_C = NR * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
@@ -103,6 +105,7 @@ struct BwdCfg {
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
+  static_assert(!(F32 && D == 128) || KIND != kBwdDKV, "tf32 head_dim 128: dV and dK run as separate passes");
   // Each SM sub-partition has 16,384 registers and takes a quarter of the resident warps (rounded up):
   // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
   static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 255;

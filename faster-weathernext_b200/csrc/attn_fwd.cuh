@@ -54,9 +54,9 @@ struct FwdCfg {
   static constexpr int CB = D / EPB;          // column blocks of a head_dim row
   static constexpr int ROWS = 128;            // query rows per item
   static constexpr int SUB = 32;              // keys per tile
-  // Tiles per chunk: one at head_dim 128 in bf16 (keeps two CTAs per SM, so that one CTA's softmax overlaps
-  // the other's MMAs), and in 3xTF32; else two.
-  static constexpr int CH = (X3 || (D == 128 && !F32)) ? 1 : 2;
+  // Tiles per chunk: one at head_dim 128 (bf16: keeps two CTAs per SM, so that one CTA's softmax overlaps
+  // the other's MMAs; tf32: the operands' size) and in 3xTF32; else two.
+  static constexpr int CH = (X3 || D == 128) ? 1 : 2;
   static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
   static constexpr int NS = X3 ? 2 : 3;       // K/V pipeline stages

@@ -477,10 +477,10 @@ fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, cons
                       void* dk, void* dv, float* delta, int parts, cudaStream_t stream) {
   // 32-column chunks for tf32 and at head_dim 128 (two CTAs per SM in bf16), else 64.
   constexpr int CH = (F32 || D == 128) ? 1 : 2;
-  // dV and dK as separate passes where one dK/dV pass does not fit: 3xTF32 (shared memory) and bf16 at
-  // head_dim 128 (dK and dV accumulators plus S and dP exceed the 256 TMEM columns of a CTA that shares
-  // its SM).
-  constexpr bool kSplit = X3 || (D == 128 && !F32);
+  // dV and dK as separate passes where one dK/dV pass does not fit: 3xTF32 and tf32 at head_dim 128 (shared
+  // memory), bf16 at head_dim 128 (dK and dV accumulators plus S and dP exceed the 256 TMEM columns of a CTA
+  // that shares its SM).
+  constexpr bool kSplit = X3 || D == 128;
   fwn_status s;
   if ((parts & kDelta) && (s = launch_delta<D, F32>(d, o, d_o, delta, stream)) != FWN_OK) return s;
   if constexpr (!F32) {
@@ -711,6 +711,9 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
   if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
     return g ? launch_fwd<64, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
              : launch_fwd<64, true, false>(d, q, k, v, *tiles, o, lse, layout, st);
+  if (d.mode == FWN_MODE_TF32)
+    return g ? launch_fwd<128, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
+             : launch_fwd<128, true, false>(d, q, k, v, *tiles, o, lse, layout, st);
   if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
     return g ? launch_fwd<64, true, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
              : launch_fwd<64, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
@@ -807,6 +810,8 @@ fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k,
   }
   if (d.mode == FWN_MODE_TF32 && d.head_dim == 64)
     return launch_bwd<64, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
+  if (d.mode == FWN_MODE_TF32)
+    return launch_bwd<128, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
   if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
     return launch_bwd<64, true, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
   return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);

@@ -201,3 +201,43 @@ def test_grads_dense_masks_wide_passes(cuda, head_dim, mask_kind):
   ref = oa.sparse_attention_vjp(*_rounded("bf16", (q, k, v, do)), m, head_dim ** -0.5)
   for name, a, r in zip(("dq", "dk", "dv"), got, ref):
     assert oa.rel_rms(a, r) < TOL["bf16"], (name, oa.rel_rms(a, r))
+
+
+@pytest.mark.parametrize("mask_kind", ["ref_sym", "ref_nonsym", "khop"])
+def test_tf32_head_dim_128(golden, cuda, mask_kind):
+  """TF32 at head_dim 128 (the WeatherNext 2 head size in the reference's default precision): forward and
+  gradients within 5e-3 rel RMS and the reference test's max-abs bounds (2e-2 output, 3e-2 gradients)."""
+  from faster_weathernext import _lib
+  from faster_weathernext import tiled_attn as ta
+  if mask_kind == "khop":
+    m = _khop_mask(4, 6)
+  else:
+    m = golden_mask(golden["tiles"], "k_sym" if mask_kind == "ref_sym" else "k_nonsym")
+  n = m.shape[0]
+  q, k, v, do = kernel_inputs(41, (2, n, 2, 128), 4)
+  scale = 128 ** -0.5
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  tq, tk, tv, tdo = (torch.from_numpy(x).to(cuda) for x in (q, k, v, do))
+  o, lse = ta.attention_forward(tq, tk, tv, tiles, scale, _lib.MODE_TF32, with_lse=True)
+  dq, dk, dv = ta.attention_backward(tq, tk, tv, o, lse, tdo, tiles, scale, _lib.MODE_TF32)
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  ref_o, _ = oa.sparse_attention(q, k, v, m, scale)
+  assert oa.rel_rms(o.cpu().numpy(), ref_o) < TOL["tf32"]
+  assert oa.max_rel(o.cpu().numpy(), ref_o) < 2e-2
+  ref = oa.sparse_attention_vjp(q, k, v, do, m, scale)
+  for name, a, r in zip(("dq", "dk", "dv"), (dq, dk, dv), ref):
+    a = a.cpu().numpy()
+    assert oa.rel_rms(a, r) < TOL["tf32"], (name, oa.rel_rms(a, r))
+    assert oa.max_rel(a, r) < 3e-2, (name, oa.max_rel(a, r))
+
+
+def test_tf32x3_head_dim_128_is_refused(cuda):
+  """3xTF32 at head_dim 128 is not built: a clean NotImplementedError, nothing launched."""
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext import mesh
+  m, _, _ = mesh.config_mask(1)
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  q = torch.randn(1, 642, 2, 128, device=cuda)
+  with pytest.raises(NotImplementedError):
+    ta.attention(q, q, q, tiles, scale=0.1, precision="highest")
