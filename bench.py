@@ -476,15 +476,23 @@ def run_model_workload(args):
     dist.destroy_process_group()
 
 
+def _all_host_threads():
+  """Raise the BLAS / OpenMP pools to every host core (torchrun sets OMP_NUM_THREADS=1 for its ranks) and
+  return the thread count now in use."""
+  n = os.cpu_count() or 1
+  try:
+    from threadpoolctl import threadpool_info, threadpool_limits
+    threadpool_limits(limits=n)
+    return max([p.get("num_threads", 1) for p in threadpool_info()] or [n])
+  except Exception:
+    return n
+
+
 def cpu_baseline(mask, heads, head_dim, seconds=15.0, steps=None, name="attention"):
   """The reference's CPU path (XLA chunked attention fwd + autodiff bwd, float32, NumPy/BLAS on all
   host cores) timed on a bounded sample of query chunks; returned in useful TFLOP/s."""
   from oracle import attention as oa
-  try:
-    from threadpoolctl import threadpool_info
-    cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count()])
-  except Exception:
-    cores = os.cpu_count()
+  cores = _all_host_threads()
   n = mask.shape[0]
   rng = np.random.default_rng(0)
   q, k, v, do = (rng.standard_normal((1, n, heads, head_dim)).astype(np.float32) for _ in range(4))
@@ -518,6 +526,7 @@ def run_reference(args):
     return
   from faster_weathernext import mesh
   from oracle import attention as oa
+  cores = _all_host_threads()
   mask, _, _ = mesh.config_mask(CFG)
   _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
   n = mask.shape[0]
@@ -550,11 +559,6 @@ def run_reference(args):
   flops = sum(step(args.warmup + i) for i in range(args.steps))
   el = time.perf_counter() - t0
   value = flops / el / 1e12
-  try:
-    from threadpoolctl import threadpool_info
-    cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count()])
-  except Exception:
-    cores = os.cpu_count()
   sample = (f"per step {rows} query rows of one of the {path.n_chunks} query chunks (key window {path.window}) "
             "of cfg3, fwd + autodiff bwd, float32 NumPy/BLAS restatement of the XLA path (JAX absent)")
   print(json.dumps({
