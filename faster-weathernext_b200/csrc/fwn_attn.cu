@@ -646,6 +646,23 @@ fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32
   return ok();
 }
 
+fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                              const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
+  if (rows < 0 || rows_per_sample <= 0 || !(eps > 0.f))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld, rows_per_sample=%d or eps", static_cast<long long>(rows),
+                rows_per_sample);
+  if (d != 128 && d != 256 && d != 512 && d != 1024) return fail(FWN_ERR_UNSUPPORTED, "d=%d not built", d);
+  if (out_dtype != FWN_DTYPE_BF16 && out_dtype != FWN_DTYPE_F32)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown out dtype %d", out_dtype);
+  if (rows > 0 && (!x || !scale_offset || !out)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rows > 0 && (!aligned16(x) || !aligned16(scale_offset) || !aligned16(out)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  cudaError_t e = fwn::launch_cond_layernorm(x, rows, d, rows_per_sample, scale_offset, eps, out,
+                                             out_dtype == FWN_DTYPE_BF16, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cond_layernorm");
+  return ok();
+}
+
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }
 
 fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops, uint32_t* reach,

@@ -9,9 +9,11 @@ with LayerNorm without scale / offset, a norm conditioning (per-sample scale and
 conditioning vector, as the official LinearNormConditioning), a final LN + conditioning (patch.py:288-290),
 q/k/v/out projections and a GELU MLP. The official modules (`weathernext.utils.sparse_transformer`,
 `dense.LinearNormConditioning`) are third-party and not available here, so this is a synthetic processor of
-the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU; Glorot-uniform weights from a
-seed), not a numerical copy of the official one. The projections run as cuBLAS GEMMs; the attention is
-faster_weathernext's kernel (q, k, v are strided views of one fused projection, no copies).
+the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU in the tanh form that is
+jax.nn.gelu's default; Glorot-uniform weights from a seed), not a numerical copy of the official one. The
+projections run as cuBLAS GEMMs; the attention is faster_weathernext's kernel (q, k, v are strided views of one
+fused projection, no copies). Without autograd (inference), each norm is one fused kernel and bias + GELU run
+in the GEMM epilogue.
 """
 
 import dataclasses
@@ -20,6 +22,7 @@ import math
 import torch
 import torch.nn.functional as F
 
+from faster_weathernext import _lib
 from faster_weathernext import tiled_attn
 
 
@@ -79,6 +82,8 @@ class Processor(torch.nn.Module):
   def forward(self, x: torch.Tensor, cond: torch.Tensor, tiles: "tiled_attn.AttentionTiles",
               dtype=torch.bfloat16) -> torch.Tensor:
     """x [B, n, d_model] (float32 residual stream), cond [B, cond_dim] -> [B, n, d_model]."""
+    if not torch.is_grad_enabled() and dtype == torch.bfloat16 and x.shape[-1] in (128, 256, 512, 1024):
+      return self._forward_fused(x, cond, tiles)
     cfg = self.cfg
     b, n, d = x.shape
     scale = cfg.head_dim ** -0.5
@@ -90,9 +95,42 @@ class Processor(torch.nn.Module):
       o = self._attend(q, k, v, tiles, scale)
       x = x + (o.reshape(b, n, cfg.heads * cfg.head_dim) @ blk.w_out.to(dtype)).to(x.dtype)
       h = self._cond_norm(x, c, blk.cond2).to(dtype)
-      m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype))
+      m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype), approximate="tanh")
       x = x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
     return self._cond_norm(x, c, self.cond_final).to(x.dtype)
+
+  def _forward_fused(self, x, cond, tiles):
+    """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm
+    (fwn_cond_layernorm), bias and GELU in the GEMM epilogue (cuBLASLt), and the residual stream updated in
+    place (float32 += bf16 in one pass)."""
+    cfg = self.cfg
+    b, n, d = x.shape
+    m_rows = b * n
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    bf = torch.bfloat16
+    scale = cfg.head_dim ** -0.5
+    xs = x.contiguous().clone()
+    x2 = xs.view(m_rows, d)
+    h = torch.empty(m_rows, d, dtype=bf, device=x.device)
+    cf = cond.float()
+
+    def norm(w, out, out_dtype):
+      so = (cf @ w.float()).contiguous()                    # [B, 2d]: per-sample scale, offset
+      _lib.check(lib.fwn_cond_layernorm(x2.data_ptr(), m_rows, d, n, so.data_ptr(), 1e-5, out.data_ptr(),
+                                        out_dtype, stream))
+
+    for blk in self.blocks:
+      norm(blk.cond1, h, _lib.DTYPE_BF16)
+      qkv = (h @ blk.w_qkv.to(bf)).view(b, n, cfg.heads, 3, cfg.head_dim)
+      o = self._attend(qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2], tiles, scale)
+      x2.add_(o.reshape(m_rows, cfg.heads * cfg.head_dim) @ blk.w_out.to(bf))
+      norm(blk.cond2, h, _lib.DTYPE_BF16)
+      mlp = torch._addmm_activation(blk.b1.to(bf), h, blk.w1.to(bf), use_gelu=True)
+      x2.add_(torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf)))
+    out = torch.empty_like(xs)
+    norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32)
+    return out
 
   def gemm_flops_per_forward(self, n: int) -> float:
     """Projection + MLP GEMM FLOPs of one member's forward (2 n (4 d^2 + 2 d m) per block)."""

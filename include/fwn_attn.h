@@ -169,6 +169,17 @@ FWN_API fwn_status fwn_bitset_csr_count(const uint32_t* bits, int32_t n_rows, in
 FWN_API fwn_status fwn_bitset_csr_fill(const uint32_t* bits, int32_t n_rows, int32_t n_cols, const int32_t* indptr,
                                        int32_t* indices, void* stream);
 
+/* ---- the processor around the attention ---------------------------------------------------------------- */
+
+/* Conditioned LayerNorm of the pre-LN blocks (src/faster_weathernext/patch.py:238-252, 288-290: LayerNorm without
+ * scale / offset, then the norm conditioning's per-sample scale and offset):
+ *   out[r, :] = (x[r, :] - mean) / sqrt(var + eps) * (1 + scale_offset[s, :d]) + scale_offset[s, d:],
+ *   s = r / rows_per_sample. x float32 [rows, d] contiguous, d in {128, 256, 512, 1024}; scale_offset float32
+ *   [rows / rows_per_sample, 2 d]; out [rows, d] in `out_dtype` (FWN_DTYPE_BF16 or FWN_DTYPE_F32). */
+FWN_API fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                      const float* scale_offset, float eps, void* out, int32_t out_dtype,
+                                      void* stream);
+
 /* ---- attention --------------------------------------------------------------------------------------- */
 
 /* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)

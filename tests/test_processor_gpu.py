@@ -72,3 +72,41 @@ def test_finetune_step_runs_and_lowers_the_loss(cuda):
   ts = [torch.randn(1, n, cfg.d_model, device=cuda, generator=g) for _ in range(2)]
   losses = [float(step.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles))) for _ in range(4)]
   assert all(np.isfinite(losses)) and losses[-1] < losses[0]
+
+
+def test_processor_fused_inference_matches_autograd_path(cuda):
+  """The inference path (fused conditioned LayerNorm kernel, GEMM-epilogue bias + GELU, in-place residual) gives
+  the autograd path's output within bf16 rounding (rel RMS <= 1e-2), at the configurations' width."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor, ProcessorConfig
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = ProcessorConfig(layers=3)
+  model = Processor(cfg, seed=4, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(6)
+  x = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(2, cfg.cond_dim, device=cuda, generator=g)
+  y_grad = model(x, c, tiles)
+  with torch.no_grad():
+    y_fused = model(x, c, tiles)
+  assert _rel(y_fused, y_grad.detach()) < 1e-2
+
+
+def test_cond_layernorm_kernel_matches_torch(cuda):
+  """fwn_cond_layernorm against torch: LayerNorm (eps 1e-5) * (1 + scale) + offset per sample, bf16 and fp32."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  g = torch.Generator(device=cuda).manual_seed(0)
+  for d in (128, 512, 1024):
+    b, n = 3, 257
+    x = torch.randn(b * n, d, device=cuda, generator=g) * 3 + 1
+    so = torch.randn(b, 2 * d, device=cuda, generator=g) * 0.2
+    ref = torch.nn.functional.layer_norm(x.view(b, n, d), (d,))
+    ref = (ref * (1 + so[:, None, :d]) + so[:, None, d:]).view(b * n, d)
+    for dt, tol in ((_lib.DTYPE_F32, 1e-5), (_lib.DTYPE_BF16, 1e-2)):
+      out = torch.empty(b * n, d, device=cuda, dtype=torch.float32 if dt == _lib.DTYPE_F32 else torch.bfloat16)
+      _lib.check(lib.fwn_cond_layernorm(x.data_ptr(), b * n, d, n, so.data_ptr(), 1e-5, out.data_ptr(), dt, 0))
+      torch.cuda.synchronize()
+      assert float((out.float() - ref).abs().max() / ref.abs().max()) < tol, (d, dt)
