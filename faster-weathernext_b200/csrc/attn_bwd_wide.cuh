@@ -19,11 +19,12 @@
 // three slots, one read only by S / dP in a ring of two. Rows are keys for dV / dK: their columns' lse and
 // delta come with the chunk (a ring of vectors); for dQ they are per thread.
 //
-// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM allocation and single-thread MMA issue (S and dP
-// of chunk c+1 ahead of the accumulating MMA of chunk c); warps 2-9 elementwise, warps w and w+4 sharing
-// TMEM lane quadrant w % 4 (thread = row) and taking columns 0-63 / 64-127 of each chunk; the mask words
-// are read from global memory one chunk ahead. Epilogue: each warp stores half of the accumulator
-// columns. Every mbarrier wait is bounded (common.cuh).
+// Roles (576 threads): warp 0 TMA producer; warp 1 TMEM allocation and MMA issue (the warp runs the loop
+// with warp-uniform descriptors, one elected lane issues; S and dP of chunk c+1 ahead of the accumulating MMA
+// of chunk c); warps 2-17 elementwise, four per TMEM lane
+// quadrant (thread = row), one 32-column tile of each chunk each; the mask words are read from global
+// memory one chunk ahead. Epilogue: each warp stores a quarter of the accumulator columns. Every mbarrier
+// wait is bounded (common.cuh).
 #pragma once
 
 #include <cuda.h>
@@ -65,13 +66,17 @@ struct BwdWideCfg {
   static constexpr int ACC_COL = DP_COL + (NEED_DP ? 128 : 0);
   static constexpr int G_COL = ACC_COL + D;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int THREADS = 320;
+  // Elementwise warps: four per TMEM lane quadrant, one 32-column tile of the chunk each (18 warps: at most
+  // 102 registers per thread, as each sub-partition holds 16,384 and takes five warps).
+  static constexpr int EW = 16;
+  static constexpr int THREADS = 64 + 32 * EW;
+  static constexpr int MAX_REGS = 96;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(G_COL + 128 <= TMEM_COLS, "TMEM budget");
 };
 
 template <int KIND, int D>
-__global__ void __maxnreg__(168)
+__global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
     attn_bwd_wide_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
                          const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
                          const __grid_constant__ CUtensorMap tm_c0w, const __grid_constant__ CUtensorMap tm_c1w,
@@ -127,18 +132,18 @@ __global__ void __maxnreg__(168)
     }
     for (int s = 0; s < C::NVEC; ++s) {
       mbar_init(v_full(s), 1);
-      mbar_init(v_empty(s), 8);
+      mbar_init(v_empty(s), C::EW);
     }
     for (int b = 0; b < C::NSB; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), 8);
+      mbar_init(s_empty(b), C::EW);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(g_full(b), 8);
+      mbar_init(g_full(b), C::EW);
       mbar_init(g_empty(b), 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 8);
+    mbar_init(acc_empty, C::EW);
     mbar_init(drain, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -263,81 +268,89 @@ __global__ void __maxnreg__(168)
       if (pending_r) mbar_wait(r_full, qc & 1, &never);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdescAcc = instr_desc(false, 128, D, false, true);
-      uint32_t g = 0, qc = 0;
-      bool ok = true;
-      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-        const int nch = (n_sub + C::CH - 1) / C::CH;
-        if (nch == 0) continue;
-        if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
-        const uint32_t g0 = g;
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch) {
-            const uint32_t gg = g0 + c;
-            const int sb = gg % C::NSB;
-            const int n_in = min(C::CH, n_sub - C::CH * c);
-            if (!(ok = mbar_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
-            if (C::NEED_DP && !(ok = mbar_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
-            if (!(ok = mbar_wait(s_empty(sb), ((gg / C::NSB) & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
-            const uint32_t c0t = c0_slot(gg % C::N0);
+    // ------------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
+    constexpr uint32_t kIdescAcc = instr_desc(false, 128, D, false, true);
+    const uint64_t r0desc = smem_desc(r_op(0), 16, 1024), r1desc = smem_desc(r_op(1), 16, 1024);
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + C::CH - 1) / C::CH;
+      if (nch == 0) continue;
+      if (!(ok = warp_wait(r_full, qc & 1, abort_flag))) break;
+      const uint32_t g0 = g;
+      for (int c = 0; c <= nch && ok; ++c) {
+        if (c < nch) {
+          const uint32_t gg = g0 + c;
+          const int sb = gg % C::NSB;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!(ok = warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
+          if (C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(s_empty(sb), ((gg / C::NSB) & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
+          const uint64_t c0desc = smem_desc(c0_slot(gg % C::N0), 16, 1024);
+          const uint64_t c1desc = smem_desc(c1_slot(gg % C::N1), 16, 1024);
+          if (elect_one_sync()) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<false>(tmem + 128 * sb, smem_desc(r_op(0) + cb * C::ROWS * 128 + within, 16, 1024),
-                            smem_desc(c0t + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+              mma_ss<false>(tmem + 128 * sb, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
+                            c0desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
             }
             if constexpr (C::NEED_DP) {
-              const uint32_t c1t = c1_slot(gg % C::N1);
 #pragma unroll
               for (int kk = 0; kk < D / 16; ++kk) {
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                mma_ss<false>(tmem + C::DP_COL, smem_desc(r_op(1) + cb * C::ROWS * 128 + within, 16, 1024),
-                              smem_desc(c1t + cb * C::COLS * 128 + within, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
+                              c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
               }
               mma_commit(c1_empty(gg % C::N1));  // C1 is read only by dP here
             } else {
               mma_commit(c0_empty(gg % C::N0));  // dV only: C0 (Q) is read only by S
             }
             mma_commit(s_full(sb));
-            FWN_TR(11, c);
             if (c == nch - 1) mma_commit(r_empty);
           }
-          if (c >= 1) {
-            const uint32_t gg = g0 + c - 1;
-            const int gb = gg & 1;
-            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-            if (!(ok = mbar_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
-            if (!C::NEED_DP && !(ok = mbar_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
-            if (c == 1 && !(ok = mbar_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t bt = C::ACC_ON_C0 ? c0_slot(gg % C::N0) : c1_slot(gg % C::N1);
-            const int ksteps = 2 * n_in;
+          __syncwarp();
+          if (lane == 0) FWN_TR(11, c);
+        }
+        if (c >= 1) {
+          const uint32_t gg = g0 + c - 1;
+          const int gb = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+          if (!(ok = warp_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
+          if (!C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+          if (c == 1 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint64_t bdesc = smem_desc(C::ACC_ON_C0 ? c0_slot(gg % C::N0) : c1_slot(gg % C::N1), C::COLS * 128, 1024);
+          const uint32_t gcol = tmem + C::G_COL + 64 * gb;
+          const int ksteps = 2 * n_in;
+          if (elect_one_sync()) {
             for (int kk = 0; kk < ksteps; ++kk)
-              mma_ts(tmem + C::ACC_COL, tmem + C::G_COL + 64 * gb + 8 * kk,
-                     smem_desc(bt + kk * 16 * 128, C::COLS * 128, 1024), kIdescAcc, (c == 1 && kk == 0) ? 0u : 1u);
+              mma_ts(tmem + C::ACC_COL, gcol + 8 * kk, bdesc + ((kk * 16 * 128) >> 4), kIdescAcc,
+                     (c == 1 && kk == 0) ? 0u : 1u);
             mma_commit(g_empty(gb));
             if (C::ACC_ON_C0) mma_commit(c0_empty(gg % C::N0));
             else mma_commit(c1_empty(gg % C::N1));
-            FWN_TR(12, c - 1);
             if (c == nch) mma_commit(acc_full);
           }
+          __syncwarp();
+          if (lane == 0) FWN_TR(12, c - 1);
         }
-        g = g0 + nch;
-        ++qc;
       }
-      mma_commit(drain);
-      volatile int never = 0;
-      mbar_wait(drain, 0, &never);
+      g = g0 + nch;
+      ++qc;
     }
+    if (elect_one_sync()) mma_commit(drain);
+    __syncwarp();
+    volatile int never = 0;
+    mbar_wait(drain, 0, &never);
   } else {
-    // ------------------------------------------------------------------ elementwise + epilogue (warps 2-9)
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    // ------------------------------------------------------------------ elementwise + epilogue (warps 2-17)
+    // Warp w: TMEM lane quadrant w % 4 (thread = row), tile j = (w - 2) / 4 of each chunk (32 columns).
+    const int quarter = warp & 3, j = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     constexpr float kLog2e = 1.4426950408889634f;
@@ -354,97 +367,87 @@ __global__ void __maxnreg__(168)
         nl2_row = -p.lse[static_cast<size_t>(bh) * p.lse_rows + grow] * kLog2e;
         delta_row = p.delta[static_cast<size_t>(bh) * p.lse_rows + grow];
       }
-      // Mask words of this half's two tiles of chunk c (global memory, read one chunk ahead).
-      auto words = [&](int c, uint32_t& w0, uint32_t& w1) {
-        const int i = C::CH * c + 2 * half;
-        w0 = i < n_sub ? __ldg(p.bits2 + static_cast<size_t>(t0 + i) * 128 + row) : 0u;
-        w1 = i + 1 < n_sub ? __ldg(p.bits2 + static_cast<size_t>(t0 + i + 1) * 128 + row) : 0u;
+      // Mask word of this warp's tile of chunk c (global memory, read one chunk ahead).
+      auto word = [&](int c) -> uint32_t {
+        const int i = C::CH * c + j;
+        return i < n_sub ? __ldg(p.bits2 + static_cast<size_t>(t0 + i) * 128 + row) : 0u;
       };
-      uint32_t nw0 = 0, nw1 = 0;
-      if (nch > 0) words(0, nw0, nw1);
+      uint32_t nw = nch > 0 ? word(0) : 0u;
       const uint32_t g0 = g;
       for (int c = 0; c < nch; ++c) {
         const uint32_t gg = g0 + c;
         const int sb = gg % C::NSB, gb = gg & 1;
         const int n_in = min(C::CH, n_sub - C::CH * c);
-        const int j0 = 2 * half;
-        const uint32_t w0 = nw0, w1 = nw1;
-        if (c + 1 < nch) words(c + 1, nw0, nw1);
-        const uint32_t a0 = __reduce_or_sync(0xffffffffu, w0), a1 = __reduce_or_sync(0xffffffffu, w1);
+        const uint32_t w = nw;
+        if (c + 1 < nch) nw = word(c + 1);
+        const uint32_t a = __reduce_or_sync(0xffffffffu, w);
         if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
         if (warp == 2 && lane == 0) FWN_TR(20, c);
         tc_fence_after();
-        // Column lse (as -lse * log2 e) and delta of this half (rows are keys).
+        // S (and dP) of this tile -> registers; then the buffer is released for the next S MMA.
+        float s[32], dp[32];
+        if (j < n_in) {
+          tmem_ld32(trow + 128 * sb + 32 * j, s);
+          if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty(sb));
+        // Column lse (as -lse * log2 e) and delta of this tile (rows are keys).
         uint32_t vslot = 0;
         if constexpr (C::ROWS_ARE_KEYS) {
           const uint32_t vs = gg % C::NVEC_RING;
           if (!(ok = mbar_wait(v_full(vs), (gg / C::NVEC_RING) & 1, abort_flag))) break;
-          vslot = vec_slot(vs) + 64 * half * 4;
+          vslot = vec_slot(vs) + 128 * j;
         }
-        // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs, one 32-column sub-tile at a time;
-        // the S / dP buffer is released once the second sub-tile is in registers.
-        uint32_t pk[32];
+        // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs.
+        uint32_t pk[16];
         const float2 cc = make_float2(c2, c2);
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          float s[32], dp[32];
-          if (j0 + jj < n_in) {
-            tmem_ld32(trow + 128 * sb + 64 * half + 32 * jj, s);
-            if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 64 * half + 32 * jj, dp);
-          }
-          tmem_wait_ld();
-          if (jj == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_empty(sb));
-          }
-          const uint32_t w = jj ? w1 : w0;
-          const uint32_t a = jj ? a1 : a0;
+        for (int gi = 0; gi < 4; ++gi) {
+          if ((a >> (8 * gi)) & 0xFFu) {
+            float lv[8], dv[8];
+            if constexpr (C::ROWS_ARE_KEYS) {
+              const uint32_t va = vslot + 32 * gi;
+              const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
+              lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
 #pragma unroll
-          for (int gi = 0; gi < 4; ++gi) {
-            if ((a >> (8 * gi)) & 0xFFu) {
-              float lv[8], dv[8];
-              if constexpr (C::ROWS_ARE_KEYS) {
-                const uint32_t va = vslot + 32 * (4 * jj + gi);
-                const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
-                lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
-                if constexpr (C::NEED_DP) {
-                  const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
-                  dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  lv[i] = nl2_row;
-                  dv[i] = delta_row;
-                }
-              }
-#pragma unroll
-              for (int i = 0; i < 8; i += 2) {
-                const int k = 8 * gi + i;
-                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
-                float2 e;
-                if (i < 2) {
-                  e = exp2_poly2(x);
-                } else {
-                  e.x = ex2(x.x);
-                  e.y = ex2(x.y);
-                }
-                e.x = (w >> k) & 1u ? e.x : 0.f;
-                e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
-                if constexpr (C::NEED_DP) {
-                  const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
-                  pk[16 * jj + (k >> 1)] = pack_bf16(ds.x, ds.y);
-                } else {
-                  pk[16 * jj + (k >> 1)] = pack_bf16(e.x, e.y);
-                }
+              for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
+              if constexpr (C::NEED_DP) {
+                const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
+                dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
               }
             } else {
 #pragma unroll
-              for (int i = 0; i < 4; ++i) pk[16 * jj + 4 * gi + i] = 0u;
+              for (int i = 0; i < 8; ++i) {
+                lv[i] = nl2_row;
+                dv[i] = delta_row;
+              }
             }
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+              const int k = 8 * gi + i;
+              const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
+              float2 e;
+              if (i < 2) {
+                e = exp2_poly2(x);
+              } else {
+                e.x = ex2(x.x);
+                e.y = ex2(x.y);
+              }
+              e.x = (w >> k) & 1u ? e.x : 0.f;
+              e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
+              if constexpr (C::NEED_DP) {
+                const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
+                pk[k >> 1] = pack_bf16(ds.x, ds.y);
+              } else {
+                pk[k >> 1] = pack_bf16(e.x, e.y);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pk[4 * gi + i] = 0u;
           }
         }
         if constexpr (C::ROWS_ARE_KEYS) {
@@ -454,7 +457,7 @@ __global__ void __maxnreg__(168)
         if (warp == 2 && lane == 0) FWN_TR(26, c);
         // G buffer free once the accumulating MMA of chunk gg-2 is complete.
         if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-        if (j0 < n_in) tmem_st32(trow + C::G_COL + 64 * gb + 32 * half, *reinterpret_cast<const float(*)[32]>(pk));
+        if (j < n_in) tmem_st16(trow + C::G_COL + 64 * gb + 16 * j, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -463,28 +466,29 @@ __global__ void __maxnreg__(168)
       }
       if (!ok) break;
       g = g0 + nch;
-      // ---------------------------------------------------------------- epilogue: this half's D / 2 columns
+      // ---------------------------------------------------------------- epilogue: this warp's D / 4 columns
+      constexpr int OC = D / 4;
       const bool store = grow < p.n;
       const int64_t roff = (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sn +
-                            static_cast<int64_t>(h) * p.o_sh) * C::ES + (D / 2) * C::ES * half;
+                            static_cast<int64_t>(h) * p.o_sh) * C::ES + OC * C::ES * j;
       uint8_t* dst = reinterpret_cast<uint8_t*>(C::ACC_ON_C0 ? p.out0 : p.out1) + roff;
       const float mul = C::ACC_ON_C0 ? p.scale : 1.f;
       if (nch == 0) {
         if (store)
-          for (int i = 0; i < D * C::ES / 32; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < OC * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
         continue;
       }
       if (!(ok = mbar_wait(acc_full, qc & 1, abort_flag))) break;
       tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < D / 64; ++j) {
-        float o[32];
-        tmem_ld32(trow + C::ACC_COL + (D / 2) * half + 32 * j, o);
+      for (int jj = 0; jj < OC / 16; ++jj) {
+        float o[16];
+        tmem_ld16(trow + C::ACC_COL + OC * j + 16 * jj, o);
         tmem_wait_ld();
         if (store) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4*>(dst + j * 64)[i] =
+          for (int i = 0; i < 2; ++i)
+            reinterpret_cast<uint4*>(dst + jj * 32)[i] =
                 make_uint4(pack_bf16(o[8 * i] * mul, o[8 * i + 1] * mul), pack_bf16(o[8 * i + 2] * mul, o[8 * i + 3] * mul),
                            pack_bf16(o[8 * i + 4] * mul, o[8 * i + 5] * mul), pack_bf16(o[8 * i + 6] * mul, o[8 * i + 7] * mul));
         }

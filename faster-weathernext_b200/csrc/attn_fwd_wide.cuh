@@ -15,8 +15,9 @@
 //   warp 0      TMA producer: Q once per item; per chunk K, the mask words, then V of the previous chunk.
 //               Four tiles with consecutive key blocks are one 128-row box per column block, otherwise
 //               one 32-row box per tile; copies are issued from several lanes at once.
-//   warp 1      TMEM allocation; one thread issues S = Q K^T (A, B from shared memory) into S[c & 1] and
-//               O += P V (A = P from TMEM, B = V MN-major); S of chunk c+1 goes ahead of P V of chunk c.
+//   warp 1      TMEM allocation; the warp runs the MMA loop (descriptors warp-uniform) and one elected lane
+//               issues S = Q K^T (A, B from shared memory) into S[c & 1] and O += P V (A = P from TMEM,
+//               B = V MN-major); S of chunk c+1 goes ahead of P V of chunk c.
 //   warps 2-9   softmax. Warps w and w+4 share TMEM lane quadrant w % 4 (thread = query row) and take
 //               columns 0-63 and 64-127 of each chunk. One pass against the row's reference max (the exact
 //               masked max of the first chunk with an allowed key); if a half-row's sum exceeds 2^8 the
@@ -239,65 +240,72 @@ __global__ void __maxnreg__(168)
       if (pending_q) mbar_wait(q_full, (qc & 1), &never);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdescPV = instr_desc(false, 128, D, false, true);
-      uint32_t g = 0, qc = 0;
-      bool ok = true;
-      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-        const int nch = (n_sub + C::CH - 1) / C::CH;
-        if (nch == 0) continue;
-        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
-        const uint32_t g0 = g;
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch) {
-            const uint32_t gg = g0 + c;
-            const int sb = gg & 1;
-            const int n_in = min(C::CH, n_sub - C::CH * c);
-            if (!(ok = mbar_wait(k_full(gg % C::NK), (gg / C::NK) & 1, abort_flag))) break;
-            if (!(ok = mbar_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t idesc_s = instr_desc(false, 128, 32 * n_in, false, false);
-            const uint32_t kt = k_slot(gg % C::NK);
+    // ------------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
+    constexpr uint32_t kIdescPV = instr_desc(false, 128, D, false, true);
+    const uint64_t qdesc = smem_desc(q_smem, 16, 1024);
+    uint32_t g = 0, qc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      const int pb = it % per_bh;
+      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int nch = (n_sub + C::CH - 1) / C::CH;
+      if (nch == 0) continue;
+      if (!(ok = warp_wait(q_full, qc & 1, abort_flag))) break;
+      const uint32_t g0 = g;
+      for (int c = 0; c <= nch && ok; ++c) {
+        if (c < nch) {
+          const uint32_t gg = g0 + c;
+          const int sb = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!(ok = warp_wait(k_full(gg % C::NK), (gg / C::NK) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t idesc_s = instr_desc(false, 128, 32 * n_in, false, false);
+          const uint64_t kdesc = smem_desc(k_slot(gg % C::NK), 16, 1024);
+          if (elect_one_sync()) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<false>(tmem + sb * C::KEYS, smem_desc(q_smem + cb * C::ROWS * 128 + within, 16, 1024),
-                            smem_desc(kt + cb * C::KEYS * 128 + within, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+              mma_ss<false>(tmem + sb * C::KEYS, qdesc + ((cb * C::ROWS * 128 + within) >> 4),
+                            kdesc + ((cb * C::KEYS * 128 + within) >> 4), idesc_s, kk > 0 ? 1u : 0u);
             }
             mma_commit(s_full(sb));
             mma_commit(k_empty(gg % C::NK));
-            FWN_TR(11, c);
             if (c == nch - 1) mma_commit(q_empty);
           }
-          if (c >= 1) {
-            const uint32_t gg = g0 + c - 1;
-            const int pbuf = gg & 1;
-            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-            if (!(ok = mbar_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag))) break;
-            if (!(ok = mbar_wait(v_full(gg % C::NV), (gg / C::NV) & 1, abort_flag))) break;
-            if (c == 1 && !(ok = mbar_wait(o_empty, (qc & 1) ^ 1, abort_flag))) break;
-            tc_fence_after();
-            const uint32_t vt = v_slot(gg % C::NV);
-            const int ksteps = 2 * n_in;
+          __syncwarp();
+          if (lane == 0) FWN_TR(11, c);
+        }
+        if (c >= 1) {
+          const uint32_t gg = g0 + c - 1;
+          const int pbuf = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+          if (!(ok = warp_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(v_full(gg % C::NV), (gg / C::NV) & 1, abort_flag))) break;
+          if (c == 1 && !(ok = warp_wait(o_empty, (qc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint64_t vdesc = smem_desc(v_slot(gg % C::NV), C::KEYS * 128, 1024);
+          const uint32_t pcol = tmem + C::P_COL + 64 * pbuf;
+          const int ksteps = 2 * n_in;
+          if (elect_one_sync()) {
             for (int kk = 0; kk < ksteps; ++kk)
-              mma_ts(tmem + C::O_COL, tmem + C::P_COL + 64 * pbuf + 8 * kk,
-                     smem_desc(vt + kk * 16 * 128, C::KEYS * 128, 1024), kIdescPV, (c == 1 && kk == 0) ? 0u : 1u);
+              mma_ts(tmem + C::O_COL, pcol + 8 * kk, vdesc + ((kk * 16 * 128) >> 4), kIdescPV,
+                     (c == 1 && kk == 0) ? 0u : 1u);
             mma_commit(p_empty(pbuf));
             mma_commit(v_empty(gg % C::NV));
-            FWN_TR(12, c - 1);
             if (c == nch) mma_commit(o_full);
           }
+          __syncwarp();
+          if (lane == 0) FWN_TR(12, c - 1);
         }
-        g = g0 + nch;
-        ++qc;
       }
-      mma_commit(drain);
-      volatile int never = 0;
-      mbar_wait(drain, 0, &never);
+      g = g0 + nch;
+      ++qc;
     }
+    if (elect_one_sync()) mma_commit(drain);
+    __syncwarp();
+    volatile int never = 0;
+    mbar_wait(drain, 0, &never);
   } else {
     // ------------------------------------------------------------------ softmax + epilogue (warps 2-9)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
