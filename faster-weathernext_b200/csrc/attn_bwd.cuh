@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr bool kElect = F32;  // MMA issue style (see the MMA issuer role)
   if (threadIdx.x == 0) {
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
@@ -349,116 +350,128 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       if (pending_r) mbar_wait(r_full, qc & 1, &never);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
-    constexpr uint32_t kIdescAcc = instr_desc(F32, 128, D, false, true);
-    // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
-    constexpr int kPasses = X3 ? 3 : 1;
-    uint32_t g = 0, qc = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-      const int pb = it % per_bh;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-      const int nch = (n_sub + CH - 1) / CH;
-      if (nch == 0) continue;
-      if (!(ok = warp_wait(X3 ? r_ready : r_full, qc & 1, abort_flag))) break;
-      const uint32_t g0 = g;
-      // S (and dP) of chunk c: S = R0 C0^T at TMEM column 0, dP = R1 C1^T at column 64 (both K-major).
-      auto issue_sd = [&](int c) -> bool {
-        const uint32_t gg = g0 + c;
-        const int st = gg % C::NS;
-        const int n_in = min(CH, n_sub - CH * c);
-        if (!warp_wait(X3 ? c_ready(st) : c_full(st), (gg / C::NS) & 1, abort_flag)) return false;
-        if (!warp_wait(sd_empty, (gg & 1) ^ 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
-        const uint32_t sb = stage(st);
-#pragma unroll
-        for (int op = 0; op < C::NR; ++op) {
-          const int cs = op == 0 ? 0 : C::SLOT_C1;
-          const uint64_t r_hi = smem_desc(r_op(op, 0), 16, 1024), r_lo = smem_desc(r_op(op, 1), 16, 1024);
-          const uint64_t c_hi = smem_desc(slot(sb, cs, 0), 16, 1024), c_lo = smem_desc(slot(sb, cs, 1), 16, 1024);
-#pragma unroll
-          for (int pass = 0; pass < kPasses; ++pass) {
-#pragma unroll
-            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint64_t a = (pass == 2 ? r_lo : r_hi) + ((cb * C::ROWS * 128 + within) >> 4);
-              const uint64_t bd = (pass == 1 ? c_lo : c_hi) + ((cb * C::COLS * 128 + within) >> 4);
-              if (elect_one_sync()) mma_ss<F32>(tmem + 64 * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u);
-              __syncwarp();
+    if (kElect || lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      // tf32 / 3xTF32 (many K = 8 MMAs per chunk): the whole warp runs the loop with warp-uniform descriptors and
+      // one elected lane issues; bf16 (a few short MMAs per chunk on sparse masks): lane 0 alone, which measured
+      // 2 % faster there.
+      auto wait_ = [&](uint32_t bar, uint32_t parity) -> bool {
+        if constexpr (kElect) return warp_wait(bar, parity, abort_flag);
+        else return mbar_wait(bar, parity, abort_flag);
+      };
+      auto issue_ = [&](auto&& fn) {
+        if constexpr (kElect) {
+          if (elect_one_sync()) fn();
+          __syncwarp();
+        } else {
+          fn();
+        }
+      };
+      constexpr uint32_t kIdescAcc = instr_desc(F32, 128, D, false, true);
+      // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
+      constexpr int kPasses = X3 ? 3 : 1;
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + CH - 1) / CH;
+        if (nch == 0) continue;
+        if (!(ok = wait_(X3 ? r_ready : r_full, qc & 1))) break;
+        const uint32_t g0 = g;
+        // S (and dP) of chunk c: S = R0 C0^T at TMEM column 0, dP = R1 C1^T at column 64 (both K-major).
+        auto issue_sd = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS;
+          const int n_in = min(CH, n_sub - CH * c);
+          if (!wait_(X3 ? c_ready(st) : c_full(st), (gg / C::NS) & 1)) return false;
+          if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
+          tc_fence_after();
+          const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
+          const uint32_t sb = stage(st);
+  #pragma unroll
+          for (int op = 0; op < C::NR; ++op) {
+            const int cs = op == 0 ? 0 : C::SLOT_C1;
+            const uint64_t r_hi = smem_desc(r_op(op, 0), 16, 1024), r_lo = smem_desc(r_op(op, 1), 16, 1024);
+            const uint64_t c_hi = smem_desc(slot(sb, cs, 0), 16, 1024), c_lo = smem_desc(slot(sb, cs, 1), 16, 1024);
+  #pragma unroll
+            for (int pass = 0; pass < kPasses; ++pass) {
+  #pragma unroll
+              for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = (pass == 2 ? r_lo : r_hi) + ((cb * C::ROWS * 128 + within) >> 4);
+                const uint64_t bd = (pass == 1 ? c_lo : c_hi) + ((cb * C::COLS * 128 + within) >> 4);
+                issue_([&] { mma_ss<F32>(tmem + 64 * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
+              }
             }
           }
-        }
-        if (elect_one_sync()) {
-          mma_commit(sd_full);
-          if (c == nch - 1) mma_commit(r_empty);
-        }
-        __syncwarp();
-        return true;
-      };
-      // acc0 += dS C0 and / or acc1 += P C1 of chunk c (C0 / C1 as MN-major B operands: the K-major tile
-      // itself for bf16, the 32-byte-atom copy for tf32).
-      auto issue_acc = [&](int c) -> bool {
-        const uint32_t gg = g0 + c;
-        const int st = gg % C::NS, gb = gg % C::NB;
-        const int n_in = min(CH, n_sub - CH * c);
-        if (!warp_wait(g_full(gb), (gg / C::NB) & 1, abort_flag)) return false;
-        if (c == 0 && !warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t sb = stage(st);
-        const int ksteps = n_in * C::SUB / C::KSTEP;
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          if (which == 0 && !C::ACC_DS) continue;
-          if (which == 1 && !C::ACC_P) continue;
-          const int bs = which == 0 ? (F32 ? C::SLOT_C0MN : 0) : (F32 ? C::SLOT_C1MN : C::SLOT_C1);
-          const int gi = which == 0 ? G_DS : G_P;
-          const uint32_t acc = tmem + (which == 0 ? C::ACC0 : C::ACC1);
-          const uint64_t g_hi = C::G64 ? smem_desc(g_tile(gb, gi, 0), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 0), 16, 1024);
-          const uint64_t g_lo = C::G64 ? smem_desc(g_tile(gb, gi, 1), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 1), 16, 1024);
-          const uint64_t b_hi = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
-                                    : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
-          const uint64_t b_lo = F32 ? smem_desc(slot(sb, bs, 1), C::COLS * 128, 512, kLayoutSW128Base32B)
-                                    : smem_desc(slot(sb, bs, 1), C::COLS * 128, 1024);
-          for (int pass = 0; pass < kPasses; ++pass) {
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint32_t aoff = C::G64 ? kk * 32 : cb * C::ROWS * 128 + within;
-              const uint64_t a = (pass == 2 ? g_lo : g_hi) + (aoff >> 4);
-              const uint64_t bd = (pass == 1 ? b_lo : b_hi) + ((kk * C::KSTEP * 128) >> 4);
-              if (elect_one_sync()) mma_ss<F32>(acc, a, bd, kIdescAcc, (c == 0 && pass == 0 && kk == 0) ? 0u : 1u);
-              __syncwarp();
+          issue_([&] {
+            mma_commit(sd_full);
+            if (c == nch - 1) mma_commit(r_empty);
+          });
+          return true;
+        };
+        // acc0 += dS C0 and / or acc1 += P C1 of chunk c (C0 / C1 as MN-major B operands: the K-major tile
+        // itself for bf16, the 32-byte-atom copy for tf32).
+        auto issue_acc = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS, gb = gg % C::NB;
+          const int n_in = min(CH, n_sub - CH * c);
+          if (!wait_(g_full(gb), (gg / C::NB) & 1)) return false;
+          if (c == 0 && !wait_(acc_empty, (qc & 1) ^ 1)) return false;
+          tc_fence_after();
+          const uint32_t sb = stage(st);
+          const int ksteps = n_in * C::SUB / C::KSTEP;
+  #pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            if (which == 0 && !C::ACC_DS) continue;
+            if (which == 1 && !C::ACC_P) continue;
+            const int bs = which == 0 ? (F32 ? C::SLOT_C0MN : 0) : (F32 ? C::SLOT_C1MN : C::SLOT_C1);
+            const int gi = which == 0 ? G_DS : G_P;
+            const uint32_t acc = tmem + (which == 0 ? C::ACC0 : C::ACC1);
+            const uint64_t g_hi = C::G64 ? smem_desc(g_tile(gb, gi, 0), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 0), 16, 1024);
+            const uint64_t g_lo = C::G64 ? smem_desc(g_tile(gb, gi, 1), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 1), 16, 1024);
+            const uint64_t b_hi = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
+                                      : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
+            const uint64_t b_lo = F32 ? smem_desc(slot(sb, bs, 1), C::COLS * 128, 512, kLayoutSW128Base32B)
+                                      : smem_desc(slot(sb, bs, 1), C::COLS * 128, 1024);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              for (int kk = 0; kk < ksteps; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint32_t aoff = C::G64 ? kk * 32 : cb * C::ROWS * 128 + within;
+                const uint64_t a = (pass == 2 ? g_lo : g_hi) + (aoff >> 4);
+                const uint64_t bd = (pass == 1 ? b_lo : b_hi) + ((kk * C::KSTEP * 128) >> 4);
+                issue_([&] { mma_ss<F32>(acc, a, bd, kIdescAcc, (c == 0 && pass == 0 && kk == 0) ? 0u : 1u); });
+              }
             }
           }
+          issue_([&] {
+            mma_commit(g_empty(gb));
+            mma_commit(c_empty(st));
+            if (c == nch - 1) mma_commit(acc_full);
+          });
+          return true;
+        };
+        if constexpr (C::NS >= 2) {
+          // S / dP of chunk c+1 go ahead of the accumulating MMAs of chunk c (two stages in flight).
+          for (int c = 0; c <= nch && ok; ++c) {
+            if (c < nch && !(ok = issue_sd(c))) break;
+            if (c >= 1 && !(ok = issue_acc(c - 1))) break;
+          }
+        } else {
+          // One stage: the accumulating MMAs of chunk c free it before chunk c+1 can land.
+          for (int c = 0; c < nch && ok; ++c) {
+            if (!(ok = issue_sd(c))) break;
+            if (!(ok = issue_acc(c))) break;
+          }
         }
-        if (elect_one_sync()) {
-          mma_commit(g_empty(gb));
-          mma_commit(c_empty(st));
-          if (c == nch - 1) mma_commit(acc_full);
-        }
-        __syncwarp();
-        return true;
-      };
-      if constexpr (C::NS >= 2) {
-        // S / dP of chunk c+1 go ahead of the accumulating MMAs of chunk c (two stages in flight).
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch && !(ok = issue_sd(c))) break;
-          if (c >= 1 && !(ok = issue_acc(c - 1))) break;
-        }
-      } else {
-        // One stage: the accumulating MMAs of chunk c free it before chunk c+1 can land.
-        for (int c = 0; c < nch && ok; ++c) {
-          if (!(ok = issue_sd(c))) break;
-          if (!(ok = issue_acc(c))) break;
-        }
+        g = g0 + nch;
+        ++qc;
       }
-      g = g0 + nch;
-      ++qc;
+      issue_([&] { mma_commit(drain); });
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
     }
-    if (elect_one_sync()) mma_commit(drain);
-    __syncwarp();
-    volatile int never = 0;
-    mbar_wait(drain, 0, &never);
   } else if (X3 && warp >= 6) {
     // ------------------------------------------------------------------ 3xTF32 converter (warps 6-9)
     const int ctid = threadIdx.x - 192;

@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr bool kElect = F32;  // MMA issue style (see the MMA issuer role)
   __shared__ int trace_count;
   const long long trace_t0 = clock64();
 #define FWN_TR(code, arg) trace_event(p.trace, &trace_count, trace_t0, (code), (arg))
@@ -257,93 +258,106 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       if (pending_q) mbar_wait(q_full, (qc & 1), &never);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (whole warp, one lane issues)
-    constexpr uint32_t kIdescPV = instr_desc(F32, 128, D, false, true);
-    // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
-    constexpr int kPasses = X3 ? 3 : 1;
-    const uint64_t qdesc = smem_desc(q_smem, 16, 1024), qlo_desc = smem_desc(q_lo, 16, 1024);
-    uint32_t g = 0, qc = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-      const int pb = it % per_bh;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
-      const int nch = (n_sub + C::CH - 1) / C::CH;
-      if (nch == 0) continue;
-      if (!(ok = warp_wait(X3 ? q_ready : q_full, qc & 1, abort_flag))) break;
-      if (lane == 0) FWN_TR(10, it);
-      const uint32_t g0 = g;
-      for (int c = 0; c <= nch && ok; ++c) {
-        if (c < nch) {
-          const uint32_t gg = g0 + c;
-          const int st = gg % C::NS, sb = gg & 1;
-          const int n_in = min(C::CH, n_sub - C::CH * c);
-          if (!(ok = warp_wait(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-          tc_fence_after();
-          const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
-          const uint64_t kdesc = smem_desc(stage_k(st), 16, 1024), klo_desc = smem_desc(stage_klo(st), 16, 1024);
-#pragma unroll
-          for (int pass = 0; pass < kPasses; ++pass) {
-#pragma unroll
-            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
-              const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
-              if (elect_one_sync()) mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u);
-              __syncwarp();
-            }
-          }
-          if (elect_one_sync()) {
-            mma_commit(s_full(sb));
-            if (c == nch - 1) mma_commit(q_empty);
-          }
+    if (kElect || lane == 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      // tf32 / 3xTF32 (many K = 8 MMAs per chunk): the whole warp runs the loop with warp-uniform descriptors and
+      // one elected lane issues; bf16 (a few short MMAs per chunk on sparse masks): lane 0 alone, which measured
+      // 2 % faster there.
+      auto wait_ = [&](uint32_t bar, uint32_t parity) -> bool {
+        if constexpr (kElect) return warp_wait(bar, parity, abort_flag);
+        else return mbar_wait(bar, parity, abort_flag);
+      };
+      auto issue_ = [&](auto&& fn) {
+        if constexpr (kElect) {
+          if (elect_one_sync()) fn();
           __syncwarp();
-          if (lane == 0) FWN_TR(11, c);
+        } else {
+          fn();
         }
-        if (c >= 1) {
-          const uint32_t gg = g0 + c - 1;
-          const int st = gg % C::NS, pbuf = gg & 1;
-          const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-          if (!(ok = warp_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag))) break;
-          if (c == 1 && !(ok = warp_wait(o_empty, (qc & 1) ^ 1, abort_flag))) break;
-          tc_fence_after();
-          const int ksteps = n_in * C::SUB / C::KSTEP;
-          // P (K-major A; 64-byte rows for 32 bf16 keys) and V (MN-major B: 128-byte swizzle for bf16, the
-          // 32-byte-atom variant for tf32), hi and lo copies.
-          const uint64_t pdesc = C::P64 ? smem_desc(p_smem(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_smem(pbuf), 16, 1024);
-          const uint64_t plo_desc = C::P64 ? smem_desc(p_lo(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_lo(pbuf), 16, 1024);
-          const uint64_t vdesc = F32 ? smem_desc(stage_v(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
-                                     : smem_desc(stage_v(st), C::KEYS * 128, 1024);
-          const uint64_t vlo_desc = F32 ? smem_desc(stage_vlo(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
-                                        : smem_desc(stage_vlo(st), C::KEYS * 128, 1024);
-          for (int pass = 0; pass < kPasses; ++pass) {
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              const uint32_t aoff = C::P64 ? kk * 32 : cb * C::ROWS * 128 + within;
-              const uint64_t a = (pass == 2 ? plo_desc : pdesc) + (aoff >> 4);
-              const uint64_t bd = (pass == 1 ? vlo_desc : vdesc) + ((kk * C::KSTEP * 128) >> 4);
-              if (elect_one_sync())
-                mma_ss<F32>(tmem + C::O_COL, a, bd, kIdescPV, (c == 1 && pass == 0 && kk == 0) ? 0u : 1u);
-              __syncwarp();
+      };
+      constexpr uint32_t kIdescPV = instr_desc(F32, 128, D, false, true);
+      // 3xTF32: each product is hi*hi + hi*lo + lo*hi (the lo*lo term is below fp32 precision).
+      constexpr int kPasses = X3 ? 3 : 1;
+      const uint64_t qdesc = smem_desc(q_smem, 16, 1024), qlo_desc = smem_desc(q_lo, 16, 1024);
+      uint32_t g = 0, qc = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+        const int pb = it % per_bh;
+        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int nch = (n_sub + C::CH - 1) / C::CH;
+        if (nch == 0) continue;
+        if (!(ok = wait_(X3 ? q_ready : q_full, qc & 1))) break;
+        if (!kElect || lane == 0) FWN_TR(10, it);
+        const uint32_t g0 = g;
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {
+            const uint32_t gg = g0 + c;
+            const int st = gg % C::NS, sb = gg & 1;
+            const int n_in = min(C::CH, n_sub - C::CH * c);
+            if (!(ok = wait_(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1))) break;
+            if (!(ok = wait_(s_empty(sb), ((gg >> 1) & 1) ^ 1))) break;
+            tc_fence_after();
+            const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
+            const uint64_t kdesc = smem_desc(stage_k(st), 16, 1024), klo_desc = smem_desc(stage_klo(st), 16, 1024);
+  #pragma unroll
+            for (int pass = 0; pass < kPasses; ++pass) {
+  #pragma unroll
+              for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
+                const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
+                issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
+              }
             }
+            issue_([&] {
+              mma_commit(s_full(sb));
+              if (c == nch - 1) mma_commit(q_empty);
+            });
+            if (!kElect || lane == 0) FWN_TR(11, c);
           }
-          if (elect_one_sync()) {
-            mma_commit(p_empty(pbuf));
-            mma_commit(kv_empty(st));
-            if (c == nch) mma_commit(o_full);
+          if (c >= 1) {
+            const uint32_t gg = g0 + c - 1;
+            const int st = gg % C::NS, pbuf = gg & 1;
+            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+            if (!(ok = wait_(p_full(pbuf), (gg >> 1) & 1))) break;
+            if (c == 1 && !(ok = wait_(o_empty, (qc & 1) ^ 1))) break;
+            tc_fence_after();
+            const int ksteps = n_in * C::SUB / C::KSTEP;
+            // P (K-major A; 64-byte rows for 32 bf16 keys) and V (MN-major B: 128-byte swizzle for bf16, the
+            // 32-byte-atom variant for tf32), hi and lo copies.
+            const uint64_t pdesc = C::P64 ? smem_desc(p_smem(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_smem(pbuf), 16, 1024);
+            const uint64_t plo_desc = C::P64 ? smem_desc(p_lo(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_lo(pbuf), 16, 1024);
+            const uint64_t vdesc = F32 ? smem_desc(stage_v(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
+                                       : smem_desc(stage_v(st), C::KEYS * 128, 1024);
+            const uint64_t vlo_desc = F32 ? smem_desc(stage_vlo(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
+                                          : smem_desc(stage_vlo(st), C::KEYS * 128, 1024);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              for (int kk = 0; kk < ksteps; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                const uint32_t aoff = C::P64 ? kk * 32 : cb * C::ROWS * 128 + within;
+                const uint64_t a = (pass == 2 ? plo_desc : pdesc) + (aoff >> 4);
+                const uint64_t bd = (pass == 1 ? vlo_desc : vdesc) + ((kk * C::KSTEP * 128) >> 4);
+                issue_([&] {
+                  mma_ss<F32>(tmem + C::O_COL, a, bd, kIdescPV, (c == 1 && pass == 0 && kk == 0) ? 0u : 1u);
+                });
+              }
+            }
+            issue_([&] {
+              mma_commit(p_empty(pbuf));
+              mma_commit(kv_empty(st));
+              if (c == nch) mma_commit(o_full);
+            });
+            if (!kElect || lane == 0) FWN_TR(12, c - 1);
           }
-          __syncwarp();
-          if (lane == 0) FWN_TR(12, c - 1);
         }
+        g = g0 + nch;
+        ++qc;
       }
-      g = g0 + nch;
-      ++qc;
+      // Drain the tensor pipe before TMEM is released.
+      issue_([&] { mma_commit(drain); });
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
     }
-    // Drain the tensor pipe before TMEM is released.
-    if (elect_one_sync()) mma_commit(drain);
-    __syncwarp();
-    volatile int never = 0;
-    mbar_wait(drain, 0, &never);
   } else if (X3 && warp >= 6) {
     // ------------------------------------------------------------------ 3xTF32 converter (warps 6-9)
     const int ctid = threadIdx.x - 192;
