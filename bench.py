@@ -436,7 +436,7 @@ def run_model_workload(args):
     trainer = DataParallelStep(model, members, lr=1e-5)
 
     def step():
-      return trainer.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles))
+      return trainer.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles), micro_batch=args.micro_batch)
   else:
     x = torch.randn(local_m, n, cfg.d_model, device=device, generator=g)
     c = torch.randn(local_m, cfg.cond_dim, device=device, generator=g)
@@ -491,6 +491,8 @@ def run_model_workload(args):
                      "peak": tc, "unit": "TFLOP/s", "frac": round(achieved / tc, 4), "peak_source": peak_kind,
                      "traffic": None},
         "attention_useful_gflop_per_gpu": round(attn / 1e9, 1), "gemm_gflop_per_gpu": round(gemm / 1e9, 1),
+        "peak_memory_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1),
+        "micro_batch": args.micro_batch if finetune else None,
         "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
         "gpu_launches": None,
     }), flush=True)
@@ -610,6 +612,8 @@ def main():
   ap.add_argument("--lists", choices=["auto", "gathered", "paired"], default="auto",
                   help="tile lists the kernels walk: gathered (distinct keys per block), paired 32-key tiles, or "
                        "auto (the public API's choice: gathered for sparse masks, paired for dense ones / D 128)")
+  ap.add_argument("--micro-batch", type=int, default=4,
+                  help="fine-tune: members per forward / backward on a rank (activations ~29 GB per member)")
   ap.add_argument("--no-e2e", action="store_true")
   ap.add_argument("--no-cpu", action="store_true")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)

@@ -69,3 +69,31 @@ def test_two_rank_step_matches_single_process():
       params, loss = out[r]
       torch.testing.assert_close(params, ref, rtol=1e-5, atol=1e-6)
       assert abs(loss - float(loss1)) < 1e-5
+
+
+def test_batched_step_equals_member_loop():
+  """Micro-batches of 1, 2 or 3 members give the same gradient and loss (CPU, tiny model)."""
+  import torch
+  from faster_weathernext.finetune import DataParallelStep
+
+  class Tiny(torch.nn.Module):
+    def __init__(self):
+      super().__init__()
+      self.w = torch.nn.Parameter(torch.linspace(-1, 1, 12).reshape(3, 4))
+
+    def forward(self, x, c):
+      return torch.tanh(x @ self.w) * (1 + c[:, None, :1])
+
+  g = torch.Generator().manual_seed(0)
+  xs = [torch.randn(1, 5, 3, generator=g) for _ in range(3)]
+  cs = [torch.randn(1, 2, generator=g) for _ in range(3)]
+  ts = [torch.randn(1, 5, 4, generator=g) for _ in range(3)]
+  grads, losses = [], []
+  for mb in (1, 2, 3):
+    model = Tiny()
+    step = DataParallelStep(model, members=3, lr=0.0)
+    losses.append(float(step.step(xs, cs, ts, micro_batch=mb)))
+    grads.append(model.w.grad.clone())
+  for loss, grad in zip(losses[1:], grads[1:]):
+    assert abs(losses[0] - loss) < 1e-6
+    assert torch.allclose(grads[0], grad, atol=1e-6)
