@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_r0, const __grid_constant__ CUtensorMap tm_r1,
                     const __grid_constant__ CUtensorMap tm_c0, const __grid_constant__ CUtensorMap tm_c1,
                     const __grid_constant__ CUtensorMap tm_c0mn, const __grid_constant__ CUtensorMap tm_c1mn,
+                    const __grid_constant__ CUtensorMap tm_c0r, const __grid_constant__ CUtensorMap tm_c1r,
+                    const __grid_constant__ CUtensorMap tm_c0mnr, const __grid_constant__ CUtensorMap tm_c1mnr,
                     const BwdParams p) {
+  // tm_c*r: 4D maps of 32-row boxes (gathered mode: tiles whose 32 columns are consecutive).
   using C = BwdCfg<KIND, D, F32, CH, X3>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,6 +224,12 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
     if (C::LOAD_C1) tma_prefetch_desc(&tm_c1);
     if (C::LOAD_C0MN) tma_prefetch_desc(&tm_c0mn);
     if (C::LOAD_C1MN) tma_prefetch_desc(&tm_c1mn);
+    if (GATHER) {
+      tma_prefetch_desc(&tm_c0r);
+      if (C::LOAD_C1) tma_prefetch_desc(&tm_c1r);
+      if (C::LOAD_C0MN) tma_prefetch_desc(&tm_c0mnr);
+      if (C::LOAD_C1MN) tma_prefetch_desc(&tm_c1mnr);
+    }
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
   tc_fence_before();
@@ -287,7 +296,22 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               const int j = lane & 7, which = lane >> 3;  // which: the column slot this lane octet loads
               const int r0 = __shfl_sync(0xffffffffu, row, 4 * j), r1 = __shfl_sync(0xffffffffu, row, 4 * j + 1);
               const int r2 = __shfl_sync(0xffffffffu, row, 4 * j + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * j + 3);
-              if (which < C::NC) {
+              const int col0 = __shfl_sync(0xffffffffu, col, 0);
+              if (__all_sync(0xffffffffu, col == col0 + lane)) {
+                // The tile's 32 columns are consecutive: one 32-row box per slot and column block.
+                if (lane == 0) {
+                  for (int cb = 0; cb < C::CB; ++cb) {
+                    const uint32_t off = cb * C::COLS * 128 + s * C::SUB * 128;
+                    tma_load_4d(slot(sb, 0, 0) + off, &tm_c0r, cb * C::EPB, h, col0, b, c_full(st));
+                    if (C::LOAD_C1)
+                      tma_load_4d(slot(sb, C::SLOT_C1, 0) + off, &tm_c1r, cb * C::EPB, h, col0, b, c_full(st));
+                    if (C::LOAD_C0MN)
+                      tma_load_4d(slot(sb, C::SLOT_C0MN, 0) + off, &tm_c0mnr, cb * C::EPB, h, col0, b, c_full(st));
+                    if (C::LOAD_C1MN)
+                      tma_load_4d(slot(sb, C::SLOT_C1MN, 0) + off, &tm_c1mnr, cb * C::EPB, h, col0, b, c_full(st));
+                  }
+                }
+              } else if (which < C::NC) {
                 const void* tm = which == 0                                  ? static_cast<const void*>(&tm_c0)
                                  : (C::LOAD_C1 && which == C::SLOT_C1)       ? static_cast<const void*>(&tm_c1)
                                  : (C::LOAD_C0MN && which == C::SLOT_C0MN)   ? static_cast<const void*>(&tm_c0mn)

@@ -231,15 +231,19 @@ template <int D, bool F32, bool GATHER, bool X3 = false>
 fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
                       void* o, float* lse, int layout, cudaStream_t stream) {
   using C = fwn::FwdCfg<D, F32, X3>;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tk32, tv32;
   fwn_status s;
   if ((s = make_map(&tq, q, d, C::ROWS)) != FWN_OK) return s;
+  // 4D maps of 32-row boxes: the tile loads of the 32-key lists, and in gathered mode the tiles whose keys are
+  // consecutive.
+  if ((s = make_map(&tk32, k, d, C::SUB)) != FWN_OK) return s;
+  if ((s = make_map(&tv32, v, d, C::SUB, F32)) != FWN_OK) return s;
   if (GATHER) {
     if ((s = make_map_rows(&tk, k, d, layout, false, false)) != FWN_OK) return s;
     if ((s = make_map_rows(&tv, v, d, layout, F32, false)) != FWN_OK) return s;
   } else {
-    if ((s = make_map(&tk, k, d, C::SUB)) != FWN_OK) return s;
-    if ((s = make_map(&tv, v, d, C::SUB, F32)) != FWN_OK) return s;
+    tk = tk32;
+    tv = tv32;
   }
   fwn::FwdParams p{};
   p.ptr2 = t.ptr;
@@ -265,7 +269,7 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   auto kernel = fwn::attn_fwd_kernel<D, F32, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tq, tk, tv, tk32, tv32, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
   return ok();
@@ -352,6 +356,19 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
       if ((s = make_map(&c1mn, cp1, d, C::SUB, true, c1_out)) != FWN_OK) return s;
     }
   }
+  // 32-row 4D maps for gathered tiles whose columns are consecutive (the tile-mode maps themselves otherwise).
+  CUtensorMap c0r = c0, c1r = c1, c0mnr = c0mn, c1mnr = c1mn;
+  if (GATHER) {
+    if ((s = make_map(&c0r, cp0, d, C::SUB)) != FWN_OK) return s;
+    if ((s = make_map(&c1r, cp1, d, C::SUB, false, c1_out)) != FWN_OK) return s;
+    if (F32) {
+      if ((s = make_map(&c0mnr, cp0, d, C::SUB, true)) != FWN_OK) return s;
+      if ((s = make_map(&c1mnr, cp1, d, C::SUB, true, c1_out)) != FWN_OK) return s;
+    } else {
+      c0mnr = c0r;
+      c1mnr = c1r;
+    }
+  }
   fwn::BwdParams p{};
   p.ptr2 = t.ptr;
   p.kb2 = t.kb;
@@ -375,7 +392,7 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   auto kernel = fwn::attn_bwd_kernel<KIND, D, F32, CH, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, p);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, c0r, c1r, c0mnr, c1mnr, p);
   cudaError_t e = cudaGetLastError();
   static const char* const kNames[] = {"attn_bwd dq launch", "attn_bwd dkv launch", "attn_bwd dv launch",
                                        "attn_bwd dk launch"};
