@@ -194,6 +194,8 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kElect = F32;  // MMA issue style (see the MMA issuer role)
+  int trace_count = 0;  // FWN_TRACE builds: this lane's event count
+#define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
@@ -279,8 +281,22 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       // each prefetched register pair is consumed in place (a register move would wait for the load).
       auto issue_chunk = [&](int c, const ChunkMeta<CH>& meta) -> bool {
           const int st = g % C::NS;
-          if (!mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
           const int n_in = min(CH, n_sub - CH * c);
+          // Gathered key rows: the lse / delta of the chunk's gathered queries go to shared memory through the
+          // lanes' registers; their loads are issued before the stage wait so that their latency overlaps it.
+          float vec_lse[CH], vec_delta[CH];
+          if constexpr (GATHER && C::ROWS_ARE_KEYS) {
+  #pragma unroll
+            for (int s = 0; s < CH; ++s) {
+              if (s < n_in) {
+                const size_t vo = static_cast<size_t>(bh) * p.lse_rows + meta.v[s];
+                vec_lse[s] = __ldg(p.lse + vo);
+                vec_delta[s] = __ldg(p.delta + vo);
+              }
+            }
+          }
+          if (!mbar_wait(c_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
+          if (lane == 0) FWN_TR(3, c);
           // Gathered key rows: lse / delta of the gathered queries are stored by the lanes, not copied.
           const uint32_t per_tile = C::NC * kColBytes + 512 + ((C::ROWS_ARE_KEYS && !GATHER) ? 256 : 0);
           if (lane == 0) mbar_arrive_expect_tx(c_full(st), n_in * per_tile);
@@ -320,14 +336,6 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                 for (int cb = 0; cb < C::CB; ++cb)
                   tma_gather4(dst + cb * C::COLS * 128, tm, cb * C::EPB, r0, r1, r2, r3, c_full(st));
               }
-              if constexpr (C::ROWS_ARE_KEYS) {
-                const size_t vo = static_cast<size_t>(bh) * p.lse_rows + col;
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(p.lse[vo])
-                             : "memory");
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + 128 + lane * 4),
-                             "f"(p.delta[vo])
-                             : "memory");
-              }
             } else if (lane == 0) {
               const int col0 = meta.v[s] * C::SUB;
               for (int cb = 0; cb < C::CB; ++cb) {
@@ -349,6 +357,16 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
           }
           if constexpr (GATHER && C::ROWS_ARE_KEYS) {
             // Second arrival of c_full: publishes the lanes' lse / delta stores.
+  #pragma unroll
+            for (int s = 0; s < CH; ++s) {
+              if (s < n_in) {
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + lane * 4), "f"(vec_lse[s])
+                             : "memory");
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + C::VEC_OFF + s * 256 + 128 + lane * 4),
+                             "f"(vec_delta[s])
+                             : "memory");
+              }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(c_full(st));
           }
@@ -396,9 +414,18 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       constexpr int kPasses = X3 ? 3 : 1;
       uint32_t g = 0, qc = 0;
       bool ok = true;
+      // The item's list range is read one item ahead (a dependent global load at each item start would stall).
+      int nt0 = 0, nt1 = 0;
+      if (blockIdx.x < p.n_items) {
+        nt0 = __ldg(p.ptr2 + blockIdx.x % per_bh);
+        nt1 = __ldg(p.ptr2 + blockIdx.x % per_bh + 1);
+      }
       for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int n_sub = nt1 - nt0;
+        if (it + static_cast<int>(gridDim.x) < p.n_items) {
+          nt0 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh);
+          nt1 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh + 1);
+        }
         const int nch = (n_sub + CH - 1) / CH;
         if (nch == 0) continue;
         if (!(ok = wait_(X3 ? r_ready : r_full, qc & 1))) break;
@@ -433,6 +460,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             mma_commit(sd_full);
             if (c == nch - 1) mma_commit(r_empty);
           });
+          if (!kElect || lane == 0) FWN_TR(11, c);
           return true;
         };
         // acc0 += dS C0 and / or acc1 += P C1 of chunk c (C0 / C1 as MN-major B operands: the K-major tile
@@ -474,6 +502,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             mma_commit(c_empty(st));
             if (c == nch - 1) mma_commit(acc_full);
           });
+          if (!kElect || lane == 0) FWN_TR(12, c);
           return true;
         };
         if constexpr (C::NS >= 2) {
@@ -530,9 +559,18 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
     constexpr float kLog2e = 1.4426950408889634f;
     uint32_t g = 0, qc = 0;
     bool ok = true;
+    int nt0 = 0, nt1 = 0;  // list range, read one item ahead
+    if (blockIdx.x < p.n_items) {
+      nt0 = __ldg(p.ptr2 + blockIdx.x % per_bh);
+      nt1 = __ldg(p.ptr2 + blockIdx.x % per_bh + 1);
+    }
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
       const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int n_sub = nt1 - nt0;
+      if (it + static_cast<int>(gridDim.x) < p.n_items) {
+        nt0 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh);
+        nt1 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh + 1);
+      }
       const int nch = (n_sub + CH - 1) / CH;
       const int grow = pb * C::ROWS + row;
       float lse2_row = 0.f, delta_row = 0.f;
@@ -546,8 +584,10 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         const int st = gg % C::NS, gb = gg % C::NB;
         const int n_in = min(CH, n_sub - CH * c);
         if (!(ok = mbar_wait(sd_full, gg & 1, abort_flag))) break;
+        if (lane == 0) FWN_TR(20, c);
         if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
         if (!(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
+        if (lane == 0) FWN_TR(29, c);
         tc_fence_after();
         const uint32_t sb = stage(st);
         // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into the shared-memory
@@ -644,6 +684,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(g_full(gb));
+        if (lane == 0) FWN_TR(21, c);
       }
       if (!ok) break;
       g = g0 + nch;
@@ -702,6 +743,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+#undef FWN_TR
 }
 
 }  // namespace fwn

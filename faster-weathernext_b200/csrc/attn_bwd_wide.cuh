@@ -113,13 +113,11 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
   const uint32_t acc_full = bar4 + 32, acc_empty = bar4 + 40, drain = bar4 + 48;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
-  int* trace_count = reinterpret_cast<int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 8);
-  const long long trace_t0 = clock64();
-#define FWN_TR(code, arg) trace_event(p.trace, trace_count, trace_t0, (code), (arg))
+  int trace_count = 0;  // FWN_TRACE builds: this lane's event count
+#define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    *trace_count = 0;
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
     for (int s = 0; s < C::N0; ++s) {

@@ -15,11 +15,12 @@
 //               8 gathers at 512-byte steps build the same 32-row tile.
 //   warp 1      TMEM allocation; one thread issues the tcgen05 MMAs:
 //                 S[buf] = Q K^T  (M=128, N=32|64, K=D)        -> TMEM, fp32
-//                 O     += P V    (M=128, N=D,     K=32|64)     -> TMEM, fp32 (P from shared memory)
+//                 O     += P V    (M=128, N=D,     K=32|64)     -> TMEM, fp32 (P from TMEM for bf16,
+//                                                                          from shared memory for tf32)
 //               S of chunk c+1 is issued before P V of chunk c, so the tensor core overlaps softmax.
 //   warps 2-5   softmax: thread = query row = TMEM lane. Reads S with tcgen05.ld, applies the row's
-//               mask word, keeps a running max m (log2 domain) and sum l, writes P (bf16 / fp32) to
-//               shared memory for the P V MMA. O is rescaled in TMEM only when the row max grows by
+//               mask word, keeps a running max m (log2 domain) and sum l, writes P (bf16 to TMEM,
+//               fp32 to shared memory) for the P V MMA. O is rescaled in TMEM only when the row max grows by
 //               more than 2^8 (the final O / l is exact either way). Exponentials are issued only for
 //               columns that some row of the warp may attend to.
 //               Epilogue: O / l -> global, LSE -> global.
@@ -59,23 +60,36 @@ struct FwdCfg {
   static constexpr int CH = (X3 || D == 128) ? 1 : 2;
   static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
-  static constexpr int NS = X3 ? 2 : 3;       // K/V pipeline stages
   static constexpr int Q_BYTES = CB * ROWS * 128;
   static constexpr int KV_BYTES = CB * KEYS * 128;
   // Stage: K, V, (3xTF32: K_lo, V_lo), mask words.
   static constexpr int BITS_OFF = (X3 ? 4 : 2) * KV_BYTES;
   static constexpr int STAGE_BYTES = (BITS_OFF + CH * 512 + 1023) / 1024 * 1024;
-  static constexpr int PCB = KEYS * ES / 128;  // 128-byte column blocks of a P row (0: one 64-byte row)
-  static constexpr bool P64 = PCB == 0;         // 32 bf16 keys: P rows of 64 bytes, 64-byte swizzle
-  static constexpr int P_BYTES = P64 ? ROWS * 64 : PCB * ROWS * 128;
+  // bf16: P goes to TMEM (packed bf16 pairs, the A operand of P V read from tensor memory); tf32 P is
+  // twice as wide and stays in shared memory (128-byte swizzle).
+  static constexpr bool P_TMEM = !F32;
+  static constexpr int PCB = KEYS * ES / 128;  // 128-byte column blocks of a shared-memory P row
+  static constexpr int P_BYTES = P_TMEM ? 0 : PCB * ROWS * 128;
   static constexpr int PBUF_BYTES = P_BYTES * (X3 ? 2 : 1);  // P (3xTF32: P_hi, P_lo)
   static constexpr int OFF_STAGE = Q_BYTES * (X3 ? 2 : 1);    // Q (3xTF32: Q_hi in place, Q_lo)
+  // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word, alignment slack.
+  static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16 + 1024; }
+  // K/V stages: bf16 takes as many as two CTAs per SM leave room for (at most 6), so that the copies of the
+  // next chunks are in flight while the softmax works; tf32 3, 3xTF32 2.
+  static constexpr int NS = X3 ? 2 : F32 ? 3
+                              : smem_bytes(6) <= 227 * 1024 / 2 ? 6
+                              : smem_bytes(5) <= 227 * 1024 / 2 ? 5
+                              : smem_bytes(4) <= 227 * 1024 / 2 ? 4 : 3;
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment
   static constexpr int TMEM_COLS = 256;
   static constexpr int O_COL = 128;
+  // TMEM P buffers (bf16): 64 keys -> 32 columns after O (head_dim 64); 32 keys -> 16 columns in the unused
+  // upper half of each 64-column S buffer (head_dim 128, one 32-key tile per chunk).
+  static constexpr int P_COL = CH == 1 ? 32 : O_COL + D;
+  static constexpr int P_STRIDE = CH == 1 ? 64 : 32;
   static constexpr int THREADS = X3 ? 320 : 192;  // 3xTF32: + a warpgroup splitting tiles into hi / lo
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
@@ -84,7 +98,9 @@ struct FwdCfg {
   // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
   static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 200;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
-  static_assert(!P64 || (!F32 && CH == 1), "64-byte P rows hold 32 bf16 keys");
+  static_assert(N_BAR == 14 + 3 * NS && SMEM_BYTES == smem_bytes(NS), "shared memory layout");
+  static_assert(!P_TMEM || (P_COL + P_STRIDE + KEYS / 2 <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)),
+                "TMEM budget");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
@@ -127,11 +143,9 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kElect = F32;  // MMA issue style (see the MMA issuer role)
-  __shared__ int trace_count;
-  const long long trace_t0 = clock64();
-#define FWN_TR(code, arg) trace_event(p.trace, &trace_count, trace_t0, (code), (arg))
+  int trace_count = 0;  // FWN_TRACE builds: this lane's event count
+#define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
-    trace_count = 0;
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
@@ -298,74 +312,100 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       const uint64_t qdesc = smem_desc(q_smem, 16, 1024), qlo_desc = smem_desc(q_lo, 16, 1024);
       uint32_t g = 0, qc = 0;
       bool ok = true;
+      // The item's list range is read one item ahead (a dependent global load at each item start would stall).
+      int nt0 = 0, nt1 = 0;
+      if (blockIdx.x < p.n_items) {
+        nt0 = __ldg(p.ptr2 + blockIdx.x % per_bh);
+        nt1 = __ldg(p.ptr2 + blockIdx.x % per_bh + 1);
+      }
       for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-        const int pb = it % per_bh;
-        const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+        const int n_sub = nt1 - nt0;
+        if (it + static_cast<int>(gridDim.x) < p.n_items) {
+          nt0 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh);
+          nt1 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh + 1);
+        }
         const int nch = (n_sub + C::CH - 1) / C::CH;
         if (nch == 0) continue;
         if (!(ok = wait_(X3 ? q_ready : q_full, qc & 1))) break;
         if (!kElect || lane == 0) FWN_TR(10, it);
         const uint32_t g0 = g;
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch) {
-            const uint32_t gg = g0 + c;
-            const int st = gg % C::NS, sb = gg & 1;
-            const int n_in = min(C::CH, n_sub - C::CH * c);
-            if (!(ok = wait_(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1))) break;
-            if (!(ok = wait_(s_empty(sb), ((gg >> 1) & 1) ^ 1))) break;
-            tc_fence_after();
-            const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
-            const uint64_t kdesc = smem_desc(stage_k(st), 16, 1024), klo_desc = smem_desc(stage_klo(st), 16, 1024);
+        // S = Q K^T of chunk c (K / V must have landed and the S buffer must be free).
+        auto issue_s = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS, sb = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!kElect || lane == 0) FWN_TR(15, c);
+          if (!wait_(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1)) return false;
+          if (!kElect || lane == 0) FWN_TR(16, c);
+          if (!wait_(s_empty(sb), ((gg >> 1) & 1) ^ 1)) return false;
+          if (!kElect || lane == 0) FWN_TR(13, c);
+          tc_fence_after();
+          const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
+          const uint64_t kdesc = smem_desc(stage_k(st), 16, 1024), klo_desc = smem_desc(stage_klo(st), 16, 1024);
   #pragma unroll
-            for (int pass = 0; pass < kPasses; ++pass) {
+          for (int pass = 0; pass < kPasses; ++pass) {
   #pragma unroll
-              for (int kk = 0; kk < D / C::KSTEP; ++kk) {
-                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
-                const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
-                issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
-              }
+            for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
+              const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
+              issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
             }
-            issue_([&] {
-              mma_commit(s_full(sb));
-              if (c == nch - 1) mma_commit(q_empty);
-            });
-            if (!kElect || lane == 0) FWN_TR(11, c);
           }
-          if (c >= 1) {
-            const uint32_t gg = g0 + c - 1;
-            const int st = gg % C::NS, pbuf = gg & 1;
-            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-            if (!(ok = wait_(p_full(pbuf), (gg >> 1) & 1))) break;
-            if (c == 1 && !(ok = wait_(o_empty, (qc & 1) ^ 1))) break;
-            tc_fence_after();
-            const int ksteps = n_in * C::SUB / C::KSTEP;
-            // P (K-major A; 64-byte rows for 32 bf16 keys) and V (MN-major B: 128-byte swizzle for bf16, the
-            // 32-byte-atom variant for tf32), hi and lo copies.
-            const uint64_t pdesc = C::P64 ? smem_desc(p_smem(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_smem(pbuf), 16, 1024);
-            const uint64_t plo_desc = C::P64 ? smem_desc(p_lo(pbuf), 16, 512, kLayoutSW64) : smem_desc(p_lo(pbuf), 16, 1024);
-            const uint64_t vdesc = F32 ? smem_desc(stage_v(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
-                                       : smem_desc(stage_v(st), C::KEYS * 128, 1024);
-            const uint64_t vlo_desc = F32 ? smem_desc(stage_vlo(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
-                                          : smem_desc(stage_vlo(st), C::KEYS * 128, 1024);
+          issue_([&] {
+            mma_commit(s_full(sb));
+            if (c == nch - 1) mma_commit(q_empty);
+          });
+          if (!kElect || lane == 0) FWN_TR(11, c);
+          return true;
+        };
+        // O += P V of chunk c (P written by the softmax; O free once the previous item's epilogue read it).
+        auto issue_pv = [&](int c) -> bool {
+          const uint32_t gg = g0 + c;
+          const int st = gg % C::NS, pbuf = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!wait_(p_full(pbuf), (gg >> 1) & 1)) return false;
+          if (c == 0 && !wait_(o_empty, (qc & 1) ^ 1)) return false;
+          if (!kElect || lane == 0) FWN_TR(14, c);
+          tc_fence_after();
+          const int ksteps = n_in * C::SUB / C::KSTEP;
+          // V: MN-major B (128-byte swizzle for bf16, the 32-byte-atom variant for tf32), hi and lo copies.
+          const uint64_t vdesc = F32 ? smem_desc(stage_v(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
+                                     : smem_desc(stage_v(st), C::KEYS * 128, 1024);
+          if constexpr (C::P_TMEM) {
+            // bf16 P from TMEM: K = 16 keys per MMA = 8 columns of packed pairs.
+            const uint32_t pcol = tmem + C::P_COL + C::P_STRIDE * pbuf;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint64_t bd = vdesc + ((kk * C::KSTEP * 128) >> 4);
+              issue_([&] { mma_ts(tmem + C::O_COL, pcol + 8 * kk, bd, kIdescPV, (c == 0 && kk == 0) ? 0u : 1u); });
+            }
+          } else {
+            // P in shared memory (K-major A), hi and lo copies.
+            const uint64_t pdesc = smem_desc(p_smem(pbuf), 16, 1024), plo_desc = smem_desc(p_lo(pbuf), 16, 1024);
+            const uint64_t vlo_desc = smem_desc(stage_vlo(st), C::KEYS * 128, 512, kLayoutSW128Base32B);
             for (int pass = 0; pass < kPasses; ++pass) {
               for (int kk = 0; kk < ksteps; ++kk) {
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                const uint32_t aoff = C::P64 ? kk * 32 : cb * C::ROWS * 128 + within;
-                const uint64_t a = (pass == 2 ? plo_desc : pdesc) + (aoff >> 4);
+                const uint64_t a = (pass == 2 ? plo_desc : pdesc) + ((cb * C::ROWS * 128 + within) >> 4);
                 const uint64_t bd = (pass == 1 ? vlo_desc : vdesc) + ((kk * C::KSTEP * 128) >> 4);
                 issue_([&] {
-                  mma_ss<F32>(tmem + C::O_COL, a, bd, kIdescPV, (c == 1 && pass == 0 && kk == 0) ? 0u : 1u);
+                  mma_ss<F32>(tmem + C::O_COL, a, bd, kIdescPV, (c == 0 && pass == 0 && kk == 0) ? 0u : 1u);
                 });
               }
             }
-            issue_([&] {
-              mma_commit(p_empty(pbuf));
-              mma_commit(kv_empty(st));
-              if (c == nch) mma_commit(o_full);
-            });
-            if (!kElect || lane == 0) FWN_TR(12, c - 1);
           }
+          issue_([&] {
+            mma_commit(p_empty(pbuf));
+            mma_commit(kv_empty(st));
+            if (c == nch - 1) mma_commit(o_full);
+          });
+          if (!kElect || lane == 0) FWN_TR(12, c);
+          return true;
+        };
+        // S of chunk c goes ahead of P V of chunk c-1, so that the tensor core overlaps the softmax.
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch && !(ok = issue_s(c))) break;
+          if (c >= 1 && !(ok = issue_pv(c - 1))) break;
         }
         g = g0 + nch;
         ++qc;
@@ -408,9 +448,18 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     uint32_t g = 0, qc = 0;
     bool ok = true;
+    int nt0 = 0, nt1 = 0;  // list range, read one item ahead
+    if (blockIdx.x < p.n_items) {
+      nt0 = __ldg(p.ptr2 + blockIdx.x % per_bh);
+      nt1 = __ldg(p.ptr2 + blockIdx.x % per_bh + 1);
+    }
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
       const int pb = it % per_bh, bh = it / per_bh, h = bh % p.heads, b = bh / p.heads;
-      const int t0 = p.ptr2[pb], n_sub = p.ptr2[pb + 1] - t0;
+      const int n_sub = nt1 - nt0;
+      if (it + static_cast<int>(gridDim.x) < p.n_items) {
+        nt0 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh);
+        nt1 = __ldg(p.ptr2 + (it + gridDim.x) % per_bh + 1);
+      }
       const int nch = (n_sub + C::CH - 1) / C::CH;
       const int qrow = pb * C::ROWS + row;
       float m_ref = -INFINITY, l = 0.f;
@@ -421,19 +470,26 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         const int n_in = min(C::CH, n_sub - C::CH * c);
         float s[64];
         if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
-        if (warp == 2 && lane == 0) FWN_TR(20, c);
+        if (lane == 0) FWN_TR(20, c);
         tc_fence_after();
         tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
         if (C::CH == 2 && n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        // While S is read from TMEM: the chunk's mask words (they land with its K / V tiles) and, for bf16, the
+        // P buffer (free once P V of chunk gg-2 is complete).
+        ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag);
+        if (C::P_TMEM && ok) ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag);
+        uint32_t w0 = 0u, w1 = 0u;
+        if (ok) {
+          w0 = ld_shared_u32(stage_bits(st) + row * 4);
+          if (C::CH == 2 && n_in == 2) w1 = ld_shared_u32(stage_bits(st) + 512 + row * 4);
+        }
         tmem_wait_ld();
-        if (warp == 2 && lane == 0) FWN_TR(24, c);
+        reg_fence(s);
+        if (!ok) break;
+        if (lane == 0) FWN_TR(24, c);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty(sb));
-        if (!(ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag))) break;
-        if (warp == 2 && lane == 0) FWN_TR(25, c);
-        const uint32_t w0 = ld_shared_u32(stage_bits(st) + row * 4);
-        const uint32_t w1 = (C::CH == 2 && n_in == 2) ? ld_shared_u32(stage_bits(st) + 512 + row * 4) : 0u;
         const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
         const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
         // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
@@ -489,14 +545,14 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
         };
         if constexpr (!F32) {
-          // One pass against the current reference, exact as long as no allowed p exceeds 2^8 (the lazy
-          // rescale threshold). Rows with nothing accumulated yet take this chunk's unmasked row max as
-          // their reference (an upper bound of the allowed logits); they are accepted only if their
-          // largest allowed p is at least 2^-60, so whatever underflowed is negligible. Otherwise the whole
-          // warp redoes the chunk with the exact two-pass update.
+          // One pass against the current reference, accepted while the row's chunk sum is at most 2^16 (so is
+          // every p: bf16 P keeps its relative precision, the fp32 accumulators stay far from overflow). Rows
+          // with nothing accumulated yet take this chunk's unmasked row max as their reference (an upper bound of
+          // the allowed logits); they are accepted only if their sum is at least 2^-54 (their largest allowed p
+          // is then at least 2^-60, so whatever underflowed is negligible). Otherwise the whole warp redoes the
+          // chunk with the exact two-pass update. Paired f32x2 arithmetic for the scaling and the sums.
           uint32_t pk[32];
-          float lp[4] = {0.f, 0.f, 0.f, 0.f};
-          float top = 0.f;
+          float2 lp2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
           const bool fresh = l == 0.f;
           float m_use = m_ref;
           if (__any_sync(0xffffffffu, fresh)) {
@@ -507,7 +563,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
             const float umax = fmaxf(fmaxf(up[0], up[1]), fmaxf(up[2], up[3])) * p.scale_log2;
             if (fresh) m_use = umax;
           }
-          const float neg_m = -m_use;
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             const uint32_t w = g < 4 ? w0 : w1;
@@ -516,13 +572,11 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
 #pragma unroll
               for (int i = 0; i < 8; i += 2) {
                 const int j = 8 * g + i;
-                const float t0 = ex2(fmaf(s[j], p.scale_log2, neg_m));
-                const float t1 = ex2(fmaf(s[j + 1], p.scale_log2, neg_m));
+                const float2 x = ffma2(make_float2(s[j], s[j + 1]), sc2, nm2);
+                const float t0 = ex2(x.x), t1 = ex2(x.y);
                 const float e0 = (w & (1u << (j & 31))) ? t0 : 0.f;
                 const float e1 = (w & (1u << ((j + 1) & 31))) ? t1 : 0.f;
-                lp[i & 3] += e0;
-                lp[(i + 1) & 3] += e1;
-                top = fmaxf(top, fmaxf(e0, e1));
+                lp2[(i >> 1) & 1] = fadd2(lp2[(i >> 1) & 1], make_float2(e0, e1));
                 pk[j >> 1] = pack_bf16(e0, e1);
               }
             } else {
@@ -530,7 +584,9 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
               for (int i = 0; i < 4; ++i) pk[4 * g + i] = 0u;
             }
           }
-          const bool bad = !(top <= 256.f) || (fresh && (w0 | w1) != 0u && !(top >= 8.673617e-19f));  // 2^-60
+          const float sum = (lp2[0].x + lp2[0].y) + (lp2[1].x + lp2[1].y);
+          const bool bad = !(sum <= 65536.f) ||
+                           (fresh && (w0 | w1) != 0u && !(sum >= 5.5511151231257827e-17f));  // 2^-54
           if (__any_sync(0xffffffffu, bad)) {
             float e[64];
             two_pass(e);
@@ -538,28 +594,18 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
             for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(e[2 * j], e[2 * j + 1]);
           } else {
             m_ref = m_use;
-            l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+            l += sum;
           }
-          if (warp == 2 && lane == 0) FWN_TR(26, c);
-          // P -> shared memory (wait until P V of chunk gg-2 released this buffer).
-          if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-          if (warp == 2 && lane == 0) FWN_TR(29, c);
-          const uint32_t pbase = p_smem(sb);
-          if constexpr (C::P64) {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-              st_shared_v4(pbase + sw64_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-          } else {
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-              if (cc < 4 * n_in)
-                st_shared_v4(pbase + sw128_offset(row, cc), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-            }
-          }
+          if (lane == 0) FWN_TR(26, c);
+          // P -> TMEM (the buffer was released above); the row's packed pairs go to its lane.
+          const uint32_t pcol = trow + C::P_COL + C::P_STRIDE * sb;
+          tmem_st16(pcol, *reinterpret_cast<const uint32_t(*)[16]>(&pk[0]));
+          if (C::CH == 2 && n_in == 2) tmem_st16(pcol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&pk[16]));
+          tmem_wait_st();
         } else {
           float e[64];
           two_pass(e);
-          if (warp == 2 && lane == 0) FWN_TR(26, c);
+          if (lane == 0) FWN_TR(26, c);
           if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
           const uint32_t pbase = p_smem(sb);
 #pragma unroll
@@ -583,13 +629,13 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
             }
           }
         }
-        fence_proxy_async_smem();
-        if (warp == 2 && lane == 0) FWN_TR(27, c);
+        if constexpr (!C::P_TMEM) fence_proxy_async_smem();  // shared-memory P -> tensor core reads
+        if (lane == 0) FWN_TR(27, c);
         // Rescale O rows whose reference max grew (only rows that accumulated something: grow needs l > 0).
         const bool rescale = grow;
         if (__any_sync(0xffffffffu, rescale)) {
           const uint32_t prev = gg - 1;
-          if (warp == 2 && lane == 0) FWN_TR(28, c);
+          if (lane == 0) FWN_TR(28, c);
           if (!(ok = mbar_wait(p_empty(prev & 1), (prev >> 1) & 1, abort_flag))) break;
           tc_fence_after();
 #pragma unroll
@@ -606,7 +652,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(sb));
-        if (warp == 2 && lane == 0) FWN_TR(21, c);
+        if (lane == 0) FWN_TR(21, c);
       }
       if (!ok) break;
       g = g0 + nch;
@@ -628,7 +674,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         continue;
       }
       if (!(ok = mbar_wait(o_full, qc & 1, abort_flag))) break;
-      if (warp == 2 && lane == 0) FWN_TR(22, it);
+      if (lane == 0) FWN_TR(22, it);
       tc_fence_after();
 #pragma unroll
       for (int j = 0; j < D / 32; ++j) {
@@ -653,7 +699,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_empty);
-      if (warp == 2 && lane == 0) FWN_TR(23, it);
+      if (lane == 0) FWN_TR(23, it);
       ++qc;
     }
   }

@@ -106,11 +106,9 @@ __global__ void __maxnreg__(168)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ int trace_count;
-  const long long trace_t0 = clock64();
-#define FWN_TR(code, arg) trace_event(p.trace, &trace_count, trace_t0, (code), (arg))
+  int trace_count = 0;  // FWN_TRACE builds: this lane's event count
+#define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
-    trace_count = 0;
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int s = 0; s < C::NK; ++s) {

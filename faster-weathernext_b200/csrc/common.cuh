@@ -25,25 +25,26 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 // ---------------------------------------------------------------------------------------------------
-// Event tracing (builds with -DFWN_TRACE only): CTAs < kTraceCtas append (clock64 delta, role event
-// code, argument) records to a caller buffer of kTraceCtas x kTraceEvents words, for per-role timelines.
+// Event tracing (builds with -DFWN_TRACE only): in CTAs < kTraceCtas, each warp appends (SM clock,
+// event code, argument) records to its own slice of a caller buffer (kTraceCtas x kTraceWarps x
+// kTraceWarpEvents words), counting in a register of the tracing lane, so that an event costs a clock read
+// and one store.
 
 constexpr int kTraceCtas = 4;
-constexpr int kTraceEvents = 4096;
+constexpr int kTraceWarps = 32;
+constexpr int kTraceWarpEvents = 1024;
+constexpr int kTraceEvents = kTraceWarps * kTraceWarpEvents;  // per CTA
 
-__device__ __forceinline__ void trace_event(unsigned long long* buf, int* counter, long long t0, int code,
-                                            int arg) {
+__device__ __forceinline__ void trace_event(unsigned long long* buf, int& count, int code, int arg) {
 #ifdef FWN_TRACE
-  if (buf != nullptr && blockIdx.x < kTraceCtas) {
-    const int i = atomicAdd(counter, 1);
-    if (i < kTraceEvents) {
-      const unsigned long long dt = static_cast<unsigned long long>(clock64() - t0) & 0xFFFFFFFFFFull;
-      buf[blockIdx.x * kTraceEvents + i] = dt | (static_cast<unsigned long long>(code & 0xFF) << 56) |
-                                           (static_cast<unsigned long long>(arg & 0xFFFF) << 40);
-    }
+  if (buf != nullptr && blockIdx.x < kTraceCtas && count < kTraceWarpEvents) {
+    const unsigned long long t = static_cast<unsigned long long>(clock64()) & 0xFFFFFFFFFFull;
+    buf[(blockIdx.x * kTraceWarps + (threadIdx.x >> 5)) * kTraceWarpEvents + count] =
+        t | (static_cast<unsigned long long>(code & 0xFF) << 56) | (static_cast<unsigned long long>(arg & 0xFFFF) << 40);
+    ++count;
   }
 #else
-  (void)buf; (void)counter; (void)t0; (void)code; (void)arg;
+  (void)buf; (void)count; (void)code; (void)arg;
 #endif
 }
 
@@ -289,6 +290,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Registers written by tcgen05.ld are valid only after tcgen05.wait::ld; this empty asm makes every later use
+// depend on a point after the wait, so that the compiler cannot move a use above it.
+template <int N>
+__device__ __forceinline__ void reg_fence(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (tcgen05 format: version 1 at bits 46-47, layout type at 61-63).

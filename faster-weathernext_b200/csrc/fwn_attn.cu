@@ -389,6 +389,9 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale = d.scale;
   p.scale_log2 = d.scale * 1.4426950408889634f;
+#ifdef FWN_TRACE
+  p.trace = trace_buffer();
+#endif
   auto kernel = fwn::attn_bwd_kernel<KIND, D, F32, CH, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
