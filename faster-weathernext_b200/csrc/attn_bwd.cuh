@@ -76,9 +76,13 @@ struct BwdCfg {
   static constexpr int SLOT_C0MN = 1 + (LOAD_C1 ? 1 : 0);
   static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
   static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
+  // bf16: dS / P (packed pairs) go to TMEM over the S / dP columns they are computed from, and the
+  // accumulating MMAs read them as the A operand from tensor memory; S / dP are double-buffered (one 32-wide
+  // tile per chunk), so the elementwise stage of chunk c overlaps the S / dP MMAs of chunk c+1. tf32 keeps
+  // dS / P in shared memory with one S / dP buffer.
+  static constexpr bool G_TMEM = !F32;
   // One stage where the hi / lo (3xTF32) or fp32 head_dim-128 operands leave room for no second one.
   static constexpr bool BIG = X3 || (F32 && D == 128);
-  static constexpr int NS = BIG ? (KIND == kBwdDV ? 2 : 1) : 2;
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
   static constexpr bool G64 = COLS * ES == 64;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
@@ -87,18 +91,30 @@ struct BwdCfg {
   static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (rows are keys)
   static constexpr int STAGE_RAW = VEC_OFF + (ROWS_ARE_KEYS ? CH * 256 : 0);
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int G_BYTES = G64 ? ROWS * 64 : (COLS * ES / 128) * ROWS * 128;  // one dS (or P) tile
+  static constexpr int G_BYTES = G_TMEM ? 0 : G64 ? ROWS * 64 : (COLS * ES / 128) * ROWS * 128;  // one dS (or P) tile
   static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
-  // dS / P buffers: one where two would not leave room for a second CTA per SM (bf16 dK/dV at head_dim 64,
-  // bf16 dQ / dK only at head_dim 128) or would not fit at all (3xTF32 except dV only); else two.
-  static constexpr int NB = ((KIND == kBwdDKV && !F32 && D == 64) || (D == 128 && KIND != kBwdDV) ||
-                             (X3 && KIND != kBwdDV)) ? 1 : 2;
+  // dS / P buffers: the two TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32
+  // except dV only), else two.
+  static constexpr int NB = G_TMEM ? 2 : (X3 && KIND != kBwdDV) ? 1 : 2;
+  static constexpr int n_bar(int ns) { return 2 + 2 * ns + 2 + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
+  static constexpr int smem_bytes(int ns) {
+    return NR * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + 1024;
+  }
+  static constexpr int fit(int ns) { return smem_bytes(ns) <= 227 * 1024 / 2; }
+  // Column stages: bf16 as many as two CTAs per SM leave room for (at most 8), so that the copies of the next
+  // chunks are in flight during the elementwise stage; tf32 2, 3xTF32 and fp32 head_dim 128 one or two.
+  static constexpr int NS = BIG ? (KIND == kBwdDV ? 2 : 1)
+                            : !G_TMEM ? 2
+                            : fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : 2;
   static constexpr int OFF_C = NR * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
-  static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 * NB + 2 + 1 + (X3 ? 1 + NS : 0);
+  static constexpr int N_BAR = n_bar(NS);
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
+  // TMEM: S / dP buffer b at column 64 b (S) and 64 b + 32 (dP) with dS / P in bf16 over their first 16 columns
+  // (bf16); S at 0 and dP at 64 (tf32, CH 32-wide tiles each); then the accumulators.
+  static constexpr int DP_OFF = G_TMEM ? 32 : 64;
   static constexpr int ACC0 = 128;
   static constexpr int ACC1 = 128 + (ACC_DS ? D : 0);
   static constexpr int TMEM_NEED = 128 + (ACC_DS ? D : 0) + (ACC_P ? D : 0);
@@ -114,6 +130,8 @@ struct BwdCfg {
   static_assert(!G64 || (!F32 && CH == 1), "64-byte dS rows hold 32 bf16 columns");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
+  static_assert(!G_TMEM || CH == 1, "TMEM dS / P: one 32-wide tile per chunk");
+  static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
 };
 
 // delta[b, h, r] = sum_d O[b, r, h, d] * dO[b, r, h, d] (fp32); rows r in [n, lse_rows) get 0.
@@ -181,7 +199,10 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   auto c_full = [&](int s) { return bar0 + 16 + 8 * s; };
   auto c_empty = [&](int s) { return bar0 + 16 + 8 * (C::NS + s); };
   const uint32_t bar1 = bar0 + 16 + 16 * C::NS;
+  // One S / dP buffer (sd_full, sd_empty) or, with dS / P in TMEM, two (sd_full_b(0), sd_full_b(1); the buffer
+  // is free again once the accumulating MMAs that read its dS / P are complete: g_empty).
   const uint32_t sd_full = bar1, sd_empty = bar1 + 8;
+  auto sd_full_b = [&](int b) { return bar1 + 8 * b; };
   auto g_full = [&](int b) { return bar1 + 16 + 8 * b; };
   auto g_empty = [&](int b) { return bar1 + 16 + 8 * (C::NB + b); };
   const uint32_t bar2 = bar1 + 16 + 16 * C::NB;
@@ -204,7 +225,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       mbar_init(c_empty(s), 1);
     }
     mbar_init(sd_full, 1);
-    mbar_init(sd_empty, 4);
+    mbar_init(sd_empty, C::G_TMEM ? 1 : 4);
     for (int b = 0; b < C::NB; ++b) {
       mbar_init(g_full(b), 4);
       mbar_init(g_empty(b), 1);
@@ -435,9 +456,15 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
           const uint32_t gg = g0 + c;
           const int st = gg % C::NS;
           const int n_in = min(CH, n_sub - CH * c);
+          const int sdb = gg & 1;
           if (!wait_(X3 ? c_ready(st) : c_full(st), (gg / C::NS) & 1)) return false;
-          if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
+          if constexpr (C::G_TMEM) {
+            if (!wait_(g_empty(sdb), ((gg >> 1) & 1) ^ 1)) return false;
+          } else {
+            if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
+          }
           tc_fence_after();
+          const uint32_t sd_col = C::G_TMEM ? 64 * sdb : 0;
           const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
           const uint32_t sb = stage(st);
   #pragma unroll
@@ -452,12 +479,12 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
                 const uint64_t a = (pass == 2 ? r_lo : r_hi) + ((cb * C::ROWS * 128 + within) >> 4);
                 const uint64_t bd = (pass == 1 ? c_lo : c_hi) + ((cb * C::COLS * 128 + within) >> 4);
-                issue_([&] { mma_ss<F32>(tmem + 64 * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
+                issue_([&] { mma_ss<F32>(tmem + sd_col + C::DP_OFF * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
               }
             }
           }
           issue_([&] {
-            mma_commit(sd_full);
+            mma_commit(C::G_TMEM ? sd_full_b(sdb) : sd_full);
             if (c == nch - 1) mma_commit(r_empty);
           });
           if (!kElect || lane == 0) FWN_TR(11, c);
@@ -481,6 +508,16 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             const int bs = which == 0 ? (F32 ? C::SLOT_C0MN : 0) : (F32 ? C::SLOT_C1MN : C::SLOT_C1);
             const int gi = which == 0 ? G_DS : G_P;
             const uint32_t acc = tmem + (which == 0 ? C::ACC0 : C::ACC1);
+            if constexpr (C::G_TMEM) {
+              // dS (over dP) / P (over S) from TMEM: K = 16 columns per MMA = 8 TMEM columns of packed pairs.
+              const uint32_t a_col = tmem + 64 * gb + (which == 0 ? C::DP_OFF : 0);
+              const uint64_t b_desc = smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
+              for (int kk = 0; kk < ksteps; ++kk)
+                issue_([&] {
+                  mma_ts(acc, a_col + 8 * kk, b_desc + ((kk * C::KSTEP * 128) >> 4), kIdescAcc, (c == 0 && kk == 0) ? 0u : 1u);
+                });
+              continue;
+            }
             const uint64_t g_hi = C::G64 ? smem_desc(g_tile(gb, gi, 0), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 0), 16, 1024);
             const uint64_t g_lo = C::G64 ? smem_desc(g_tile(gb, gi, 1), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 1), 16, 1024);
             const uint64_t b_hi = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
@@ -583,23 +620,28 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         const uint32_t gg = g0 + c;
         const int st = gg % C::NS, gb = gg % C::NB;
         const int n_in = min(CH, n_sub - CH * c);
-        if (!(ok = mbar_wait(sd_full, gg & 1, abort_flag))) break;
+        // bf16: S / dP buffer gb (= gg & 1), whose columns take dS / P; tf32: the one S / dP buffer and shared-memory
+        // dS / P buffer gb.
+        if (!(ok = mbar_wait(C::G_TMEM ? sd_full_b(gb) : sd_full, C::G_TMEM ? (gg >> 1) & 1 : gg & 1, abort_flag))) break;
         if (lane == 0) FWN_TR(20, c);
         if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
-        if (!(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
+        if (!C::G_TMEM && !(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
         if (lane == 0) FWN_TR(29, c);
         tc_fence_after();
         const uint32_t sb = stage(st);
-        // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into the shared-memory
-        // tiles of buffer gb (TMEM is released once the last tile's values are in registers).
+        const uint32_t sd_col = C::G_TMEM ? 64 * gb : 0;
+        // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into TMEM over them (bf16) or into
+        // the shared-memory tiles of buffer gb (tf32: TMEM is released once the last tile's values are in registers).
 #pragma unroll
         for (int j = 0; j < CH; ++j) {
           if (j < n_in) {
             float s[32], dp[32];
-            tmem_ld32(trow + 32 * j, s);
-            if constexpr (C::NEED_DP) tmem_ld32(trow + 64 + 32 * j, dp);
+            tmem_ld32(trow + sd_col + 32 * j, s);
+            if constexpr (C::NEED_DP) tmem_ld32(trow + sd_col + C::DP_OFF + 32 * j, dp);
             tmem_wait_ld();
-            if (j == n_in - 1) {
+            reg_fence(s);
+            if constexpr (C::NEED_DP) reg_fence(dp);
+            if (!C::G_TMEM && j == n_in - 1) {
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(sd_empty);
@@ -640,7 +682,13 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               if (which == 1 && !C::ACC_P) continue;
               const float* src = which == 0 ? dp : s;
               const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
-              if constexpr (C::G64) {
+              if constexpr (C::G_TMEM) {
+                // 32 bf16 columns = 16 TMEM columns of packed pairs over the first half of S (P) or dP (dS).
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(src[2 * i], src[2 * i + 1]);
+                tmem_st16(trow + sd_col + (which == 0 ? C::DP_OFF : 0), pk);
+              } else if constexpr (C::G64) {
                 // 32 bf16 columns = one 64-byte row.
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
@@ -680,7 +728,11 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             }
           }
         }
-        fence_proxy_async_smem();
+        if constexpr (C::G_TMEM) {
+          tmem_wait_st();
+        } else {
+          fence_proxy_async_smem();  // shared-memory dS / P -> tensor core reads
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(g_full(gb));
