@@ -38,8 +38,8 @@ CFG = 3
 # dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
 USEFUL_PER_PAIR = 14
 # DRAM bytes (read + write) per launch at this workload from one ncu capture (profiles/ncu_cfg3_bf16.md).
-NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 152_893_952, "attn_bwd_dq": 201_407_296,
-                                                   "attn_bwd_dkv": 229_749_760}}
+NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 150_649_088, "attn_bwd_dq": 199_965_952,
+                                                   "attn_bwd_dkv": 229_626_880}}
 
 
 def peaks():

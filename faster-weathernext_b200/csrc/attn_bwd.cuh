@@ -88,15 +88,22 @@ struct BwdCfg {
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
   static constexpr int BITS_OFF = NC * XL * C_BYTES;
-  static constexpr int VEC_OFF = BITS_OFF + CH * 512;   // lse / delta of the columns (rows are keys)
+  // lse / delta of the columns (rows are keys): lse times log2 e where the producer stores them through registers
+  // (gathered mode), the natural-log values where they are bulk-copied (tile mode).
+  static constexpr int VEC_OFF = BITS_OFF + CH * 512;
   static constexpr int STAGE_RAW = VEC_OFF + (ROWS_ARE_KEYS ? CH * 256 : 0);
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int G_BYTES = G_TMEM ? 0 : G64 ? ROWS * 64 : (COLS * ES / 128) * ROWS * 128;  // one dS (or P) tile
   static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
-  // dS / P buffers: the two TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32
-  // except dV only), else two.
-  static constexpr int NB = G_TMEM ? 2 : (X3 && KIND != kBwdDV) ? 1 : 2;
-  static constexpr int n_bar(int ns) { return 2 + 2 * ns + 2 + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
+  static constexpr int ACC_COLS = (ACC_DS ? D : 0) + (ACC_P ? D : 0);  // TMEM columns of the accumulators
+  // S / dP buffers (64 TMEM columns each): bf16 three where the accumulators leave room (dQ at head_dim 64), else
+  // two; tf32 one.
+  static constexpr int NSD = !G_TMEM ? 1 : 3 * 64 + ACC_COLS <= 256 ? 3 : 2;
+  // dS / P buffers: the TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32 except
+  // dV only), else two.
+  static constexpr int NB = G_TMEM ? NSD : (X3 && KIND != kBwdDV) ? 1 : 2;
+  static constexpr int SDB = NSD < 2 ? 2 : NSD;  // barrier slots: sd_full / sd_empty, or one sd_full per buffer
+  static constexpr int n_bar(int ns) { return 2 + 2 * ns + SDB + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
   static constexpr int smem_bytes(int ns) {
     return NR * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + 1024;
   }
@@ -115,9 +122,9 @@ struct BwdCfg {
   // TMEM: S / dP buffer b at column 64 b (S) and 64 b + 32 (dP) with dS / P in bf16 over their first 16 columns
   // (bf16); S at 0 and dP at 64 (tf32, CH 32-wide tiles each); then the accumulators.
   static constexpr int DP_OFF = G_TMEM ? 32 : 64;
-  static constexpr int ACC0 = 128;
-  static constexpr int ACC1 = 128 + (ACC_DS ? D : 0);
-  static constexpr int TMEM_NEED = 128 + (ACC_DS ? D : 0) + (ACC_P ? D : 0);
+  static constexpr int ACC0 = G_TMEM ? 64 * NSD : 128;
+  static constexpr int ACC1 = ACC0 + (ACC_DS ? D : 0);
+  static constexpr int TMEM_NEED = ACC0 + ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
@@ -131,6 +138,7 @@ struct BwdCfg {
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
   static_assert(!G_TMEM || CH == 1, "TMEM dS / P: one 32-wide tile per chunk");
+  static_assert(!G_TMEM || TMEM_NEED <= 256, "TMEM dS / P: two CTAs per SM");
   static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
 };
 
@@ -199,13 +207,13 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   auto c_full = [&](int s) { return bar0 + 16 + 8 * s; };
   auto c_empty = [&](int s) { return bar0 + 16 + 8 * (C::NS + s); };
   const uint32_t bar1 = bar0 + 16 + 16 * C::NS;
-  // One S / dP buffer (sd_full, sd_empty) or, with dS / P in TMEM, two (sd_full_b(0), sd_full_b(1); the buffer
-  // is free again once the accumulating MMAs that read its dS / P are complete: g_empty).
+  // One S / dP buffer (sd_full, sd_empty) or, with dS / P in TMEM, NSD (sd_full_b(b); a buffer is free again once
+  // the accumulating MMAs that read its dS / P are complete: g_empty).
   const uint32_t sd_full = bar1, sd_empty = bar1 + 8;
   auto sd_full_b = [&](int b) { return bar1 + 8 * b; };
-  auto g_full = [&](int b) { return bar1 + 16 + 8 * b; };
-  auto g_empty = [&](int b) { return bar1 + 16 + 8 * (C::NB + b); };
-  const uint32_t bar2 = bar1 + 16 + 16 * C::NB;
+  auto g_full = [&](int b) { return bar1 + 8 * C::SDB + 8 * b; };
+  auto g_empty = [&](int b) { return bar1 + 8 * C::SDB + 8 * (C::NB + b); };
+  const uint32_t bar2 = bar1 + 8 * C::SDB + 16 * C::NB;
   const uint32_t acc_full = bar2, acc_empty = bar2 + 8, drain = bar2 + 16;
   // 3xTF32: the converter's "split done" barriers; the MMA waits on these instead of the TMA ones.
   const uint32_t r_ready = bar2 + 24;
@@ -223,8 +231,12 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       mbar_init(c_full(s), (GATHER && C::ROWS_ARE_KEYS) ? 2 : 1);
       mbar_init(c_empty(s), 1);
     }
-    mbar_init(sd_full, 1);
-    mbar_init(sd_empty, C::G_TMEM ? 1 : 4);
+    if constexpr (C::G_TMEM) {
+      for (int b = 0; b < C::NSD; ++b) mbar_init(sd_full_b(b), 1);
+    } else {
+      mbar_init(sd_full, 1);
+      mbar_init(sd_empty, 4);
+    }
     for (int b = 0; b < C::NB; ++b) {
       mbar_init(g_full(b), 4);
       mbar_init(g_empty(b), 1);
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             for (int s = 0; s < CH; ++s) {
               if (s < n_in) {
                 const size_t vo = static_cast<size_t>(bh) * p.lse_rows + meta.v[s];
-                vec_lse[s] = __ldg(p.lse + vo);
+                vec_lse[s] = __ldg(p.lse + vo) * 1.4426950408889634f;  // log2 units for the elementwise warps
                 vec_delta[s] = __ldg(p.delta + vo);
               }
             }
@@ -447,10 +459,10 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
           const uint32_t gg = g0 + c;
           const int st = gg % C::NS;
           const int n_in = min(CH, n_sub - CH * c);
-          const int sdb = gg & 1;
+          const int sdb = gg % C::NSD;
           if (!wait_(X3 ? c_ready(st) : c_full(st), (gg / C::NS) & 1)) return false;
           if constexpr (C::G_TMEM) {
-            if (!wait_(g_empty(sdb), ((gg >> 1) & 1) ^ 1)) return false;
+            if (!wait_(g_empty(sdb), ((gg / C::NSD) & 1) ^ 1)) return false;
           } else {
             if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
           }
@@ -611,9 +623,9 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         const uint32_t gg = g0 + c;
         const int st = gg % C::NS, gb = gg % C::NB;
         const int n_in = min(CH, n_sub - CH * c);
-        // bf16: S / dP buffer gb (= gg & 1), whose columns take dS / P; tf32: the one S / dP buffer and shared-memory
-        // dS / P buffer gb.
-        if (!(ok = mbar_wait(C::G_TMEM ? sd_full_b(gb) : sd_full, C::G_TMEM ? (gg >> 1) & 1 : gg & 1, abort_flag))) break;
+        // bf16: S / dP buffer gb (= gg % NSD), whose columns take dS / P; tf32: the one S / dP buffer and
+        // shared-memory dS / P buffer gb.
+        if (!(ok = mbar_wait(C::G_TMEM ? sd_full_b(gb) : sd_full, C::G_TMEM ? (gg / C::NB) & 1 : gg & 1, abort_flag))) break;
         if (lane == 0) FWN_TR(20, c);
         if (!(ok = mbar_wait(c_full(st), (gg / C::NS) & 1, abort_flag))) break;
         if (!C::G_TMEM && !(ok = mbar_wait(g_empty(gb), ((gg / C::NB) & 1) ^ 1, abort_flag))) break;
@@ -629,6 +641,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             float s[32], dp[32];
             tmem_ld32(trow + sd_col + 32 * j, s);
             if constexpr (C::NEED_DP) tmem_ld32(trow + sd_col + C::DP_OFF + 32 * j, dp);
+            const uint32_t w = ld_shared_u32(sb + C::BITS_OFF + j * 512 + row * 4);  // while S / dP are read
             tmem_wait_ld();
             reg_fence(s);
             if constexpr (C::NEED_DP) reg_fence(dp);
@@ -637,27 +650,48 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               __syncwarp();
               if (lane == 0) mbar_arrive(sd_empty);
             }
-            const uint32_t w = ld_shared_u32(sb + C::BITS_OFF + j * 512 + row * 4);
             const uint32_t any = __reduce_or_sync(0xffffffffu, w);
-            // Groups of 8 columns that no row of the warp may attend to are skipped by the whole warp.
+            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+            // Groups of 8 columns that no row of the warp may attend to are skipped by the whole warp. Column
+            // pairs in f32x2 arithmetic; the columns' lse (log2 units, see the producer) and delta (rows are
+            // keys) as broadcast 16-byte shared-memory loads.
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               if ((any >> (8 * g)) & 0xFFu) {
+                float l2v[8], dlv[8];
+                if constexpr (C::ROWS_ARE_KEYS) {
+                  const uint32_t va = sb + C::VEC_OFF + j * 256 + g * 32;
+                  const float4 a0 = ld_shared_f32x4(va), a1 = ld_shared_f32x4(va + 16);
+                  const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                for (int ii = 0; ii < 8; ++ii) {
-                  const int i = 8 * g + ii;
-                  float l2, dl;
-                  if constexpr (C::ROWS_ARE_KEYS) {
-                    l2 = ld_shared_f32(sb + C::VEC_OFF + j * 256 + i * 4) * kLog2e;
-                    dl = C::NEED_DP ? ld_shared_f32(sb + C::VEC_OFF + j * 256 + 128 + i * 4) : 0.f;
-                  } else {
-                    l2 = lse2_row;
-                    dl = delta_row;
+                  for (int ii = 0; ii < 8; ++ii) l2v[ii] = GATHER ? av[ii] : av[ii] * kLog2e;
+                  if constexpr (C::NEED_DP) {
+                    const float4 d0 = ld_shared_f32x4(va + 128), d1 = ld_shared_f32x4(va + 144);
+                    const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+                    for (int ii = 0; ii < 8; ++ii) dlv[ii] = dv[ii];
                   }
-                  const float e = ex2(fmaf(s[i], p.scale_log2, -l2));
-                  const float pv = (w & (1u << i)) ? e : 0.f;
-                  s[i] = pv;
-                  if constexpr (C::NEED_DP) dp[i] = pv * (dp[i] - dl);
+                } else {
+#pragma unroll
+                  for (int ii = 0; ii < 8; ++ii) {
+                    l2v[ii] = lse2_row;
+                    dlv[ii] = delta_row;
+                  }
+                }
+#pragma unroll
+                for (int ii = 0; ii < 8; ii += 2) {
+                  const int i = 8 * g + ii;
+                  const float2 x = ffma2(make_float2(s[i], s[i + 1]), sc2, make_float2(-l2v[ii], -l2v[ii + 1]));
+                  const float e0 = ex2(x.x), e1 = ex2(x.y);
+                  const float p0 = (w & (1u << i)) ? e0 : 0.f, p1 = (w & (1u << (i + 1))) ? e1 : 0.f;
+                  s[i] = p0;
+                  s[i + 1] = p1;
+                  if constexpr (C::NEED_DP) {
+                    const float2 ds = fmul2(make_float2(p0, p1),
+                                            fsub2(make_float2(dp[i], dp[i + 1]), make_float2(dlv[ii], dlv[ii + 1])));
+                    dp[i] = ds.x;
+                    dp[i + 1] = ds.y;
+                  }
                 }
               } else {
 #pragma unroll
