@@ -286,6 +286,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           if (!(ok = warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
           if (C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
           if (!(ok = warp_wait(s_empty(sb), ((gg / C::NSB) & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(13, c);
           tc_fence_after();
           const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
           const uint64_t c0desc = smem_desc(c0_slot(gg % C::N0), 16, 1024);
@@ -321,6 +322,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           if (!(ok = warp_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
           if (!C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
           if (c == 1 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(14, c - 1);
           tc_fence_after();
           const uint64_t bdesc = smem_desc(C::ACC_ON_C0 ? c0_slot(gg % C::N0) : c1_slot(gg % C::N1), C::COLS * 128, 1024);
           const uint32_t gcol = tmem + C::G_COL + 64 * gb;
@@ -380,7 +382,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
         if (c + 1 < nch) nw = word(c + 1);
         const uint32_t a = __reduce_or_sync(0xffffffffu, w);
         if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
-        if (warp == 2 && lane == 0) FWN_TR(20, c);
+        if (lane == 0) FWN_TR(20, c);
         tc_fence_after();
         // S (and dP) of this tile -> registers; then the buffer is released for the next S MMA.
         float s[32], dp[32];
@@ -452,7 +454,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           __syncwarp();
           if (lane == 0) mbar_arrive(v_empty(gg % C::NVEC_RING));
         }
-        if (warp == 2 && lane == 0) FWN_TR(26, c);
+        if (lane == 0) FWN_TR(26, c);
         // G buffer free once the accumulating MMA of chunk gg-2 is complete.
         if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
         if (j < n_in) tmem_st16(trow + C::G_COL + 64 * gb + 16 * j, pk);
@@ -460,7 +462,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(g_full(gb));
-        if (warp == 2 && lane == 0) FWN_TR(21, c);
+        if (lane == 0) FWN_TR(21, c);
       }
       if (!ok) break;
       g = g0 + nch;

@@ -257,6 +257,7 @@ __global__ void __maxnreg__(168)
           const int n_in = min(C::CH, n_sub - C::CH * c);
           if (!(ok = warp_wait(k_full(gg % C::NK), (gg / C::NK) & 1, abort_flag))) break;
           if (!(ok = warp_wait(s_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(13, c);
           tc_fence_after();
           const uint32_t idesc_s = instr_desc(false, 128, 32 * n_in, false, false);
           const uint64_t kdesc = smem_desc(k_slot(gg % C::NK), 16, 1024);
@@ -281,6 +282,7 @@ __global__ void __maxnreg__(168)
           if (!(ok = warp_wait(p_full(pbuf), (gg >> 1) & 1, abort_flag))) break;
           if (!(ok = warp_wait(v_full(gg % C::NV), (gg / C::NV) & 1, abort_flag))) break;
           if (c == 1 && !(ok = warp_wait(o_empty, (qc & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(14, c - 1);
           tc_fence_after();
           const uint64_t vdesc = smem_desc(v_slot(gg % C::NV), C::KEYS * 128, 1024);
           const uint32_t pcol = tmem + C::P_COL + 64 * pbuf;
@@ -349,7 +351,7 @@ __global__ void __maxnreg__(168)
         const int j0 = 2 * half;  // this half's first tile of the chunk
         // S columns of this half -> registers; the S buffer is free for the next S MMA right away.
         if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
-        if (warp == 2 && lane == 0) FWN_TR(20, c);
+        if (lane == 0) FWN_TR(20, c);
         tc_fence_after();
         float s[64];
         if (j0 < n_in) tmem_ld32(trow + sb * C::KEYS + 64 * half, *reinterpret_cast<float(*)[32]>(&s[0]));
@@ -418,7 +420,7 @@ __global__ void __maxnreg__(168)
           if (fresh) m_use = fmaxf(hm, om) * c2;
         }
         float sum = exps(m_use);
-        if (warp == 2 && lane == 0) FWN_TR(26, c);
+        if (lane == 0) FWN_TR(26, c);
         // A half-row sum above 2^16 means some p may exceed 2^16 (the accumulators stay far from fp32
         // overflow below that): then the pair redoes the chunk exactly against the chunk's max. The flag is
         // posted now and collected after P is in TMEM.
@@ -429,7 +431,7 @@ __global__ void __maxnreg__(168)
         if (lane == 0) mbar_arrive(xbar);
         // P buffer free once the P V MMA that last read it (chunk gg-2) is complete.
         if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-        if (warp == 2 && lane == 0) FWN_TR(29, c);
+        if (lane == 0) FWN_TR(29, c);
         const uint32_t pcol = trow + C::P_COL + 64 * sb + 32 * half;
         if (j0 < n_in) tmem_st32(pcol, *reinterpret_cast<const float(*)[32]>(pk));
         if (!(ok = mbar_wait(xbar, xk & 1, abort_flag))) break;
@@ -438,7 +440,7 @@ __global__ void __maxnreg__(168)
         bool grow = false;
         float corr = 1.f;
         if (bad) {
-          if (warp == 2 && lane == 0) FWN_TR(28, c);
+          if (lane == 0) FWN_TR(28, c);
           const float hm = half_max();
           float om;
           if (!(ok = exchange(1, hm, om))) break;
@@ -480,7 +482,7 @@ __global__ void __maxnreg__(168)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(sb));
-        if (warp == 2 && lane == 0) FWN_TR(21, c);
+        if (lane == 0) FWN_TR(21, c);
       }
       if (!ok) break;
       g = g0 + nch;

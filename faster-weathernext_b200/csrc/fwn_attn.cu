@@ -666,8 +666,10 @@ fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32
   return ok();
 }
 
-fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
-                              const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
+namespace {
+
+fwn_status cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample, const int32_t* out_node,
+                          const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
   if (rows < 0 || rows_per_sample <= 0 || !(eps > 0.f))
     return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld, rows_per_sample=%d or eps", static_cast<long long>(rows),
                 rows_per_sample);
@@ -677,10 +679,27 @@ fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t r
   if (rows > 0 && (!x || !scale_offset || !out)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
   if (rows > 0 && (!aligned16(x) || !aligned16(scale_offset) || !aligned16(out)))
     return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
-  cudaError_t e = fwn::launch_cond_layernorm(x, rows, d, rows_per_sample, scale_offset, eps, out,
+  if (rows % rows_per_sample != 0)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "rows=%lld is not a multiple of rows_per_sample=%d",
+                static_cast<long long>(rows), rows_per_sample);
+  cudaError_t e = fwn::launch_cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out,
                                              out_dtype == FWN_DTYPE_BF16, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cond_layernorm");
   return ok();
+}
+
+}  // namespace
+
+fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                              const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
+  return cond_layernorm(x, rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype, stream);
+}
+
+fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                      const int32_t* out_node, const float* scale_offset, float eps, void* out,
+                                      int32_t out_dtype, void* stream) {
+  if (rows > 0 && !out_node) return fail(FWN_ERR_INVALID_ARGUMENT, "null out_node");
+  return cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream);
 }
 
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }

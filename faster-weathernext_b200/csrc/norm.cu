@@ -3,7 +3,9 @@
 // offset): y = (x - mean) / sqrt(var + eps) * (1 + scale[s]) + offset[s], x float32 [rows, d], s = row / rows
 // per sample, y bf16 or float32. One warp per row, the row in registers (d / 32 values per lane, float4
 // loads), two passes over registers for the mean and the variance; HBM-bound (4 d bytes read, 2 d or 4 d
-// written per row).
+// written per row). With an output node map (the node permutation of the reference's transformer, patch.py:
+// 275-276, 291-292, fused into the final norm's store), row r of sample s goes to row s * rows_per_sample +
+// out_node[r % rows_per_sample]; a map entry outside [0, rows_per_sample) drops its row (no write).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -16,6 +18,7 @@ namespace {
 template <int D, bool BF16_OUT>
 __global__ void __launch_bounds__(256) cond_layernorm_kernel(const float* __restrict__ x, int64_t rows,
                                                               int rows_per_sample,
+                                                              const int32_t* __restrict__ out_node,
                                                               const float* __restrict__ scale_offset, float eps,
                                                               void* __restrict__ out) {
   constexpr int V = D / 128;  // float4 per lane
@@ -42,7 +45,14 @@ __global__ void __launch_bounds__(256) cond_layernorm_kernel(const float* __rest
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
   const float rstd = rsqrtf(sq * (1.0f / D) + eps);
-  const float* so = scale_offset + static_cast<int64_t>(row / rows_per_sample) * 2 * D;
+  const int64_t sample = row / rows_per_sample;
+  const float* so = scale_offset + sample * 2 * D;
+  int64_t orow = row;
+  if (out_node != nullptr) {
+    const int node = __ldg(out_node + (row - sample * rows_per_sample));
+    if (node < 0 || node >= rows_per_sample) return;  // not a permutation entry: no write (whole warp)
+    orow = sample * rows_per_sample + node;
+  }
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int col = 4 * (lane + 32 * i);
@@ -58,35 +68,35 @@ __global__ void __launch_bounds__(256) cond_layernorm_kernel(const float* __rest
       uint2 packed;
       packed.x = *reinterpret_cast<const uint32_t*>(&lo);
       packed.y = *reinterpret_cast<const uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + row * D)[lane + 32 * i] = packed;
+      reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + orow * D)[lane + 32 * i] = packed;
     } else {
-      reinterpret_cast<float4*>(static_cast<float*>(out) + row * D)[lane + 32 * i] = y;
+      reinterpret_cast<float4*>(static_cast<float*>(out) + orow * D)[lane + 32 * i] = y;
     }
   }
 }
 
 template <int D>
-cudaError_t launch(const float* x, int64_t rows, int rows_per_sample, const float* so, float eps, void* out,
-                   bool bf16_out, cudaStream_t stream) {
+cudaError_t launch(const float* x, int64_t rows, int rows_per_sample, const int32_t* out_node, const float* so,
+                   float eps, void* out, bool bf16_out, cudaStream_t stream) {
   const int64_t threads = rows * 32;
   const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
   if (bf16_out)
-    cond_layernorm_kernel<D, true><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, so, eps, out);
+    cond_layernorm_kernel<D, true><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, out_node, so, eps, out);
   else
-    cond_layernorm_kernel<D, false><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, so, eps, out);
+    cond_layernorm_kernel<D, false><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, out_node, so, eps, out);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_cond_layernorm(const float* x, int64_t rows, int d, int rows_per_sample, const float* so,
-                                  float eps, void* out, bool bf16_out, cudaStream_t stream) {
+cudaError_t launch_cond_layernorm(const float* x, int64_t rows, int d, int rows_per_sample, const int32_t* out_node,
+                                  const float* so, float eps, void* out, bool bf16_out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   switch (d) {
-    case 128: return launch<128>(x, rows, rows_per_sample, so, eps, out, bf16_out, stream);
-    case 256: return launch<256>(x, rows, rows_per_sample, so, eps, out, bf16_out, stream);
-    case 512: return launch<512>(x, rows, rows_per_sample, so, eps, out, bf16_out, stream);
-    case 1024: return launch<1024>(x, rows, rows_per_sample, so, eps, out, bf16_out, stream);
+    case 128: return launch<128>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, stream);
+    case 256: return launch<256>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, stream);
+    case 512: return launch<512>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, stream);
+    case 1024: return launch<1024>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -14,6 +14,11 @@ jax.nn.gelu's default; Glorot-uniform weights from a seed), not a numerical copy
 projections run as cuBLAS GEMMs; the attention is faster_weathernext's kernel (q, k, v are strided views of one
 fused projection, no copies). Without autograd (inference), each norm is one fused kernel and bias + GELU run
 in the GEMM epilogue.
+
+Node order: the reference's transformer gathers the latents into the mask's node order with `perm` before the
+first block and takes them back with argsort(perm) after the final norm (patch.py:275-276, 291-292). `forward`
+does the same when given `perm`; on the inference path the gather is the residual stream's initial copy and the
+un-permutation is fused into the final norm's store (fwn_cond_layernorm_scatter).
 """
 
 import dataclasses
@@ -80,14 +85,22 @@ class Processor(torch.nn.Module):
     return y * (1 + scale) + offset
 
   def forward(self, x: torch.Tensor, cond: torch.Tensor, tiles: "tiled_attn.AttentionTiles",
-              dtype=torch.bfloat16) -> torch.Tensor:
-    """x [B, n, d_model] (float32 residual stream), cond [B, cond_dim] -> [B, n, d_model]."""
+              dtype=torch.bfloat16, perm: torch.Tensor = None) -> torch.Tensor:
+    """x [B, n, d_model] (float32 residual stream), cond [B, cond_dim] -> [B, n, d_model]. `perm` (int, [n],
+    a permutation of the nodes; optional): `tiles` is built in the permuted order, node i of the blocks is node
+    perm[i] of x, and the output is returned in x's order."""
+    if perm is not None:
+      perm = torch.as_tensor(perm, device=x.device).to(torch.int64)
+      if perm.shape != (x.shape[1],):
+        raise ValueError(f"perm has shape {tuple(perm.shape)}, expected ({x.shape[1]},)")
     if not torch.is_grad_enabled() and dtype == torch.bfloat16 and x.shape[-1] in (128, 256, 512, 1024):
-      return self._forward_fused(x, cond, tiles)
+      return self._forward_fused(x, cond, tiles, perm)
     cfg = self.cfg
     b, n, d = x.shape
     scale = cfg.head_dim ** -0.5
     c = cond.to(dtype)
+    if perm is not None:
+      x = x.index_select(1, perm)
     for blk in self.blocks:
       h = self._cond_norm(x, c, blk.cond1).to(dtype)
       qkv = (h @ blk.w_qkv.to(dtype)).view(b, n, cfg.heads, 3, cfg.head_dim)
@@ -97,9 +110,12 @@ class Processor(torch.nn.Module):
       h = self._cond_norm(x, c, blk.cond2).to(dtype)
       m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype), approximate="tanh")
       x = x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
-    return self._cond_norm(x, c, self.cond_final).to(x.dtype)
+    y = self._cond_norm(x, c, self.cond_final).to(x.dtype)
+    if perm is not None:
+      y = y.index_select(1, torch.argsort(perm))
+    return y
 
-  def _forward_fused(self, x, cond, tiles):
+  def _forward_fused(self, x, cond, tiles, perm=None):
     """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm
     (fwn_cond_layernorm), bias and GELU in the GEMM epilogue (cuBLASLt), and the residual stream updated in
     place (float32 += bf16 in one pass)."""
@@ -110,7 +126,8 @@ class Processor(torch.nn.Module):
     stream = torch.cuda.current_stream().cuda_stream
     bf = torch.bfloat16
     scale = cfg.head_dim ** -0.5
-    xs = x.contiguous().clone()
+    # The residual stream: a copy of x, gathered into the blocks' node order when permuted.
+    xs = x.index_select(1, perm).contiguous() if perm is not None else x.contiguous().clone()
     x2 = xs.view(m_rows, d)
     h = torch.empty(m_rows, d, dtype=bf, device=x.device)
     cf = cond.float()
@@ -129,7 +146,14 @@ class Processor(torch.nn.Module):
       mlp = torch._addmm_activation(blk.b1.to(bf), h, blk.w1.to(bf), use_gelu=True)
       x2.add_(torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf)))
     out = torch.empty_like(xs)
-    norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32)
+    if perm is None:
+      norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32)
+    else:
+      # Final norm with the un-permutation fused into its store: row i of each sample goes to row perm[i].
+      so = (cf @ self.cond_final.float()).contiguous()
+      out_node = perm.to(torch.int32).contiguous()
+      _lib.check(lib.fwn_cond_layernorm_scatter(x2.data_ptr(), m_rows, d, n, out_node.data_ptr(), so.data_ptr(),
+                                                1e-5, out.data_ptr(), _lib.DTYPE_F32, stream))
     return out
 
   def gemm_flops_per_forward(self, n: int) -> float:

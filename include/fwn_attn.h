@@ -180,6 +180,14 @@ FWN_API fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, i
                                       const float* scale_offset, float eps, void* out, int32_t out_dtype,
                                       void* stream);
 
+/* The same norm with the node un-permutation of the reference's transformer fused into the store
+ * (src/faster_weathernext/patch.py:291-292, x = take(x, argsort(perm)) after the final norm): row i of each sample
+ * goes to row out_node[i] of that sample, out_node int32 [rows_per_sample], a permutation of
+ * [0, rows_per_sample) (pass the forward permutation perm itself). An entry outside that range drops its row. */
+FWN_API fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                              const int32_t* out_node, const float* scale_offset, float eps,
+                                              void* out, int32_t out_dtype, void* stream);
+
 /* ---- attention --------------------------------------------------------------------------------------- */
 
 /* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)

@@ -110,3 +110,64 @@ def test_cond_layernorm_kernel_matches_torch(cuda):
       _lib.check(lib.fwn_cond_layernorm(x.data_ptr(), b * n, d, n, so.data_ptr(), 1e-5, out.data_ptr(), dt, 0))
       torch.cuda.synchronize()
       assert float((out.float() - ref).abs().max() / ref.abs().max()) < tol, (d, dt)
+
+
+def test_cond_layernorm_scatter_kernel(cuda):
+  """fwn_cond_layernorm_scatter: the conditioned norm with row i of each sample stored at row out_node[i]
+  (the un-permutation after the final norm, patch.py:291-292), bit-equal to the plain kernel followed by the
+  scatter; an out-of-range entry drops its row."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  g = torch.Generator(device=cuda).manual_seed(2)
+  b, n, d = 2, 300, 512
+  x = torch.randn(b * n, d, device=cuda, generator=g)
+  so = torch.randn(b, 2 * d, device=cuda, generator=g) * 0.2
+  perm = torch.randperm(n, device=cuda, generator=g).to(torch.int32)
+  plain = torch.empty(b * n, d, device=cuda)
+  _lib.check(lib.fwn_cond_layernorm(x.data_ptr(), b * n, d, n, so.data_ptr(), 1e-5, plain.data_ptr(),
+                                    _lib.DTYPE_F32, 0))
+  out = torch.full((b * n, d), 7.0, device=cuda)
+  _lib.check(lib.fwn_cond_layernorm_scatter(x.data_ptr(), b * n, d, n, perm.data_ptr(), so.data_ptr(), 1e-5,
+                                            out.data_ptr(), _lib.DTYPE_F32, 0))
+  expected = torch.empty_like(plain).view(b, n, d)
+  expected[:, perm.long()] = plain.view(b, n, d)
+  torch.cuda.synchronize()
+  assert torch.equal(out.view(b, n, d), expected)
+  # An entry outside [0, n) drops its row; the row it would have replaced keeps its old content.
+  bad = perm.clone()
+  victim = int(bad[5])
+  bad[5] = n + 3
+  out2 = torch.full((b * n, d), 7.0, device=cuda)
+  _lib.check(lib.fwn_cond_layernorm_scatter(x.data_ptr(), b * n, d, n, bad.data_ptr(), so.data_ptr(), 1e-5,
+                                            out2.data_ptr(), _lib.DTYPE_F32, 0))
+  torch.cuda.synchronize()
+  assert torch.all(out2.view(b, n, d)[:, victim] == 7.0)
+  assert _lib.lib().fwn_cond_layernorm_scatter(x.data_ptr(), b * n, d, n, None, so.data_ptr(), 1e-5,
+                                               out2.data_ptr(), _lib.DTYPE_F32, 0) != 0
+
+
+def test_processor_node_permutation(cuda):
+  """forward(x, perm=perm) = forward(x[:, perm])[:, argsort(perm)] (patch.py:275-276, 291-292): bit-equal on the
+  inference path (gather as the residual copy, un-permutation fused into the final norm), and the autograd
+  path agrees within bf16 rounding."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor, ProcessorConfig
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = ProcessorConfig(layers=2)
+  model = Processor(cfg, seed=7, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(8)
+  x = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(2, cfg.cond_dim, device=cuda, generator=g)
+  perm = torch.randperm(n, device=cuda, generator=g)
+  inv = torch.argsort(perm)
+  with torch.no_grad():
+    y_perm = model(x, c, tiles, perm=perm)
+    y_ref = model(x[:, perm], c, tiles)[:, inv]
+  assert torch.equal(y_perm, y_ref)
+  y_grad = model(x, c, tiles, perm=perm)
+  assert _rel(y_grad.detach(), y_ref) < 1e-2
+  with pytest.raises(ValueError):
+    model(x, c, tiles, perm=perm[:-1])
