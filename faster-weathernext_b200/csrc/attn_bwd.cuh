@@ -76,11 +76,11 @@ struct BwdCfg {
   static constexpr int SLOT_C0MN = 1 + (LOAD_C1 ? 1 : 0);
   static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
   static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
-  // bf16: dS / P (packed pairs) go to TMEM over the S / dP columns they are computed from, and the
-  // accumulating MMAs read them as the A operand from tensor memory; S / dP are double-buffered (one 32-wide
-  // tile per chunk), so the elementwise stage of chunk c overlaps the S / dP MMAs of chunk c+1. tf32 keeps
-  // dS / P in shared memory with one S / dP buffer.
-  static constexpr bool G_TMEM = !F32;
+  // bf16 and tf32: dS / P (bf16 packed pairs, or fp32) go to TMEM over the S / dP columns they are computed from,
+  // and the accumulating MMAs read them as the A operand from tensor memory; S / dP are double-buffered (one
+  // 32-wide tile per chunk), so the elementwise stage of chunk c overlaps the S / dP MMAs of chunk c+1. 3xTF32
+  // keeps dS / P (hi and lo copies) in shared memory with one S / dP buffer.
+  static constexpr bool G_TMEM = !X3;
   // One stage where the hi / lo (3xTF32) or fp32 head_dim-128 operands leave room for no second one.
   static constexpr bool BIG = X3 || (F32 && D == 128);
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
@@ -104,23 +104,24 @@ struct BwdCfg {
   static constexpr int NB = G_TMEM ? NSD : (X3 && KIND != kBwdDV) ? 1 : 2;
   static constexpr int SDB = NSD < 2 ? 2 : NSD;  // barrier slots: sd_full / sd_empty, or one sd_full per buffer
   static constexpr int n_bar(int ns) { return 2 + 2 * ns + SDB + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
+  // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
   static constexpr int smem_bytes(int ns) {
-    return NR * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + 1024;
+    return NR * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16;
   }
-  static constexpr int fit(int ns) { return smem_bytes(ns) <= 227 * 1024 / 2; }
-  // Column stages: bf16 as many as two CTAs per SM leave room for (at most 8), so that the copies of the next
-  // chunks are in flight during the elementwise stage; tf32 2, 3xTF32 and fp32 head_dim 128 one or two.
-  static constexpr int NS = BIG ? (KIND == kBwdDV ? 2 : 1)
-                            : !G_TMEM ? 2
-                            : fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : 2;
+  // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
+  static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
+  // Column stages: as many as fit (at most 8), so that the copies of the next chunks are in flight during the
+  // elementwise stage; 3xTF32 one or two.
+  static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1)
+                            : fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
   static constexpr int OFF_C = NR * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
   static constexpr int N_BAR = n_bar(NS);
-  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
-  // TMEM: S / dP buffer b at column 64 b (S) and 64 b + 32 (dP) with dS / P in bf16 over their first 16 columns
-  // (bf16); S at 0 and dP at 64 (tf32, CH 32-wide tiles each); then the accumulators.
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
+  // TMEM: S / dP buffer b at column 64 b (S) and 64 b + 32 (dP) with P / dS over them (bf16: packed pairs in their
+  // first 16 columns; tf32: all 32); 3xTF32 S at 0 and dP at 64; then the accumulators.
   static constexpr int DP_OFF = G_TMEM ? 32 : 64;
   static constexpr int ACC0 = G_TMEM ? 64 * NSD : 128;
   static constexpr int ACC1 = ACC0 + (ACC_DS ? D : 0);
@@ -191,9 +192,14 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                     const BwdParams p) {
   // tm_c*r: 4D maps of 32-row boxes (gathered mode: tiles whose 32 columns are consecutive).
   using C = BwdCfg<KIND, D, F32, CH, X3>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  uint8_t* smem = smem_bwd;
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {
+    // The tile layouts need 1024-byte aligned shared memory; report and leave (uniformly, before any wait).
+    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
+    return;
+  }
   // Row operand i (hi, or the operand itself), its lo copy at +NR; column slot s of a stage, lo copy at +NC.
   auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR + i) * C::R_BYTES; };
   auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };
@@ -513,11 +519,14 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             const uint32_t acc = tmem + (which == 0 ? C::ACC0 : C::ACC1);
             if constexpr (C::G_TMEM) {
               // dS (over dP) / P (over S) from TMEM: K = 16 columns per MMA = 8 TMEM columns of packed pairs.
+              // K = 16 bf16 (8 columns of pairs) or 8 tf32 (8 columns) per MMA.
               const uint32_t a_col = tmem + 64 * gb + (which == 0 ? C::DP_OFF : 0);
-              const uint64_t b_desc = smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
+              const uint64_t b_desc = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
+                                          : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
               for (int kk = 0; kk < ksteps; ++kk)
                 issue_([&] {
-                  mma_ts(acc, a_col + 8 * kk, b_desc + ((kk * C::KSTEP * 128) >> 4), kIdescAcc, (c == 0 && kk == 0) ? 0u : 1u);
+                  mma_ts<F32>(acc, a_col + 8 * kk, b_desc + ((kk * C::KSTEP * 128) >> 4), kIdescAcc,
+                              (c == 0 && kk == 0) ? 0u : 1u);
                 });
               continue;
             }
@@ -707,7 +716,11 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               if (which == 1 && !C::ACC_P) continue;
               const float* src = which == 0 ? dp : s;
               const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
-              if constexpr (C::G_TMEM) {
+              if constexpr (C::G_TMEM && F32) {
+                // 32 fp32 columns over S (P) or dP (dS).
+                tmem_st32(trow + sd_col + (which == 0 ? C::DP_OFF : 0),
+                          *reinterpret_cast<const float(*)[32]>(src));
+              } else if constexpr (C::G_TMEM) {
                 // 32 bf16 columns = 16 TMEM columns of packed pairs over the first half of S (P) or dP (dS).
                 uint32_t pk[16];
 #pragma unroll

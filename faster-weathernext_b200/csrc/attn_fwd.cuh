@@ -65,31 +65,31 @@ struct FwdCfg {
   // Stage: K, V, (3xTF32: K_lo, V_lo), mask words.
   static constexpr int BITS_OFF = (X3 ? 4 : 2) * KV_BYTES;
   static constexpr int STAGE_BYTES = (BITS_OFF + CH * 512 + 1023) / 1024 * 1024;
-  // bf16: P goes to TMEM (packed bf16 pairs, the A operand of P V read from tensor memory); tf32 P is
-  // twice as wide and stays in shared memory (128-byte swizzle).
-  static constexpr bool P_TMEM = !F32;
+  // bf16 and tf32: P goes to TMEM (packed bf16 pairs or fp32, the A operand of P V read from tensor memory);
+  // 3xTF32 keeps P (hi and lo copies) in shared memory (128-byte swizzle).
+  static constexpr bool P_TMEM = !X3;
   static constexpr int PCB = KEYS * ES / 128;  // 128-byte column blocks of a shared-memory P row
   static constexpr int P_BYTES = P_TMEM ? 0 : PCB * ROWS * 128;
   static constexpr int PBUF_BYTES = P_BYTES * (X3 ? 2 : 1);  // P (3xTF32: P_hi, P_lo)
   static constexpr int OFF_STAGE = Q_BYTES * (X3 ? 2 : 1);    // Q (3xTF32: Q_hi in place, Q_lo)
-  // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word, alignment slack.
-  static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16 + 1024; }
-  // K/V stages: bf16 takes as many as two CTAs per SM leave room for (at most 6), so that the copies of the
-  // next chunks are in flight while the softmax works; tf32 3, 3xTF32 2.
-  static constexpr int NS = X3 ? 2 : F32 ? 3
-                              : smem_bytes(6) <= 227 * 1024 / 2 ? 6
-                              : smem_bytes(5) <= 227 * 1024 / 2 ? 5
-                              : smem_bytes(4) <= 227 * 1024 / 2 ? 4 : 3;
+  // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word. The dynamic shared
+  // memory base is 1024-byte aligned (checked at run time): no alignment slack.
+  static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16; }
+  static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
+  // K/V stages: as many as fit (bf16: two CTAs per SM; tf32: one) up to 6, so that the copies of the next chunks
+  // are in flight while the softmax works; 3xTF32 2.
+  static constexpr int NS = X3 ? 2 : fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : 3;
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
-  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment
-  static constexpr int TMEM_COLS = 256;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;  // + tmem holder / abort word
   static constexpr int O_COL = 128;
-  // TMEM P buffers (bf16): 64 keys -> 32 columns after O (head_dim 64); 32 keys -> 16 columns in the unused
-  // upper half of each 64-column S buffer (head_dim 128, one 32-key tile per chunk).
+  // TMEM P buffers: KEYS / 2 columns (bf16 pairs) or KEYS (tf32). One 32-key tile per chunk: in the unused upper
+  // half of each 64-column S buffer; two: after O (tf32 head_dim 64 then needs 512 columns, one CTA per SM).
+  static constexpr int PW = F32 ? KEYS : KEYS / 2;
   static constexpr int P_COL = CH == 1 ? 32 : O_COL + D;
-  static constexpr int P_STRIDE = CH == 1 ? 64 : 32;
+  static constexpr int P_STRIDE = CH == 1 ? 64 : PW;
+  static constexpr int TMEM_COLS = (CH == 1 || P_COL + 2 * PW <= 256) ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;  // 3xTF32: + a warpgroup splitting tiles into hi / lo
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
@@ -99,8 +99,8 @@ struct FwdCfg {
   static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 200;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
   static_assert(N_BAR == 14 + 3 * NS && SMEM_BYTES == smem_bytes(NS), "shared memory layout");
-  static_assert(!P_TMEM || (P_COL + P_STRIDE + KEYS / 2 <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)),
-                "TMEM budget");
+  static_assert(!P_TMEM || (P_COL + P_STRIDE + PW <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)), "TMEM budget");
+  static_assert(TMEM_COLS == 256 || MIN_BLOCKS == 1, "512 TMEM columns: one CTA per SM");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
@@ -112,9 +112,14 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k32,
                     const __grid_constant__ CUtensorMap tm_v32, const FwdParams p) {
   using C = FwdCfg<D, F32, X3>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_fwd[];
+  uint8_t* smem = smem_fwd;
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {
+    // The tile layouts need 1024-byte aligned shared memory; report and leave (uniformly, before any wait).
+    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
+    return;
+  }
   const uint32_t q_smem = sbase;
   auto stage_k = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES; };
   auto stage_v = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + C::KV_BYTES; };
@@ -364,11 +369,11 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           const uint64_t vdesc = F32 ? smem_desc(stage_v(st), C::KEYS * 128, 512, kLayoutSW128Base32B)
                                      : smem_desc(stage_v(st), C::KEYS * 128, 1024);
           if constexpr (C::P_TMEM) {
-            // bf16 P from TMEM: K = 16 keys per MMA = 8 columns of packed pairs.
+            // P from TMEM: K = 16 bf16 keys (8 columns of packed pairs) or 8 tf32 keys (8 columns) per MMA.
             const uint32_t pcol = tmem + C::P_COL + C::P_STRIDE * pbuf;
             for (int kk = 0; kk < ksteps; ++kk) {
               const uint64_t bd = vdesc + ((kk * C::KSTEP * 128) >> 4);
-              issue_([&] { mma_ts(tmem + C::O_COL, pcol + 8 * kk, bd, kIdescPV, (c == 0 && kk == 0) ? 0u : 1u); });
+              issue_([&] { mma_ts<F32>(tmem + C::O_COL, pcol + 8 * kk, bd, kIdescPV, (c == 0 && kk == 0) ? 0u : 1u); });
             }
           } else {
             // P in shared memory (K-major A), hi and lo copies.
@@ -597,14 +602,22 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           float e[64];
           two_pass(e);
           if (lane == 0) FWN_TR(26, c);
-          if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-          const uint32_t pbase = p_smem(sb);
+          if constexpr (C::P_TMEM) {
+            // tf32 P -> TMEM (the buffer was released above), one 32-key tile at a time.
+            const uint32_t pcol = trow + C::P_COL + C::P_STRIDE * sb;
+            tmem_st32(pcol, *reinterpret_cast<const float(*)[32]>(&e[0]));
+            if (C::CH == 2 && n_in == 2) tmem_st32(pcol + 32, *reinterpret_cast<const float(*)[32]>(&e[32]));
+            tmem_wait_st();
+          }
+          if constexpr (!C::P_TMEM) {
+            // 3xTF32: P hi (13 low mantissa bits cleared) and lo = P - hi into shared memory.
+            if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+            const uint32_t pbase = p_smem(sb);
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc) {
-            if (cc < 8 * n_in) {
-              const int blk = cc >> 3, ch = cc & 7;
-              const uint32_t off = blk * C::ROWS * 128 + sw128_offset(row, ch);
-              if constexpr (X3) {
+            for (int cc = 0; cc < 16; ++cc) {
+              if (cc < 8 * n_in) {
+                const int blk = cc >> 3, ch = cc & 7;
+                const uint32_t off = blk * C::ROWS * 128 + sw128_offset(row, ch);
                 uint32_t h[4], lo[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -613,9 +626,6 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
                 }
                 st_shared_v4(pbase + off, h[0], h[1], h[2], h[3]);
                 st_shared_v4(p_lo(sb) + off, lo[0], lo[1], lo[2], lo[3]);
-              } else {
-                st_shared_v4(pbase + off, __float_as_uint(e[4 * cc]), __float_as_uint(e[4 * cc + 1]),
-                             __float_as_uint(e[4 * cc + 2]), __float_as_uint(e[4 * cc + 3]));
               }
             }
           }
