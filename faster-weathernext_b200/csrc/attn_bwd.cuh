@@ -96,9 +96,13 @@ struct BwdCfg {
   static constexpr int G_BYTES = G_TMEM ? 0 : G64 ? ROWS * 64 : (COLS * ES / 128) * ROWS * 128;  // one dS (or P) tile
   static constexpr int NG = (ACC_DS ? 1 : 0) + (ACC_P ? 1 : 0);        // dS, P tiles per buffer
   static constexpr int ACC_COLS = (ACC_DS ? D : 0) + (ACC_P ? D : 0);  // TMEM columns of the accumulators
-  // S / dP buffers (64 TMEM columns each): bf16 three where the accumulators leave room (dQ at head_dim 64), else
-  // two; tf32 one.
-  static constexpr int NSD = !G_TMEM ? 1 : 3 * 64 + ACC_COLS <= 256 ? 3 : 2;
+  // TMEM S / dP buffers: S (32 CH columns) then dP; as many as the accumulators leave room for in 256 columns
+  // (bf16, two CTAs per SM) or 512 (tf32, one), at most 3 (bf16) or 4; 3xTF32 one.
+  static constexpr int SD_W = 32 * CH;
+  static constexpr int SD_STRIDE = 2 * SD_W;
+  static constexpr int TMEM_MAX = F32 ? 512 : 256;
+  static constexpr int NSD_FIT = (TMEM_MAX - ACC_COLS) / SD_STRIDE;
+  static constexpr int NSD = !G_TMEM ? 1 : NSD_FIT < (F32 ? 4 : 3) ? NSD_FIT : (F32 ? 4 : 3);
   // dS / P buffers: the TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32 except
   // dV only), else two.
   static constexpr int NB = G_TMEM ? NSD : (X3 && KIND != kBwdDV) ? 1 : 2;
@@ -120,10 +124,11 @@ struct BwdCfg {
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
   static constexpr int N_BAR = n_bar(NS);
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
-  // TMEM: S / dP buffer b at column 64 b (S) and 64 b + 32 (dP) with P / dS over them (bf16: packed pairs in their
-  // first 16 columns; tf32: all 32); 3xTF32 S at 0 and dP at 64; then the accumulators.
-  static constexpr int DP_OFF = G_TMEM ? 32 : 64;
-  static constexpr int ACC0 = G_TMEM ? 64 * NSD : 128;
+  // TMEM: S / dP buffer b at column SD_STRIDE b (S) and SD_STRIDE b + SD_W (dP) with P / dS over them (tile j of
+  // the chunk at + GW j: bf16 packed pairs, tf32 fp32); 3xTF32 S at 0 and dP at 64; then the accumulators.
+  static constexpr int DP_OFF = G_TMEM ? SD_W : 64;
+  static constexpr int GW = F32 ? 32 : 16;  // TMEM columns of one 32-wide tile's dS or P (fp32, or bf16 pairs)
+  static constexpr int ACC0 = G_TMEM ? SD_STRIDE * NSD : 128;
   static constexpr int ACC1 = ACC0 + (ACC_DS ? D : 0);
   static constexpr int TMEM_NEED = ACC0 + ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
@@ -138,8 +143,8 @@ struct BwdCfg {
   static_assert(!G64 || (!F32 && CH == 1), "64-byte dS rows hold 32 bf16 columns");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
-  static_assert(!G_TMEM || CH == 1, "TMEM dS / P: one 32-wide tile per chunk");
-  static_assert(!G_TMEM || TMEM_NEED <= 256, "TMEM dS / P: two CTAs per SM");
+  static_assert(!G_TMEM || (NSD >= 2 && TMEM_NEED <= TMEM_MAX), "TMEM dS / P: two S / dP buffers and the accumulators");
+  static_assert(F32 || TMEM_NEED <= 256, "bf16: two CTAs per SM");
   static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
 };
 
@@ -473,7 +478,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
           }
           tc_fence_after();
-          const uint32_t sd_col = C::G_TMEM ? 64 * sdb : 0;
+          const uint32_t sd_col = C::G_TMEM ? C::SD_STRIDE * sdb : 0;
           const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
           const uint32_t sb = stage(st);
   #pragma unroll
@@ -520,7 +525,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             if constexpr (C::G_TMEM) {
               // dS (over dP) / P (over S) from TMEM: K = 16 columns per MMA = 8 TMEM columns of packed pairs.
               // K = 16 bf16 (8 columns of pairs) or 8 tf32 (8 columns) per MMA.
-              const uint32_t a_col = tmem + 64 * gb + (which == 0 ? C::DP_OFF : 0);
+              const uint32_t a_col = tmem + C::SD_STRIDE * gb + (which == 0 ? C::DP_OFF : 0);
               const uint64_t b_desc = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
                                           : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
               for (int kk = 0; kk < ksteps; ++kk)
@@ -641,7 +646,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         if (lane == 0) FWN_TR(29, c);
         tc_fence_after();
         const uint32_t sb = stage(st);
-        const uint32_t sd_col = C::G_TMEM ? 64 * gb : 0;
+        const uint32_t sd_col = C::G_TMEM ? C::SD_STRIDE * gb : 0;
         // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into TMEM over them (bf16) or into
         // the shared-memory tiles of buffer gb (tf32: TMEM is released once the last tile's values are in registers).
 #pragma unroll
@@ -718,14 +723,14 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
               if constexpr (C::G_TMEM && F32) {
                 // 32 fp32 columns over S (P) or dP (dS).
-                tmem_st32(trow + sd_col + (which == 0 ? C::DP_OFF : 0),
+                tmem_st32(trow + sd_col + (which == 0 ? C::DP_OFF : 0) + C::GW * j,
                           *reinterpret_cast<const float(*)[32]>(src));
               } else if constexpr (C::G_TMEM) {
                 // 32 bf16 columns = 16 TMEM columns of packed pairs over the first half of S (P) or dP (dS).
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(src[2 * i], src[2 * i + 1]);
-                tmem_st16(trow + sd_col + (which == 0 ? C::DP_OFF : 0), pk);
+                tmem_st16(trow + sd_col + (which == 0 ? C::DP_OFF : 0) + C::GW * j, pk);
               } else if constexpr (C::G64) {
                 // 32 bf16 columns = one 64-byte row.
 #pragma unroll

@@ -495,7 +495,8 @@ template <int D, bool F32, bool X3 = false>
 fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const void* o,
                       const float* lse, const void* d_o, const fwn_tile_list* t, const fwn_tile_list* tt, void* dq,
                       void* dk, void* dv, float* delta, int parts, cudaStream_t stream) {
-  // 32-column chunks (bf16: two S / dP buffers in TMEM with dS / P over them; tf32: operand sizes).
+  // 32-column chunks. (64-column chunks with N = 64 S / dP MMAs were measured for tf32 at head_dim 64, where one
+  // CTA per SM has the TMEM columns: dQ 3 % faster, dK/dV 8 % slower with half the column stages.)
   constexpr int CH = 1;
   // dV and dK as separate passes where one dK/dV pass does not fit: 3xTF32 and tf32 at head_dim 128 (shared
   // memory), bf16 at head_dim 128 (dK and dV accumulators plus S and dP exceed the 256 TMEM columns of a CTA
