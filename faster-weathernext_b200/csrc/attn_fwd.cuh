@@ -55,8 +55,9 @@ struct FwdCfg {
   static constexpr int CB = D / EPB;          // column blocks of a head_dim row
   static constexpr int ROWS = 128;            // query rows per item
   static constexpr int SUB = 32;              // keys per tile
-  // Tiles per chunk: one at head_dim 128 (bf16: keeps two CTAs per SM, so that one CTA's softmax overlaps
-  // the other's MMAs; tf32: the operands' size) and in 3xTF32; else two.
+  // Tiles per chunk: one at head_dim 128 (bf16: keeps two CTAs per SM, so that one CTA's softmax overlaps the
+  // other's MMAs; tf32: two tiles would leave room for two K/V stages instead of four, measured 11 % slower at the
+  // WN2 shape) and in 3xTF32 (operand copies); else two.
   static constexpr int CH = (X3 || D == 128) ? 1 : 2;
   static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
@@ -78,7 +79,7 @@ struct FwdCfg {
   static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
   // K/V stages: as many as fit (bf16: two CTAs per SM; tf32: one) up to 6, so that the copies of the next chunks
   // are in flight while the softmax works; 3xTF32 2.
-  static constexpr int NS = X3 ? 2 : fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : 3;
+  static constexpr int NS = X3 ? 2 : fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : fit(3) ? 3 : 2;
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
