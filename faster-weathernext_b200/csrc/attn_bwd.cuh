@@ -49,6 +49,10 @@ struct BwdParams {
   float scale;         // softmax scale (applied to acc0)
   float scale_log2;    // scale * log2(e)
   unsigned long long* trace;  // FWN_TRACE builds: event records (else unused)
+  // Row operands and their element strides (read by the elementwise warps where the rows live in TMEM).
+  const void* r0;
+  const void* r1;
+  int64_t r0_sb, r0_sn, r0_sh, r1_sb, r1_sn, r1_sh;
 };
 
 template <int KIND, int D, bool F32, int CH, bool X3>
@@ -86,6 +90,12 @@ struct BwdCfg {
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
   static constexpr bool G64 = COLS * ES == 64;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
+  // tf32 at head_dim 128 (one CTA per SM): the row operands live in TMEM, one fp32 element per column (the A
+  // operands of S / dP, loaded by the elementwise warps: thread = row = lane); shared memory then holds only
+  // column stages (four instead of two for the dQ / dK passes).
+  static constexpr bool R_TMEM = F32 && !X3 && D == 128;
+  static constexpr int R_COLS = R_TMEM ? NR * D : 0;
+  static constexpr int R_SMEM = R_TMEM ? 0 : R_BYTES;   // shared memory of one row operand
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
   static constexpr int BITS_OFF = NC * XL * C_BYTES;
   // lse / delta of the columns (rows are keys): lse times log2 e where the producer stores them through registers
@@ -101,7 +111,7 @@ struct BwdCfg {
   static constexpr int SD_W = 32 * CH;
   static constexpr int SD_STRIDE = 2 * SD_W;
   static constexpr int TMEM_MAX = F32 ? 512 : 256;
-  static constexpr int NSD_FIT = (TMEM_MAX - ACC_COLS) / SD_STRIDE;
+  static constexpr int NSD_FIT = (TMEM_MAX - R_COLS - ACC_COLS) / SD_STRIDE;
   static constexpr int NSD = !G_TMEM ? 1 : NSD_FIT < (F32 ? 4 : 3) ? NSD_FIT : (F32 ? 4 : 3);
   // dS / P buffers: the TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32 except
   // dV only), else two.
@@ -110,7 +120,7 @@ struct BwdCfg {
   static constexpr int n_bar(int ns) { return 2 + 2 * ns + SDB + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
   // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
   static constexpr int smem_bytes(int ns) {
-    return NR * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16;
+    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16;
   }
   // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
   static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
@@ -118,7 +128,7 @@ struct BwdCfg {
   // elementwise stage; 3xTF32 one or two.
   static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1)
                             : fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
-  static constexpr int OFF_C = NR * XL * R_BYTES;
+  static constexpr int OFF_C = NR * XL * R_SMEM;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
@@ -128,7 +138,8 @@ struct BwdCfg {
   // the chunk at + GW j: bf16 packed pairs, tf32 fp32); 3xTF32 S at 0 and dP at 64; then the accumulators.
   static constexpr int DP_OFF = G_TMEM ? SD_W : 64;
   static constexpr int GW = F32 ? 32 : 16;  // TMEM columns of one 32-wide tile's dS or P (fp32, or bf16 pairs)
-  static constexpr int ACC0 = G_TMEM ? SD_STRIDE * NSD : 128;
+  static constexpr int SD0 = R_COLS;  // first S / dP buffer column (after row operands in TMEM)
+  static constexpr int ACC0 = G_TMEM ? SD0 + SD_STRIDE * NSD : 128;
   static constexpr int ACC1 = ACC0 + (ACC_DS ? D : 0);
   static constexpr int TMEM_NEED = ACC0 + ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
@@ -145,6 +156,7 @@ struct BwdCfg {
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
   static_assert(!G_TMEM || (NSD >= 2 && TMEM_NEED <= TMEM_MAX), "TMEM dS / P: two S / dP buffers and the accumulators");
   static_assert(F32 || TMEM_NEED <= 256, "bf16: two CTAs per SM");
+  static_assert(!R_TMEM || (G_TMEM && MIN_BLOCKS == 1), "TMEM row operands: tf32, one CTA per SM");
   static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
 };
 
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   int trace_count = 0;  // FWN_TRACE builds: this lane's event count
 #define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
-    mbar_init(r_full, 1);
+    mbar_init(r_full, C::R_TMEM ? 4 : 1);
     mbar_init(r_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(c_full(s), (GATHER && C::ROWS_ARE_KEYS) ? 2 : 1);
@@ -308,16 +320,18 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       if (nch == 0) continue;
       ChunkMeta<CH> m0 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
       ChunkMeta<CH> m1 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
-      if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(r_full, C::NR * C::R_BYTES);
-        for (int cb = 0; cb < C::CB; ++cb) {
-          tma_load_4d(r_op(0, 0) + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
-          if (C::NR == 2)
-            tma_load_4d(r_op(1, 0) + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+      if constexpr (!C::R_TMEM) {
+        if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(r_full, C::NR * C::R_BYTES);
+          for (int cb = 0; cb < C::CB; ++cb) {
+            tma_load_4d(r_op(0, 0) + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+            if (C::NR == 2)
+              tma_load_4d(r_op(1, 0) + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+          }
         }
+        pending_r = 1;
       }
-      pending_r = 1;
       const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
       const int row_mul = p.head_major ? 1 : p.heads;
       // Chunk c's copies; `meta` was loaded two chunks earlier. The loop below is unrolled by two so that
@@ -478,7 +492,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             if (!wait_(sd_empty, (gg & 1) ^ 1)) return false;
           }
           tc_fence_after();
-          const uint32_t sd_col = C::G_TMEM ? C::SD_STRIDE * sdb : 0;
+          const uint32_t sd_col = C::G_TMEM ? C::SD0 + C::SD_STRIDE * sdb : 0;
           const uint32_t idesc = instr_desc(F32, 128, 32 * n_in, false, false);
           const uint32_t sb = stage(st);
   #pragma unroll
@@ -493,7 +507,12 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
                 const uint64_t a = (pass == 2 ? r_lo : r_hi) + ((cb * C::ROWS * 128 + within) >> 4);
                 const uint64_t bd = (pass == 1 ? c_lo : c_hi) + ((cb * C::COLS * 128 + within) >> 4);
-                issue_([&] { mma_ss<F32>(tmem + sd_col + C::DP_OFF * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
+                if constexpr (C::R_TMEM) {
+                  // A = the row operand in TMEM: K = 8 tf32 elements = 8 columns per MMA.
+                  issue_([&] { mma_ts<true>(tmem + sd_col + C::DP_OFF * op, tmem + op * D + 8 * kk, bd, idesc, kk > 0 ? 1u : 0u); });
+                } else {
+                  issue_([&] { mma_ss<F32>(tmem + sd_col + C::DP_OFF * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
+                }
               }
             }
           }
@@ -525,7 +544,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             if constexpr (C::G_TMEM) {
               // dS (over dP) / P (over S) from TMEM: K = 16 columns per MMA = 8 TMEM columns of packed pairs.
               // K = 16 bf16 (8 columns of pairs) or 8 tf32 (8 columns) per MMA.
-              const uint32_t a_col = tmem + C::SD_STRIDE * gb + (which == 0 ? C::DP_OFF : 0);
+              const uint32_t a_col = tmem + C::SD0 + C::SD_STRIDE * gb + (which == 0 ? C::DP_OFF : 0);
               const uint64_t b_desc = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
                                           : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
               for (int kk = 0; kk < ksteps; ++kk)
@@ -632,6 +651,42 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         lse2_row = p.lse[static_cast<size_t>(bh) * p.lse_rows + grow] * kLog2e;
         delta_row = p.delta[static_cast<size_t>(bh) * p.lse_rows + grow];
       }
+      if constexpr (C::R_TMEM) {
+        // The item's row operands into TMEM (this thread's row into its lane), once the previous item's last S / dP
+        // MMA is complete; rows past n are zero (as the TMA loads' out-of-range fill).
+        if (nch > 0) {
+          if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int op = 0; op < C::NR; ++op) {
+            const float* src = nullptr;
+            if (grow < p.n) {
+              src = static_cast<const float*>(op == 0 ? p.r0 : p.r1) +
+                    (op == 0 ? static_cast<int64_t>(b) * p.r0_sb + static_cast<int64_t>(grow) * p.r0_sn +
+                                   static_cast<int64_t>(h) * p.r0_sh
+                             : static_cast<int64_t>(b) * p.r1_sb + static_cast<int64_t>(grow) * p.r1_sn +
+                                   static_cast<int64_t>(h) * p.r1_sh);
+            }
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 x = src ? __ldg(reinterpret_cast<const float4*>(src + 32 * j) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[4 * i] = x.x;
+                v[4 * i + 1] = x.y;
+                v[4 * i + 2] = x.z;
+                v[4 * i + 3] = x.w;
+              }
+              tmem_st32(trow + op * D + 32 * j, v);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(r_full);
+        }
+      }
       const uint32_t g0 = g;
       for (int c = 0; c < nch; ++c) {
         const uint32_t gg = g0 + c;
@@ -646,7 +701,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
         if (lane == 0) FWN_TR(29, c);
         tc_fence_after();
         const uint32_t sb = stage(st);
-        const uint32_t sd_col = C::G_TMEM ? C::SD_STRIDE * gb : 0;
+        const uint32_t sd_col = C::G_TMEM ? C::SD0 + C::SD_STRIDE * gb : 0;
         // One 32-column tile at a time: S and dP of the tile from TMEM, P and dS into TMEM over them (bf16) or into
         // the shared-memory tiles of buffer gb (tf32: TMEM is released once the last tile's values are in registers).
 #pragma unroll

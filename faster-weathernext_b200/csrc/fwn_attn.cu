@@ -389,6 +389,14 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale = d.scale;
   p.scale_log2 = d.scale * 1.4426950408889634f;
+  p.r0 = rp0;
+  p.r1 = rp1;
+  p.r0_sb = d.stride_b;
+  p.r0_sn = d.stride_n;
+  p.r0_sh = d.stride_h;
+  p.r1_sb = r1_out ? d.out_stride_b : d.stride_b;
+  p.r1_sn = r1_out ? d.out_stride_n : d.stride_n;
+  p.r1_sh = r1_out ? d.out_stride_h : d.stride_h;
 #ifdef FWN_TRACE
   p.trace = trace_buffer();
 #endif
