@@ -46,6 +46,8 @@ struct FwdParams {
   int batch, heads, n, np, lse_rows, n_items;
   float scale_log2;       // scale * log2(e)
   unsigned long long* trace;  // FWN_TRACE builds: kTraceCtas x kTraceEvents event records (else unused)
+  const void* q;          // Q and its element strides (read by the softmax warps where Q lives in TMEM)
+  int64_t q_sb, q_sn, q_sh;
 };
 
 template <int D, bool F32, bool X3 = false>
@@ -72,7 +74,11 @@ struct FwdCfg {
   static constexpr int PCB = KEYS * ES / 128;  // 128-byte column blocks of a shared-memory P row
   static constexpr int P_BYTES = P_TMEM ? 0 : PCB * ROWS * 128;
   static constexpr int PBUF_BYTES = P_BYTES * (X3 ? 2 : 1);  // P (3xTF32: P_hi, P_lo)
-  static constexpr int OFF_STAGE = Q_BYTES * (X3 ? 2 : 1);    // Q (3xTF32: Q_hi in place, Q_lo)
+  // tf32 (one CTA per SM): Q lives in TMEM, one fp32 element per column (the A operand of S, loaded by the softmax
+  // warps: thread = row = lane), and shared memory holds only K / V stages; MMAs that take A from TMEM read a
+  // quarter of the shared-memory bytes.
+  static constexpr bool Q_TMEM = F32 && !X3;
+  static constexpr int OFF_STAGE = Q_TMEM ? 0 : Q_BYTES * (X3 ? 2 : 1);  // Q (3xTF32: Q_hi in place, Q_lo)
   // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word. The dynamic shared
   // memory base is 1024-byte aligned (checked at run time): no alignment slack.
   static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16; }
@@ -90,7 +96,8 @@ struct FwdCfg {
   static constexpr int PW = F32 ? KEYS : KEYS / 2;
   static constexpr int P_COL = CH == 1 ? 32 : O_COL + D;
   static constexpr int P_STRIDE = CH == 1 ? 64 : PW;
-  static constexpr int TMEM_COLS = (CH == 1 || P_COL + 2 * PW <= 256) ? 256 : 512;
+  static constexpr int Q_COL = CH == 1 ? O_COL + D : P_COL + 2 * PW;  // TMEM Q (tf32)
+  static constexpr int TMEM_COLS = Q_TMEM ? 512 : (CH == 1 || P_COL + 2 * PW <= 256) ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;  // 3xTF32: + a warpgroup splitting tiles into hi / lo
   static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
@@ -102,6 +109,7 @@ struct FwdCfg {
   static_assert(N_BAR == 14 + 3 * NS && SMEM_BYTES == smem_bytes(NS), "shared memory layout");
   static_assert(!P_TMEM || (P_COL + P_STRIDE + PW <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)), "TMEM budget");
   static_assert(TMEM_COLS == 256 || MIN_BLOCKS == 1, "512 TMEM columns: one CTA per SM");
+  static_assert(!Q_TMEM || Q_COL + D <= TMEM_COLS, "TMEM budget (Q)");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
@@ -151,7 +159,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
   int trace_count = 0;  // FWN_TRACE builds: this lane's event count
 #define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, C::Q_TMEM ? 4 : 1);
     mbar_init(q_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(kv_full(s), 1);
@@ -212,14 +220,16 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       ChunkMeta<C::CH> m0 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
       ChunkMeta<C::CH> m1 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
       if (lane == 0) FWN_TR(1, it);
-      if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
-      if (lane == 0) {
-        FWN_TR(2, nch);
-        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-        for (int cb = 0; cb < C::CB; ++cb)
-          tma_load_4d(q_smem + cb * C::ROWS * 128, &tm_q, cb * C::EPB, h, pb * C::ROWS, b, q_full);
+      if constexpr (!C::Q_TMEM) {
+        if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+        if (lane == 0) {
+          FWN_TR(2, nch);
+          mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+          for (int cb = 0; cb < C::CB; ++cb)
+            tma_load_4d(q_smem + cb * C::ROWS * 128, &tm_q, cb * C::EPB, h, pb * C::ROWS, b, q_full);
+        }
+        pending_q = 1;
       }
-      pending_q = 1;
       // Gathered mode: row of the 2D view of K / V holding (batch b, node `key`, head h).
       const int row_base = p.head_major ? (b * p.heads + h) * p.n : b * p.n * p.heads + h;
       const int row_mul = p.head_major ? 1 : p.heads;
@@ -346,7 +356,12 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
               const uint32_t cb = kk / 4, within = (kk % 4) * 32;
               const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
               const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
-              issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
+              if constexpr (C::Q_TMEM) {
+                // A = Q in TMEM: K = 8 tf32 elements = 8 columns per MMA.
+                issue_([&] { mma_ts<true>(tmem + sb * 64, tmem + C::Q_COL + 8 * kk, bd, idesc_s, kk > 0 ? 1u : 0u); });
+              } else {
+                issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
+              }
             }
           }
           issue_([&] {
@@ -460,6 +475,34 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       const int nch = (n_sub + C::CH - 1) / C::CH;
       const int qrow = pb * C::ROWS + row;
       float m_ref = -INFINITY, l = 0.f;
+      if constexpr (C::Q_TMEM) {
+        // The item's Q into TMEM (this thread's row into its lane), once the previous item's last S MMA is
+        // complete; rows past n are zero (as the TMA load's out-of-range fill).
+        if (nch > 0) {
+          if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const float* src = qrow < p.n ? static_cast<const float*>(p.q) + static_cast<int64_t>(b) * p.q_sb +
+                                              static_cast<int64_t>(qrow) * p.q_sn + static_cast<int64_t>(h) * p.q_sh
+                                        : nullptr;
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = src ? __ldg(reinterpret_cast<const float4*>(src + 32 * j) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              v[4 * i] = x.x;
+              v[4 * i + 1] = x.y;
+              v[4 * i + 2] = x.z;
+              v[4 * i + 3] = x.w;
+            }
+            tmem_st32(trow + C::Q_COL + 32 * j, v);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(q_full);
+        }
+      }
       const uint32_t g0 = g;
       for (int c = 0; c < nch; ++c) {
         const uint32_t gg = g0 + c;

@@ -263,6 +263,10 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   p.lse_rows = fwn_lse_rows(d.n);
   p.n_items = d.batch * d.heads * t.n_blocks;
   p.scale_log2 = d.scale * 1.4426950408889634f;
+  p.q = q;
+  p.q_sb = d.stride_b;
+  p.q_sn = d.stride_n;
+  p.q_sh = d.stride_h;
 #ifdef FWN_TRACE
   p.trace = trace_buffer();
 #endif
