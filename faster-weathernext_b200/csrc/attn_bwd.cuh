@@ -90,10 +90,10 @@ struct BwdCfg {
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
   static constexpr bool G64 = COLS * ES == 64;
   static constexpr int R_BYTES = CB * ROWS * 128;       // one row operand
-  // tf32 at head_dim 128 (one CTA per SM): the row operands live in TMEM, one fp32 element per column (the A
-  // operands of S / dP, loaded by the elementwise warps: thread = row = lane); shared memory then holds only
-  // column stages (four instead of two for the dQ / dK passes).
-  static constexpr bool R_TMEM = F32 && !X3 && D == 128;
+  // tf32 (one CTA per SM): the row operands live in TMEM, one fp32 element per column (the A operands of S / dP,
+  // loaded by the elementwise warps: thread = row = lane); shared memory then holds only column stages (at head_dim
+  // 128 four instead of two for the dQ / dK passes), and the S / dP MMAs read a fifth of the shared-memory bytes.
+  static constexpr bool R_TMEM = F32 && !X3;
   static constexpr int R_COLS = R_TMEM ? NR * D : 0;
   static constexpr int R_SMEM = R_TMEM ? 0 : R_BYTES;   // shared memory of one row operand
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
