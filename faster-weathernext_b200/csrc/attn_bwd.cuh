@@ -118,9 +118,9 @@ struct BwdCfg {
   static constexpr int NB = G_TMEM ? NSD : (X3 && KIND != kBwdDV) ? 1 : 2;
   static constexpr int SDB = NSD < 2 ? 2 : NSD;  // barrier slots: sd_full / sd_empty, or one sd_full per buffer
   static constexpr int n_bar(int ns) { return 2 + 2 * ns + SDB + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
-  // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
+  // + 1 KB of slack to align the dynamic shared memory base up to 1024 bytes.
   static constexpr int smem_bytes(int ns) {
-    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16;
+    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + 1024;
   }
   // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
   static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
@@ -133,7 +133,7 @@ struct BwdCfg {
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
   static constexpr int N_BAR = n_bar(NS);
-  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
   // TMEM: S / dP buffer b at column SD_STRIDE b (S) and SD_STRIDE b + SD_W (dP) with P / dS over them (tile j of
   // the chunk at + GW j: bf16 packed pairs, tf32 fp32); 3xTF32 S at 0 and dP at 64; then the accumulators.
   static constexpr int DP_OFF = G_TMEM ? SD_W : 64;
@@ -209,14 +209,9 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                     const BwdParams p) {
   // tm_c*r: 4D maps of 32-row boxes (gathered mode: tiles whose 32 columns are consecutive).
   using C = BwdCfg<KIND, D, F32, CH, X3>;
-  extern __shared__ __align__(1024) uint8_t smem_bwd[];
-  uint8_t* smem = smem_bwd;
+  extern __shared__ uint8_t smem_bwd[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_bwd) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  if (sbase & 1023u) {
-    // The tile layouts need 1024-byte aligned shared memory; report and leave (uniformly, before any wait).
-    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
-    return;
-  }
   // Row operand i (hi, or the operand itself), its lo copy at +NR; column slot s of a stage, lo copy at +NC.
   auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR + i) * C::R_BYTES; };
   auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };

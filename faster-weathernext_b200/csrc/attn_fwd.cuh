@@ -79,9 +79,9 @@ struct FwdCfg {
   // quarter of the shared-memory bytes.
   static constexpr bool Q_TMEM = F32 && !X3;
   static constexpr int OFF_STAGE = Q_TMEM ? 0 : Q_BYTES * (X3 ? 2 : 1);  // Q (3xTF32: Q_hi in place, Q_lo)
-  // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word. The dynamic shared
-  // memory base is 1024-byte aligned (checked at run time): no alignment slack.
-  static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16; }
+  // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word, 1 KB of slack to
+  // align the dynamic shared memory base up to 1024 bytes.
+  static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16 + 1024; }
   static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
   // K/V stages: as many as fit (bf16: two CTAs per SM; tf32: one) up to 6, so that the copies of the next chunks
   // are in flight while the softmax works; 3xTF32 2.
@@ -89,7 +89,7 @@ struct FwdCfg {
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
-  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;  // + tmem holder / abort word
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder / abort word + slack
   static constexpr int O_COL = 128;
   // TMEM P buffers: KEYS / 2 columns (bf16 pairs) or KEYS (tf32). One 32-key tile per chunk: in the unused upper
   // half of each 64-column S buffer; two: after O (tf32 head_dim 64 then needs 512 columns, one CTA per SM).
@@ -121,14 +121,9 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k32,
                     const __grid_constant__ CUtensorMap tm_v32, const FwdParams p) {
   using C = FwdCfg<D, F32, X3>;
-  extern __shared__ __align__(1024) uint8_t smem_fwd[];
-  uint8_t* smem = smem_fwd;
+  extern __shared__ uint8_t smem_fwd[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_fwd) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  if (sbase & 1023u) {
-    // The tile layouts need 1024-byte aligned shared memory; report and leave (uniformly, before any wait).
-    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
-    return;
-  }
   const uint32_t q_smem = sbase;
   auto stage_k = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES; };
   auto stage_v = [&](int s) { return sbase + C::OFF_STAGE + s * C::STAGE_BYTES + C::KV_BYTES; };
