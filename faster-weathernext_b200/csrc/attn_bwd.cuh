@@ -80,11 +80,12 @@ struct BwdCfg {
   static constexpr int SLOT_C0MN = 1 + (LOAD_C1 ? 1 : 0);
   static constexpr int SLOT_C1MN = SLOT_C0MN + (LOAD_C0MN ? 1 : 0);
   static constexpr int NC = SLOT_C1MN + (LOAD_C1MN ? 1 : 0);
-  // bf16 and tf32: dS / P (bf16 packed pairs, or fp32) go to TMEM over the S / dP columns they are computed from,
-  // and the accumulating MMAs read them as the A operand from tensor memory; S / dP are double-buffered (one
-  // 32-wide tile per chunk), so the elementwise stage of chunk c overlaps the S / dP MMAs of chunk c+1. 3xTF32
-  // keeps dS / P (hi and lo copies) in shared memory with one S / dP buffer.
-  static constexpr bool G_TMEM = !X3;
+  // dS / P (bf16 packed pairs, or fp32) go to TMEM over the S / dP columns they are computed from, and the
+  // accumulating MMAs read them as the A operand from tensor memory; S / dP are double-buffered (one 32-wide tile
+  // per chunk), so the elementwise stage of chunk c overlaps the S / dP MMAs of chunk c+1. 3xTF32 passes have one
+  // of dS / P: its hi copy goes over S, its lo copy over dP. (The shared-memory dS / P path below serves no
+  // configuration now and is kept for kernels whose TMEM would not hold two buffers.)
+  static constexpr bool G_TMEM = true;
   // One stage where the hi / lo (3xTF32) or fp32 head_dim-128 operands leave room for no second one.
   static constexpr bool BIG = X3 || (F32 && D == 128);
   // dS / P rows of 32 bf16 columns are 64 bytes: 64-byte swizzle (half the shared memory of a 128-byte row).
@@ -118,22 +119,23 @@ struct BwdCfg {
   static constexpr int NB = G_TMEM ? NSD : (X3 && KIND != kBwdDV) ? 1 : 2;
   static constexpr int SDB = NSD < 2 ? 2 : NSD;  // barrier slots: sd_full / sd_empty, or one sd_full per buffer
   static constexpr int n_bar(int ns) { return 2 + 2 * ns + SDB + 2 * NB + 2 + 1 + (X3 ? 1 + ns : 0); }
-  // + 1 KB of slack to align the dynamic shared memory base up to 1024 bytes.
+  // + 1 KB of slack to align the dynamic shared memory base up to 1024 bytes; 3xTF32, whose second stage would
+  // miss by a few hundred bytes, sizes it to the byte and checks the alignment at run time instead.
+  static constexpr int SLACK = X3 ? 0 : 1024;
   static constexpr int smem_bytes(int ns) {
-    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + 1024;
+    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + SLACK;
   }
   // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
   static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
   // Column stages: as many as fit (at most 8), so that the copies of the next chunks are in flight during the
   // elementwise stage; 3xTF32 one or two.
-  static constexpr int NS = X3 ? (KIND == kBwdDV ? 2 : 1)
-                            : fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
+  static constexpr int NS = fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
   static constexpr int OFF_C = NR * XL * R_SMEM;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
   static constexpr int N_BAR = n_bar(NS);
-  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + SLACK;
   // TMEM: S / dP buffer b at column SD_STRIDE b (S) and SD_STRIDE b + SD_W (dP) with P / dS over them (tile j of
   // the chunk at + GW j: bf16 packed pairs, tf32 fp32); 3xTF32 S at 0 and dP at 64; then the accumulators.
   static constexpr int DP_OFF = G_TMEM ? SD_W : 64;
@@ -155,6 +157,7 @@ struct BwdCfg {
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
   static_assert(!G_TMEM || (NSD >= 2 && TMEM_NEED <= TMEM_MAX), "TMEM dS / P: two S / dP buffers and the accumulators");
+  static_assert(!(G_TMEM && X3) || (CH == 1 && NG == 1), "3xTF32 TMEM dS / P: one of dS / P, 32-wide tiles");
   static_assert(F32 || TMEM_NEED <= 256, "bf16: two CTAs per SM");
   static_assert(!R_TMEM || (G_TMEM && MIN_BLOCKS == 1), "TMEM row operands: tf32, one CTA per SM");
   static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
@@ -210,8 +213,15 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   // tm_c*r: 4D maps of 32-row boxes (gathered mode: tiles whose 32 columns are consecutive).
   using C = BwdCfg<KIND, D, F32, CH, X3>;
   extern __shared__ uint8_t smem_bwd[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_bwd) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = C::SLACK ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_bwd) + 1023) & ~uintptr_t(1023))
+                           : smem_bwd;
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {
+    // No slack and an unaligned base: the tile layouts need 1024-byte alignment; report and leave (uniformly,
+    // before any wait).
+    if (threadIdx.x == 0) atomicOr(&g_device_error, 0x100u);
+    return;
+  }
   // Row operand i (hi, or the operand itself), its lo copy at +NR; column slot s of a stage, lo copy at +NC.
   auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR + i) * C::R_BYTES; };
   auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };
@@ -539,14 +549,20 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
             if constexpr (C::G_TMEM) {
               // dS (over dP) / P (over S) from TMEM: K = 16 columns per MMA = 8 TMEM columns of packed pairs.
               // K = 16 bf16 (8 columns of pairs) or 8 tf32 (8 columns) per MMA.
-              const uint32_t a_col = tmem + C::SD0 + C::SD_STRIDE * gb + (which == 0 ? C::DP_OFF : 0);
-              const uint64_t b_desc = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
-                                          : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
-              for (int kk = 0; kk < ksteps; ++kk)
-                issue_([&] {
-                  mma_ts<F32>(acc, a_col + 8 * kk, b_desc + ((kk * C::KSTEP * 128) >> 4), kIdescAcc,
-                              (c == 0 && kk == 0) ? 0u : 1u);
-                });
+              // 3xTF32: G hi (over S) and lo (over dP); hi*hi + hi*lo + lo*hi.
+              const uint32_t g_col = tmem + C::SD0 + C::SD_STRIDE * gb;
+              const uint64_t b_hi = F32 ? smem_desc(slot(sb, bs, 0), C::COLS * 128, 512, kLayoutSW128Base32B)
+                                        : smem_desc(slot(sb, bs, 0), C::COLS * 128, 1024);
+              const uint64_t b_lo = smem_desc(slot(sb, bs, 1), C::COLS * 128, 512, kLayoutSW128Base32B);
+              for (int pass = 0; pass < kPasses; ++pass) {
+                const uint32_t a_col = g_col + (X3 ? (pass == 2 ? C::DP_OFF : 0) : (which == 0 ? C::DP_OFF : 0));
+                const uint64_t b_desc = pass == 1 ? b_lo : b_hi;
+                for (int kk = 0; kk < ksteps; ++kk)
+                  issue_([&] {
+                    mma_ts<F32>(acc, a_col + 8 * kk, b_desc + ((kk * C::KSTEP * 128) >> 4), kIdescAcc,
+                                (c == 0 && pass == 0 && kk == 0) ? 0u : 1u);
+                  });
+              }
               continue;
             }
             const uint64_t g_hi = C::G64 ? smem_desc(g_tile(gb, gi, 0), 16, 512, kLayoutSW64) : smem_desc(g_tile(gb, gi, 0), 16, 1024);
@@ -771,7 +787,17 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
               if (which == 1 && !C::ACC_P) continue;
               const float* src = which == 0 ? dp : s;
               const uint32_t base = g_tile(gb, which == 0 ? G_DS : G_P, 0);
-              if constexpr (C::G_TMEM && F32) {
+              if constexpr (C::G_TMEM && X3) {
+                // hi (13 low mantissa bits cleared) over S, lo = x - hi over dP.
+                float hv[32], lv[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  hv[i] = __uint_as_float(__float_as_uint(src[i]) & 0xFFFFE000u);
+                  lv[i] = src[i] - hv[i];
+                }
+                tmem_st32(trow + sd_col + C::GW * j, hv);
+                tmem_st32(trow + sd_col + C::DP_OFF + C::GW * j, lv);
+              } else if constexpr (C::G_TMEM && F32) {
                 // 32 fp32 columns over S (P) or dP (dS).
                 tmem_st32(trow + sd_col + (which == 0 ? C::DP_OFF : 0) + C::GW * j,
                           *reinterpret_cast<const float(*)[32]>(src));
