@@ -94,9 +94,12 @@ struct BwdCfg {
   // tf32 (one CTA per SM): the row operands live in TMEM, one fp32 element per column (the A operands of S / dP,
   // loaded by the elementwise warps: thread = row = lane); shared memory then holds only column stages (at head_dim
   // 128 four instead of two for the dQ / dK passes), and the S / dP MMAs read a fifth of the shared-memory bytes.
-  static constexpr bool R_TMEM = F32 && !X3;
-  static constexpr int R_COLS = R_TMEM ? NR * D : 0;
-  static constexpr int R_SMEM = R_TMEM ? 0 : R_BYTES;   // shared memory of one row operand
+  // 3xTF32: the first row operand in TMEM (hi and lo copies, split by the elementwise warps); the second stays in
+  // shared memory, split there by the converter warps.
+  static constexpr int NR_TMEM = X3 ? 1 : F32 ? NR : 0;
+  static constexpr int NR_SMEM = NR - NR_TMEM;
+  static constexpr bool R_TMEM = NR_TMEM > 0;
+  static constexpr int R_COLS = NR_TMEM * D * XL;
   static constexpr int C_BYTES = CB * COLS * 128;       // one column operand per stage
   static constexpr int BITS_OFF = NC * XL * C_BYTES;
   // lse / delta of the columns (rows are keys): lse times log2 e where the producer stores them through registers
@@ -123,14 +126,14 @@ struct BwdCfg {
   // miss by a few hundred bytes, sizes it to the byte and checks the alignment at run time instead.
   static constexpr int SLACK = X3 ? 0 : 1024;
   static constexpr int smem_bytes(int ns) {
-    return NR * XL * R_SMEM + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + SLACK;
+    return NR_SMEM * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + SLACK;
   }
   // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
   static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
   // Column stages: as many as fit (at most 8), so that the copies of the next chunks are in flight during the
   // elementwise stage; 3xTF32 one or two.
   static constexpr int NS = fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
-  static constexpr int OFF_C = NR * XL * R_SMEM;
+  static constexpr int OFF_C = NR_SMEM * XL * R_BYTES;
   static constexpr int OFF_G = OFF_C + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_G + NB * NG * XL * G_BYTES;
   // r_full/empty, c_full/empty, sd_full/empty, g_full/empty, acc_full/empty, drain; 3xTF32: r_ready, c_ready.
@@ -159,7 +162,7 @@ struct BwdCfg {
   static_assert(!G_TMEM || (NSD >= 2 && TMEM_NEED <= TMEM_MAX), "TMEM dS / P: two S / dP buffers and the accumulators");
   static_assert(!(G_TMEM && X3) || (CH == 1 && NG == 1), "3xTF32 TMEM dS / P: one of dS / P, 32-wide tiles");
   static_assert(F32 || TMEM_NEED <= 256, "bf16: two CTAs per SM");
-  static_assert(!R_TMEM || (G_TMEM && MIN_BLOCKS == 1), "TMEM row operands: tf32, one CTA per SM");
+  static_assert(!R_TMEM || (G_TMEM && MIN_BLOCKS == 1), "TMEM row operands: one CTA per SM");
   static_assert(SMEM_BYTES == smem_bytes(NS), "shared memory layout");
 };
 
@@ -223,7 +226,8 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
     return;
   }
   // Row operand i (hi, or the operand itself), its lo copy at +NR; column slot s of a stage, lo copy at +NC.
-  auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR + i) * C::R_BYTES; };
+  // Row operand i >= NR_TMEM (the ones in shared memory), its lo copy at +NR_SMEM.
+  auto r_op = [&](int i, int lo) { return sbase + (lo * C::NR_SMEM + (i - C::NR_TMEM)) * C::R_BYTES; };
   auto stage = [&](int s) { return sbase + C::OFF_C + s * C::STAGE_BYTES; };
   auto slot = [&](uint32_t sb, int s, int lo) { return sb + (lo * C::NC + s) * C::C_BYTES; };
   auto g_tile = [&](int b, int which, int lo) {
@@ -253,7 +257,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   int trace_count = 0;  // FWN_TRACE builds: this lane's event count
 #define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
   if (threadIdx.x == 0) {
-    mbar_init(r_full, C::R_TMEM ? 4 : 1);
+    mbar_init(r_full, (C::NR_TMEM > 0 ? 4 : 0) + (C::NR_SMEM > 0 ? 1 : 0));
     mbar_init(r_empty, 1);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(c_full(s), (GATHER && C::ROWS_ARE_KEYS) ? 2 : 1);
@@ -325,14 +329,15 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       if (nch == 0) continue;
       ChunkMeta<CH> m0 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 0, lane);
       ChunkMeta<CH> m1 = load_chunk_meta<CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
-      if constexpr (!C::R_TMEM) {
+      if constexpr (C::NR_SMEM > 0) {
+        // The row operands that live in shared memory.
         if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
         if (lane == 0) {
-          mbar_arrive_expect_tx(r_full, C::NR * C::R_BYTES);
+          mbar_arrive_expect_tx(r_full, C::NR_SMEM * C::R_BYTES);
           for (int cb = 0; cb < C::CB; ++cb) {
-            tma_load_4d(r_op(0, 0) + cb * C::ROWS * 128, &tm_r0, cb * C::EPB, h, pb * C::ROWS, b, r_full);
-            if (C::NR == 2)
-              tma_load_4d(r_op(1, 0) + cb * C::ROWS * 128, &tm_r1, cb * C::EPB, h, pb * C::ROWS, b, r_full);
+            for (int op = C::NR_TMEM; op < C::NR; ++op)
+              tma_load_4d(r_op(op, 0) + cb * C::ROWS * 128, op == 0 ? &tm_r0 : &tm_r1, cb * C::EPB, h, pb * C::ROWS, b,
+                          r_full);
           }
         }
         pending_r = 1;
@@ -512,9 +517,11 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                 const uint32_t cb = kk / 4, within = (kk % 4) * 32;
                 const uint64_t a = (pass == 2 ? r_lo : r_hi) + ((cb * C::ROWS * 128 + within) >> 4);
                 const uint64_t bd = (pass == 1 ? c_lo : c_hi) + ((cb * C::COLS * 128 + within) >> 4);
-                if constexpr (C::R_TMEM) {
-                  // A = the row operand in TMEM: K = 8 tf32 elements = 8 columns per MMA.
-                  issue_([&] { mma_ts<true>(tmem + sd_col + C::DP_OFF * op, tmem + op * D + 8 * kk, bd, idesc, kk > 0 ? 1u : 0u); });
+                if (op < C::NR_TMEM) {
+                  // A = the row operand in TMEM (3xTF32: its lo copy D columns on in the third pass): K = 8 tf32
+                  // elements = 8 columns per MMA.
+                  const uint32_t a_t = tmem + op * D * C::XL + (pass == 2 ? D : 0) + 8 * kk;
+                  issue_([&] { mma_ts<true>(tmem + sd_col + C::DP_OFF * op, a_t, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
                 } else {
                   issue_([&] { mma_ss<F32>(tmem + sd_col + C::DP_OFF * op, a, bd, idesc, (pass > 0 || kk > 0) ? 1u : 0u); });
                 }
@@ -620,7 +627,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
       const int nch = (n_sub + CH - 1) / CH;
       if (nch == 0) continue;
       if (!(ok = mbar_wait(r_full, qc & 1, abort_flag))) break;
-      for (int op = 0; op < C::NR; ++op) split_tf32(r_op(op, 0), r_op(op, 1), C::R_BYTES, ctid, 128);
+      for (int op = C::NR_TMEM; op < C::NR; ++op) split_tf32(r_op(op, 0), r_op(op, 1), C::R_BYTES, ctid, 128);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(r_ready);
@@ -669,7 +676,7 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
           if (!(ok = mbar_wait(r_empty, (qc & 1) ^ 1, abort_flag))) break;
           tc_fence_after();
 #pragma unroll
-          for (int op = 0; op < C::NR; ++op) {
+          for (int op = 0; op < C::NR_TMEM; ++op) {
             const float* src = nullptr;
             if (grow < p.n) {
               src = static_cast<const float*>(op == 0 ? p.r0 : p.r1) +
@@ -689,7 +696,18 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
                 v[4 * i + 2] = x.z;
                 v[4 * i + 3] = x.w;
               }
-              tmem_st32(trow + op * D + 32 * j, v);
+              if constexpr (X3) {
+                // hi (13 low mantissa bits cleared) and lo = x - hi, D columns apart.
+                float lo[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const float hi = __uint_as_float(__float_as_uint(v[i]) & 0xFFFFE000u);
+                  lo[i] = v[i] - hi;
+                  v[i] = hi;
+                }
+                tmem_st32(trow + op * D * C::XL + D + 32 * j, lo);
+              }
+              tmem_st32(trow + op * D * C::XL + 32 * j, v);
             }
           }
           tmem_wait_st();

@@ -77,15 +77,15 @@ struct FwdCfg {
   // tf32 (one CTA per SM): Q lives in TMEM, one fp32 element per column (the A operand of S, loaded by the softmax
   // warps: thread = row = lane), and shared memory holds only K / V stages; MMAs that take A from TMEM read a
   // quarter of the shared-memory bytes.
-  static constexpr bool Q_TMEM = F32 && !X3;
-  static constexpr int OFF_STAGE = Q_TMEM ? 0 : Q_BYTES * (X3 ? 2 : 1);  // Q (3xTF32: Q_hi in place, Q_lo)
+  static constexpr bool Q_TMEM = F32;
+  static constexpr int OFF_STAGE = Q_TMEM ? 0 : Q_BYTES;
   // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word, 1 KB of slack to
   // align the dynamic shared memory base up to 1024 bytes.
   static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16 + 1024; }
   static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
   // K/V stages: as many as fit (bf16: two CTAs per SM; tf32: one) up to 6, so that the copies of the next chunks
   // are in flight while the softmax works; 3xTF32 2.
-  static constexpr int NS = X3 ? 2 : fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : fit(3) ? 3 : 2;
+  static constexpr int NS = fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : fit(3) ? 3 : 2;
   static constexpr int OFF_P = OFF_STAGE + NS * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
@@ -109,7 +109,7 @@ struct FwdCfg {
   static_assert(N_BAR == 14 + 3 * NS && SMEM_BYTES == smem_bytes(NS), "shared memory layout");
   static_assert(!P_TMEM || (P_COL + P_STRIDE + PW <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)), "TMEM budget");
   static_assert(TMEM_COLS == 256 || MIN_BLOCKS == 1, "512 TMEM columns: one CTA per SM");
-  static_assert(!Q_TMEM || Q_COL + D <= TMEM_COLS, "TMEM budget (Q)");
+  static_assert(!Q_TMEM || Q_COL + D * (X3 ? 2 : 1) <= TMEM_COLS, "TMEM budget (Q)");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         }
         const int nch = (n_sub + C::CH - 1) / C::CH;
         if (nch == 0) continue;
-        if (!(ok = wait_(X3 ? q_ready : q_full, qc & 1))) break;
+        if (!(ok = wait_((X3 && !C::Q_TMEM) ? q_ready : q_full, qc & 1))) break;
         if (lane == 0) FWN_TR(10, it);
         const uint32_t g0 = g;
         // S = Q K^T of chunk c (K / V must have landed and the S buffer must be free).
@@ -352,8 +352,10 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
               const uint64_t a = (pass == 2 ? qlo_desc : qdesc) + ((cb * C::ROWS * 128 + within) >> 4);
               const uint64_t bd = (pass == 1 ? klo_desc : kdesc) + ((cb * C::KEYS * 128 + within) >> 4);
               if constexpr (C::Q_TMEM) {
-                // A = Q in TMEM: K = 8 tf32 elements = 8 columns per MMA.
-                issue_([&] { mma_ts<true>(tmem + sb * 64, tmem + C::Q_COL + 8 * kk, bd, idesc_s, kk > 0 ? 1u : 0u); });
+                // A = Q in TMEM (3xTF32: its lo copy D columns on in the third pass): K = 8 tf32 elements = 8
+                // columns per MMA.
+                const uint32_t a_t = tmem + C::Q_COL + (pass == 2 ? D : 0) + 8 * kk;
+                issue_([&] { mma_ts<true>(tmem + sb * 64, a_t, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
               } else {
                 issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
               }
@@ -432,11 +434,13 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       const int n_sub = p.ptr2[pb + 1] - p.ptr2[pb];
       const int nch = (n_sub + C::CH - 1) / C::CH;
       if (nch == 0) continue;
-      if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
-      split_tf32(q_smem, q_lo, C::Q_BYTES, ctid, 128);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_ready);
+      if constexpr (!C::Q_TMEM) {
+        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+        split_tf32(q_smem, q_lo, C::Q_BYTES, ctid, 128);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_ready);
+      }
       for (int c = 0; c < nch; ++c, ++g) {
         const int st = g % C::NS;
         if (!(ok = mbar_wait(kv_full(st), (g / C::NS) & 1, abort_flag))) break;
@@ -489,6 +493,17 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
               v[4 * i + 1] = x.y;
               v[4 * i + 2] = x.z;
               v[4 * i + 3] = x.w;
+            }
+            if constexpr (X3) {
+              // hi (13 low mantissa bits cleared) and lo = x - hi, D columns apart.
+              float lo[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float hi = __uint_as_float(__float_as_uint(v[i]) & 0xFFFFE000u);
+                lo[i] = v[i] - hi;
+                v[i] = hi;
+              }
+              tmem_st32(trow + C::Q_COL + D + 32 * j, lo);
             }
             tmem_st32(trow + C::Q_COL + 32 * j, v);
           }

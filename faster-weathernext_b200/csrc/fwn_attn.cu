@@ -786,7 +786,8 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
   if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
     return g ? launch_fwd<64, true, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
              : launch_fwd<64, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
-  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
+  return g ? launch_fwd<128, true, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
+           : launch_fwd<128, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
 }
 
 fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes) {
@@ -883,7 +884,7 @@ fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k,
     return launch_bwd<128, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
   if (d.mode == FWN_MODE_TF32X3 && d.head_dim == 64)
     return launch_bwd<64, true, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
-  return fail(FWN_ERR_UNSUPPORTED, "mode %d with head_dim %d is not built yet", d.mode, d.head_dim);
+  return launch_bwd<128, true, true>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);
 }
 
 }  // namespace

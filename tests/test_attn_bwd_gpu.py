@@ -232,12 +232,32 @@ def test_tf32_head_dim_128(golden, cuda, mask_kind):
     assert oa.max_rel(a, r) < 3e-2, (name, oa.max_rel(a, r))
 
 
-def test_tf32x3_head_dim_128_is_refused(cuda):
-  """3xTF32 at head_dim 128 is not built: a clean NotImplementedError, nothing launched."""
+@pytest.mark.parametrize("mask_kind", ["khop", "ref_nonsym"])
+@pytest.mark.parametrize("gather", [True, False])
+def test_tf32x3_head_dim_128(golden, cuda, mask_kind, gather):
+  """3xTF32 at head_dim 128 (the WeatherNext 2 head size in the fp32-equivalent mode; Q / the first row operand in
+  TMEM as hi and lo copies): forward and gradients within 2e-5 rel RMS of the float64 reference, and the reference
+  test's max-abs bounds (1e-5 output, 1e-4 gradients, tests/test_pallas_kernel.py:36, 98)."""
+  from faster_weathernext import _lib
   from faster_weathernext import tiled_attn as ta
-  from faster_weathernext import mesh
-  m, _, _ = mesh.config_mask(1)
-  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
-  q = torch.randn(1, 642, 2, 128, device=cuda)
-  with pytest.raises(NotImplementedError):
-    ta.attention(q, q, q, tiles, scale=0.1, precision="highest")
+  if mask_kind == "khop":
+    m = _khop_mask(4, 6)
+  else:
+    m = golden_mask(golden["tiles"], "k_nonsym")
+  n = m.shape[0]
+  q, k, v, do = kernel_inputs(43, (2, n, 2, 128), 4)
+  scale = 128 ** -0.5
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda, gather=gather)
+  tq, tk, tv, tdo = (torch.from_numpy(x).to(cuda) for x in (q, k, v, do))
+  o, lse = ta.attention_forward(tq, tk, tv, tiles, scale, _lib.MODE_TF32X3, with_lse=True)
+  dq, dk, dv = ta.attention_backward(tq, tk, tv, o, lse, tdo, tiles, scale, _lib.MODE_TF32X3)
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  ref_o, _ = oa.sparse_attention(q, k, v, m, scale)
+  assert oa.rel_rms(o.cpu().numpy(), ref_o) < TOL["tf32x3"]
+  assert oa.max_rel(o.cpu().numpy(), ref_o) < 1e-5
+  ref = oa.sparse_attention_vjp(q, k, v, do, m, scale)
+  for name, a, r in zip(("dq", "dk", "dv"), (dq, dk, dv), ref):
+    a = a.cpu().numpy()
+    assert oa.rel_rms(a, r) < TOL["tf32x3"], (name, oa.rel_rms(a, r))
+    assert oa.max_rel(a, r) < 1e-4, (name, oa.max_rel(a, r))
