@@ -6,22 +6,24 @@
 //
 // Why separate kernels: as in the forward, tcgen05.mma instructions with N = 32 or 64 leave most of the
 // tensor core idle on dense masks. Here a chunk is four consecutive tiles of the list (128 columns), so
-// S and dP are N = 128 MMAs and the accumulating MMAs have K = 128. At head_dim 128 the operands of one
-// dK/dV pass do not fit one CTA, so there are three passes ("kinds"), each one CTA per SM:
-//               dQ              dV only         dK only
-//   rows        queries         keys            keys            (128 per work item, held all item long)
-//   R0, R1      Q, dO           K               K, V
-//   C0, C1      K, V            Q, dO           Q, dO           (per chunk, in rings)
+// S and dP are N = 128 MMAs and the accumulating MMAs have K = 128. Passes ("kinds"), one CTA per SM each:
+//               dQ              dK and dV       (dV only         dK only)
+//   rows        queries         keys            keys             keys     (128 per work item, held all item long)
+//   R0, R1      Q, dO           K, V            K                K, V
+//   C0, C1      K, V            Q, dO           Q, dO            Q, dO    (per chunk, in rings)
 //   S  = R0 C0^T, dP = R1 C1^T  (dV only: no dP)
 //   acc += G C                  G = dS, C = C0 (dQ, dK); G = P, C = C1 (dV); C read MN-major
-// G (bf16, 128 x 128) is written by the elementwise warps into TMEM and is the A operand of the
-// accumulating MMA (two G buffers). A column operand read again by the accumulating MMA lives in a ring of
-// three slots, one read only by S / dP in a ring of two. Rows are keys for dV / dK: their columns' lse and
-// delta come with the chunk (a ring of vectors); for dQ they are per thread.
+// dQ: G (bf16, 128 x 128) is written by the elementwise warps into TMEM and is the A operand of the
+// accumulating MMA (two G buffers); a column operand read again by the accumulating MMA lives in a ring of
+// three slots, one read only by S / dP in a ring of two. dK and dV: S, dP and both accumulators take all 512
+// TMEM columns, so P is written over S and dS over dP (one S / dP buffer; chunks follow one another, with P
+// computed while dP runs and dS while dV runs) and both column operands sit in rings of two. The dV-only and
+// dK-only kinds are the same passes split (one accumulator each, S recomputed by both). Rows are keys for dK /
+// dV: their columns' lse and delta come with the chunk (a ring of vectors); for dQ they are per thread.
 //
 // Roles (576 threads): warp 0 TMA producer; warp 1 TMEM allocation and MMA issue (the warp runs the loop
-// with warp-uniform descriptors, one elected lane issues; S and dP of chunk c+1 ahead of the accumulating MMA
-// of chunk c); warps 2-17 elementwise, four per TMEM lane
+// with warp-uniform descriptors, one elected lane issues; except in the dK and dV pass, S and dP of chunk c+1
+// ahead of the accumulating MMA of chunk c); warps 2-17 elementwise, four per TMEM lane
 // quadrant (thread = row), one 32-column tile of each chunk each; the mask words are read from global
 // memory one chunk ahead. Epilogue: each warp stores a quarter of the accumulator columns. Every mbarrier
 // wait is bounded (common.cuh).
@@ -36,9 +38,12 @@ namespace fwn {
 
 template <int KIND, int D>
 struct BwdWideCfg {
+  // dK and dV in one pass (kBwdDKV): one S / dP buffer, P written over S and dS over dP (bf16 pairs, in the
+  // first 16 of each 32-column tile's columns), accumulators dV and dK in the other 256 columns.
+  static constexpr bool FUSED = KIND == kBwdDKV;
   static constexpr bool ROWS_ARE_KEYS = KIND != kBwdDQ;
   static constexpr bool NEED_DP = KIND != kBwdDV;
-  static constexpr bool ACC_ON_C0 = KIND != kBwdDV;   // dS C0 (dQ, dK) or P C1 (dV)
+  static constexpr bool ACC_ON_C0 = KIND != kBwdDV;   // dS C0 (dQ, dK) or P C1 (dV); fused: both
   static constexpr int ES = 2;
   static constexpr int EPB = 64;
   static constexpr int CB = D / EPB;
@@ -49,8 +54,10 @@ struct BwdWideCfg {
   static constexpr int NR = NEED_DP ? 2 : 1;
   static constexpr int R_BYTES = CB * ROWS * 128;
   static constexpr int C_BYTES = CB * COLS * 128;
-  static constexpr int N0 = ACC_ON_C0 ? 3 : 2;      // C0 ring
-  static constexpr int N1 = ACC_ON_C0 ? 2 : 3;      // C1 ring
+  // C0 / C1 rings. Fused: both operands are read again by an accumulating MMA; chunks run one after the other
+  // (one S / dP buffer), so two slots each keep the next chunk's copies in flight.
+  static constexpr int N0 = FUSED ? (D == 128 ? 2 : 3) : ACC_ON_C0 ? 3 : 2;
+  static constexpr int N1 = FUSED ? (D == 128 ? 2 : 3) : ACC_ON_C0 ? 2 : 3;
   static constexpr int NVEC = ROWS_ARE_KEYS ? 2 : 0;  // lse / delta vectors of the chunk's columns (1 KB)
   static constexpr int NVEC_RING = NVEC > 0 ? NVEC : 1; // ring arithmetic (no vectors for dQ)
   static constexpr int OFF_C0 = NR * R_BYTES;
@@ -61,10 +68,11 @@ struct BwdWideCfg {
   static constexpr int N_BAR = 2 + 2 * N0 + 2 * N1 + 2 * NVEC + 2 * NSB + 4 + 3;
   // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
-  // TMEM: S[NSB] (128 each), dP (128), acc (D), G[2] (64 each).
+  // TMEM: S[NSB] (128 each), dP (128), acc (D), G[2] (64 each); fused: S (P), dP (dS), dV (D), dK (D).
   static constexpr int DP_COL = 128 * NSB;
   static constexpr int ACC_COL = DP_COL + (NEED_DP ? 128 : 0);
   static constexpr int G_COL = ACC_COL + D;
+  static constexpr int ACC_K_COL = ACC_COL + D;  // fused: dK
   static constexpr int TMEM_COLS = 512;
   // Elementwise warps: four per TMEM lane quadrant, one 32-column tile of the chunk each (18 warps: at most
   // 102 registers per thread, as each sub-partition holds 16,384 and takes five warps).
@@ -72,7 +80,7 @@ struct BwdWideCfg {
   static constexpr int THREADS = 64 + 32 * EW;
   static constexpr int MAX_REGS = 96;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(G_COL + 128 <= TMEM_COLS, "TMEM budget");
+  static_assert(FUSED ? (NSB == 1 && ACC_K_COL + D <= TMEM_COLS) : G_COL + 128 <= TMEM_COLS, "TMEM budget");
 };
 
 template <int KIND, int D>
@@ -111,6 +119,10 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
   auto g_full = [&](int b) { return bar4 + 8 * b; };
   auto g_empty = [&](int b) { return bar4 + 16 + 8 * b; };
   const uint32_t acc_full = bar4 + 32, acc_empty = bar4 + 40, drain = bar4 + 48;
+  // Fused dK / dV pass (the same slots): S and dP done (MMA commits), P and dS written (elementwise arrivals),
+  // S and dP columns free again (the dV / dK MMAs that read P / dS are complete).
+  [[maybe_unused]] const uint32_t f_s_full = s_full(0), f_dp_full = s_empty(0);
+  [[maybe_unused]] const uint32_t f_p_full = g_full(0), f_ds_full = g_full(1), f_s_free = g_empty(0), f_dp_free = g_empty(1);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
   int trace_count = 0;  // FWN_TRACE builds: this lane's event count
@@ -134,7 +146,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
     }
     for (int b = 0; b < C::NSB; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), C::EW);
+      mbar_init(s_empty(b), C::FUSED ? 1 : C::EW);  // fused: dP done (MMA commit)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(g_full(b), C::EW);
@@ -278,6 +290,78 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       if (nch == 0) continue;
       if (!(ok = warp_wait(r_full, qc & 1, abort_flag))) break;
       const uint32_t g0 = g;
+      if constexpr (C::FUSED) {
+        // Per chunk, in this order on the tensor pipe: S (over the previous chunk's P, once its dV MMAs are
+        // complete), dP (likewise over dS), dV += P^T dO once P is written, dK += dS^T Q once dS is written.
+        // The elementwise warps compute P while dP runs and dS while dV runs.
+        for (int c = 0; c < nch && ok; ++c) {
+          const uint32_t gg = g0 + c;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          const int s0 = gg % C::N0, s1 = gg % C::N1;
+          if (!(ok = warp_wait(c0_full(s0), (gg / C::N0) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(c1_full(s1), (gg / C::N1) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(f_s_free, (gg & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(13, c);
+          tc_fence_after();
+          const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
+          const uint64_t c0desc = smem_desc(c0_slot(s0), 16, 1024);
+          const uint64_t c1desc = smem_desc(c1_slot(s1), 16, 1024);
+          if (elect_one_sync()) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<false>(tmem, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
+                            c0desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(f_s_full);
+          }
+          __syncwarp();
+          if (!(ok = warp_wait(f_dp_free, (gg & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          if (elect_one_sync()) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
+                            c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(f_dp_full);
+            if (c == nch - 1) mma_commit(r_empty);
+          }
+          __syncwarp();
+          if (lane == 0) FWN_TR(11, c);
+          // A = P / dS from TMEM: K-step kk reads 8 columns of packed pairs at 32 (kk / 2) + 8 (kk % 2).
+          const int ksteps = 2 * n_in;
+          if (!(ok = warp_wait(f_p_full, gg & 1, abort_flag))) break;
+          if (c == 0 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          if (elect_one_sync()) {
+            const uint64_t bdesc = smem_desc(c1_slot(s1), C::COLS * 128, 1024);
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_ts(tmem + C::ACC_COL, tmem + 32 * (kk >> 1) + 8 * (kk & 1), bdesc + ((kk * 16 * 128) >> 4),
+                     kIdescAcc, (c == 0 && kk == 0) ? 0u : 1u);
+            mma_commit(f_s_free);
+            mma_commit(c1_empty(s1));
+          }
+          __syncwarp();
+          if (!(ok = warp_wait(f_ds_full, gg & 1, abort_flag))) break;
+          tc_fence_after();
+          if (elect_one_sync()) {
+            const uint64_t bdesc = smem_desc(c0_slot(s0), C::COLS * 128, 1024);
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_ts(tmem + C::ACC_K_COL, tmem + C::DP_COL + 32 * (kk >> 1) + 8 * (kk & 1),
+                     bdesc + ((kk * 16 * 128) >> 4), kIdescAcc, (c == 0 && kk == 0) ? 0u : 1u);
+            mma_commit(f_dp_free);
+            mma_commit(c0_empty(s0));
+            if (c == nch - 1) mma_commit(acc_full);
+          }
+          __syncwarp();
+          if (lane == 0) FWN_TR(12, c);
+        }
+        g = g0 + nch;
+        ++qc;
+        continue;
+      }
       for (int c = 0; c <= nch && ok; ++c) {
         if (c < nch) {
           const uint32_t gg = g0 + c;
@@ -374,95 +458,179 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       };
       uint32_t nw = nch > 0 ? word(0) : 0u;
       const uint32_t g0 = g;
-      for (int c = 0; c < nch; ++c) {
-        const uint32_t gg = g0 + c;
-        const int sb = gg % C::NSB, gb = gg & 1;
-        const int n_in = min(C::CH, n_sub - C::CH * c);
-        const uint32_t w = nw;
-        if (c + 1 < nch) nw = word(c + 1);
-        const uint32_t a = __reduce_or_sync(0xffffffffu, w);
-        if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
-        if (lane == 0) FWN_TR(20, c);
-        tc_fence_after();
-        // S (and dP) of this tile -> registers; then the buffer is released for the next S MMA.
-        float s[32], dp[32];
-        if (j < n_in) {
-          tmem_ld32(trow + 128 * sb + 32 * j, s);
-          if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(s_empty(sb));
-        // Column lse (as -lse * log2 e) and delta of this tile (rows are keys).
-        uint32_t vslot = 0;
-        if constexpr (C::ROWS_ARE_KEYS) {
+      if constexpr (C::FUSED) {
+        for (int c = 0; c < nch; ++c) {
+          const uint32_t gg = g0 + c;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          const uint32_t w = nw;
+          if (c + 1 < nch) nw = word(c + 1);
+          const uint32_t a = __reduce_or_sync(0xffffffffu, w);
           const uint32_t vs = gg % C::NVEC_RING;
           if (!(ok = mbar_wait(v_full(vs), (gg / C::NVEC_RING) & 1, abort_flag))) break;
-          vslot = vec_slot(vs) + 128 * j;
-        }
-        // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs.
-        uint32_t pk[16];
-        const float2 cc = make_float2(c2, c2);
+          const uint32_t vslot = vec_slot(vs) + 128 * j;
+          if (!(ok = mbar_wait(f_s_full, gg & 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(20, c);
+          tc_fence_after();
+          // P = exp2(S scale log2 e - lse log2 e) on the allowed columns, kept in s (fp32) for dS and written
+          // as packed bf16 pairs over this tile's own S columns (read above by this warp only).
+          float s[32];
+          if (j < n_in) tmem_ld32(trow + 32 * j, s);
+          tmem_wait_ld();
+          uint32_t pk[16];
+          const float2 cc = make_float2(c2, c2);
 #pragma unroll
-        for (int gi = 0; gi < 4; ++gi) {
-          if ((a >> (8 * gi)) & 0xFFu) {
-            float lv[8], dv[8];
-            if constexpr (C::ROWS_ARE_KEYS) {
+          for (int gi = 0; gi < 4; ++gi) {
+            if ((a >> (8 * gi)) & 0xFFu) {
               const uint32_t va = vslot + 32 * gi;
               const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
-              lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
+              const float lv[8] = {l0.x * -kLog2e, l0.y * -kLog2e, l0.z * -kLog2e, l0.w * -kLog2e,
+                                   l1.x * -kLog2e, l1.y * -kLog2e, l1.z * -kLog2e, l1.w * -kLog2e};
 #pragma unroll
-              for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
-              if constexpr (C::NEED_DP) {
-                const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
-                dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
+              for (int i = 0; i < 8; i += 2) {
+                const int k = 8 * gi + i;
+                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
+                float2 e;
+                if (i < 2) {
+                  e = exp2_poly2(x);
+                } else {
+                  e.x = ex2(x.x);
+                  e.y = ex2(x.y);
+                }
+                s[k] = (w >> k) & 1u ? e.x : 0.f;
+                s[k + 1] = (w >> (k + 1)) & 1u ? e.y : 0.f;
+                pk[k >> 1] = pack_bf16(s[k], s[k + 1]);
               }
             } else {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                lv[i] = nl2_row;
-                dv[i] = delta_row;
-              }
+              for (int i = 0; i < 4; ++i) pk[4 * gi + i] = 0u;
             }
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-              const int k = 8 * gi + i;
-              const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
-              float2 e;
-              if (i < 2) {
-                e = exp2_poly2(x);
-              } else {
-                e.x = ex2(x.x);
-                e.y = ex2(x.y);
-              }
-              e.x = (w >> k) & 1u ? e.x : 0.f;
-              e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
-              if constexpr (C::NEED_DP) {
-                const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
-                pk[k >> 1] = pack_bf16(ds.x, ds.y);
-              } else {
-                pk[k >> 1] = pack_bf16(e.x, e.y);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) pk[4 * gi + i] = 0u;
           }
-        }
-        if constexpr (C::ROWS_ARE_KEYS) {
+          if (j < n_in) tmem_st16(trow + 32 * j, pk);
+          tmem_wait_st();
+          tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(v_empty(gg % C::NVEC_RING));
+          if (lane == 0) mbar_arrive(f_p_full);
+          // dS = P (dP - delta), over this tile's dP columns.
+          if (!(ok = mbar_wait(f_dp_full, gg & 1, abort_flag))) break;
+          tc_fence_after();
+          float dp[32];
+          if (j < n_in) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int gi = 0; gi < 4; ++gi) {
+            if ((a >> (8 * gi)) & 0xFFu) {
+              const uint32_t va = vslot + 512 + 32 * gi;
+              const float4 d0 = ld_shared_f32x4(va), d1 = ld_shared_f32x4(va + 16);
+              const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const int k = 8 * gi + i;
+                const float2 ds = fmul2(make_float2(s[k], s[k + 1]),
+                                        fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
+                pk[k >> 1] = pack_bf16(ds.x, ds.y);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(v_empty(vs));
+          if (j < n_in) tmem_st16(trow + C::DP_COL + 32 * j, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(f_ds_full);
+          if (lane == 0) FWN_TR(21, c);
         }
-        if (lane == 0) FWN_TR(26, c);
-        // G buffer free once the accumulating MMA of chunk gg-2 is complete.
-        if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
-        if (j < n_in) tmem_st16(trow + C::G_COL + 64 * gb + 16 * j, pk);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(g_full(gb));
-        if (lane == 0) FWN_TR(21, c);
+      } else {
+        for (int c = 0; c < nch; ++c) {
+          const uint32_t gg = g0 + c;
+          const int sb = gg % C::NSB, gb = gg & 1;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          const uint32_t w = nw;
+          if (c + 1 < nch) nw = word(c + 1);
+          const uint32_t a = __reduce_or_sync(0xffffffffu, w);
+          if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(20, c);
+          tc_fence_after();
+          // S (and dP) of this tile -> registers; then the buffer is released for the next S MMA.
+          float s[32], dp[32];
+          if (j < n_in) {
+            tmem_ld32(trow + 128 * sb + 32 * j, s);
+            if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
+          }
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_empty(sb));
+          // Column lse (as -lse * log2 e) and delta of this tile (rows are keys).
+          uint32_t vslot = 0;
+          if constexpr (C::ROWS_ARE_KEYS) {
+            const uint32_t vs = gg % C::NVEC_RING;
+            if (!(ok = mbar_wait(v_full(vs), (gg / C::NVEC_RING) & 1, abort_flag))) break;
+            vslot = vec_slot(vs) + 128 * j;
+          }
+          // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs.
+          uint32_t pk[16];
+          const float2 cc = make_float2(c2, c2);
+  #pragma unroll
+          for (int gi = 0; gi < 4; ++gi) {
+            if ((a >> (8 * gi)) & 0xFFu) {
+              float lv[8], dv[8];
+              if constexpr (C::ROWS_ARE_KEYS) {
+                const uint32_t va = vslot + 32 * gi;
+                const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
+                lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
+  #pragma unroll
+                for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
+                if constexpr (C::NEED_DP) {
+                  const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
+                  dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
+                }
+              } else {
+  #pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  lv[i] = nl2_row;
+                  dv[i] = delta_row;
+                }
+              }
+  #pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const int k = 8 * gi + i;
+                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
+                float2 e;
+                if (i < 2) {
+                  e = exp2_poly2(x);
+                } else {
+                  e.x = ex2(x.x);
+                  e.y = ex2(x.y);
+                }
+                e.x = (w >> k) & 1u ? e.x : 0.f;
+                e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
+                if constexpr (C::NEED_DP) {
+                  const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
+                  pk[k >> 1] = pack_bf16(ds.x, ds.y);
+                } else {
+                  pk[k >> 1] = pack_bf16(e.x, e.y);
+                }
+              }
+            } else {
+  #pragma unroll
+              for (int i = 0; i < 4; ++i) pk[4 * gi + i] = 0u;
+            }
+          }
+          if constexpr (C::ROWS_ARE_KEYS) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(v_empty(gg % C::NVEC_RING));
+          }
+          if (lane == 0) FWN_TR(26, c);
+          // G buffer free once the accumulating MMA of chunk gg-2 is complete.
+          if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+          if (j < n_in) tmem_st16(trow + C::G_COL + 64 * gb + 16 * j, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(g_full(gb));
+          if (lane == 0) FWN_TR(21, c);
+        }
       }
       if (!ok) break;
       g = g0 + nch;
@@ -471,26 +639,36 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       const bool store = grow < p.n;
       const int64_t roff = (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sn +
                             static_cast<int64_t>(h) * p.o_sh) * C::ES + OC * C::ES * j;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(C::ACC_ON_C0 ? p.out0 : p.out1) + roff;
-      const float mul = C::ACC_ON_C0 ? p.scale : 1.f;
+      // Accumulators: dK (scaled, to out0) and / or dV (to out1); fused passes store both.
+      constexpr int NACC = C::FUSED ? 2 : 1;
       if (nch == 0) {
         if (store)
-          for (int i = 0; i < OC * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+          for (int ai = 0; ai < NACC; ++ai) {
+            uint8_t* dst = reinterpret_cast<uint8_t*>((C::FUSED ? ai == 1 : C::ACC_ON_C0) ? p.out0 : p.out1) + roff;
+            for (int i = 0; i < OC * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+          }
         continue;
       }
       if (!(ok = mbar_wait(acc_full, qc & 1, abort_flag))) break;
       tc_fence_after();
 #pragma unroll
-      for (int jj = 0; jj < OC / 16; ++jj) {
-        float o[16];
-        tmem_ld16(trow + C::ACC_COL + OC * j + 16 * jj, o);
-        tmem_wait_ld();
-        if (store) {
+      for (int ai = 0; ai < NACC; ++ai) {
+        const bool is_dk = C::FUSED ? ai == 1 : C::ACC_ON_C0;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(is_dk ? p.out0 : p.out1) + roff;
+        const float mul = is_dk ? p.scale : 1.f;
+        const uint32_t acc_col = C::FUSED && ai == 1 ? C::ACC_K_COL : C::ACC_COL;
 #pragma unroll
-          for (int i = 0; i < 2; ++i)
-            reinterpret_cast<uint4*>(dst + jj * 32)[i] =
-                make_uint4(pack_bf16(o[8 * i] * mul, o[8 * i + 1] * mul), pack_bf16(o[8 * i + 2] * mul, o[8 * i + 3] * mul),
-                           pack_bf16(o[8 * i + 4] * mul, o[8 * i + 5] * mul), pack_bf16(o[8 * i + 6] * mul, o[8 * i + 7] * mul));
+        for (int jj = 0; jj < OC / 16; ++jj) {
+          float o[16];
+          tmem_ld16(trow + acc_col + OC * j + 16 * jj, o);
+          tmem_wait_ld();
+          if (store) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              reinterpret_cast<uint4*>(dst + jj * 32)[i] =
+                  make_uint4(pack_bf16(o[8 * i] * mul, o[8 * i + 1] * mul), pack_bf16(o[8 * i + 2] * mul, o[8 * i + 3] * mul),
+                             pack_bf16(o[8 * i + 4] * mul, o[8 * i + 5] * mul), pack_bf16(o[8 * i + 6] * mul, o[8 * i + 7] * mul));
+          }
         }
       }
       tc_fence_before();

@@ -461,7 +461,7 @@ fwn_status launch_bwd_wide(const fwn_attn_desc& d, const void* q, const void* k,
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0w, c1w, p);
   cudaError_t e = cudaGetLastError();
-  static const char* const kNames[] = {"attn_bwd_wide dq launch", "", "attn_bwd_wide dv launch",
+  static const char* const kNames[] = {"attn_bwd_wide dq launch", "attn_bwd_wide dkv launch", "attn_bwd_wide dv launch",
                                        "attn_bwd_wide dk launch"};
   if (e != cudaSuccess) return cuda_fail(e, kNames[KIND]);
   return FWN_OK;
@@ -523,8 +523,8 @@ fwn_status launch_bwd(const fwn_attn_desc& d, const void* q, const void* k, cons
       parts &= ~kDq;
     }
     if ((parts & kDkv) && use_wide(d, *tt)) {
-      if ((s = launch_bwd_wide<fwn::kBwdDV, D>(d, q, k, v, d_o, lse, delta, *tt, nullptr, dv, stream)) != FWN_OK) return s;
-      if ((s = launch_bwd_wide<fwn::kBwdDK, D>(d, q, k, v, d_o, lse, delta, *tt, dk, nullptr, stream)) != FWN_OK) return s;
+      // dK and dV in one pass (P / dS written over S / dP in TMEM).
+      if ((s = launch_bwd_wide<fwn::kBwdDKV, D>(d, q, k, v, d_o, lse, delta, *tt, dk, dv, stream)) != FWN_OK) return s;
       parts &= ~kDkv;
     }
   }
