@@ -37,9 +37,13 @@ CFG = 3
 # Kernel FLOP counts per allowed (query, key) pair per head and head_dim element: forward S and P V (4);
 # dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
 USEFUL_PER_PAIR = 14
-# DRAM bytes (read + write) per launch at this workload from one ncu capture (profiles/ncu_cfg3_bf16.md).
+# DRAM bytes (read + write) per launch from one ncu capture of each workload (summaries under profiles/):
+# configuration 3 bf16 (dram__bytes_read.sum + dram__bytes_write.sum) and the WN2 shape bf16
+# (dram__bytes.sum.per_second x gpu__time_duration.sum of the same launch).
 NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 150_649_088, "attn_bwd_dq": 199_965_952,
-                                                   "attn_bwd_dkv": 229_626_880}}
+                                                   "attn_bwd_dkv": 229_626_880},
+               ("wn2", "bf16", "paired"): {"attn_fwd": 372_406_272, "attn_bwd_dq": 474_326_016,
+                                           "attn_bwd_dkv": 544_704_512}}
 
 
 def peaks():
