@@ -6,24 +6,23 @@
 //
 // Why separate kernels: as in the forward, tcgen05.mma instructions with N = 32 or 64 leave most of the
 // tensor core idle on dense masks. Here a chunk is four consecutive tiles of the list (128 columns), so
-// S and dP are N = 128 MMAs and the accumulating MMAs have K = 128. Passes ("kinds"), one CTA per SM each:
-//               dQ              dK and dV       (dV only         dK only)
-//   rows        queries         keys            keys             keys     (128 per work item, held all item long)
-//   R0, R1      Q, dO           K, V            K                K, V
-//   C0, C1      K, V            Q, dO           Q, dO            Q, dO    (per chunk, in rings)
-//   S  = R0 C0^T, dP = R1 C1^T  (dV only: no dP)
-//   acc += G C                  G = dS, C = C0 (dQ, dK); G = P, C = C1 (dV); C read MN-major
-// dQ: G (bf16, 128 x 128) is written by the elementwise warps into TMEM and is the A operand of the
-// accumulating MMA (two G buffers); a column operand read again by the accumulating MMA lives in a ring of
-// three slots, one read only by S / dP in a ring of two. dK and dV: S, dP and both accumulators take all 512
-// TMEM columns, so P is written over S and dS over dP (one S / dP buffer; chunks follow one another, with P
-// computed while dP runs and dS while dV runs) and both column operands sit in rings of two. The dV-only and
-// dK-only kinds are the same passes split (one accumulator each, S recomputed by both). Rows are keys for dK /
-// dV: their columns' lse and delta come with the chunk (a ring of vectors); for dQ they are per thread.
+// S and dP are N = 128 MMAs and the accumulating MMAs have K = 128. Two passes ("kinds"), one CTA per SM each:
+//               dQ              dK and dV
+//   rows        queries         keys            (128 per work item, held all item long)
+//   R0, R1      Q, dO           K, V
+//   C0, C1      K, V            Q, dO           (per chunk, in rings)
+//   S  = R0 C0^T, dP = R1 C1^T
+//   acc += G C                  dQ += dS K; dV += P^T dO, dK += dS^T Q (C read MN-major)
+// dQ: G = dS (bf16, 128 x 128) is written by the elementwise warps into TMEM and is the A operand of the
+// accumulating MMA (two G buffers); K (read again by the dQ MMA) lives in a ring of three slots, V in a ring of
+// two; S and dP of chunk c+1 go ahead of the dQ MMA of chunk c. dK and dV: S, dP and both accumulators take all
+// 512 TMEM columns at head_dim 128, so P is written over S and dS over dP (packed bf16 pairs in the first 16
+// columns of each 32-column tile); one S / dP buffer, chunks follow one another, P is computed while dP runs
+// and dS while dV runs; Q and dO in rings of two (three at head_dim 64). Rows are keys for dK / dV: the
+// columns' lse and delta come with the chunk (a ring of vectors); for dQ they are per thread.
 //
 // Roles (576 threads): warp 0 TMA producer; warp 1 TMEM allocation and MMA issue (the warp runs the loop
-// with warp-uniform descriptors, one elected lane issues; except in the dK and dV pass, S and dP of chunk c+1
-// ahead of the accumulating MMA of chunk c); warps 2-17 elementwise, four per TMEM lane
+// with warp-uniform descriptors, one elected lane issues); warps 2-17 elementwise, four per TMEM lane
 // quadrant (thread = row), one 32-column tile of each chunk each; the mask words are read from global
 // memory one chunk ahead. Epilogue: each warp stores a quarter of the accumulator columns. Every mbarrier
 // wait is bounded (common.cuh).
@@ -38,12 +37,11 @@ namespace fwn {
 
 template <int KIND, int D>
 struct BwdWideCfg {
+  static_assert(KIND == kBwdDQ || KIND == kBwdDKV, "wide passes: dQ; dK and dV");
   // dK and dV in one pass (kBwdDKV): one S / dP buffer, P written over S and dS over dP (bf16 pairs, in the
   // first 16 of each 32-column tile's columns), accumulators dV and dK in the other 256 columns.
   static constexpr bool FUSED = KIND == kBwdDKV;
-  static constexpr bool ROWS_ARE_KEYS = KIND != kBwdDQ;
-  static constexpr bool NEED_DP = KIND != kBwdDV;
-  static constexpr bool ACC_ON_C0 = KIND != kBwdDV;   // dS C0 (dQ, dK) or P C1 (dV); fused: both
+  static constexpr bool ROWS_ARE_KEYS = FUSED;
   static constexpr int ES = 2;
   static constexpr int EPB = 64;
   static constexpr int CB = D / EPB;
@@ -51,27 +49,27 @@ struct BwdWideCfg {
   static constexpr int SUB = 32;
   static constexpr int CH = 4;
   static constexpr int COLS = SUB * CH;
-  static constexpr int NR = NEED_DP ? 2 : 1;
+  static constexpr int NR = 2;
   static constexpr int R_BYTES = CB * ROWS * 128;
   static constexpr int C_BYTES = CB * COLS * 128;
-  // C0 / C1 rings. Fused: both operands are read again by an accumulating MMA; chunks run one after the other
-  // (one S / dP buffer), so two slots each keep the next chunk's copies in flight.
-  static constexpr int N0 = FUSED ? (D == 128 ? 2 : 3) : ACC_ON_C0 ? 3 : 2;
-  static constexpr int N1 = FUSED ? (D == 128 ? 2 : 3) : ACC_ON_C0 ? 2 : 3;
+  // C0 / C1 rings. dQ: C0 (K) is read again by the dQ MMA (three slots), C1 (V) only by dP (two). Fused: both
+  // operands are read again by an accumulating MMA; chunks run one after the other (one S / dP buffer), so two
+  // slots each keep the next chunk's copies in flight.
+  static constexpr int N0 = FUSED ? (D == 128 ? 2 : 3) : 3;
+  static constexpr int N1 = FUSED ? (D == 128 ? 2 : 3) : 2;
   static constexpr int NVEC = ROWS_ARE_KEYS ? 2 : 0;  // lse / delta vectors of the chunk's columns (1 KB)
   static constexpr int NVEC_RING = NVEC > 0 ? NVEC : 1; // ring arithmetic (no vectors for dQ)
   static constexpr int OFF_C0 = NR * R_BYTES;
   static constexpr int OFF_C1 = OFF_C0 + N0 * C_BYTES;
   static constexpr int OFF_VEC = OFF_C1 + N1 * C_BYTES;
   static constexpr int OFF_BAR = OFF_VEC + NVEC * 1024;
-  static constexpr int NSB = NEED_DP ? 1 : 2;        // S (and dP) buffers
-  static constexpr int N_BAR = 2 + 2 * N0 + 2 * N1 + 2 * NVEC + 2 * NSB + 4 + 3;
+  static constexpr int N_BAR = 2 + 2 * N0 + 2 * N1 + 2 * NVEC + 2 + 4 + 3;
   // The dynamic shared memory base is 1024-byte aligned (checked at run time): no alignment slack.
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16;
-  // TMEM: S[NSB] (128 each), dP (128), acc (D), G[2] (64 each); fused: S (P), dP (dS), dV (D), dK (D).
-  static constexpr int DP_COL = 128 * NSB;
-  static constexpr int ACC_COL = DP_COL + (NEED_DP ? 128 : 0);
-  static constexpr int G_COL = ACC_COL + D;
+  // TMEM: S (128), dP (128), then dQ (D) and G[2] (64 each), or (fused) dV (D) and dK (D).
+  static constexpr int DP_COL = 128;
+  static constexpr int ACC_COL = 256;
+  static constexpr int G_COL = ACC_COL + D;      // dQ
   static constexpr int ACC_K_COL = ACC_COL + D;  // fused: dK
   static constexpr int TMEM_COLS = 512;
   // Elementwise warps: four per TMEM lane quadrant, one 32-column tile of the chunk each (18 warps: at most
@@ -80,7 +78,7 @@ struct BwdWideCfg {
   static constexpr int THREADS = 64 + 32 * EW;
   static constexpr int MAX_REGS = 96;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(FUSED ? (NSB == 1 && ACC_K_COL + D <= TMEM_COLS) : G_COL + 128 <= TMEM_COLS, "TMEM budget");
+  static_assert(FUSED ? ACC_K_COL + D <= TMEM_COLS : G_COL + 128 <= TMEM_COLS, "TMEM budget");
 };
 
 template <int KIND, int D>
@@ -113,15 +111,14 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
   auto v_full = [&](int s) { return bar2 + 8 * s; };
   auto v_empty = [&](int s) { return bar2 + 8 * (C::NVEC + s); };
   const uint32_t bar3 = bar2 + 16 * C::NVEC;
-  auto s_full = [&](int b) { return bar3 + 8 * b; };
-  auto s_empty = [&](int b) { return bar3 + 8 * (C::NSB + b); };
-  const uint32_t bar4 = bar3 + 16 * C::NSB;
+  const uint32_t s_full = bar3, s_empty = bar3 + 8;  // fused: s_empty is "dP done"
+  const uint32_t bar4 = bar3 + 16;
   auto g_full = [&](int b) { return bar4 + 8 * b; };
   auto g_empty = [&](int b) { return bar4 + 16 + 8 * b; };
   const uint32_t acc_full = bar4 + 32, acc_empty = bar4 + 40, drain = bar4 + 48;
   // Fused dK / dV pass (the same slots): S and dP done (MMA commits), P and dS written (elementwise arrivals),
   // S and dP columns free again (the dV / dK MMAs that read P / dS are complete).
-  [[maybe_unused]] const uint32_t f_s_full = s_full(0), f_dp_full = s_empty(0);
+  [[maybe_unused]] const uint32_t f_s_full = s_full, f_dp_full = s_empty;
   [[maybe_unused]] const uint32_t f_p_full = g_full(0), f_ds_full = g_full(1), f_s_free = g_empty(0), f_dp_free = g_empty(1);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
@@ -144,10 +141,8 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), C::EW);
     }
-    for (int b = 0; b < C::NSB; ++b) {
-      mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), C::FUSED ? 1 : C::EW);  // fused: dP done (MMA commit)
-    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, C::FUSED ? 1 : C::EW);  // fused: dP done (MMA commit)
     for (int b = 0; b < 2; ++b) {
       mbar_init(g_full(b), C::EW);
       mbar_init(g_empty(b), 1);
@@ -235,7 +230,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
         ++nvec;
         return true;
       };
-      int kb_cur = meta(0), kb_prev = 0;
+      int kb_cur = meta(0);
       for (int c = 0; c <= nch && ok; ++c) {
         const int kb_next = c + 1 < nch ? meta(c + 1) : 0;
         if (c < nch) {
@@ -244,25 +239,13 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           if (lane == 0) FWN_TR(3, c);
           load_op(c0_slot(n0 % C::N0), &tm_c0, &tm_c0w, kb_cur, n_in, c0_full(n0 % C::N0));
           ++n0;
-          if constexpr (C::NEED_DP) {
-            if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
-            load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_cur, n_in, c1_full(n1 % C::N1));
-            ++n1;
-          }
+          if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
+          load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_cur, n_in, c1_full(n1 % C::N1));
+          ++n1;
           if constexpr (C::ROWS_ARE_KEYS) {
             if (!(ok = load_vec(kb_cur, n_in))) break;
           }
         }
-        if constexpr (!C::NEED_DP) {
-          // dV only: dO (C1) is read by the accumulating MMA, one chunk after Q.
-          if (c >= 1) {
-            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-            if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
-            load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_prev, n_in, c1_full(n1 % C::N1));
-            ++n1;
-          }
-        }
-        kb_prev = kb_cur;
         kb_cur = kb_next;
       }
       if (!ok) break;
@@ -362,14 +345,14 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
         ++qc;
         continue;
       }
+      // dQ: S and dP of chunk c+1 ahead of the dQ MMA of chunk c (which reads dS from one of two G buffers).
       for (int c = 0; c <= nch && ok; ++c) {
         if (c < nch) {
           const uint32_t gg = g0 + c;
-          const int sb = gg % C::NSB;
           const int n_in = min(C::CH, n_sub - C::CH * c);
           if (!(ok = warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
-          if (C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(s_empty(sb), ((gg / C::NSB) & 1) ^ 1, abort_flag))) break;
+          if (!(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+          if (!(ok = warp_wait(s_empty, (gg & 1) ^ 1, abort_flag))) break;
           if (lane == 0) FWN_TR(13, c);
           tc_fence_after();
           const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
@@ -379,21 +362,17 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<false>(tmem + 128 * sb, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
+              mma_ss<false>(tmem, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
                             c0desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
             }
-            if constexpr (C::NEED_DP) {
 #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-                mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
-                              c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
-              }
-              mma_commit(c1_empty(gg % C::N1));  // C1 is read only by dP here
-            } else {
-              mma_commit(c0_empty(gg % C::N0));  // dV only: C0 (Q) is read only by S
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+              mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
+                            c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
             }
-            mma_commit(s_full(sb));
+            mma_commit(c1_empty(gg % C::N1));  // C1 (V) is read only by dP
+            mma_commit(s_full);
             if (c == nch - 1) mma_commit(r_empty);
           }
           __syncwarp();
@@ -404,11 +383,10 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           const int gb = gg & 1;
           const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
           if (!(ok = warp_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
-          if (!C::NEED_DP && !(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
           if (c == 1 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
           if (lane == 0) FWN_TR(14, c - 1);
           tc_fence_after();
-          const uint64_t bdesc = smem_desc(C::ACC_ON_C0 ? c0_slot(gg % C::N0) : c1_slot(gg % C::N1), C::COLS * 128, 1024);
+          const uint64_t bdesc = smem_desc(c0_slot(gg % C::N0), C::COLS * 128, 1024);
           const uint32_t gcol = tmem + C::G_COL + 64 * gb;
           const int ksteps = 2 * n_in;
           if (elect_one_sync()) {
@@ -416,8 +394,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
               mma_ts(tmem + C::ACC_COL, gcol + 8 * kk, bdesc + ((kk * 16 * 128) >> 4), kIdescAcc,
                      (c == 1 && kk == 0) ? 0u : 1u);
             mma_commit(g_empty(gb));
-            if (C::ACC_ON_C0) mma_commit(c0_empty(gg % C::N0));
-            else mma_commit(c1_empty(gg % C::N1));
+            mma_commit(c0_empty(gg % C::N0));
             if (c == nch) mma_commit(acc_full);
           }
           __syncwarp();
@@ -541,61 +518,37 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           if (lane == 0) FWN_TR(21, c);
         }
       } else {
+        // dQ: rows are queries (lse and delta per thread); dS = P (dP - delta) into G buffer gg & 1.
         for (int c = 0; c < nch; ++c) {
           const uint32_t gg = g0 + c;
-          const int sb = gg % C::NSB, gb = gg & 1;
+          const int gb = gg & 1;
           const int n_in = min(C::CH, n_sub - C::CH * c);
           const uint32_t w = nw;
           if (c + 1 < nch) nw = word(c + 1);
           const uint32_t a = __reduce_or_sync(0xffffffffu, w);
-          if (!(ok = mbar_wait(s_full(sb), (gg / C::NSB) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(s_full, gg & 1, abort_flag))) break;
           if (lane == 0) FWN_TR(20, c);
           tc_fence_after();
-          // S (and dP) of this tile -> registers; then the buffer is released for the next S MMA.
+          // S and dP of this tile -> registers; then the buffer is released for the next S / dP MMAs.
           float s[32], dp[32];
           if (j < n_in) {
-            tmem_ld32(trow + 128 * sb + 32 * j, s);
-            if constexpr (C::NEED_DP) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
+            tmem_ld32(trow + 32 * j, s);
+            tmem_ld32(trow + C::DP_COL + 32 * j, dp);
           }
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(s_empty(sb));
-          // Column lse (as -lse * log2 e) and delta of this tile (rows are keys).
-          uint32_t vslot = 0;
-          if constexpr (C::ROWS_ARE_KEYS) {
-            const uint32_t vs = gg % C::NVEC_RING;
-            if (!(ok = mbar_wait(v_full(vs), (gg / C::NVEC_RING) & 1, abort_flag))) break;
-            vslot = vec_slot(vs) + 128 * j;
-          }
-          // G = P (dV) or dS = P (dP - delta) (dQ, dK) as packed bf16 pairs.
+          if (lane == 0) mbar_arrive(s_empty);
           uint32_t pk[16];
-          const float2 cc = make_float2(c2, c2);
-  #pragma unroll
+          const float2 cc = make_float2(c2, c2), nl2 = make_float2(nl2_row, nl2_row);
+          const float2 dl = make_float2(delta_row, delta_row);
+#pragma unroll
           for (int gi = 0; gi < 4; ++gi) {
             if ((a >> (8 * gi)) & 0xFFu) {
-              float lv[8], dv[8];
-              if constexpr (C::ROWS_ARE_KEYS) {
-                const uint32_t va = vslot + 32 * gi;
-                const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
-                lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
-  #pragma unroll
-                for (int i = 0; i < 8; ++i) lv[i] *= -kLog2e;
-                if constexpr (C::NEED_DP) {
-                  const float4 d0 = ld_shared_f32x4(va + 512), d1 = ld_shared_f32x4(va + 528);
-                  dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
-                }
-              } else {
-  #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  lv[i] = nl2_row;
-                  dv[i] = delta_row;
-                }
-              }
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 8; i += 2) {
                 const int k = 8 * gi + i;
-                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, make_float2(lv[i], lv[i + 1]));
+                const float2 x = ffma2(make_float2(s[k], s[k + 1]), cc, nl2);
                 float2 e;
                 if (i < 2) {
                   e = exp2_poly2(x);
@@ -605,24 +558,16 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
                 }
                 e.x = (w >> k) & 1u ? e.x : 0.f;
                 e.y = (w >> (k + 1)) & 1u ? e.y : 0.f;
-                if constexpr (C::NEED_DP) {
-                  const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), make_float2(dv[i], dv[i + 1])));
-                  pk[k >> 1] = pack_bf16(ds.x, ds.y);
-                } else {
-                  pk[k >> 1] = pack_bf16(e.x, e.y);
-                }
+                const float2 ds = fmul2(e, fsub2(make_float2(dp[k], dp[k + 1]), dl));
+                pk[k >> 1] = pack_bf16(ds.x, ds.y);
               }
             } else {
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 4; ++i) pk[4 * gi + i] = 0u;
             }
           }
-          if constexpr (C::ROWS_ARE_KEYS) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(v_empty(gg % C::NVEC_RING));
-          }
           if (lane == 0) FWN_TR(26, c);
-          // G buffer free once the accumulating MMA of chunk gg-2 is complete.
+          // G buffer free once the dQ MMA of chunk gg-2 is complete.
           if (!(ok = mbar_wait(g_empty(gb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
           if (j < n_in) tmem_st16(trow + C::G_COL + 64 * gb + 16 * j, pk);
           tmem_wait_st();
@@ -644,7 +589,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       if (nch == 0) {
         if (store)
           for (int ai = 0; ai < NACC; ++ai) {
-            uint8_t* dst = reinterpret_cast<uint8_t*>((C::FUSED ? ai == 1 : C::ACC_ON_C0) ? p.out0 : p.out1) + roff;
+            uint8_t* dst = reinterpret_cast<uint8_t*>((!C::FUSED || ai == 1) ? p.out0 : p.out1) + roff;
             for (int i = 0; i < OC * C::ES / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
           }
         continue;
@@ -653,7 +598,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       tc_fence_after();
 #pragma unroll
       for (int ai = 0; ai < NACC; ++ai) {
-        const bool is_dk = C::FUSED ? ai == 1 : C::ACC_ON_C0;
+        const bool is_dk = !C::FUSED || ai == 1;  // dQ or (fused) dK: scaled, to out0
         uint8_t* dst = reinterpret_cast<uint8_t*>(is_dk ? p.out0 : p.out1) + roff;
         const float mul = is_dk ? p.scale : 1.f;
         const uint32_t acc_col = C::FUSED && ai == 1 ? C::ACC_K_COL : C::ACC_COL;

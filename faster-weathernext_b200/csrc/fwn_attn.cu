@@ -461,9 +461,7 @@ fwn_status launch_bwd_wide(const fwn_attn_desc& d, const void* q, const void* k,
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0w, c1w, p);
   cudaError_t e = cudaGetLastError();
-  static const char* const kNames[] = {"attn_bwd_wide dq launch", "attn_bwd_wide dkv launch", "attn_bwd_wide dv launch",
-                                       "attn_bwd_wide dk launch"};
-  if (e != cudaSuccess) return cuda_fail(e, kNames[KIND]);
+  if (e != cudaSuccess) return cuda_fail(e, KIND == fwn::kBwdDQ ? "attn_bwd_wide dq launch" : "attn_bwd_wide dkv launch");
   return FWN_OK;
 }
 
