@@ -18,8 +18,9 @@
 //   dP = R1 C1^T            dQ, dK/dV, dK only
 //   acc0 += dS C0           dQ, dK/dV, dK only   (MN-major B)
 //   acc1 += P  C1           dK/dV, dV only       (MN-major B)
-// dV only + dK only are the 3xTF32 replacement of the dK/dV pass, whose hi / lo operand copies do not fit
-// one CTA's shared memory. Roles: warp 0 TMA producer; warp 1 TMEM allocation + single-thread MMA issue;
+// dV only + dK only replace the dK/dV pass where it does not fit one CTA: 3xTF32 (hi / lo operand copies) and
+// tf32 at head_dim 128 (shared memory), bf16 at head_dim 128 (the TMEM columns of a CTA that shares its SM).
+// Roles: warp 0 TMA producer; warp 1 TMEM allocation + single-thread MMA issue;
 // warps 2-5 the elementwise stage (thread = row = TMEM lane) and the epilogue; in 3xTF32 warps 6-9 split
 // every landed tile into hi (in place) and lo copies. S / dP of chunk c+1 are issued before the
 // accumulating MMAs of chunk c. tf32 operands read MN-major use a second copy of the column tile with
