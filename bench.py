@@ -562,8 +562,25 @@ def run_reference(args):
   from faster_weathernext import mesh
   from oracle import attention as oa
   cores = _all_host_threads()
-  mask, _, _ = mesh.config_mask(CFG)
-  _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
+  if args.workload == "wn2":
+    # The WN2 shape built on the host: Hilbert order (the reference's permutation, restated in the oracle) and
+    # the 32-hop neighbourhood as a sparse matrix power (patch.py:209), about a minute on the host.
+    from oracle import tiles as ot
+    xyz, faces = mesh.icosphere(mesh.WN2["level"])
+    lat, lon = mesh.latlon(xyz)
+    adj = mesh.permute(mesh.adjacency(faces, xyz.shape[0]), ot.hilbert_order(lat, lon))
+    mask = mesh.k_hop_mask(adj, mesh.WN2["hops"])
+    heads, head_dim = mesh.WN2["heads"], mesh.WN2["head_dim"]
+    label = "the WN2 shape"
+    desc_w = (f"WN2 real shape fwd+bwd: 40,962 nodes (level-6 mesh, Hilbert order), 32-hop mask ({mask.nnz} pairs), "
+              f"B1 H{heads} D{head_dim}")
+    data = "synthetic: Q/K/V/dO ~ N(0,1); icosphere level-6 32-hop mask built on the host"
+  else:
+    mask, _, _ = mesh.config_mask(CFG)
+    _, _, _, heads, head_dim = mesh.CONFIGS[CFG]
+    label = "cfg3"
+    desc_w = f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({mask.nnz} pairs), B1 H{heads} D{head_dim}"
+    data = "synthetic: Q/K/V/dO ~ N(0,1); icosphere level-6 great-circle mask"
   n = mask.shape[0]
   rng = np.random.default_rng(0)
   q, k, v, do = (rng.standard_normal((1, n, heads, head_dim)).astype(np.float32) for _ in range(4))
@@ -575,12 +592,12 @@ def run_reference(args):
   scale = head_dim ** -0.5
 
   # Each step is one query chunk, or a slice of its rows with the same key window, sized so that the
-  # whole --warmup W --steps K run takes about a minute and a half.
+  # whole --warmup W --steps K run takes about --ref-seconds (a minute and a half by default).
   chunk_s = time.perf_counter()
   path.forward_chunk(t, 3, scale, out)
   path.vjp_chunk(t, 3, scale, dq, dk, dv)
   chunk_s = time.perf_counter() - chunk_s
-  rows = int(np.clip(512 * 90.0 / max(args.steps + args.warmup, 1) / chunk_s, 8, 512)) // 8 * 8
+  rows = int(np.clip(512 * args.ref_seconds / max(args.steps + args.warmup, 1) / chunk_s, 8, 512)) // 8 * 8
 
   def step(i):
     c = (7 * i + 3) % path.n_chunks
@@ -595,15 +612,13 @@ def run_reference(args):
   el = time.perf_counter() - t0
   value = flops / el / 1e12
   sample = (f"per step {rows} query rows of one of the {path.n_chunks} query chunks (key window {path.window}) "
-            "of cfg3, fwd + autodiff bwd, float32 NumPy/BLAS restatement of the XLA path (JAX absent)")
+            f"of {label}, fwd + autodiff bwd, float32 NumPy/BLAS restatement of the XLA path (JAX absent)")
   print(json.dumps({
       "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": args.gpus,
       "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
       "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-      "data": "synthetic: Q/K/V/dO ~ N(0,1); icosphere level-6 great-circle mask",
-      "config": {"workload": f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({mask.nnz} pairs), "
-                             f"B1 H{heads} D{head_dim}", "nodes": n, "heads": heads, "head_dim": head_dim,
-                 "parallelism": "host CPU"},
+      "data": data,
+      "config": {"workload": desc_w, "nodes": n, "heads": heads, "head_dim": head_dim, "parallelism": "host CPU"},
       "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
       "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
   }), flush=True)
@@ -628,11 +643,13 @@ def main():
   ap.add_argument("--no-e2e", action="store_true")
   ap.add_argument("--no-cpu", action="store_true")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)
+  ap.add_argument("--ref-seconds", type=float, default=90.0,
+                  help="--impl reference: host seconds the warm-up and timed steps take together")
   args = ap.parse_args()
   if args.warmup < 3:
     ap.error("--warmup must be >= 3")
   if args.impl == "reference":
-    if args.workload not in ("attention",):
+    if args.workload not in ("attention", "wn2"):
       print(json.dumps({"impl": "reference", "unavailable": "the reference's processor runs in JAX, which is not "
                         "installed on this image"}))
       return
