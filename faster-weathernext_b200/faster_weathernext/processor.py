@@ -72,6 +72,18 @@ class Processor(torch.nn.Module):
       blk.cond2 = _glorot(gen, cfg.cond_dim, 2 * d, dev)
       self.blocks.append(blk)
     self.cond_final = _glorot(gen, cfg.cond_dim, 2 * d, dev)
+    self._bf16_cache = {}
+
+  def _bf16(self, p: torch.Tensor) -> torch.Tensor:
+    """bf16 copy of parameter p for the inference path, cast again only when p has changed: the cache entry
+    holds p's storage address and in-place version counter, which optimizer steps, load_state_dict and .to()
+    change. The 16 forwards of a processor step therefore cast each weight once, not once per forward."""
+    hit = self._bf16_cache.get(id(p))
+    if hit is not None and hit[0] == p._version and hit[1] == p.data_ptr():
+      return hit[2]
+    w = p.detach().to(torch.bfloat16)
+    self._bf16_cache[id(p)] = (p._version, p.data_ptr(), w)
+    return w
 
   def _attend(self, q, k, v, tiles, scale):
     return tiled_attn.attention(q, k, v, tiles, scale=scale)
@@ -139,12 +151,12 @@ class Processor(torch.nn.Module):
 
     for blk in self.blocks:
       norm(blk.cond1, h, _lib.DTYPE_BF16)
-      qkv = (h @ blk.w_qkv.to(bf)).view(b, n, cfg.heads, 3, cfg.head_dim)
+      qkv = (h @ self._bf16(blk.w_qkv)).view(b, n, cfg.heads, 3, cfg.head_dim)
       o = self._attend(qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2], tiles, scale)
-      x2.add_(o.reshape(m_rows, cfg.heads * cfg.head_dim) @ blk.w_out.to(bf))
+      x2.add_(o.reshape(m_rows, cfg.heads * cfg.head_dim) @ self._bf16(blk.w_out))
       norm(blk.cond2, h, _lib.DTYPE_BF16)
-      mlp = torch._addmm_activation(blk.b1.to(bf), h, blk.w1.to(bf), use_gelu=True)
-      x2.add_(torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf)))
+      mlp = torch._addmm_activation(self._bf16(blk.b1), h, self._bf16(blk.w1), use_gelu=True)
+      x2.add_(torch.addmm(self._bf16(blk.b2), mlp, self._bf16(blk.w2)))
     out = torch.empty_like(xs)
     if perm is None:
       norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32)

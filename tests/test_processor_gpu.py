@@ -171,3 +171,28 @@ def test_processor_node_permutation(cuda):
   assert _rel(y_grad.detach(), y_ref) < 1e-2
   with pytest.raises(ValueError):
     model(x, c, tiles, perm=perm[:-1])
+
+
+def test_processor_fused_weight_cache_follows_updates(cuda):
+  """The inference path casts each weight to bf16 once and reuses the copy across calls; an in-place update of
+  a parameter (as an optimizer step makes) must be seen by the next call."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor, ProcessorConfig
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = ProcessorConfig(layers=2)
+  model = Processor(cfg, seed=5, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(7)
+  x = torch.randn(1, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(1, cfg.cond_dim, device=cuda, generator=g)
+  with torch.no_grad():
+    y0 = model(x, c, tiles)
+    assert torch.equal(model(x, c, tiles), y0)                    # cached copies: same result
+    model.blocks[1].w2.mul_(-2.0)
+    model.blocks[0].b1.add_(0.5)
+    y1 = model(x, c, tiles)
+  y_ref = model(x, c, tiles)                                       # autograd path, no cache
+  assert not torch.equal(y1, y0)
+  assert _rel(y1, y_ref.detach()) < 1e-2
