@@ -261,3 +261,25 @@ def test_tf32x3_head_dim_128(golden, cuda, mask_kind, gather):
     a = a.cpu().numpy()
     assert oa.rel_rms(a, r) < TOL["tf32x3"], (name, oa.rel_rms(a, r))
     assert oa.max_rel(a, r) < 1e-4, (name, oa.max_rel(a, r))
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_autograd_fused_qkv_layout_dense_mask(cuda, head_dim):
+  """Gradients through the public API (tiled_attn.attention + autograd) with q, k, v as strided views of one
+  fused [B, n, H, 3, D] projection (the processor's layout) on a dense k-hop mask: the wide dQ and one-pass dK / dV
+  kernels read the strided rows and write the gradients into the fused tensor's gradient."""
+  from faster_weathernext import tiled_attn as ta
+  m = _khop_mask(4, 6)
+  n = m.shape[0]
+  g = torch.Generator(device=cuda).manual_seed(11)
+  x = torch.randn(2, n, 2, 3, head_dim, device=cuda, generator=g).to(torch.bfloat16).requires_grad_(True)
+  do = torch.randn(2, n, 2, head_dim, device=cuda, generator=g).to(torch.bfloat16)
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  o = ta.attention(x[:, :, :, 0], x[:, :, :, 1], x[:, :, :, 2], tiles, scale=head_dim ** -0.5)
+  (gx,) = torch.autograd.grad(o, x, do)
+  torch.cuda.synchronize()
+  q, k, v = (x[:, :, :, i].detach().float().cpu().numpy() for i in range(3))
+  ref = oa.sparse_attention_vjp(q, k, v, do.float().cpu().numpy(), m, head_dim ** -0.5)
+  got = gx.float().cpu().numpy()
+  for i, name in enumerate(("dq", "dk", "dv")):
+    assert oa.rel_rms(got[:, :, :, i], ref[i]) < TOL["bf16"], (name, oa.rel_rms(got[:, :, :, i], ref[i]))
