@@ -300,6 +300,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           }
           __syncwarp();
           if (!(ok = warp_wait(f_dp_free, (gg & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(17, c);
           tc_fence_after();
           if (elect_one_sync()) {
 #pragma unroll
@@ -317,6 +318,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           const int ksteps = 2 * n_in;
           if (!(ok = warp_wait(f_p_full, gg & 1, abort_flag))) break;
           if (c == 0 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(15, c);
           tc_fence_after();
           if (elect_one_sync()) {
             const uint64_t bdesc = smem_desc(c1_slot(s1), C::COLS * 128, 1024);
@@ -328,6 +330,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           }
           __syncwarp();
           if (!(ok = warp_wait(f_ds_full, gg & 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(16, c);
           tc_fence_after();
           if (elect_one_sync()) {
             const uint64_t bdesc = smem_desc(c0_slot(s0), C::COLS * 128, 1024);
@@ -341,64 +344,62 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           __syncwarp();
           if (lane == 0) FWN_TR(12, c);
         }
-        g = g0 + nch;
-        ++qc;
-        continue;
-      }
-      // dQ: S and dP of chunk c+1 ahead of the dQ MMA of chunk c (which reads dS from one of two G buffers).
-      for (int c = 0; c <= nch && ok; ++c) {
-        if (c < nch) {
-          const uint32_t gg = g0 + c;
-          const int n_in = min(C::CH, n_sub - C::CH * c);
-          if (!(ok = warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(s_empty, (gg & 1) ^ 1, abort_flag))) break;
-          if (lane == 0) FWN_TR(13, c);
-          tc_fence_after();
-          const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
-          const uint64_t c0desc = smem_desc(c0_slot(gg % C::N0), 16, 1024);
-          const uint64_t c1desc = smem_desc(c1_slot(gg % C::N1), 16, 1024);
-          if (elect_one_sync()) {
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<false>(tmem, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
-                            c0desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+      } else {
+        // dQ: S and dP of chunk c+1 ahead of the dQ MMA of chunk c (which reads dS from one of two G buffers).
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {
+            const uint32_t gg = g0 + c;
+            const int n_in = min(C::CH, n_sub - C::CH * c);
+            if (!(ok = warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag))) break;
+            if (!(ok = warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag))) break;
+            if (!(ok = warp_wait(s_empty, (gg & 1) ^ 1, abort_flag))) break;
+            if (lane == 0) FWN_TR(13, c);
+            tc_fence_after();
+            const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
+            const uint64_t c0desc = smem_desc(c0_slot(gg % C::N0), 16, 1024);
+            const uint64_t c1desc = smem_desc(c1_slot(gg % C::N1), 16, 1024);
+            if (elect_one_sync()) {
+  #pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                mma_ss<false>(tmem, r0desc + ((cb * C::ROWS * 128 + within) >> 4),
+                              c0desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+              }
+  #pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t cb = kk / 4, within = (kk % 4) * 32;
+                mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
+                              c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+              }
+              mma_commit(c1_empty(gg % C::N1));  // C1 (V) is read only by dP
+              mma_commit(s_full);
+              if (c == nch - 1) mma_commit(r_empty);
             }
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t cb = kk / 4, within = (kk % 4) * 32;
-              mma_ss<false>(tmem + C::DP_COL, r1desc + ((cb * C::ROWS * 128 + within) >> 4),
-                            c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
+            __syncwarp();
+            if (lane == 0) FWN_TR(11, c);
+          }
+          if (c >= 1) {
+            const uint32_t gg = g0 + c - 1;
+            const int gb = gg & 1;
+            const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
+            if (!(ok = warp_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
+            if (c == 1 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
+            if (lane == 0) FWN_TR(14, c - 1);
+            tc_fence_after();
+            const uint64_t bdesc = smem_desc(c0_slot(gg % C::N0), C::COLS * 128, 1024);
+            const uint32_t gcol = tmem + C::G_COL + 64 * gb;
+            const int ksteps = 2 * n_in;
+            if (elect_one_sync()) {
+              for (int kk = 0; kk < ksteps; ++kk)
+                mma_ts(tmem + C::ACC_COL, gcol + 8 * kk, bdesc + ((kk * 16 * 128) >> 4), kIdescAcc,
+                       (c == 1 && kk == 0) ? 0u : 1u);
+              mma_commit(g_empty(gb));
+              mma_commit(c0_empty(gg % C::N0));
+              if (c == nch) mma_commit(acc_full);
             }
-            mma_commit(c1_empty(gg % C::N1));  // C1 (V) is read only by dP
-            mma_commit(s_full);
-            if (c == nch - 1) mma_commit(r_empty);
+            __syncwarp();
+            if (lane == 0) FWN_TR(12, c - 1);
           }
-          __syncwarp();
-          if (lane == 0) FWN_TR(11, c);
-        }
-        if (c >= 1) {
-          const uint32_t gg = g0 + c - 1;
-          const int gb = gg & 1;
-          const int n_in = min(C::CH, n_sub - C::CH * (c - 1));
-          if (!(ok = warp_wait(g_full(gb), (gg >> 1) & 1, abort_flag))) break;
-          if (c == 1 && !(ok = warp_wait(acc_empty, (qc & 1) ^ 1, abort_flag))) break;
-          if (lane == 0) FWN_TR(14, c - 1);
-          tc_fence_after();
-          const uint64_t bdesc = smem_desc(c0_slot(gg % C::N0), C::COLS * 128, 1024);
-          const uint32_t gcol = tmem + C::G_COL + 64 * gb;
-          const int ksteps = 2 * n_in;
-          if (elect_one_sync()) {
-            for (int kk = 0; kk < ksteps; ++kk)
-              mma_ts(tmem + C::ACC_COL, gcol + 8 * kk, bdesc + ((kk * 16 * 128) >> 4), kIdescAcc,
-                     (c == 1 && kk == 0) ? 0u : 1u);
-            mma_commit(g_empty(gb));
-            mma_commit(c0_empty(gg % C::N0));
-            if (c == nch) mma_commit(acc_full);
-          }
-          __syncwarp();
-          if (lane == 0) FWN_TR(12, c - 1);
         }
       }
       g = g0 + nch;
@@ -487,8 +488,10 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(f_p_full);
+          if (lane == 0) FWN_TR(22, c);
           // dS = P (dP - delta), over this tile's dP columns.
           if (!(ok = mbar_wait(f_dp_full, gg & 1, abort_flag))) break;
+          if (lane == 0) FWN_TR(23, c);
           tc_fence_after();
           float dp[32];
           if (j < n_in) tmem_ld32(trow + C::DP_COL + 32 * j, dp);
