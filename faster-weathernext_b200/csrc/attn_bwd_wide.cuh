@@ -17,8 +17,9 @@
 // accumulating MMA (two G buffers); K (read again by the dQ MMA) lives in a ring of three slots, V in a ring of
 // two; S and dP of chunk c+1 go ahead of the dQ MMA of chunk c. dK and dV: S, dP and both accumulators take all
 // 512 TMEM columns at head_dim 128, so P is written over S and dS over dP (packed bf16 pairs in the first 16
-// columns of each 32-column tile); one S / dP buffer, chunks follow one another, P is computed while dP runs
-// and dS while dV runs; Q and dO in rings of two (three at head_dim 64). Rows are keys for dK / dV: the
+// columns of each 32-column tile); one S / dP buffer: per chunk the pipe runs dV(c), S(c+1), dK(c), dP(c+1),
+// so that S of the next chunk runs while the elementwise warps compute dS; Q and dO in rings of two (three at
+// head_dim 64). Rows are keys for dK / dV: the
 // columns' lse and delta come with the chunk (a ring of vectors); for dQ they are per thread.
 //
 // Roles (576 threads): warp 0 TMA producer; warp 1 TMEM allocation and MMA issue (the warp runs the loop
@@ -274,21 +275,19 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       if (!(ok = warp_wait(r_full, qc & 1, abort_flag))) break;
       const uint32_t g0 = g;
       if constexpr (C::FUSED) {
-        // Per chunk, in this order on the tensor pipe: S (over the previous chunk's P, once its dV MMAs are
-        // complete), dP (likewise over dS), dV += P^T dO once P is written, dK += dS^T Q once dS is written.
-        // The elementwise warps compute P while dP runs and dS while dV runs.
-        for (int c = 0; c < nch && ok; ++c) {
+        // On the tensor pipe per chunk c: dV(c) once P(c) is written; S(c+1) over P(c) once dV(c) is complete
+        // (MMAs into different accumulators are not ordered, so the warp waits for dV's commit); dK(c) once dS(c)
+        // is written; dP(c+1) over dS(c) once dK(c) is complete. S(c+1) thus runs while the elementwise warps
+        // compute dS(c), and P(c+1) can start as soon as they are done.
+        auto issue_s = [&](int c) -> bool {  // S = K Q^T of chunk c (columns 0-127)
           const uint32_t gg = g0 + c;
           const int n_in = min(C::CH, n_sub - C::CH * c);
-          const int s0 = gg % C::N0, s1 = gg % C::N1;
-          if (!(ok = warp_wait(c0_full(s0), (gg / C::N0) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(c1_full(s1), (gg / C::N1) & 1, abort_flag))) break;
-          if (!(ok = warp_wait(f_s_free, (gg & 1) ^ 1, abort_flag))) break;
+          if (!warp_wait(c0_full(gg % C::N0), (gg / C::N0) & 1, abort_flag)) return false;
+          if (!warp_wait(f_s_free, (gg & 1) ^ 1, abort_flag)) return false;  // dV of chunk gg-1 complete
           if (lane == 0) FWN_TR(13, c);
           tc_fence_after();
           const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
-          const uint64_t c0desc = smem_desc(c0_slot(s0), 16, 1024);
-          const uint64_t c1desc = smem_desc(c1_slot(s1), 16, 1024);
+          const uint64_t c0desc = smem_desc(c0_slot(gg % C::N0), 16, 1024);
           if (elect_one_sync()) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
@@ -299,9 +298,17 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
             mma_commit(f_s_full);
           }
           __syncwarp();
-          if (!(ok = warp_wait(f_dp_free, (gg & 1) ^ 1, abort_flag))) break;
+          return true;
+        };
+        auto issue_dp = [&](int c) -> bool {  // dP = V dO^T of chunk c (columns 128-255)
+          const uint32_t gg = g0 + c;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          if (!warp_wait(c1_full(gg % C::N1), (gg / C::N1) & 1, abort_flag)) return false;
+          if (!warp_wait(f_dp_free, (gg & 1) ^ 1, abort_flag)) return false;  // dK of chunk gg-1 complete
           if (lane == 0) FWN_TR(17, c);
           tc_fence_after();
+          const uint32_t idesc = instr_desc(false, 128, 32 * n_in, false, false);
+          const uint64_t c1desc = smem_desc(c1_slot(gg % C::N1), 16, 1024);
           if (elect_one_sync()) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
@@ -310,10 +317,18 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
                             c1desc + ((cb * C::COLS * 128 + within) >> 4), idesc, kk > 0 ? 1u : 0u);
             }
             mma_commit(f_dp_full);
+            // S of every chunk of the item is issued before its last dP: the rows are free once this completes.
             if (c == nch - 1) mma_commit(r_empty);
           }
           __syncwarp();
           if (lane == 0) FWN_TR(11, c);
+          return true;
+        };
+        ok = issue_s(0) && issue_dp(0);
+        for (int c = 0; c < nch && ok; ++c) {
+          const uint32_t gg = g0 + c;
+          const int n_in = min(C::CH, n_sub - C::CH * c);
+          const int s0 = gg % C::N0, s1 = gg % C::N1;
           // A = P / dS from TMEM: K-step kk reads 8 columns of packed pairs at 32 (kk / 2) + 8 (kk % 2).
           const int ksteps = 2 * n_in;
           if (!(ok = warp_wait(f_p_full, gg & 1, abort_flag))) break;
@@ -329,6 +344,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
             mma_commit(c1_empty(s1));
           }
           __syncwarp();
+          if (c + 1 < nch && !(ok = issue_s(c + 1))) break;
           if (!(ok = warp_wait(f_ds_full, gg & 1, abort_flag))) break;
           if (lane == 0) FWN_TR(16, c);
           tc_fence_after();
@@ -343,6 +359,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
           }
           __syncwarp();
           if (lane == 0) FWN_TR(12, c);
+          if (c + 1 < nch && !(ok = issue_dp(c + 1))) break;
         }
       } else {
         // dQ: S and dP of chunk c+1 ahead of the dQ MMA of chunk c (which reads dS from one of two G buffers).
