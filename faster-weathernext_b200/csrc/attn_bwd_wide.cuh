@@ -127,6 +127,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
 #define FWN_TR(code, arg) trace_event(p.trace, trace_count, (code), (arg))
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr float kLog2e = 1.4426950408889634f;
   if (threadIdx.x == 0) {
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
@@ -139,7 +140,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
       mbar_init(c1_empty(s), 1);
     }
     for (int s = 0; s < C::NVEC; ++s) {
-      mbar_init(v_full(s), 1);
+      mbar_init(v_full(s), 2);  // delta copies (expect_tx) + the producer lanes' lse stores
       mbar_init(v_empty(s), C::EW);
     }
     mbar_init(s_full, 1);
@@ -218,34 +219,48 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
         }
       };
       // lse and delta of the chunk's columns (rows are keys): lane s < n_in copies tile s's 32 + 32 floats.
+      // delta by bulk copies (lane s < n_in: tile s); lse stored by the lanes as -lse log2 e (lane j of tile s:
+      // column 32 s + j), so that the elementwise warps add it without a multiply; v_full takes both arrivals.
       auto load_vec = [&](int kbl, int n_in) -> bool {
+        float nl2[C::CH];
+#pragma unroll
+        for (int s = 0; s < C::CH; ++s) {
+          const int kb_s = __shfl_sync(0xffffffffu, kbl, s);
+          nl2[s] = s < n_in ? __ldg(p.lse + static_cast<size_t>(bh) * p.lse_rows +
+                                    static_cast<size_t>(kb_s) * C::SUB + lane) * -kLog2e
+                            : 0.f;
+        }
         if (!mbar_wait(v_empty(nvec % C::NVEC_RING), ((nvec / C::NVEC_RING) & 1) ^ 1, abort_flag)) return false;
-        const uint32_t dst = vec_slot(nvec % C::NVEC_RING), bar = v_full(nvec % C::NVEC_RING);
-        if (lane == 0) mbar_arrive_expect_tx(bar, n_in * 256);
+        const int slot = nvec % C::NVEC_RING;
+        const uint32_t dst = vec_slot(slot), bar = v_full(slot);
+        if (lane == 0) mbar_arrive_expect_tx(bar, n_in * 128);
         __syncwarp();
         if (lane < n_in) {
           const size_t vo = static_cast<size_t>(bh) * p.lse_rows + static_cast<size_t>(kbl) * C::SUB;
-          bulk_load(dst + lane * 128, p.lse + vo, 128, bar);
           bulk_load(dst + 512 + lane * 128, p.delta + vo, 128, bar);
         }
+        float* vl = reinterpret_cast<float*>(smem + C::OFF_VEC + slot * 1024);
+#pragma unroll
+        for (int s = 0; s < C::CH; ++s)
+          if (s < n_in) vl[32 * s + lane] = nl2[s];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar);  // second arrival: publishes the lanes' stores
         ++nvec;
         return true;
       };
       int kb_cur = meta(0);
-      for (int c = 0; c <= nch && ok; ++c) {
+      for (int c = 0; c < nch && ok; ++c) {
         const int kb_next = c + 1 < nch ? meta(c + 1) : 0;
-        if (c < nch) {
-          const int n_in = min(C::CH, n_sub - C::CH * c);
-          if (!(ok = mbar_wait(c0_empty(n0 % C::N0), ((n0 / C::N0) & 1) ^ 1, abort_flag))) break;
-          if (lane == 0) FWN_TR(3, c);
-          load_op(c0_slot(n0 % C::N0), &tm_c0, &tm_c0w, kb_cur, n_in, c0_full(n0 % C::N0));
-          ++n0;
-          if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
-          load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_cur, n_in, c1_full(n1 % C::N1));
-          ++n1;
-          if constexpr (C::ROWS_ARE_KEYS) {
-            if (!(ok = load_vec(kb_cur, n_in))) break;
-          }
+        const int n_in = min(C::CH, n_sub - C::CH * c);
+        if (!(ok = mbar_wait(c0_empty(n0 % C::N0), ((n0 / C::N0) & 1) ^ 1, abort_flag))) break;
+        if (lane == 0) FWN_TR(3, c);
+        load_op(c0_slot(n0 % C::N0), &tm_c0, &tm_c0w, kb_cur, n_in, c0_full(n0 % C::N0));
+        ++n0;
+        if (!(ok = mbar_wait(c1_empty(n1 % C::N1), ((n1 / C::N1) & 1) ^ 1, abort_flag))) break;
+        load_op(c1_slot(n1 % C::N1), &tm_c1, &tm_c1w, kb_cur, n_in, c1_full(n1 % C::N1));
+        ++n1;
+        if constexpr (C::ROWS_ARE_KEYS) {
+          if (!(ok = load_vec(kb_cur, n_in))) break;
         }
         kb_cur = kb_next;
       }
@@ -432,7 +447,6 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
     const int quarter = warp & 3, j = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    constexpr float kLog2e = 1.4426950408889634f;
     const float c2 = p.scale_log2;
     uint32_t g = 0, qc = 0;
     bool ok = true;
@@ -478,8 +492,7 @@ __global__ void __maxnreg__((BwdWideCfg<KIND, D>::MAX_REGS))
             if ((a >> (8 * gi)) & 0xFFu) {
               const uint32_t va = vslot + 32 * gi;
               const float4 l0 = ld_shared_f32x4(va), l1 = ld_shared_f32x4(va + 16);
-              const float lv[8] = {l0.x * -kLog2e, l0.y * -kLog2e, l0.z * -kLog2e, l0.w * -kLog2e,
-                                   l1.x * -kLog2e, l1.y * -kLog2e, l1.z * -kLog2e, l1.w * -kLog2e};
+              const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};  // -lse log2 e
 #pragma unroll
               for (int i = 0; i < 8; i += 2) {
                 const int k = 8 * gi + i;
