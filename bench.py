@@ -304,9 +304,12 @@ def run_ours(args):
       roof["mode_peak"] = round(tc / 2, 1)
       roof["mode_frac"] = round(achieved / (tc / 2), 4)
       roof["mode_peak_source"] = "half the " + peak_kind + " bf16 rate"
-  # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile.
+  # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile in one pass, 5
+  # where dK/dV runs as a dV-only (S, dV) and a dK-only (S, dP, dK) pass (3xTF32, and TF32 at head_dim 128).
   # 3xTF32 issues three products per MMA.
-  issued = 2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + 4 * lb.n_tiles) * (3 if args.mode == "tf32x3" else 1)
+  split = args.mode == "tf32x3" or (args.mode == "tf32" and head_dim == 128)
+  issued = (2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + (5 if split else 4) * lb.n_tiles) *
+            (3 if args.mode == "tf32x3" else 1))
 
   # End to end through the public API with host buffers: pinned H2D of q, k, v, dO, forward + backward
   # through torch.autograd, D2H of o, dq, dk, dv, every step.
