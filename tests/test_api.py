@@ -29,3 +29,23 @@ def test_attention_impl_refuses_other_backends():
       patch.attention_impl()
   finally:
     patch.OPTIONS.attention = "auto"
+
+
+def test_processor_bf16_weight_cache_on_host():
+  """The inference path's bf16 weight copies: reused while a parameter is unchanged, recast after an in-place
+  update (the version counter moves) or a new storage (.data replaced)."""
+  import torch
+  from faster_weathernext.processor import Processor, ProcessorConfig
+  model = Processor(ProcessorConfig(layers=1, d_model=64, heads=2, head_dim=32, mlp_hidden=128, cond_dim=8),
+                    seed=1, device="cpu")
+  w = model.blocks[0].w1
+  a = model._bf16(w)
+  assert a.dtype == torch.bfloat16 and torch.equal(a, w.detach().to(torch.bfloat16))
+  assert model._bf16(w) is a
+  with torch.no_grad():
+    w.mul_(2.0)
+  b = model._bf16(w)
+  assert b is not a and torch.equal(b, w.detach().to(torch.bfloat16))
+  w.data = torch.zeros_like(w)
+  c = model._bf16(w)
+  assert c is not b and not c.any()
