@@ -49,3 +49,25 @@ def test_processor_bf16_weight_cache_on_host():
   w.data = torch.zeros_like(w)
   c = model._bf16(w)
   assert c is not b and not c.any()
+
+
+def test_layout_helpers_on_host():
+  """Host-side layout logic of the op: which strided views gathered row loads accept, the descriptor's strides,
+  and the refusal of a non-contiguous head_dim."""
+  import torch
+  from faster_weathernext import tiled_attn as ta
+  x = torch.zeros(2, 50, 4, 64)
+  assert ta._gather_layout(x) == 0                                   # [B, n, H, D] contiguous
+  fused = torch.zeros(2, 50, 4, 3, 64)
+  assert ta._gather_layout(fused[:, :, :, 1]) == 0                   # fused q/k/v: one 2D view, rows 3 D apart
+  assert ta._gather_layout(x[:, :, :2]) == -1                        # a head slice: rows are not evenly spaced
+  head_major = torch.zeros(2, 4, 50, 64).transpose(1, 2)
+  assert ta._gather_layout(head_major) == 1
+  d = ta._desc(fused[:, :, :, 0], x, 0.125, 0)
+  assert (d.batch, d.heads, d.n, d.head_dim) == (2, 4, 50, 64)
+  assert (d.stride_b, d.stride_n, d.stride_h) == (50 * 4 * 3 * 64, 4 * 3 * 64, 3 * 64)
+  assert (d.out_stride_b, d.out_stride_n, d.out_stride_h) == (50 * 4 * 64, 4 * 64, 64)
+  with pytest.raises(ValueError):
+    ta._desc(torch.zeros(2, 50, 4, 64).transpose(2, 3).transpose(2, 3)[..., ::2], x, 0.125, 0)
+  a, b = ta._canon(head_major, x)
+  assert a.stride() == b.stride() == x.stride()
