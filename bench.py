@@ -168,24 +168,81 @@ def kernel_costs(nnz, n, heads, head_dim, es, lf, lb):
   }
 
 
-def run_ours(args):
+class Ranks:
+  """One process per GPU (torchrun env) or a single process: device, barrier and max over ranks."""
+
+  def __init__(self, timeout_s=120):
+    import torch
+    import torch.distributed as dist
+    self.world = int(os.environ.get("WORLD_SIZE", "1"))
+    self.rank = int(os.environ.get("RANK", "0"))
+    self.local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(self.local)
+    self.device = torch.device("cuda", self.local)
+    if self.world > 1:
+      dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=self.device)
+
+  def barrier(self):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    if self.world > 1:
+      dist.barrier()
+
+  def max(self, x):
+    import torch
+    import torch.distributed as dist
+    if self.world == 1:
+      return x
+    t = torch.tensor([x], dtype=torch.float64, device=self.device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+  def close(self):
+    import torch.distributed as dist
+    if self.world > 1:
+      dist.barrier()
+      dist.destroy_process_group()
+
+
+def _sample_rows(n, q_blocks, k_blocks):
+  """Query rows (q_blocks blocks of 128 spread over the nodes) and key rows (k_blocks adjacent blocks)."""
+  nb = (n + 127) // 128
+  rows = lambda starts: np.concatenate([np.arange(b * 128, min(b * 128 + 128, n)) for b in starts])
+  qb = np.linspace(0, nb - 1, q_blocks).astype(int)
+  kb = nb // 3 + np.arange(k_blocks)
+  return rows(qb), rows(np.minimum(kb, nb - 1))
+
+
+def sampled_parity(mask_host, arrays, outs, scale, q_blocks, k_blocks):
+  """rel RMS of o, dq, dk, dv (and max |lse error|) at sampled rows against the float64 oracle."""
+  from oracle import attention as oa
+  n = mask_host.shape[0]
+  q_rows, k_rows = _sample_rows(n, q_blocks, k_blocks)
+  t0 = time.perf_counter()
+  ref = oa.sampled_attention(*(a[0] for a in arrays), mask_host, scale, q_rows, k_rows)
+  got = {"out": outs["o"][0][q_rows], "dq": outs["dq"][0][q_rows], "dk": outs["dk"][0][k_rows],
+         "dv": outs["dv"][0][k_rows]}
+  res = {name: float(f"{oa.rel_rms(got[name], ref[name]):.3e}") for name in got}
+  res["lse_max_abs"] = float(f"{np.abs(outs['lse'][0][:, q_rows] - ref['lse']).max():.3e}")
+  res["sample"] = f"{len(q_rows)} query rows, {len(k_rows)} key rows; float64 oracle {time.perf_counter() - t0:.1f} s"
+  return res
+
+
+def attention_block(args, ranks, workload_name, mode_name, steps, warmup, e2e=False, parity=False, clocks=None):
+  """Time `steps` steps (fwd + delta + dQ + dK/dV) of one workload / mode on resident inputs; per-kernel times,
+  roofline of the dominant kernel, issued-tile rate; optionally e2e through the public API and sampled parity."""
+  import ctypes
   import torch
-  import torch.distributed as dist
   from faster_weathernext import _lib
   from faster_weathernext import tiled_attn as ta
 
-  world = int(os.environ.get("WORLD_SIZE", "1"))
-  rank = int(os.environ.get("RANK", "0"))
-  local = int(os.environ.get("LOCAL_RANK", "0"))
-  torch.cuda.set_device(local)
-  device = torch.device("cuda", local)
-  if world > 1:
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-  mode = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[args.mode]
-  mask, tiles, sets, heads, head_dim = workload(device, 1000 + rank, args.mode, args.workload)
+  device = ranks.device
+  mode = {"bf16": _lib.MODE_BF16, "tf32": _lib.MODE_TF32, "tf32x3": _lib.MODE_TF32X3}[mode_name]
+  mask, tiles, sets, heads, head_dim = workload(device, 1000 + ranks.rank, mode_name, workload_name)
   n, nnz = mask.n, mask.nnz
   scale = head_dim ** -0.5
-  es = 2 if args.mode == "bf16" else 4
+  es = 2 if mode_name == "bf16" else 4
   useful = USEFUL_PER_PAIR * heads * nnz * head_dim
   stream = torch.cuda.current_stream()
   lib = _lib.lib()
@@ -198,7 +255,6 @@ def run_ours(args):
                dq=torch.empty_like(q0), dk=torch.empty_like(q0), dv=torch.empty_like(q0)) for _ in sets]
   ws_bytes = heads * lse_rows * 4
   ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
-  import ctypes
   if args.lists == "auto":
     lf, lb = ta._lists(tiles, q0, o_like)   # what the public API walks for this mask and layout
   else:
@@ -235,45 +291,33 @@ def run_ours(args):
         events.setdefault(name, []).append((e0, e1))
     return len(calls)
 
-  def barrier():
-    torch.cuda.synchronize()
-    if world > 1:
-      dist.barrier()
-
-  def max_over_ranks(x):
-    if world == 1:
-      return x
-    t = torch.tensor([x], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-  clocks = ClockSampler(local)
-  clocks.start()
-  for i in range(args.warmup):
+  for i in range(warmup):
     launch(i)
-  barrier()
+  ranks.barrier()
   if _lib.device_error(stream.cuda_stream):
     raise RuntimeError("device timeout during warm-up")
   start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-  clocks.mark("t0")
+  if clocks is not None:
+    clocks.mark("t0")
   start.record(stream)
   launches = 0
-  for i in range(args.steps):
+  for i in range(steps):
     launches += launch(i)
   end.record(stream)
-  barrier()
-  clocks.mark("t1")
-  ms = max_over_ranks(start.elapsed_time(end)) / args.steps
-  clocks.stop()
-  value = world * useful / (ms * 1e-3) / 1e12
+  ranks.barrier()
+  if clocks is not None:
+    clocks.mark("t1")
+  ms = ranks.max(start.elapsed_time(end)) / steps
+  if _lib.device_error(stream.cuda_stream):
+    raise RuntimeError("device timeout in the timed steps")
+  value = ranks.world * useful / (ms * 1e-3) / 1e12
 
   # Per-kernel durations (events on the launching stream around each C-ABI call), outside the timed region.
   events = {}
-  barrier()
-  per_kernel_steps = min(args.steps, 200)
-  for i in range(per_kernel_steps):
+  ranks.barrier()
+  for i in range(min(steps, 200)):
     launch(i, events)
-  barrier()
+  ranks.barrier()
   kernel_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in events.items()}
   costs = kernel_costs(nnz, n, heads, head_dim, es, lf, lb)
   hbm, tc, peak_kind = peaks()
@@ -284,7 +328,7 @@ def run_ours(args):
                   "algorithmic_gbs": round(nbytes / (ms_k * 1e-3) / 1e9, 1),
                   "bound": "tensor" if flops / (tc * 1e12) > nbytes / (hbm * 1e9) else "hbm"}
   dom = max(kernel_ms, key=kernel_ms.get)
-  traffic = NCU_TRAFFIC.get((args.workload, args.mode, lists_used), {})
+  traffic = NCU_TRAFFIC.get((workload_name, mode_name, lists_used), {})
   flops, nbytes = costs[dom]
   bound = kernels[dom]["bound"]
   if bound == "hbm":
@@ -297,37 +341,52 @@ def run_ours(args):
     roof = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 2), "peak": tc, "unit": "TFLOP/s",
             "frac": round(achieved / tc, 4), "peak_source": peak_kind,
             "algorithmic_flops": flops, "traffic": traffic.get(dom)}
-    if args.mode != "bf16":
-      # The mode's own peak as well: dense TF32 runs at half the bf16 rate on B200 (1.1 vs 2.25 PFLOP/s nominal);
-      # only the bf16 rate is measured, so the TF32 peak is taken as half of it. 3xTF32 counts useful FLOPs
-      # once against the same TF32 peak.
-      roof["mode_peak"] = round(tc / 2, 1)
-      roof["mode_frac"] = round(achieved / (tc / 2), 4)
-      roof["mode_peak_source"] = "half the " + peak_kind + " bf16 rate"
+  if mode_name != "bf16":
+    # The mode's own peak as well: dense TF32 runs at half the bf16 rate on B200 (1.1 vs 2.25 PFLOP/s nominal);
+    # only the bf16 rate is measured, so the TF32 peak is taken as half of it. 3xTF32 counts useful FLOPs
+    # once against the same TF32 peak.
+    mode_tflops = flops / (kernel_ms[dom] * 1e-3) / 1e12
+    roof["mode_peak"] = round(tc / 2, 1)
+    roof["mode_frac"] = round(mode_tflops / (tc / 2), 4)
+    roof["mode_peak_source"] = "half the " + peak_kind + " bf16 rate"
   # Tensor-core work actually issued on 128 x 32 tiles: forward 2 MMAs, dQ 3, dK/dV 4 per tile in one pass, 5
   # where dK/dV runs as a dV-only (S, dV) and a dK-only (S, dP, dK) pass (3xTF32, and TF32 at head_dim 128).
   # 3xTF32 issues three products per MMA.
-  split = args.mode == "tf32x3" or (args.mode == "tf32" and head_dim == 128)
+  split = mode_name == "tf32x3" or (mode_name == "tf32" and head_dim == 128)
   issued = (2 * heads * head_dim * 128 * 32 * (5 * lf.n_tiles + (5 if split else 4) * lb.n_tiles) *
-            (3 if args.mode == "tf32x3" else 1))
+            (3 if mode_name == "tf32x3" else 1))
 
-  # End to end through the public API with host buffers: pinned H2D of q, k, v, dO, forward + backward
-  # through torch.autograd, D2H of o, dq, dk, dv, every step.
-  e2e = None
-  if not args.no_e2e:
+  block = {"workload": workload_name, "mode": mode_name, "nodes": n, "pairs": nnz, "heads": heads,
+           "head_dim": head_dim, "tile_lists": lists_used, "steps": steps, "warmup": warmup,
+           "ms_per_step": round(ms, 5), "value": round(value, 3), "unit": UNIT, "kernels": kernels,
+           "roofline": roof, "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2), "gpu_launches": launches,
+           "l2": f"inputs larger than L2: 3 rotating input sets of "
+                 f"{4 * q0.numel() * q0.element_size() / 1e6:.0f} MB"}
+
+  if parity and ranks.rank == 0:
+    torch.cuda.synchronize()
+    arrays = [x.float().cpu().numpy() for x in sets[0]]
+    host_outs = {k: v.float().cpu().numpy() for k, v in outs[0].items()}
+    qb, kb = (4, 2) if workload_name == "wn2" else (8, 8)
+    block["parity"] = sampled_parity(mask.host(), arrays, host_outs, scale, qb, kb)
+    bound_ = 5e-3 if mode_name in ("bf16", "tf32") else 2e-5
+    block["parity"]["bound_rel_rms"] = bound_
+    block["parity"]["ok"] = all(block["parity"][k] <= bound_ for k in ("out", "dq", "dk", "dv"))
+
+  if e2e:
     # End to end through the public API: every step copies its q, k, v, dO from pinned host memory, runs
     # tiled_attn.attention + torch.autograd.grad, and copies o, dq, dk, dv back to pinned host memory. As in a
     # training loop, the copies run on their own streams (two buffer slots), so that step i's upload, step
     # i-1's compute and step i-2's download overlap; all of them lie inside the timed region.
-    dt = torch.bfloat16 if args.mode == "bf16" else torch.float32
-    host_in = [[x.cpu().pin_memory() for x in s] for s in sets[:2]]
+    dt = torch.bfloat16 if mode_name == "bf16" else torch.float32
+    host_in = [[x.cpu().pin_memory() for x in s_] for s_ in sets[:2]]
     host_out = [[torch.empty(q0.shape, dtype=dt).pin_memory() for _ in range(4)] for _ in range(2)]
     dev_in = [[torch.empty_like(x) for x in sets[0]] for _ in range(2)]
     s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_cmp = [torch.cuda.Event() for _ in range(2)]
-    e2e_steps = min(args.steps, 50)
-    precision = "highest" if args.mode == "tf32x3" else None
+    e2e_steps = min(steps, 50)
+    precision = "highest" if mode_name == "tf32x3" else None
 
     def e2e_step(i):
       sl = i % 2
@@ -350,7 +409,7 @@ def run_ours(args):
 
     for i in range(3):
       e2e_step(i)
-    barrier()
+    ranks.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     s_h2d.wait_event(a)
@@ -358,20 +417,127 @@ def run_ours(args):
       e2e_step(i)
     stream.wait_stream(s_d2h)
     b.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(a.elapsed_time(b)) / e2e_steps
+    ranks.barrier()
+    e2e_ms = ranks.max(a.elapsed_time(b)) / e2e_steps
     tb = q0.numel() * q0.element_size()
-    e2e = {"value": round(world * useful / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
-           "h2d_bytes_per_step": 4 * tb, "d2h_bytes_per_step": 4 * tb,
-           "overlap": "H2D, compute and D2H on three streams, two buffer slots"}
+    block["e2e"] = {"value": round(ranks.world * useful / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": 4 * tb, "d2h_bytes_per_step": 4 * tb,
+                    "overlap": "H2D, compute and D2H on three streams, two buffer slots"}
+  block["_mask"] = mask
+  del sets, outs, ws
+  return block
 
+
+def finetune_block(args, ranks, steps, warmup):
+  """Configuration 5 (fine-tune step: 8 members split over the ranks, forward + backward through the custom-VJP
+  attention, gradient all-reduce, Adam) with the all-reduce overlapped with the backward (bucketed, issued from
+  gradient hooks) and without it (one all-reduce after the backward); plus the gradient all-reduce alone."""
+  import torch
+  import torch.distributed as dist
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.finetune import DataParallelStep, RankWatchdog
+  from faster_weathernext.processor import Processor, ProcessorConfig
+
+  device = ranks.device
+  mask, _, _ = mesh.config_mask(CFG)
+  n = mask.shape[0]
+  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  cfg = ProcessorConfig()
+  members = 8
+  local_m = members // ranks.world
+  g = torch.Generator(device=device).manual_seed(100 + ranks.rank)
+  xs = [torch.randn(1, n, cfg.d_model, device=device, generator=g) for _ in range(local_m)]
+  cs = [torch.randn(1, cfg.cond_dim, device=device, generator=g) for _ in range(local_m)]
+  ts = [torch.randn(1, n, cfg.d_model, device=device, generator=g) for _ in range(local_m)]
+  dog = None
+  if ranks.world > 1:
+    from torch.distributed import distributed_c10d as c10d
+    dog = RankWatchdog(c10d._get_default_store(), ranks.rank, ranks.world, timeout=60.0).start()
+  out = {"workload": "cfg5: 8 members, MSE, fwd + bwd + gradient all-reduce + Adam, level-6 mesh 0.06 rad",
+         "members_per_gpu": local_m, "micro_batch": args.micro_batch, "steps": steps, "warmup": warmup}
+  stream = torch.cuda.current_stream()
+  for overlap in (True, False):
+    model = Processor(cfg, seed=0, device=device)
+    trainer = DataParallelStep(model, members, lr=1e-5, overlap=overlap, watchdog=dog)
+
+    def step():
+      return trainer.step(xs, cs, ts, forward=lambda x, c: model(x, c, tiles), micro_batch=args.micro_batch)
+    for _ in range(warmup):
+      step()
+    ranks.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+      loss = step()
+    b.record(stream)
+    ranks.barrier()
+    ms = ranks.max(a.elapsed_time(b)) / steps
+    key = "overlapped" if overlap else "not_overlapped"
+    out[key] = {"ms_per_step": round(ms, 3), "buckets": len(trainer.buckets) if overlap else 1,
+                "loss": round(float(loss), 6)}
+    out["grad_bytes"] = trainer.numel * 4
+    del model, trainer
+    torch.cuda.empty_cache()
+  out["peak_memory_gb"] = round(torch.cuda.max_memory_allocated(device) / 1e9, 1)
+  if ranks.world > 1:
+    # The gradient all-reduce alone: one float32 buffer of the model's gradient size, NCCL over NVLink.
+    buf = torch.ones(out["grad_bytes"] // 4, dtype=torch.float32, device=device)
+    for _ in range(3):
+      dist.all_reduce(buf)
+    ranks.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    a.record(stream)
+    for _ in range(reps):
+      dist.all_reduce(buf)
+    b.record(stream)
+    ranks.barrier()
+    ar_ms = ranks.max(a.elapsed_time(b)) / reps
+    busbw = out["grad_bytes"] * 2 * (ranks.world - 1) / ranks.world / (ar_ms * 1e-3) / 1e9
+    out["allreduce"] = {"ms": round(ar_ms, 3), "bytes": out["grad_bytes"], "busbw_gbs": round(busbw, 1),
+                        "reference_busbw_gbs": 725.0,
+                        "note": "NCCL all-reduce of the float32 gradient buffer; busbw = 2 (N-1) / N x bytes / time"}
+    del buf
+    dog.stop()
+  else:
+    out["allreduce"] = None
+  return out
+
+
+def run_ours(args):
+  import torch
+
+  ranks = Ranks()
+  clocks = ClockSampler(ranks.local)
+  clocks.start()
+  head = attention_block(args, ranks, args.workload, args.mode, args.steps, args.warmup, e2e=not args.no_e2e,
+                         parity=False, clocks=clocks)
+  clocks.stop()
+  mask = head.pop("_mask")
   cpu = None
-  if rank == 0 and world == 1 and not args.no_cpu:
-    cpu = cpu_baseline(mask.host(), heads, head_dim, seconds=args.cpu_seconds, name=args.workload)
+  if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu:
+    cpu = cpu_baseline(mask.host(), head["heads"], head["head_dim"], seconds=args.cpu_seconds, name=args.workload)
+  del mask
+  torch.cuda.empty_cache()
 
-  if world > 1:
-    dist.barrier()
-  if rank == 0:
+  # Other modes and shapes in the same run (default run only): config 3 in the reference's own precision (TF32)
+  # and its `highest` (3xTF32), and the real WN2 shape in bf16; each with sampled-row parity against the oracle.
+  modes = {}
+  if not args.no_blocks and args.workload == "attention" and args.mode == "bf16":
+    blk_steps, blk_warmup = min(args.steps, 20), max(3, min(args.warmup, 5))
+    for wl, md in (("attention", "tf32"), ("attention", "tf32x3"), ("wn2", "bf16")):
+      blk = attention_block(args, ranks, wl, md, blk_steps, blk_warmup, parity=True)
+      blk.pop("_mask")
+      modes[("cfg3" if wl == "attention" else wl) + "_" + md] = blk
+      torch.cuda.empty_cache()
+  finetune = None
+  if not args.no_finetune and args.workload == "attention" and args.mode == "bf16":
+    finetune = finetune_block(args, ranks, steps=min(args.steps, 5), warmup=3)
+
+  if ranks.rank == 0:
+    world, n, nnz = ranks.world, head["nodes"], head["pairs"]
+    heads, head_dim = head["heads"], head["head_dim"]
     if args.workload == "wn2":
       desc_w = (f"WN2 real shape fwd+bwd: 40,962 nodes (level-6 mesh, Hilbert order), 32-hop mask ({nnz} pairs, "
                 f"built on the device), B1 H{heads} D{head_dim} per GPU")
@@ -380,22 +546,20 @@ def run_ours(args):
       desc_w = (f"cfg3 fwd+bwd: 40,962 nodes (Morton), mask <= 0.06 rad ({nnz} pairs), "
                 f"B1 H{heads} D{head_dim} per GPU")
       data = "synthetic: Q/K/V/dO ~ N(0,1) seeded per rank; icosphere level-6 great-circle mask built on the host"
-    set_mb = 4 * sets[0][0].numel() * sets[0][0].element_size() / 1e6
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": published_ratio(args, value, nnz, heads, head_dim),
+        "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": published_ratio(args, head["value"], nnz, heads, head_dim),
         "dtype": {"bf16": "bf16", "tf32": "tf32", "tf32x3": "3xtf32"}[args.mode], "data": data,
         "config": {"workload": desc_w, "global_batch": world, "nodes": n,
                    "heads": heads, "head_dim": head_dim, "parallelism": f"replicas x{world} (no communication)",
-                   "l2": f"inputs larger than L2: 3 rotating input sets of {set_mb:.0f} MB", "tile_lists": lists_used},
-        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-        "clocks": clocks.summary(), "kernels": kernels,
-        "issued_tile_tflops": round(issued / (ms * 1e-3) / 1e12, 2),
+                   "l2": head["l2"], "tile_lists": head["tile_lists"]},
+        "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"), "gpu_launches": head["gpu_launches"],
+        "clocks": clocks.summary(), "kernels": head["kernels"], "issued_tile_tflops": head["issued_tile_tflops"],
+        "modes": modes or None, "finetune": finetune,
     }
     print(json.dumps(line), flush=True)
-  if world > 1:
-    dist.destroy_process_group()
+  ranks.close()
 
 
 # The reference's published fwd+bwd times at the WN2 shape (RTX 5090, one layer, 6 x 128 heads, 32-hop mask,
@@ -645,6 +809,9 @@ def main():
                   help="fine-tune: members per forward / backward on a rank (activations ~29 GB per member)")
   ap.add_argument("--no-e2e", action="store_true")
   ap.add_argument("--no-cpu", action="store_true")
+  ap.add_argument("--no-blocks", action="store_true",
+                  help="default run: skip the TF32 / 3xTF32 / WN2 blocks")
+  ap.add_argument("--no-finetune", action="store_true", help="default run: skip the configuration-5 block")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)
   ap.add_argument("--ref-seconds", type=float, default=90.0,
                   help="--impl reference: host seconds the warm-up and timed steps take together")

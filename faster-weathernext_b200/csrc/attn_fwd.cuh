@@ -48,6 +48,9 @@ struct FwdParams {
   unsigned long long* trace;  // FWN_TRACE builds: kTraceCtas x kTraceEvents event records (else unused)
   const void* q;          // Q and its element strides (read by the softmax warps where Q lives in TMEM)
   int64_t q_sb, q_sn, q_sh;
+  unsigned long long wait_limit_ns;  // bound of every mbarrier wait of the narrow kernel (kWaitLimitNs normally)
+  int fault_skip_kv;      // test launches only: the producer leaves out the first K/V load of CTA 0, so that the
+                          // MMA warp's bounded wait on it expires (nothing else is changed)
 };
 
 template <int D, bool F32, bool X3 = false>
@@ -149,6 +152,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
   auto kv_ready = [&](int s) { return bar1 + 96 + 8 * s; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
+  const unsigned long long wlim = p.wait_limit_ns;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int trace_count = 0;  // FWN_TRACE builds: this lane's event count
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
     uint32_t g = 0, qc = 0;
     bool ok = true;
     int pending_q = 0;
+    long long skipped = -1;  // fault_skip_kv launches: the stage load left out
     int it = blockIdx.x;
     int nt0 = 0, nt1 = 0;
     if (it < p.n_items) {
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       ChunkMeta<C::CH> m1 = load_chunk_meta<C::CH, GATHER>(p.kb2, p.cols, t0, n_sub, 1, lane);
       if (lane == 0) FWN_TR(1, it);
       if constexpr (!C::Q_TMEM) {
-        if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+        if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag, wlim))) break;
         if (lane == 0) {
           FWN_TR(2, nch);
           mbar_arrive_expect_tx(q_full, C::Q_BYTES);
@@ -232,7 +237,11 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       // each prefetched register pair is consumed in place (a register move would wait for the load).
       auto issue_chunk = [&](int c, const ChunkMeta<C::CH>& meta) -> bool {
           const int st = g % C::NS;
-          if (!mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag)) return false;
+          if (!mbar_wait(kv_empty(st), ((g / C::NS) & 1) ^ 1, abort_flag, wlim)) return false;
+          if (p.fault_skip_kv && it == 0 && c == 0) {
+            skipped = g;  // neither the expected bytes nor any copy: kv_full of this stage never completes
+            return true;
+          }
           const int n_in = min(C::CH, n_sub - C::CH * c);
           if (lane == 0) FWN_TR(3, c);
           if (lane == 0) mbar_arrive_expect_tx(kv_full(st), n_in * (2 * C::SUB * D * C::ES + 512));
@@ -295,15 +304,15 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       // Drain: wait (bounded, ignoring the abort flag) for every copy this warp issued.
       volatile int never = 0;
       for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k)
-        mbar_wait(kv_full(k % C::NS), (k / C::NS) & 1, &never);
-      if (pending_q) mbar_wait(q_full, (qc & 1), &never);
+        if (static_cast<long long>(k) != skipped) mbar_wait(kv_full(k % C::NS), (k / C::NS) & 1, &never, wlim);
+      if (pending_q) mbar_wait(q_full, (qc & 1), &never, wlim);
     }
   } else if (warp == 1) {
     {
       // ------------------------------------------------------------------ MMA issuer
       // The whole warp runs the loop with warp-uniform descriptors and one elected lane issues each MMA / commit
       // (measured 6 % faster on the sparse configuration-3 backward than a lane-0 loop).
-      auto wait_ = [&](uint32_t bar, uint32_t parity) -> bool { return warp_wait(bar, parity, abort_flag); };
+      auto wait_ = [&](uint32_t bar, uint32_t parity) -> bool { return warp_wait(bar, parity, abort_flag, wlim); };
       auto issue_ = [&](auto&& fn) {
         if (elect_one_sync()) fn();
         __syncwarp();
@@ -422,7 +431,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       // Drain the tensor pipe before TMEM is released.
       issue_([&] { mma_commit(drain); });
       volatile int never = 0;
-      mbar_wait(drain, 0, &never);
+      mbar_wait(drain, 0, &never, wlim);
     }
   } else if (X3 && warp >= 6) {
     // ------------------------------------------------------------------ 3xTF32 converter (warps 6-9)
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       const int nch = (n_sub + C::CH - 1) / C::CH;
       if (nch == 0) continue;
       if constexpr (!C::Q_TMEM) {
-        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(q_full, qc & 1, abort_flag, wlim))) break;
         split_tf32(q_smem, q_lo, C::Q_BYTES, ctid, 128);
         fence_proxy_async_smem();
         __syncwarp();
@@ -443,7 +452,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
       }
       for (int c = 0; c < nch; ++c, ++g) {
         const int st = g % C::NS;
-        if (!(ok = mbar_wait(kv_full(st), (g / C::NS) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(kv_full(st), (g / C::NS) & 1, abort_flag, wlim))) break;
         split_tf32(stage_k(st), stage_klo(st), C::KV_BYTES, ctid, 128);
         split_tf32(stage_v(st), stage_vlo(st), C::KV_BYTES, ctid, 128);
         fence_proxy_async_smem();
@@ -478,7 +487,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         // The item's Q into TMEM (this thread's row into its lane), once the previous item's last S MMA is
         // complete; rows past n are zero (as the TMA load's out-of-range fill).
         if (nch > 0) {
-          if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag))) break;
+          if (!(ok = mbar_wait(q_empty, (qc & 1) ^ 1, abort_flag, wlim))) break;
           tc_fence_after();
           const float* src = qrow < p.n ? static_cast<const float*>(p.q) + static_cast<int64_t>(b) * p.q_sb +
                                               static_cast<int64_t>(qrow) * p.q_sn + static_cast<int64_t>(h) * p.q_sh
@@ -519,15 +528,15 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         const int sb = gg & 1, st = gg % C::NS;
         const int n_in = min(C::CH, n_sub - C::CH * c);
         float s[64];
-        if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag, wlim))) break;
         if (lane == 0) FWN_TR(20, c);
         tc_fence_after();
         tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
         if (C::CH == 2 && n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
         // While S is read from TMEM: the chunk's mask words (they land with its K / V tiles) and, for bf16, the
         // P buffer (free once P V of chunk gg-2 is complete).
-        ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag);
-        if (C::P_TMEM && ok) ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag);
+        ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag, wlim);
+        if (C::P_TMEM && ok) ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag, wlim);
         uint32_t w0 = 0u, w1 = 0u;
         if (ok) {
           w0 = ld_shared_u32(stage_bits(st) + row * 4);
@@ -665,7 +674,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           }
           if constexpr (!C::P_TMEM) {
             // 3xTF32: P hi (13 low mantissa bits cleared) and lo = P - hi into shared memory.
-            if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag))) break;
+            if (!(ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag, wlim))) break;
             const uint32_t pbase = p_smem(sb);
 #pragma unroll
             for (int cc = 0; cc < 16; ++cc) {
@@ -691,7 +700,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         if (__any_sync(0xffffffffu, rescale)) {
           const uint32_t prev = gg - 1;
           if (lane == 0) FWN_TR(28, c);
-          if (!(ok = mbar_wait(p_empty(prev & 1), (prev >> 1) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(p_empty(prev & 1), (prev >> 1) & 1, abort_flag, wlim))) break;
           tc_fence_after();
 #pragma unroll
           for (int j = 0; j < D / 32; ++j) {
@@ -728,7 +737,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         }
         continue;
       }
-      if (!(ok = mbar_wait(o_full, qc & 1, abort_flag))) break;
+      if (!(ok = mbar_wait(o_full, qc & 1, abort_flag, wlim))) break;
       if (lane == 0) FWN_TR(22, it);
       tc_fence_after();
 #pragma unroll

@@ -102,17 +102,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of `parity` to complete. On expiry (or when another role of the CTA
-// already gave up: *abort != 0) it records the failure and returns false; the caller then leaves its
+// Bounded wait for the phase of `parity` to complete. On expiry after limit_ns (or when another role of the
+// CTA already gave up: *abort != 0) it records the failure and returns false; the caller then leaves its
 // loop so that the CTA can free its TMEM and return.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         atomicOr(&g_device_error, 5u);
         return false;
@@ -173,8 +174,9 @@ __device__ __forceinline__ bool elect_one_sync() {
   return pred != 0;
 }
 // A bounded mbarrier wait whose outcome is the same in every lane of the warp.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-  const bool ok = mbar_wait(bar, parity, abort);
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
+  const bool ok = mbar_wait(bar, parity, abort, limit_ns);
   return __all_sync(0xffffffffu, ok);
 }
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

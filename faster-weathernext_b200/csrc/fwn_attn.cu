@@ -199,7 +199,9 @@ std::mutex g_noalloc_mutex;
 constexpr int kMaxDevices = 64;
 float* g_noalloc_ptr[kMaxDevices] = {};
 
-// Device address of g_noalloc_delta on the current device (looked up on the first call per device).
+// Device address of g_noalloc_delta on the current device (looked up on the first call per device and kept:
+// valid while the device's primary context lives, i.e. until a cudaDeviceReset, after which the header forbids
+// further calls on that device).
 fwn_status noalloc_delta(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -229,7 +231,8 @@ unsigned long long* trace_buffer() {
 
 template <int D, bool F32, bool GATHER, bool X3 = false>
 fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, const void* v, const fwn_tile_list& t,
-                      void* o, float* lse, int layout, cudaStream_t stream) {
+                      void* o, float* lse, int layout, cudaStream_t stream,
+                      unsigned long long wait_limit_ns = fwn::kWaitLimitNs, int fault_skip_kv = 0) {
   using C = fwn::FwdCfg<D, F32, X3>;
   CUtensorMap tq, tk, tv, tk32, tv32;
   fwn_status s;
@@ -267,6 +270,8 @@ fwn_status launch_fwd(const fwn_attn_desc& d, const void* q, const void* k, cons
   p.q_sb = d.stride_b;
   p.q_sn = d.stride_n;
   p.q_sh = d.stride_h;
+  p.wait_limit_ns = wait_limit_ns;
+  p.fault_skip_kv = fault_skip_kv;
 #ifdef FWN_TRACE
   p.trace = trace_buffer();
 #endif
@@ -715,15 +720,30 @@ fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, i
 
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }
 
-fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops, uint32_t* reach,
-                           uint32_t* scratch, void* stream) {
+namespace {
+
+fwn_status khop_common(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops, uint32_t* reach,
+                       uint32_t* scratch, void* stream, bool include_self) {
   if (n < 0 || hops < 0 || hops > 4096) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n=%d or hops=%d", n, hops);
   if (n > 0 && (!indptr || !reach || !scratch)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
   if (n > 0 && (!aligned16(reach) || !aligned16(scratch)))
     return fail(FWN_ERR_INVALID_ARGUMENT, "reach and scratch must be 16-byte aligned");
-  cudaError_t e = fwn::launch_khop(indptr, indices, n, hops, reach, scratch, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "khop");
+  cudaError_t e = fwn::launch_khop(indptr, indices, n, hops, reach, scratch, static_cast<cudaStream_t>(stream),
+                                   include_self);
+  if (e != cudaSuccess) return cuda_fail(e, include_self ? "khop" : "walks");
   return ok();
+}
+
+}  // namespace
+
+fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops, uint32_t* reach,
+                           uint32_t* scratch, void* stream) {
+  return khop_common(indptr, indices, n, hops, reach, scratch, stream, true);
+}
+
+fwn_status fwn_walk_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t length, uint32_t* reach,
+                           uint32_t* scratch, void* stream) {
+  return khop_common(indptr, indices, n, length, reach, scratch, stream, false);
 }
 
 fwn_status fwn_bitset_csr_count(const uint32_t* bits, int32_t n_rows, int32_t n_cols, int32_t* indptr, void* ws,
@@ -786,6 +806,30 @@ fwn_status fwn_attn_fwd(const fwn_attn_desc* desc, const void* q, const void* k,
              : launch_fwd<64, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
   return g ? launch_fwd<128, true, true, true>(d, q, k, v, *tiles, o, lse, layout, st)
            : launch_fwd<128, true, false, true>(d, q, k, v, *tiles, o, lse, layout, st);
+}
+
+fwn_status fwn_test_attn_fwd_timeout(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                                     const fwn_tile_list* tiles, void* o, float* lse, uint64_t wait_limit_ns,
+                                     void* stream) {
+  fwn_status s = check_desc(desc);
+  if (s != FWN_OK) return s;
+  if ((s = check_tiles(tiles, desc, "tiles")) != FWN_OK) return s;
+  if (!q || !k || !v || !o) return fail(FWN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  if (wait_limit_ns < 100000ull || wait_limit_ns > fwn::kWaitLimitNs)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "wait_limit_ns must lie in [1e5, %llu]", fwn::kWaitLimitNs);
+  const fwn_attn_desc& d = *desc;
+  if (d.mode != FWN_MODE_BF16 || d.head_dim != 64 || use_wide(d, *tiles))
+    return fail(FWN_ERR_UNSUPPORTED, "the timeout test runs the narrow bf16 head_dim-64 forward only");
+  int layout = 0;
+  if (tiles->cols) {
+    layout = gather_layout(d, false);
+    if (layout < 0) return fail(FWN_ERR_INVALID_ARGUMENT, "gathered lists need a node-major or head-major packed layout");
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return tiles->cols ? launch_fwd<64, false, true>(d, q, k, v, *tiles, o, lse, layout, st, wait_limit_ns, 1)
+                     : launch_fwd<64, false, false>(d, q, k, v, *tiles, o, lse, layout, st, wait_limit_ns, 1);
 }
 
 fwn_status fwn_attn_bwd_workspace_size(const fwn_attn_desc* desc, size_t* bytes) {

@@ -4,7 +4,10 @@
 // whose nonzero pattern is the attention mask. reach_0 = I, reach_{s+1}[i] = reach_s[i] | OR_{j in adj(i)}
 // reach_s[j]; after `hops` steps row i holds every node within `hops` edges of i, i.e. the pattern of
 // (adj + I) ** hops. Rows are bitsets of `words` uint32 (bit c of word w = column 32 w + c), so one
-// step reads (1 + degree) rows per row: HBM-bound, coalesced 16-byte loads, no atomics.
+// step reads (1 + degree) rows per row: HBM-bound, coalesced 16-byte loads, no atomics. The walk variant
+// drops the `reach_s[i] |` term: after `length` steps row i holds the end nodes of the walks of exactly
+// `length` edges from i, the nonzero pattern of adj ** length itself (what the reference's matrix power gives
+// for any adjacency, with or without self edges).
 //
 // The CSR conversion writes ascending column indices per row (warp-wide popcount prefix over each run of
 // 32 words), which is what the tile-list builder and scipy's sorted CSR hold.
@@ -25,7 +28,9 @@ __global__ void __launch_bounds__(256) bitset_identity_kernel(uint32_t* __restri
   }
 }
 
-// One CTA per row: dst[i] = src[i] | OR of src[j] over the row's neighbours (indices outside [0, n) ignored).
+// One CTA per row: dst[i] = (kSelf ? src[i] : 0) | OR of src[j] over the row's neighbours (indices outside
+// [0, n) ignored).
+template <bool kSelf>
 __global__ void __launch_bounds__(kStepThreads) khop_step_kernel(const int32_t* __restrict__ indptr,
                                                                 const int32_t* __restrict__ indices, int n,
                                                                 int words, const uint4* __restrict__ src,
@@ -40,7 +45,7 @@ __global__ void __launch_bounds__(kStepThreads) khop_step_kernel(const int32_t* 
   for (int v0 = 0; v0 < vw; v0 += kStepThreads) {
     const int v = v0 + threadIdx.x;
     const bool active = v < vw;
-    uint4 acc = active ? own[v] : make_uint4(0, 0, 0, 0);
+    uint4 acc = (kSelf && active) ? own[v] : make_uint4(0, 0, 0, 0);
     for (int base = e0; base < e1; base += kStepThreads) {
       // Neighbour ids are staged per batch of kStepThreads edges.
       __syncthreads();
@@ -117,7 +122,7 @@ __global__ void __launch_bounds__(256) bitset_fill_kernel(const uint32_t* __rest
 int bitset_words(int n_cols) { return ((n_cols + 31) / 32 + 3) / 4 * 4; }
 
 cudaError_t launch_khop(const int32_t* indptr, const int32_t* indices, int n, int hops, uint32_t* reach,
-                        uint32_t* scratch, cudaStream_t stream) {
+                        uint32_t* scratch, cudaStream_t stream, bool include_self) {
   if (n <= 0) return cudaSuccess;
   const int words = bitset_words(n);
   // Ping-pong so that the last step writes `reach`.
@@ -127,8 +132,12 @@ cudaError_t launch_khop(const int32_t* indptr, const int32_t* indices, int n, in
   const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 32));
   bitset_identity_kernel<<<grid, 256, 0, stream>>>(a, n, words);
   for (int s = 0; s < hops; ++s) {
-    khop_step_kernel<<<n, kStepThreads, 0, stream>>>(indptr, indices, n, words, reinterpret_cast<const uint4*>(a),
-                                                     reinterpret_cast<uint4*>(b));
+    if (include_self)
+      khop_step_kernel<true><<<n, kStepThreads, 0, stream>>>(indptr, indices, n, words,
+                                                             reinterpret_cast<const uint4*>(a), reinterpret_cast<uint4*>(b));
+    else
+      khop_step_kernel<false><<<n, kStepThreads, 0, stream>>>(indptr, indices, n, words,
+                                                              reinterpret_cast<const uint4*>(a), reinterpret_cast<uint4*>(b));
     std::swap(a, b);
   }
   return cudaGetLastError();

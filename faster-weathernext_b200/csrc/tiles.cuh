@@ -41,10 +41,11 @@ cudaError_t launch_exclusive_scan(const int32_t* counts, int n, int32_t* ptr, cu
 // k-hop reach (khop.cu): uint32 words per bitset row of n_cols columns (a multiple of 4).
 int bitset_words(int n_cols);
 
-// reach[n, bitset_words(n)] = nodes within `hops` edges of each node (self included); scratch is the same
-// size. indptr / indices: CSR of the graph (any column order, duplicates allowed).
+// reach[n, bitset_words(n)] = nodes within `hops` edges of each node (self included), or with include_self
+// false the end nodes of walks of exactly `hops` edges; scratch is the same size. indptr / indices: CSR of the
+// graph (any column order, duplicates allowed).
 cudaError_t launch_khop(const int32_t* indptr, const int32_t* indices, int n, int hops, uint32_t* reach,
-                        uint32_t* scratch, cudaStream_t stream);
+                        uint32_t* scratch, cudaStream_t stream, bool include_self);
 
 // CSR of a bitset matrix: indptr[n_rows + 1] (counts: n_rows ints of workspace), then ascending indices.
 cudaError_t launch_bitset_csr_count(const uint32_t* bits, int n_rows, int n_cols, int32_t* indptr, int32_t* counts,

@@ -20,6 +20,7 @@ def enable(force: bool = False, **options):
       raise TypeError(f"unknown option {key!r}; see faster_weathernext.patch.Options")
   for key, value in options.items():
     setattr(patch.OPTIONS, key, value)
+  patch.warn_no_effect(options)
   patch.install(force=force)
   return patch.OPTIONS
 

@@ -54,7 +54,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     subprocess.run(cmd, check=True)
     objs.append(obj)
   tmp = LIB + ".tmp"
-  subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcuda" if False else "-lcudart_static", "-ldl",
+  subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-ldl",
                   "-lrt", "-lpthread"], check=True)
   os.replace(tmp, LIB)
   return LIB

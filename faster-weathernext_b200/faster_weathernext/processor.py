@@ -11,9 +11,10 @@ q/k/v/out projections and a GELU MLP. The official modules (`weathernext.utils.s
 `dense.LinearNormConditioning`) are third-party and not available here, so this is a synthetic processor of
 the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU in the tanh form that is
 jax.nn.gelu's default; Glorot-uniform weights from a seed), not a numerical copy of the official one. The
-projections run as cuBLAS GEMMs; the attention is faster_weathernext's kernel (q, k, v are strided views of one
-fused projection, no copies). Without autograd (inference), each norm is one fused kernel and bias + GELU run
-in the GEMM epilogue.
+projections run as cuBLAS GEMMs; the attention block is patch.tiled_mha (the B200 kernel; q, k, v are strided
+views of one fused projection, no copies). Without autograd (inference), each norm is one fused kernel and
+bias + GELU run in the GEMM epilogue. With autograd and patch.OPTIONS.remat, each block's activations are
+recomputed in the backward instead of stored (the reference's per-layer rematerialisation, patch.py:69-73).
 
 Node order: the reference's transformer gathers the latents into the mask's node order with `perm` before the
 first block and takes them back with argsort(perm) after the final norm (patch.py:275-276, 291-292). `forward`
@@ -26,8 +27,10 @@ import math
 
 import torch
 import torch.nn.functional as F
+import torch.utils.checkpoint
 
 from faster_weathernext import _lib
+from faster_weathernext import patch
 from faster_weathernext import tiled_attn
 
 
@@ -85,8 +88,10 @@ class Processor(torch.nn.Module):
     self._bf16_cache[id(p)] = (p._version, p.data_ptr(), w)
     return w
 
-  def _attend(self, q, k, v, tiles, scale):
-    return tiled_attn.attention(q, k, v, tiles, scale=scale)
+  def _mha(self, h, w_qkv, w_out, tiles):
+    """The attention block: patch.tiled_mha over the fused projection (h [B, n, d] in the compute dtype)."""
+    cfg = self.cfg
+    return patch.tiled_mha(h, w_qkv, w_out, tiles, cfg.heads, cfg.head_dim)
 
   @staticmethod
   def _cond_norm(x, cond, w):
@@ -101,43 +106,50 @@ class Processor(torch.nn.Module):
     """x [B, n, d_model] (float32 residual stream), cond [B, cond_dim] -> [B, n, d_model]. `perm` (int, [n],
     a permutation of the nodes; optional): `tiles` is built in the permuted order, node i of the blocks is node
     perm[i] of x, and the output is returned in x's order."""
+    b, n, d = x.shape
+    if cond.dim() != 2 or cond.shape[0] not in (1, b):
+      raise ValueError(f"cond has shape {tuple(cond.shape)}, expected ({b}, cond_dim) or (1, cond_dim)")
     if perm is not None:
       perm = torch.as_tensor(perm, device=x.device).to(torch.int64)
-      if perm.shape != (x.shape[1],):
-        raise ValueError(f"perm has shape {tuple(perm.shape)}, expected ({x.shape[1]},)")
-    if not torch.is_grad_enabled() and dtype == torch.bfloat16 and x.shape[-1] in (128, 256, 512, 1024):
-      return self._forward_fused(x, cond, tiles, perm)
-    cfg = self.cfg
-    b, n, d = x.shape
-    scale = cfg.head_dim ** -0.5
+      if perm.shape != (n,):
+        raise ValueError(f"perm has shape {tuple(perm.shape)}, expected ({n},)")
+      if n and (int(perm.min()) < 0 or int(perm.max()) >= n or
+                not bool((torch.bincount(perm, minlength=n) == 1).all())):
+        raise ValueError("perm is not a permutation of the nodes")
+    fused_ok = x.dtype == torch.float32 and d in (128, 256, 512, 1024)
+    if not torch.is_grad_enabled() and dtype == torch.bfloat16 and fused_ok:
+      return self._forward_fused(x, cond.expand(b, -1), tiles, perm)
     c = cond.to(dtype)
     if perm is not None:
       x = x.index_select(1, perm)
+    remat = patch.OPTIONS.remat and torch.is_grad_enabled()
     for blk in self.blocks:
-      h = self._cond_norm(x, c, blk.cond1).to(dtype)
-      qkv = (h @ blk.w_qkv.to(dtype)).view(b, n, cfg.heads, 3, cfg.head_dim)
-      q, k, v = qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2]
-      o = self._attend(q, k, v, tiles, scale)
-      x = x + (o.reshape(b, n, cfg.heads * cfg.head_dim) @ blk.w_out.to(dtype)).to(x.dtype)
-      h = self._cond_norm(x, c, blk.cond2).to(dtype)
-      m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype), approximate="tanh")
-      x = x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
+      if remat:
+        x = torch.utils.checkpoint.checkpoint(self._block, x, c, blk, tiles, dtype, use_reentrant=False)
+      else:
+        x = self._block(x, c, blk, tiles, dtype)
     y = self._cond_norm(x, c, self.cond_final).to(x.dtype)
     if perm is not None:
       y = y.index_select(1, torch.argsort(perm))
     return y
 
+  def _block(self, x, c, blk, tiles, dtype):
+    """One pre-LN block (patch.py:238-252): attention then MLP, each on a conditioned norm, residual adds."""
+    h = self._cond_norm(x, c, blk.cond1).to(dtype)
+    x = x + self._mha(h, blk.w_qkv.to(dtype), blk.w_out.to(dtype), tiles).to(x.dtype)
+    h = self._cond_norm(x, c, blk.cond2).to(dtype)
+    m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype), approximate="tanh")
+    return x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
+
   def _forward_fused(self, x, cond, tiles, perm=None):
     """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm
     (fwn_cond_layernorm), bias and GELU in the GEMM epilogue (cuBLASLt), and the residual stream updated in
-    place (float32 += bf16 in one pass)."""
-    cfg = self.cfg
+    place (float32 += bf16 in one pass). x float32 [B, n, d]; cond [B, cond_dim]; perm checked by forward."""
     b, n, d = x.shape
     m_rows = b * n
     lib = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     bf = torch.bfloat16
-    scale = cfg.head_dim ** -0.5
     # The residual stream: a copy of x, gathered into the blocks' node order when permuted.
     xs = x.index_select(1, perm).contiguous() if perm is not None else x.contiguous().clone()
     x2 = xs.view(m_rows, d)
@@ -151,9 +163,7 @@ class Processor(torch.nn.Module):
 
     for blk in self.blocks:
       norm(blk.cond1, h, _lib.DTYPE_BF16)
-      qkv = (h @ self._bf16(blk.w_qkv)).view(b, n, cfg.heads, 3, cfg.head_dim)
-      o = self._attend(qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2], tiles, scale)
-      x2.add_(o.reshape(m_rows, cfg.heads * cfg.head_dim) @ self._bf16(blk.w_out))
+      x2.add_(self._mha(h.view(b, n, d), self._bf16(blk.w_qkv), self._bf16(blk.w_out), tiles).view(m_rows, d))
       norm(blk.cond2, h, _lib.DTYPE_BF16)
       mlp = torch._addmm_activation(self._bf16(blk.b1), h, self._bf16(blk.w1), use_gelu=True)
       x2.add_(torch.addmm(self._bf16(blk.b2), mlp, self._bf16(blk.w2)))

@@ -16,12 +16,22 @@ Device-side building blocks (torch tensors on the current CUDA device):
   AttentionTiles.from_mask(mask) / .from_lists(...)       -> forward + transposed paired lists, cached
   attention_forward(q, k, v, tiles, scale, mode, with_lse) / attention_backward(...)
 
-Precision: bf16 tensors run in bf16; float32 tensors run in TF32 (the reference's default precision,
-pallas_attn.py:342) or, with precision="highest" / strict_fp32=True, in 3xTF32 (pallas_attn.py:338-340).
+Precision (pallas_attn.py:336-342): bf16 tensors run in bf16. float32 tensors follow the matmul precision in
+force — `precision=` of the call, else the innermost `default_matmul_precision(...)` block, the analogue of
+`jax.default_matmul_precision`: "highest" / "float32" run 3xTF32 (the reference's TF32_TF32_F32_X3), anything
+else TF32 (TF32_TF32_F32, the reference's default). `strict_fp32=True` matters only under "highest", where the
+reference switches to IEEE float32 dots (F32_F32_F32); those have no tensor-core form and are not built here,
+so that combination raises NotImplementedError instead of silently running 3xTF32.
+
+Head sizes: the kernels are built for head_dim 64 and 128; other sizes up to 128 are zero-padded to the next
+of the two inside the op (padded q / k columns add 0 to every logit, padded v columns give 0 outputs that are
+sliced off), which costs one copy of q, k, v.
 """
 
+import contextlib
 import ctypes
 import dataclasses
+import threading
 from typing import Optional
 
 import numpy as np
@@ -132,10 +142,7 @@ def build_tiles_device(indptr: torch.Tensor, indices: torch.Tensor, n_rows: int,
   return TileList64(ptr, kb, bits.view(n_tiles, block_q), n_rows, n_cols)
 
 
-def khop_csr_device(adj, hops: int, device=None):
-  """Device CSR (int32 indptr [n+1], indices [nnz], ascending) of every node within `hops` edges of each
-  node, self included: the pattern of (adj + I) ** hops, built on the GPU (bitset k-hop kernels). Stands in
-  for the host `adj_mat ** attention_k_hop` of the reference (patch.py:209)."""
+def _bitset_csr_device(adj, steps: int, device, include_self: bool):
   lib = _lib.lib()
   dev = _device(device)
   a = sparse.csr_matrix(adj).astype(bool)
@@ -147,8 +154,8 @@ def khop_csr_device(adj, hops: int, device=None):
   reach = torch.empty(n * words, dtype=torch.int32, device=dev)
   scratch = torch.empty(n * words, dtype=torch.int32, device=dev)
   s = _stream()
-  _lib.check(lib.fwn_khop_bitset(ip.data_ptr(), ix.data_ptr() if ix.numel() else 0, n, hops, reach.data_ptr(),
-                                 scratch.data_ptr(), s))
+  fn = lib.fwn_khop_bitset if include_self else lib.fwn_walk_bitset
+  _lib.check(fn(ip.data_ptr(), ix.data_ptr() if ix.numel() else 0, n, steps, reach.data_ptr(), scratch.data_ptr(), s))
   del scratch
   indptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
   ws = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
@@ -157,6 +164,18 @@ def khop_csr_device(adj, hops: int, device=None):
   indices = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)[:nnz]
   _lib.check(lib.fwn_bitset_csr_fill(reach.data_ptr(), n, n, indptr.data_ptr(), indices.data_ptr(), s))
   return indptr, indices
+
+
+def khop_csr_device(adj, hops: int, device=None):
+  """Device CSR (int32 indptr [n+1], indices [nnz], ascending) of every node within `hops` edges of each
+  node, self included: the pattern of (adj + I) ** hops, built on the GPU (bitset k-hop kernels)."""
+  return _bitset_csr_device(adj, hops, device, True)
+
+
+def power_csr_device(adj, power: int, device=None):
+  """Device CSR of the nonzero pattern of adj ** power (walks of exactly `power` edges; self edges only where
+  adj has them): the reference's `adj_mat ** attention_k_hop` (patch.py:209), built on the GPU."""
+  return _bitset_csr_device(adj, power, device, False)
 
 
 def pair_tiles(t: TileList64) -> TileList128:
@@ -217,6 +236,22 @@ def build_tile_mask(mask, block_q: int = BLOCK_Q, block_k: int = BLOCK_K, device
   return build_tiles_device(indptr, indices, n_rows, n_cols, block_q).numpy()
 
 
+def _check_lists(tile_ptr, tile_kb, tile_bits, n, what):
+  """Shape checks of a reference-format triple for an n-node mask (what pallas_attn.py:317-354 relies on:
+  ceil(n / 64) query blocks, key blocks below ceil(n / 32), one 64-word row set per tile)."""
+  ptr, kb, bits = (np.asarray(x) for x in (tile_ptr, tile_kb, tile_bits))
+  nqb = -(-n // BLOCK_Q)
+  if ptr.ndim != 1 or ptr.size != nqb + 1:
+    raise ValueError(f"{what}: tile_ptr has {ptr.size} entries, expected ceil({n} / 64) + 1 = {nqb + 1}")
+  t = int(ptr[-1]) if ptr.size else 0
+  if ptr[0] != 0 or np.any(np.diff(ptr.astype(np.int64)) < 0) or kb.size != t:
+    raise ValueError(f"{what}: tile_ptr is not a CSR pointer over {kb.size} tiles")
+  if bits.size != t * BLOCK_Q:
+    raise ValueError(f"{what}: tile_bits has {bits.size} words, expected {t} x 64")
+  if t and (kb.min() < 0 or kb.max() >= -(-n // BLOCK_K)):
+    raise ValueError(f"{what}: key blocks outside [0, ceil({n} / 32))")
+
+
 def _tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n_cols, device) -> TileList64:
   ptr = torch.as_tensor(np.asarray(tile_ptr, np.int32), device=device)
   kb = torch.as_tensor(np.asarray(tile_kb, np.int32), device=device)
@@ -275,10 +310,50 @@ class AttentionTiles:
     return cls(fwd, fwd, n, True, gather)
 
   @classmethod
+  def from_adjacency(cls, adj, k_hop: int, latlon=None, reorder: bool = True, device=None,
+                     gather: bool = True):
+    """(tiles, perm) for the attention mask adj ** k_hop, the sequence of the reference's _transformer_init
+    (patch.py:207-219) on the device:
+
+      mask = adj ** k_hop                                   the matrix-power pattern (fwn_walk_bitset)
+      perm = hilbert_order(lat, lon) if reorder and latlon  node order (None: the given order)
+      mask = mask[perm][:, perm]                            (the power of the permuted adjacency: same pattern)
+      lists of mask; lists of mask.T if adj is not symmetric
+
+    latlon: (lat_deg, lon_deg) of the nodes, or None to take them from adj._fwn_latlon (the attribute the
+    reference's patched _get_adjacency_matrix sets, patch.py:296-302) when present. perm: int64 [n] or None;
+    node i of the permuted order is node perm[i] of adj (pass it to Processor.forward(..., perm=perm))."""
+    dev = _device(device)
+    if latlon is None:
+      latlon = getattr(adj, "_fwn_latlon", None)
+    a = sparse.csr_matrix(adj).astype(bool)
+    a.eliminate_zeros()
+    n = a.shape[0]
+    assert a.shape == (n, n), "adjacency must be square"
+    perm = None
+    if reorder and latlon is not None:
+      lat, lon = (np.asarray(x, np.float64).ravel() for x in latlon)
+      if lat.size != n or lon.size != n:
+        raise ValueError(f"latlon has {lat.size} / {lon.size} points for {n} nodes")
+      perm = np.asarray(hilbert_order(lat, lon), np.int64)
+      a = a[perm][:, perm].tocsr()
+    symmetric = (a != a.T).nnz == 0
+    indptr, indices = power_csr_device(a, k_hop, dev)
+    fwd = pair_tiles(build_tiles_device(indptr, indices, n, n))
+    if symmetric:
+      return cls(fwd, fwd, n, True, gather), perm
+    ip_t, ix_t = power_csr_device(a.T.tocsr(), k_hop, dev)
+    bwd = pair_tiles(build_tiles_device(ip_t, ix_t, n, n))
+    return cls(fwd, bwd, n, False, gather), perm
+
+  @classmethod
   def from_lists(cls, tile_ptr, tile_kb, tile_bits, n: int, tiles_t=None, device=None,
                  gather: bool = True) -> "AttentionTiles":
     """From the reference's (tile_ptr, tile_kb, tile_bits) arrays (and optionally the transposed triple)."""
     dev = _device(device)
+    _check_lists(tile_ptr, tile_kb, tile_bits, n, "tiles")
+    if tiles_t is not None:
+      _check_lists(*tiles_t, n, "tiles_t")
     fwd = pair_tiles(_tiles64_from_arrays(tile_ptr, tile_kb, tile_bits, n, dev))
     if tiles_t is None:
       return cls(fwd, fwd, n, True, gather)
@@ -286,12 +361,49 @@ class AttentionTiles:
     return cls(fwd, bwd, n, False, gather)
 
 
+_PRECISION = threading.local()
+_HIGHEST = ("highest", "float32")
+_PRECISION_NAMES = ("default", "high", "highest", "bfloat16", "tensorfloat32", "float32", "bfloat16_3x",
+                    "fastest")
+
+
+@contextlib.contextmanager
+def default_matmul_precision(name: Optional[str]):
+  """with default_matmul_precision("highest"): ...  — the matmul precision of float32 attention calls in the
+  block that pass no `precision=` (jax.default_matmul_precision's role for the reference, pallas_attn.py:336).
+  Thread-local; blocks nest."""
+  if name is not None and name not in _PRECISION_NAMES:
+    raise ValueError(f"unknown matmul precision {name!r}")
+  stack = getattr(_PRECISION, "stack", None)
+  if stack is None:
+    stack = _PRECISION.stack = []
+  stack.append(name)
+  try:
+    yield
+  finally:
+    stack.pop()
+
+
+def current_matmul_precision() -> Optional[str]:
+  stack = getattr(_PRECISION, "stack", None)
+  return stack[-1] if stack else None
+
+
 def _mode_for(dtype: torch.dtype, precision: Optional[str], strict_fp32: bool) -> int:
+  """Kernel mode for q's dtype and the precision in force (pallas_attn.py:336-342)."""
   if dtype == torch.bfloat16:
     return _lib.MODE_BF16
   if dtype != torch.float32:
     raise TypeError(f"q/k/v must be bfloat16 or float32, got {dtype}")
-  if strict_fp32 or precision in ("highest", "float32"):
+  if precision is None:
+    precision = current_matmul_precision()
+  if precision is not None and precision not in _PRECISION_NAMES:
+    raise ValueError(f"unknown matmul precision {precision!r}")
+  if precision in _HIGHEST:
+    if strict_fp32:
+      raise NotImplementedError(
+          "strict_fp32 under 'highest' asks for IEEE float32 dots (the reference's F32_F32_F32), which have no "
+          "tensor-core form and are not built; 'highest' without strict_fp32 runs 3xTF32 (rel RMS <= 2e-5)")
     return _lib.MODE_TF32X3
   return _lib.MODE_TF32
 
@@ -397,14 +509,52 @@ class _TiledAttention(torch.autograd.Function):
     return dq, dk, dv, None, None, None
 
 
+_BUILT_HEAD_DIMS = (64, 128)
+
+
 def attention(q, k, v, tiles: AttentionTiles, *, scale: float, precision: Optional[str] = None,
               strict_fp32: bool = False):
   """Differentiable masked attention over prepared tiles: q, k, v [B, n, H, D] -> [B, n, H, D]."""
   mode = _mode_for(q.dtype, precision, strict_fp32)
-  return _TiledAttention.apply(q, k, v, tiles, float(scale), mode)
+  d = q.shape[-1]
+  if d in _BUILT_HEAD_DIMS:
+    return _TiledAttention.apply(q, k, v, tiles, float(scale), mode)
+  if d > _BUILT_HEAD_DIMS[-1] or d < 1:
+    raise NotImplementedError(f"head_dim {d} not built (64 or 128; smaller sizes are zero-padded)")
+  pad = next(x for x in _BUILT_HEAD_DIMS if x > d) - d
+  qp, kp, vp = (torch.nn.functional.pad(x, (0, pad)) for x in (q, k, v))
+  return _TiledAttention.apply(qp, kp, vp, tiles, float(scale), mode)[..., :d]
 
 
-_TILE_CACHE = {}
+class _TileCache:
+  """AttentionTiles of the last reference-format lists passed to tiled_flash_attention.
+
+  The entry holds the argument objects themselves, so none of them can be freed and its id reused while the
+  entry lives, and it is used only when every list argument is the same object as before (and n and the
+  device match): rebuilt lists, or lists passed as new arrays, are converted again. As with the reference,
+  whose lists become constants when the model is traced (patch.py:266), a list edited in place after its first
+  use is not seen; pass new arrays instead."""
+
+  def __init__(self):
+    self._args = None
+    self._tiles = None
+
+  def get(self, args, n, device):
+    hit = (self._args is not None and len(self._args) == len(args) and
+           all(a is b for a, b in zip(self._args, args)))
+    if hit and self._tiles.n == n and self._tiles.fwd.ptr.device == device:
+      return self._tiles
+    ptr, kb, bits = (_np(x) for x in args[:3])
+    tiles_t = tuple(_np(x) for x in args[3:6]) if len(args) > 3 else None
+    tiles = AttentionTiles.from_lists(ptr, kb, bits, n, tiles_t=tiles_t, device=device)
+    self._args, self._tiles = tuple(args), tiles
+    return tiles
+
+  def clear(self):
+    self._args = self._tiles = None
+
+
+_TILE_CACHE = _TileCache()
 
 
 def tiled_flash_attention(q, k, v, tile_ptr, tile_kb, tile_bits, *, scale, strict_fp32=False, tiles_t=None,
@@ -415,26 +565,24 @@ def tiled_flash_attention(q, k, v, tile_ptr, tile_kb, tile_bits, *, scale, stric
   tile lists are the reference's (build_tile_mask) 64-row lists, NumPy or torch; tiles_t is the
   transposed mask's list (None: the mask is symmetric). The Triton launch knobs (num_warps,
   num_stages, bwd_num_warps, bwd_split) have no meaning here and are accepted for compatibility;
-  `interpret` (Pallas interpret mode) is refused: there is no CPU path.
+  `interpret` (Pallas interpret mode) is refused: there is no CPU path. Precision: `precision=`, else the
+  enclosing default_matmul_precision block, else TF32 for float32 inputs (see the module docstring).
   """
   if interpret:
     raise NotImplementedError("interpret mode: this implementation has no CPU path")
   if block_q != BLOCK_Q or block_k != BLOCK_K:
     raise ValueError("the tile lists use 64-row query blocks and 32-key tiles")
+  if tiles_t is not None and len(tiles_t) != 3:
+    raise ValueError("tiles_t is the transposed mask's (tile_ptr, tile_kb, tile_bits)")
   n = q.shape[1]
-  key = tuple(id(x) for x in (tile_ptr, tile_kb, tile_bits)) + ((tuple(id(x) for x in tiles_t),) if tiles_t else ())
-  hit = _TILE_CACHE.get(key)
-  if hit is None or hit[0] is not tile_ptr:
-    tiles = AttentionTiles.from_lists(_np(tile_ptr), _np(tile_kb), _np(tile_bits), n,
-                                      tiles_t=tuple(_np(x) for x in tiles_t) if tiles_t else None, device=q.device)
-    _TILE_CACHE.clear()
-    _TILE_CACHE[key] = (tile_ptr, tiles)
-  else:
-    tiles = hit[1]
+  args = (tile_ptr, tile_kb, tile_bits) + (tuple(tiles_t) if tiles_t is not None else ())
+  tiles = _TILE_CACHE.get(args, n, q.device)
   return attention(q, k, v, tiles, scale=scale, precision=precision, strict_fp32=strict_fp32)
 
 
 def _np(x):
+  """NumPy view of a tile-list array. Tile bits are uint32 in the reference; an int32 array of rank 2 (the
+  same bits in signed storage, as torch holds them) is reinterpreted, every other array is taken as is."""
   if isinstance(x, torch.Tensor):
     x = x.detach().cpu().numpy()
   x = np.asarray(x)

@@ -160,6 +160,14 @@ FWN_API int32_t fwn_bitset_words(int32_t n_cols);
 FWN_API fwn_status fwn_khop_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t hops,
                                    uint32_t* reach, uint32_t* scratch, void* stream);
 
+/* Matrix-power pattern: reach row i = the end nodes of the walks of exactly `length` edges of adj from node i,
+ * the nonzero pattern of adj ** length for any adjacency (self edges count only where adj has them; length 0
+ * gives the identity). This is `adj_mat ** attention_k_hop` of the reference's _transformer_init
+ * (src/faster_weathernext/patch.py:209) exactly; for an adjacency with every self edge it equals
+ * fwn_khop_bitset. Same arguments and limits as fwn_khop_bitset. */
+FWN_API fwn_status fwn_walk_bitset(const int32_t* indptr, const int32_t* indices, int32_t n, int32_t length,
+                                   uint32_t* reach, uint32_t* scratch, void* stream);
+
 /* CSR of a bitset matrix [n_rows, fwn_bitset_words(n_cols)] (columns >= n_cols ignored), in two passes as
  * the tile builder: pass 1 writes indptr[n_rows + 1] (ws: n_rows int32; nnz = indptr[n_rows]); pass 2
  * writes indices[nnz], ascending per row. n_rows * n_cols must be below 2^31. The result feeds
@@ -228,7 +236,9 @@ FWN_API fwn_status fwn_attn_bwd_dkv(const fwn_attn_desc* desc, const void* q, co
  *   - Capacity: batch * heads * fwn_lse_rows(n) <= FWN_NOALLOC_DELTA_ROWS (4 MiB of float32); larger
  *     problems are rejected with FWN_ERR_WORKSPACE.
  *   - The first call on each device looks up the array's device address (with that device current);
- *     make that first call before any stream capture.
+ *     make that first call before any stream capture. The address is kept for the life of the process: after
+ *     cudaDeviceReset on a device (which unloads the library's device code; a later call may find it loaded
+ *     at another address) this entry point must not be called again on that device.
  *   - The array is shared by every call on a device and keeps the last call's contents; each call
  *     rewrites all of the rows it reads. Calls that overlap on the GPU (different streams, no ordering)
  *     race on it: order them, or use fwn_attn_bwd with separate workspaces.
@@ -238,6 +248,18 @@ FWN_API fwn_status fwn_attn_bwd_noalloc(const fwn_attn_desc* desc, const void* q
                                         const void* o, const float* lse, const void* d_o,
                                         const fwn_tile_list* tiles, const fwn_tile_list* tiles_t, void* dq,
                                         void* dk, void* dv, void* stream);
+
+/* ---- failure detection test -----------------------------------------------------------------------------
+ * No counterpart in the reference. fwn_attn_fwd with one input copy left out on purpose, so that a bounded
+ * device-side wait expires: the producer of CTA 0 does not issue the first K / V load of its first work item,
+ * the MMA warp's wait on it gives up after wait_limit_ns (1e5 .. 2e9 ns; every other wait of the launch has
+ * the same bound), the CTA's other roles leave at their next wait, the producer waits for the copies it did
+ * issue, the CTA frees its tensor memory and returns, and the device error word reads
+ * FWN_ERR_DEVICE_TIMEOUT (fwn_device_error). No copy, MMA or tensor-memory allocation is left behind, so the
+ * context stays usable; o / lse are incomplete. Only the narrow bf16 head_dim-64 forward (sparse lists). */
+FWN_API fwn_status fwn_test_attn_fwd_timeout(const fwn_attn_desc* desc, const void* q, const void* k, const void* v,
+                                             const fwn_tile_list* tiles, void* o, float* lse, uint64_t wait_limit_ns,
+                                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,8 @@ Tensors use the reference's public layout [batch, n, heads, head_dim]; the mask 
   sparse_attention_vjp — dQ, dK, dV of the masked softmax: dS = P * (dP - rowsum(dP * P))
                          (tests/test_pallas_kernel.py:58-69), float64.
   dense_attention(_vjp)— the float64 dense references of tests/test_pallas_kernel.py:15-21, 58-69.
+  sampled_attention    — the same float64 forward and gradients on sampled query rows (out, lse, dq) and
+                         key rows (dk, dv) of a large problem, computed block-wise with dense BLAS.
   rel_rms              — RMS(x - ref) / std(ref) (scripts/attn_bench.py:122).
 """
 
@@ -209,6 +211,68 @@ def sparse_attention_vjp(q, k, v, do, mask, scale, max_pairs=1 << 21):
         dk[bi, :, hi] += (dsm.T @ qq[r0:r1]) * scale
         dv[bi, :, hi] += pm.T @ gg[r0:r1]
   return dq, dk, dv
+
+
+def sampled_attention(q, k, v, do, mask, scale, q_rows, k_rows, block=128):
+  """float64 out, lse, dq at query rows `q_rows` and dk, dv at key rows `k_rows` of one batch element.
+
+  q, k, v, do: [n, H, D]; mask: [n, n] CSR (mask[query, key]). The math is sparse_attention /
+  sparse_attention_vjp's (P = softmax of the allowed logits, dS = P (dP - rowsum(P dP)), dQ = scale dS K,
+  dK = scale dS^T Q, dV = P^T dO), evaluated only where needed: every query row that attends to a sampled key
+  gets its full row statistics, so the sampled dk / dv are exact sums over all their queries. Rows are taken
+  in groups of `block` (ascending), each against the dense union of its keys.
+  Returns dict(out [Rq, H, D], lse [H, Rq], dq [Rq, H, D], dk [Rk, H, D], dv [Rk, H, D]) in the order given."""
+  m = sparse.csr_matrix(mask).astype(bool).tocsr()
+  m.sum_duplicates()
+  m.sort_indices()
+  n, h, d = q.shape
+  q_rows = np.asarray(q_rows, np.int64)
+  k_rows = np.asarray(k_rows, np.int64)
+  mt = m.T.tocsr()
+  users = np.unique(mt[k_rows].indices) if len(k_rows) else np.zeros(0, np.int64)
+  rows = np.union1d(q_rows, users)
+  k_slot = np.full(n, -1, np.int64)
+  k_slot[k_rows] = np.arange(len(k_rows))
+  q_slot = np.full(n, -1, np.int64)
+  q_slot[q_rows] = np.arange(len(q_rows))
+  f = lambda x: np.asarray(x, np.float64)
+  out = np.zeros((len(q_rows), h, d))
+  lse = np.zeros((h, len(q_rows)))
+  dq = np.zeros((len(q_rows), h, d))
+  dk = np.zeros((len(k_rows), h, d))
+  dv = np.zeros((len(k_rows), h, d))
+  for c0 in range(0, len(rows), block):
+    rc = rows[c0:c0 + block]
+    sub = m[rc]
+    keys = np.unique(sub.indices)
+    if keys.size == 0:
+      continue
+    pos = np.searchsorted(keys, sub.indices)
+    allowed = np.zeros((len(rc), len(keys)), bool)
+    allowed[np.repeat(np.arange(len(rc)), np.diff(sub.indptr)), pos] = True
+    qh, gh = f(q[rc]).transpose(1, 0, 2), f(do[rc]).transpose(1, 0, 2)             # [H, r, D]
+    kh, vh = f(k[keys]).transpose(1, 0, 2), f(v[keys]).transpose(1, 0, 2)           # [H, c, D]
+    s = np.where(allowed[None], np.matmul(qh, kh.transpose(0, 2, 1)) * scale, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    mx = np.where(np.isfinite(mx), mx, 0.0)
+    p = np.exp(s - mx)
+    l = p.sum(-1, keepdims=True)
+    p = p / np.maximum(l, 1e-300)
+    o = np.matmul(p, vh)
+    dp = np.matmul(gh, vh.transpose(0, 2, 1))
+    ds = p * (dp - (p * dp).sum(-1, keepdims=True))
+    sel = q_slot[rc] >= 0
+    if sel.any():
+      dst = q_slot[rc][sel]
+      out[dst] = o[:, sel].transpose(1, 0, 2)
+      lse[:, dst] = (mx + np.log(np.maximum(l, 1e-300)))[:, sel, 0]
+      dq[dst] = (np.matmul(ds[:, sel], kh) * scale).transpose(1, 0, 2)
+    kc = k_slot[keys] >= 0
+    if kc.any():
+      dst = k_slot[keys][kc]
+      dk[dst] += (np.matmul(ds[:, :, kc].transpose(0, 2, 1), qh) * scale).transpose(1, 0, 2)
+      dv[dst] += np.matmul(p[:, :, kc].transpose(0, 2, 1), gh).transpose(1, 0, 2)
+  return {"out": out, "lse": lse, "dq": dq, "dk": dk, "dv": dv}
 
 
 def dense_attention(q, k, v, mask, scale):

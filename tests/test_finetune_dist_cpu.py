@@ -1,11 +1,16 @@
-"""CPU: the data-parallel fine-tune step on 2 gloo ranks equals the single-process step.
+"""CPU: the data-parallel fine-tune step on 2 gloo ranks equals the single-process step; rank failures are
+detected on the host.
 
 The product step (faster_weathernext.finetune.DataParallelStep) is generic over the model; here it runs a
 small test-only model on the CPU (no attention kernel involved) to check the distributed logic: member
-split, gradient accumulation, the flat-bucket all-reduce and identical Adam updates on every rank.
+split, gradient accumulation, the bucketed all-reduce issued from gradient hooks during the backward (and the
+one-buffer all-reduce after it), identical Adam updates on every rank, and the RankWatchdog: a rank that
+leaves between steps, or dies without a word, makes the others raise instead of waiting in a collective.
 """
+import datetime
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -32,17 +37,17 @@ def _data(members):
   return xs, cs, ts
 
 
-def _worker(rank, world, port, members, out):
+def _worker(rank, world, port, members, out, overlap, bucket_mb):
   os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
   dist.init_process_group("gloo", rank=rank, world_size=world)
   from faster_weathernext.finetune import DataParallelStep
   model = TinyModel()
-  step = DataParallelStep(model, members, lr=1e-2)
+  step = DataParallelStep(model, members, lr=1e-2, overlap=overlap, bucket_mb=bucket_mb)
   xs, cs, ts = _data(members)
   idx = list(step.my_members())
   for _ in range(2):
-    loss = step.step([xs[i] for i in idx], [cs[i] for i in idx], [ts[i] for i in idx])
-  out[rank] = (torch.cat([p.detach().reshape(-1) for p in model.parameters()]), float(loss))
+    loss = step.step([xs[i] for i in idx], [cs[i] for i in idx], [ts[i] for i in idx], micro_batch=1)
+  out[rank] = (torch.cat([p.detach().reshape(-1) for p in model.parameters()]), float(loss), len(step.buckets))
   dist.destroy_process_group()
 
 
@@ -53,7 +58,10 @@ def _free_port():
 
 
 @pytest.mark.timeout(120)
-def test_two_rank_step_matches_single_process():
+@pytest.mark.parametrize("overlap,bucket_mb", [(True, 1e-4), (True, 25.0), (False, 25.0)])
+def test_two_rank_step_matches_single_process(overlap, bucket_mb):
+  """Two ranks (two members each, one per micro-batch) equal one process with all four members: buckets
+  of one parameter each issued from the backward's hooks, one bucket, or one all-reduce after the backward."""
   from faster_weathernext.finetune import DataParallelStep
   members = 4
   model = TinyModel()
@@ -64,11 +72,64 @@ def test_two_rank_step_matches_single_process():
   ref = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
   with mp.Manager() as m:
     out = m.dict()
-    mp.start_processes(_worker, args=(2, _free_port(), members, out), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), members, out, overlap, bucket_mb), nprocs=2, join=True,
+                       start_method="spawn")
     for r in range(2):
-      params, loss = out[r]
+      params, loss, n_buckets = out[r]
       torch.testing.assert_close(params, ref, rtol=1e-5, atol=1e-6)
       assert abs(loss - float(loss1)) < 1e-5
+      assert n_buckets == (2 if bucket_mb < 1 else 1)
+
+
+def _failing_worker(rank, world, port, how, out):
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+  from torch.distributed import distributed_c10d as c10d
+  from faster_weathernext.finetune import DataParallelStep, RankFailure, RankWatchdog, abort_group
+  store = c10d._get_default_store()
+  dog = RankWatchdog(store, rank, world, interval=0.1, timeout=1.0).start()
+  model = TinyModel()
+  step = DataParallelStep(model, 4, lr=1e-2, watchdog=dog, bucket_mb=1e-4)
+  xs, cs, ts = _data(4)
+  idx = list(step.my_members())
+  args = ([xs[i] for i in idx], [cs[i] for i in idx], [ts[i] for i in idx])
+  step.step(*args)
+  if rank == 1:
+    # Between steps, with nothing of this rank in flight: leave politely, or vanish.
+    if how == "leave":
+      dog.leave()
+    store.set("test/rank1_gone", "1")
+    os._exit(0)
+  store.wait(["test/rank1_gone"])
+  if how == "vanish":
+    time.sleep(1.5)                 # longer than the heartbeat timeout
+  t0 = time.monotonic()
+  try:
+    step.step(*args)
+    out[rank] = ("no error", time.monotonic() - t0)
+  except RankFailure as e:
+    out[rank] = ("RankFailure", time.monotonic() - t0, e.rank)
+  except RuntimeError as e:       # the collective itself failed (the peer's connection closed)
+    out[rank] = ("RuntimeError", time.monotonic() - t0)
+  dog.stop()
+  abort_group()
+
+
+@pytest.mark.timeout(120)
+@pytest.mark.parametrize("how", ["leave", "vanish"])
+def test_rank_failure_between_steps_raises_instead_of_hanging(how):
+  """A rank that leaves between steps is seen in the store before the next step's first launch (RankFailure
+  naming it, at once); one that exits without a word is seen by its stalled heartbeat, or at the latest by
+  the next collective failing, well inside the process group's 20 s timeout."""
+  with mp.Manager() as m:
+    out = m.dict()
+    mp.start_processes(_failing_worker, args=(2, _free_port(), how, out), nprocs=2, join=True,
+                       start_method="spawn")
+    res = out[0]
+  if how == "leave":
+    assert res[0] == "RankFailure" and res[2] == 1 and res[1] < 1.0, res
+  else:
+    assert res[0] in ("RankFailure", "RuntimeError") and res[1] < 10.0, res
 
 
 def test_batched_step_equals_member_loop():

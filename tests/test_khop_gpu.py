@@ -109,3 +109,30 @@ def test_khop_rejects_bad_arguments(cuda):
   with pytest.raises(NotImplementedError):
     _lib.check(lib.fwn_bitset_csr_count(0, 50000, 50000, 0, 0, 0, 0))
   assert lib.fwn_bitset_words(40962) == 1284 and lib.fwn_bitset_words(32) == 4
+
+
+@pytest.mark.parametrize("power", [0, 1, 2, 3, 7])
+def test_walk_pattern_matches_plain_matrix_power(cuda, power):
+  """fwn_walk_bitset: the pattern of adj ** power itself (the reference's `adj_mat ** attention_k_hop`) for a
+  directed graph with a few self edges, duplicate entries and isolated rows; and on a mesh without self edges,
+  where power 1 is the bare adjacency (no diagonal) and differs from the k-hop pattern."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  n = 777
+  a = sparse.random(n, n, density=0.004, random_state=31, format="coo")
+  a = sparse.coo_matrix((np.ones(a.nnz + 5), (np.r_[a.row, [3, 3, 9, 9, 40]], np.r_[a.col, [3, 3, 9, 500, 40]])),
+                        shape=(n, n)).tocsr()
+  xyz, faces = mesh.icosphere(3)
+  m = mesh.adjacency(faces, xyz.shape[0]).astype(np.float64)
+  m.setdiag(0)
+  m.eliminate_zeros()
+  for adj in (a, m):
+    ip, ix = ta.power_csr_device(adj, power, cuda)
+    got = sparse.csr_matrix((np.ones(ix.numel(), bool), ix.cpu().numpy(), ip.cpu().numpy()), shape=adj.shape)
+    plain = sparse.csr_matrix(adj, dtype=np.float64)
+    plain.data[:] = 1.0
+    want = sparse.identity(adj.shape[0], format="csr")
+    for _ in range(power):
+      want = (want @ plain).tocsr()
+      want.data[:] = 1.0
+    assert _equal(got, want.astype(bool))

@@ -18,11 +18,16 @@ def _dense_processor_class(mask_dense):
   from faster_weathernext.processor import Processor
 
   class DenseProcessor(Processor):
-    def _attend(self, q, k, v, tiles, scale):
-      qf, kf, vf = (x.float().permute(0, 2, 1, 3) for x in (q, k, v))        # [B, H, n, D]
-      s = (qf @ kf.transpose(-1, -2)) * scale
+    def _mha(self, h, w_qkv, w_out, tiles):
+      """patch.tiled_mha restated with a dense float32 masked softmax (patch.py:165-177)."""
+      cfg = self.cfg
+      b, n, _ = h.shape
+      qkv = (h @ w_qkv).view(b, n, cfg.heads, 3, cfg.head_dim)
+      qf, kf, vf = (qkv[:, :, :, i].float().permute(0, 2, 1, 3) for i in range(3))   # [B, H, n, D]
+      s = (qf @ kf.transpose(-1, -2)) * cfg.head_dim ** -0.5
       s = s.masked_fill(~mask_dense, float("-inf"))
-      return (torch.softmax(s, -1) @ vf).permute(0, 2, 1, 3).to(q.dtype)
+      o = (torch.softmax(s, -1) @ vf).permute(0, 2, 1, 3).to(h.dtype)
+      return o.reshape(b, n, -1) @ w_out
   return DenseProcessor
 
 
@@ -196,3 +201,61 @@ def test_processor_fused_weight_cache_follows_updates(cuda):
   y_ref = model(x, c, tiles)                                       # autograd path, no cache
   assert not torch.equal(y1, y0)
   assert _rel(y1, y_ref.detach()) < 1e-2
+
+
+def test_processor_input_checks(cuda):
+  """The fused inference path runs only on float32 residual streams (it reads and writes float32 rows); other
+  dtypes take the autograd-path blocks. A [1, cond_dim] conditioning vector broadcasts over the batch on both
+  paths; a cond batch that is neither 1 nor B, and a perm that is not a permutation, raise ValueError."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor, ProcessorConfig
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = ProcessorConfig(layers=1)
+  model = Processor(cfg, seed=9, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(9)
+  x = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  c1 = torch.randn(1, cfg.cond_dim, device=cuda, generator=g)
+  with torch.no_grad():
+    y_b = model(x, c1.expand(2, -1).contiguous(), tiles)
+    y_1 = model(x, c1, tiles)
+    assert torch.equal(y_1, y_b)
+    y_bf = model(x.to(torch.bfloat16), c1, tiles)              # not float32: no fused kernel on it
+    assert y_bf.dtype == torch.bfloat16 and _rel(y_bf.float(), y_b) < 2e-2
+    with pytest.raises(ValueError):
+      model(x, torch.randn(3, cfg.cond_dim, device=cuda), tiles)
+    bad = torch.arange(n, device=cuda)
+    bad[3] = 4
+    with pytest.raises(ValueError):
+      model(x, c1, tiles, perm=bad)
+    bad[3] = n
+    with pytest.raises(ValueError):
+      model(x, c1, tiles, perm=bad)
+
+
+def test_processor_remat_gives_the_same_gradients(cuda):
+  """patch.OPTIONS.remat recomputes each block in the backward (activation checkpointing); the gradients are the
+  stored-activation ones (same kernels on the same inputs; relative L2 difference <= 1e-6)."""
+  from faster_weathernext import mesh, patch
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = _small()
+  model = Processor(cfg, seed=2, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(3)
+  x = torch.randn(1, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(1, cfg.cond_dim, device=cuda, generator=g)
+  grads = []
+  for remat in (False, True):
+    patch.OPTIONS.remat = remat
+    try:
+      model.zero_grad(set_to_none=True)
+      model(x, c, tiles).square().mean().backward()
+    finally:
+      patch.OPTIONS.remat = False
+    grads.append(torch.cat([p.grad.reshape(-1) for p in model.parameters()]))
+  assert float((grads[1] - grads[0]).norm() / grads[0].norm()) <= 1e-6
