@@ -115,7 +115,10 @@ struct BwdCfg {
   // (bf16, two CTAs per SM) or 512 (tf32, one), at most 3 (bf16) or 4; 3xTF32 one.
   static constexpr int SD_W = 32 * CH;
   static constexpr int SD_STRIDE = 2 * SD_W;
-  static constexpr int TMEM_MAX = F32 ? 512 : 256;
+  // bf16 dQ at head_dim 64 (the sparse configurations) runs four CTAs per SM with 128 TMEM columns each (QUAD): the
+  // dQ accumulator and one S / dP buffer.
+  static constexpr bool QUAD = !F32 && D == 64 && KIND == kBwdDQ;
+  static constexpr int TMEM_MAX = F32 ? 512 : QUAD ? 128 : 256;
   static constexpr int NSD_FIT = (TMEM_MAX - R_COLS - ACC_COLS) / SD_STRIDE;
   static constexpr int NSD = !G_TMEM ? 1 : NSD_FIT < (F32 ? 4 : 3) ? NSD_FIT : (F32 ? 4 : 3);
   // dS / P buffers: the TMEM S / dP buffers (bf16); in shared memory one where two would not fit (3xTF32 except
@@ -130,7 +133,9 @@ struct BwdCfg {
     return NR_SMEM * XL * R_BYTES + ns * STAGE_BYTES + NB * NG * XL * G_BYTES + n_bar(ns) * 8 + 16 + SLACK;
   }
   // bf16 shares an SM between two CTAs; tf32 and 3xTF32 have one.
-  static constexpr int fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
+  static constexpr int fit(int ns) {
+    return smem_bytes(ns) <= (F32 ? 227 * 1024 : QUAD ? 227 * 1024 / 4 : 227 * 1024 / 2);
+  }
   // Column stages: as many as fit (at most 8), so that the copies of the next chunks are in flight during the
   // elementwise stage; 3xTF32 one or two.
   static constexpr int NS = fit(8) ? 8 : fit(6) ? 6 : fit(4) ? 4 : fit(3) ? 3 : fit(2) ? 2 : 1;
@@ -148,19 +153,22 @@ struct BwdCfg {
   static constexpr int ACC0 = G_TMEM ? SD0 + SD_STRIDE * NSD : 128;
   static constexpr int ACC1 = ACC0 + (ACC_DS ? D : 0);
   static constexpr int TMEM_NEED = ACC0 + ACC_COLS;
-  static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = QUAD ? 128 : TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;
-  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
+  static constexpr int MIN_BLOCKS = QUAD ? 4 : (2 * SMEM_BYTES <= 227 * 1024 && TMEM_COLS <= 256 && !X3) ? 2 : 1;
   static_assert(!(F32 && D == 128) || KIND != kBwdDKV, "tf32 head_dim 128: dV and dK run as separate passes");
   // Each SM sub-partition has 16,384 registers and takes a quarter of the resident warps (rounded up):
   // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
-  static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 255;
+  // Four CTAs (24 warps, six per sub-partition) leave 85: 80 in units of 8.
+  static constexpr int MAX_REGS = QUAD ? 80 : (MIN_BLOCKS == 2 || X3) ? 168 : 255;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(G64 || COLS * ES % 128 == 0, "dS rows must fill 64-byte or whole 128-byte column blocks");
   static_assert(!G64 || (!F32 && CH == 1), "64-byte dS rows hold 32 bf16 columns");
   static_assert(!X3 || F32, "3xTF32 takes float32 operands");
   static_assert(NC <= 4, "at most four column operands per stage (one producer lane octet each)");
-  static_assert(!G_TMEM || (NSD >= 2 && TMEM_NEED <= TMEM_MAX), "TMEM dS / P: two S / dP buffers and the accumulators");
+  static_assert(!G_TMEM || ((NSD >= 2 || QUAD) && TMEM_NEED <= TMEM_MAX),
+                "TMEM dS / P: two S / dP buffers (QUAD: one) and the accumulators");
+  static_assert(!QUAD || (NSD == 1 && TMEM_NEED <= 128 && MIN_BLOCKS * SMEM_BYTES <= 227 * 1024), "QUAD layout");
   static_assert(!(G_TMEM && X3) || (CH == 1 && NG == 1), "3xTF32 TMEM dS / P: one of dS / P, 32-wide tiles");
   static_assert(F32 || TMEM_NEED <= 256, "bf16: two CTAs per SM");
   static_assert(!R_TMEM || (G_TMEM && MIN_BLOCKS == 1), "TMEM row operands: one CTA per SM");
@@ -597,14 +605,15 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
           if (lane == 0) FWN_TR(12, c);
           return true;
         };
-        if constexpr (C::NS >= 2) {
+        if constexpr (C::NS >= 2 && C::NSD >= 2) {
           // S / dP of chunk c+1 go ahead of the accumulating MMAs of chunk c (two stages in flight).
           for (int c = 0; c <= nch && ok; ++c) {
             if (c < nch && !(ok = issue_sd(c))) break;
             if (c >= 1 && !(ok = issue_acc(c - 1))) break;
           }
         } else {
-          // One stage: the accumulating MMAs of chunk c free it before chunk c+1 can land.
+          // One stage, or one S / dP buffer (QUAD): the accumulating MMAs of chunk c free it before chunk c+1 can
+          // land; the other CTAs of the SM fill the tensor pipe meanwhile.
           for (int c = 0; c < nch && ok; ++c) {
             if (!(ok = issue_sd(c))) break;
             if (!(ok = issue_acc(c))) break;

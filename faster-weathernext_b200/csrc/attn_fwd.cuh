@@ -63,7 +63,10 @@ struct FwdCfg {
   // Tiles per chunk: one at head_dim 128 (bf16: keeps two CTAs per SM, so that one CTA's softmax overlaps the
   // other's MMAs; tf32: two tiles would leave room for two K/V stages instead of four, measured 11 % slower at the
   // WN2 shape) and in 3xTF32 (operand copies); else two.
-  static constexpr int CH = (X3 || D == 128) ? 1 : 2;
+  // bf16 head_dim 64 (the sparse configurations) runs four CTAs per SM with one 32-key tile per chunk and P written
+  // over S in TMEM (QUAD); the other bf16 / tf32 variants two CTAs or one.
+  static constexpr bool QUAD = !F32 && D == 64;
+  static constexpr int CH = (QUAD || X3 || D == 128) ? 1 : 2;
   static constexpr int KEYS = SUB * CH;       // keys per chunk
   static constexpr int KSTEP = F32 ? 8 : 16;  // K of one MMA instruction
   static constexpr int Q_BYTES = CB * ROWS * 128;
@@ -85,7 +88,7 @@ struct FwdCfg {
   // Bytes past the stages: P buffers, mbarriers (14 + 3 per stage), TMEM holder / abort word, 1 KB of slack to
   // align the dynamic shared memory base up to 1024 bytes.
   static constexpr int smem_bytes(int ns) { return OFF_STAGE + ns * STAGE_BYTES + 2 * PBUF_BYTES + (14 + 3 * ns) * 8 + 16 + 1024; }
-  static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : 227 * 1024 / 2); }
+  static constexpr bool fit(int ns) { return smem_bytes(ns) <= (F32 ? 227 * 1024 : QUAD ? 227 * 1024 / 4 : 227 * 1024 / 2); }
   // K/V stages: as many as fit (bf16: two CTAs per SM; tf32: one) up to 6, so that the copies of the next chunks
   // are in flight while the softmax works; 3xTF32 2.
   static constexpr int NS = fit(6) ? 6 : fit(5) ? 5 : fit(4) ? 4 : fit(3) ? 3 : 2;
@@ -93,25 +96,32 @@ struct FwdCfg {
   static constexpr int OFF_BAR = OFF_P + 2 * PBUF_BYTES;
   static constexpr int N_BAR = 2 + 2 * NS + 2 + 2 + 2 + 2 + 2 + 1 + 1 + NS;
   static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem holder / abort word + slack
-  static constexpr int O_COL = 128;
+  // TMEM: S buffers at 0 and S_STRIDE; O at O_COL. QUAD: two 32-column S buffers, P (packed bf16 pairs) written over
+  // the S it was computed from, O at 64: 128 columns, four CTAs per SM.
+  static constexpr bool P_OVER_S = QUAD;
+  static constexpr int S_STRIDE = QUAD ? 32 : 64;
+  static constexpr int O_COL = QUAD ? 64 : 128;
   // TMEM P buffers: KEYS / 2 columns (bf16 pairs) or KEYS (tf32). One 32-key tile per chunk: in the unused upper
   // half of each 64-column S buffer; two: after O (tf32 head_dim 64 then needs 512 columns, one CTA per SM).
   static constexpr int PW = F32 ? KEYS : KEYS / 2;
-  static constexpr int P_COL = CH == 1 ? 32 : O_COL + D;
-  static constexpr int P_STRIDE = CH == 1 ? 64 : PW;
+  static constexpr int P_COL = P_OVER_S ? 0 : CH == 1 ? 32 : O_COL + D;
+  static constexpr int P_STRIDE = P_OVER_S ? S_STRIDE : CH == 1 ? 64 : PW;
   static constexpr int Q_COL = CH == 1 ? O_COL + D : P_COL + 2 * PW;  // TMEM Q (tf32)
-  static constexpr int TMEM_COLS = Q_TMEM ? 512 : (CH == 1 || P_COL + 2 * PW <= 256) ? 256 : 512;
+  static constexpr int TMEM_COLS = QUAD ? 128 : Q_TMEM ? 512 : (CH == 1 || P_COL + 2 * PW <= 256) ? 256 : 512;
   static constexpr int THREADS = X3 ? 320 : 192;  // 3xTF32: + a warpgroup splitting tiles into hi / lo
-  static constexpr int MIN_BLOCKS = (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
+  static constexpr int MIN_BLOCKS = QUAD ? 4 : (2 * SMEM_BYTES <= 227 * 1024) ? 2 : 1;
   // Registers are allocated per warp in units of 256: 168 per thread is the most that lets two
   // 192-thread CTAs share an SM's 65,536.
   // Each SM sub-partition has 16,384 registers and takes a quarter of the resident warps (rounded up):
   // twelve warps (two CTAs) or ten (3xTF32) leave 168 per thread.
-  static constexpr int MAX_REGS = (MIN_BLOCKS == 2 || X3) ? 168 : 200;
+  // Four 192-thread CTAs (24 warps, six per sub-partition) leave 85: 80 in units of 8.
+  static constexpr int MAX_REGS = QUAD ? 80 : (MIN_BLOCKS == 2 || X3) ? 168 : 200;
   static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "1 KB alignment");
   static_assert(N_BAR == 14 + 3 * NS && SMEM_BYTES == smem_bytes(NS), "shared memory layout");
   static_assert(!P_TMEM || (P_COL + P_STRIDE + PW <= TMEM_COLS && (CH == 1 || P_COL >= O_COL + D)), "TMEM budget");
-  static_assert(TMEM_COLS == 256 || MIN_BLOCKS == 1, "512 TMEM columns: one CTA per SM");
+  static_assert(TMEM_COLS * MIN_BLOCKS <= 512, "TMEM columns of the CTAs of an SM");
+  static_assert(!QUAD || (O_COL >= 2 * S_STRIDE && O_COL + D <= TMEM_COLS && MIN_BLOCKS * SMEM_BYTES <= 227 * 1024),
+                "QUAD layout");
   static_assert(!Q_TMEM || Q_COL + D * (X3 ? 2 : 1) <= TMEM_COLS, "TMEM budget (Q)");
   static_assert(D % EPB == 0, "head_dim must fill whole 128-byte column blocks");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -348,7 +358,8 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           if (lane == 0) FWN_TR(15, c);
           if (!wait_(X3 ? kv_ready(st) : kv_full(st), (gg / C::NS) & 1)) return false;
           if (lane == 0) FWN_TR(16, c);
-          if (!wait_(s_empty(sb), ((gg >> 1) & 1) ^ 1)) return false;
+          // The S buffer is free once the softmax has read it, or (P over S) once P V of chunk gg-2 is complete.
+          if (!wait_(C::P_OVER_S ? p_empty(sb) : s_empty(sb), ((gg >> 1) & 1) ^ 1)) return false;
           if (lane == 0) FWN_TR(13, c);
           tc_fence_after();
           const uint32_t idesc_s = instr_desc(F32, 128, 32 * n_in, false, false);
@@ -364,9 +375,9 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
                 // A = Q in TMEM (3xTF32: its lo copy D columns on in the third pass): K = 8 tf32 elements = 8
                 // columns per MMA.
                 const uint32_t a_t = tmem + C::Q_COL + (pass == 2 ? D : 0) + 8 * kk;
-                issue_([&] { mma_ts<true>(tmem + sb * 64, a_t, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
+                issue_([&] { mma_ts<true>(tmem + sb * C::S_STRIDE, a_t, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
               } else {
-                issue_([&] { mma_ss<F32>(tmem + sb * 64, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
+                issue_([&] { mma_ss<F32>(tmem + sb * C::S_STRIDE, a, bd, idesc_s, (pass > 0 || kk > 0) ? 1u : 0u); });
               }
             }
           }
@@ -527,20 +538,24 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         const uint32_t gg = g0 + c;
         const int sb = gg & 1, st = gg % C::NS;
         const int n_in = min(C::CH, n_sub - C::CH * c);
-        float s[64];
+        float s[C::KEYS];
         if (!(ok = mbar_wait(s_full(sb), (gg >> 1) & 1, abort_flag, wlim))) break;
         if (lane == 0) FWN_TR(20, c);
         tc_fence_after();
-        tmem_ld32(trow + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
-        if (C::CH == 2 && n_in == 2) tmem_ld32(trow + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        tmem_ld32(trow + sb * C::S_STRIDE, *reinterpret_cast<float(*)[32]>(&s[0]));
+        if constexpr (C::CH == 2) {
+          if (n_in == 2) tmem_ld32(trow + sb * C::S_STRIDE + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        }
         // While S is read from TMEM: the chunk's mask words (they land with its K / V tiles) and, for bf16, the
         // P buffer (free once P V of chunk gg-2 is complete).
         ok = mbar_wait(kv_full(st), (gg / C::NS) & 1, abort_flag, wlim);
-        if (C::P_TMEM && ok) ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag, wlim);
+        if (C::P_TMEM && !C::P_OVER_S && ok) ok = mbar_wait(p_empty(sb), ((gg >> 1) & 1) ^ 1, abort_flag, wlim);
         uint32_t w0 = 0u, w1 = 0u;
         if (ok) {
           w0 = ld_shared_u32(stage_bits(st) + row * 4);
-          if (C::CH == 2 && n_in == 2) w1 = ld_shared_u32(stage_bits(st) + 512 + row * 4);
+          if constexpr (C::CH == 2) {
+            if (n_in == 2) w1 = ld_shared_u32(stage_bits(st) + 512 + row * 4);
+          }
         }
         tmem_wait_ld();
         reg_fence(s);
@@ -548,9 +563,9 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         if (lane == 0) FWN_TR(24, c);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(s_empty(sb));
+        if (!C::P_OVER_S && lane == 0) mbar_arrive(s_empty(sb));
         const uint32_t any0 = __reduce_or_sync(0xffffffffu, w0);
-        const uint32_t any1 = __reduce_or_sync(0xffffffffu, w1);
+        const uint32_t any1 = C::CH == 2 ? __reduce_or_sync(0xffffffffu, w1) : 0u;
         // Columns are handled in groups of 8 (one 16-byte chunk of a bf16 P row); a group that no row
         // of the warp may attend to is skipped by the whole warp. Four independent partial maxima / sums
         // keep the dependency chains short.
@@ -558,10 +573,10 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
         bool grow = false;
         float corr = 1.f;
         // Exact two-pass update: masked row max, lazy rescale of the reference, then p = 2^(s - m).
-        auto two_pass = [&](float (&e)[64]) {
+        auto two_pass = [&](float (&e)[C::KEYS]) {
           float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
+          for (int g = 0; g < C::KEYS / 8; ++g) {
             const uint32_t w = g < 4 ? w0 : w1;
             const uint32_t any = g < 4 ? any0 : any1;
             if ((any >> (8 * (g & 3))) & 0xFFu) {
@@ -585,7 +600,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           const float neg_m = -m_ref;
           float lp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
+          for (int g = 0; g < C::KEYS / 8; ++g) {
             const uint32_t w = g < 4 ? w0 : w1;
             const uint32_t any = g < 4 ? any0 : any1;
             if ((any >> (8 * (g & 3))) & 0xFFu) {
@@ -610,21 +625,21 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           // the allowed logits); they are accepted only if their sum is at least 2^-54 (their largest allowed p
           // is then at least 2^-60, so whatever underflowed is negligible). Otherwise the whole warp redoes the
           // chunk with the exact two-pass update. Paired f32x2 arithmetic for the scaling and the sums.
-          uint32_t pk[32];
+          uint32_t pk[C::KEYS / 2];
           float2 lp2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
           const bool fresh = l == 0.f;
           float m_use = m_ref;
           if (__any_sync(0xffffffffu, fresh)) {
             float up[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int j = 0; j < 64; ++j)
+            for (int j = 0; j < C::KEYS; ++j)
               if (j < 32 * n_in) up[j & 3] = fmaxf(up[j & 3], s[j]);
             const float umax = fmaxf(fmaxf(up[0], up[1]), fmaxf(up[2], up[3])) * p.scale_log2;
             if (fresh) m_use = umax;
           }
           const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
+          for (int g = 0; g < C::KEYS / 8; ++g) {
             const uint32_t w = g < 4 ? w0 : w1;
             const uint32_t any = g < 4 ? any0 : any1;
             if ((any >> (8 * (g & 3))) & 0xFFu) {
@@ -647,10 +662,10 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           const bool bad = !(sum <= 65536.f) ||
                            (fresh && (w0 | w1) != 0u && !(sum >= 5.5511151231257827e-17f));  // 2^-54
           if (__any_sync(0xffffffffu, bad)) {
-            float e[64];
+            float e[C::KEYS];
             two_pass(e);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(e[2 * j], e[2 * j + 1]);
+            for (int j = 0; j < C::KEYS / 2; ++j) pk[j] = pack_bf16(e[2 * j], e[2 * j + 1]);
           } else {
             m_ref = m_use;
             l += sum;
@@ -659,17 +674,21 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
           // P -> TMEM (the buffer was released above); the row's packed pairs go to its lane.
           const uint32_t pcol = trow + C::P_COL + C::P_STRIDE * sb;
           tmem_st16(pcol, *reinterpret_cast<const uint32_t(*)[16]>(&pk[0]));
-          if (C::CH == 2 && n_in == 2) tmem_st16(pcol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&pk[16]));
+          if constexpr (C::CH == 2) {
+            if (n_in == 2) tmem_st16(pcol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&pk[16]));
+          }
           tmem_wait_st();
         } else {
-          float e[64];
+          float e[C::KEYS];
           two_pass(e);
           if (lane == 0) FWN_TR(26, c);
           if constexpr (C::P_TMEM) {
             // tf32 P -> TMEM (the buffer was released above), one 32-key tile at a time.
             const uint32_t pcol = trow + C::P_COL + C::P_STRIDE * sb;
             tmem_st32(pcol, *reinterpret_cast<const float(*)[32]>(&e[0]));
-            if (C::CH == 2 && n_in == 2) tmem_st32(pcol + 32, *reinterpret_cast<const float(*)[32]>(&e[32]));
+            if constexpr (C::CH == 2) {
+              if (n_in == 2) tmem_st32(pcol + 32, *reinterpret_cast<const float(*)[32]>(&e[32]));
+            }
             tmem_wait_st();
           }
           if constexpr (!C::P_TMEM) {
