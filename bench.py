@@ -217,6 +217,7 @@ def _sample_rows(n, q_blocks, k_blocks):
 def sampled_parity(mask_host, arrays, outs, scale, q_blocks, k_blocks):
   """rel RMS of o, dq, dk, dv (and max |lse error|) at sampled rows against the float64 oracle."""
   from oracle import attention as oa
+  _all_host_threads()
   n = mask_host.shape[0]
   q_rows, k_rows = _sample_rows(n, q_blocks, k_blocks)
   t0 = time.perf_counter()
@@ -521,10 +522,11 @@ def run_ours(args):
   del mask
   torch.cuda.empty_cache()
 
-  # Other modes and shapes in the same run (default run only): config 3 in the reference's own precision (TF32)
-  # and its `highest` (3xTF32), and the real WN2 shape in bf16; each with sampled-row parity against the oracle.
+  # Other modes and shapes in the same run (default run at N = 1 only: at N > 1 they would be the same replicas):
+  # config 3 in the reference's own precision (TF32) and its `highest` (3xTF32), and the real WN2 shape in bf16;
+  # each with sampled-row parity against the oracle.
   modes = {}
-  if not args.no_blocks and args.workload == "attention" and args.mode == "bf16":
+  if not args.no_blocks and args.workload == "attention" and args.mode == "bf16" and ranks.world == 1:
     blk_steps, blk_warmup = min(args.steps, 20), max(3, min(args.warmup, 5))
     for wl, md in (("attention", "tf32"), ("attention", "tf32x3"), ("wn2", "bf16")):
       blk = attention_block(args, ranks, wl, md, blk_steps, blk_warmup, parity=True)
