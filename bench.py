@@ -37,13 +37,12 @@ CFG = 3
 # Kernel FLOP counts per allowed (query, key) pair per head and head_dim element: forward S and P V (4);
 # dQ kernel S, dP, dQ (6); dK/dV kernel S, dP, dV, dK (8). Useful FLOPs count S and dP once: 4 + 10.
 USEFUL_PER_PAIR = 14
-# DRAM bytes (read + write) per launch from one ncu capture of each workload (summaries under profiles/):
-# configuration 3 bf16 (dram__bytes_read.sum + dram__bytes_write.sum) and the WN2 shape bf16
-# (dram__bytes.sum.per_second x gpu__time_duration.sum of the same launch).
-NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 150_649_088, "attn_bwd_dq": 199_965_952,
-                                                   "attn_bwd_dkv": 229_626_880},
-               ("wn2", "bf16", "paired"): {"attn_fwd": 372_406_272, "attn_bwd_dq": 474_326_016,
-                                           "attn_bwd_dkv": 544_704_512}}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of each workload on the
+# current kernels (summaries under profiles/): configuration 3 bf16 and the WN2 shape bf16.
+NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 149_179_648, "attn_bwd_dq": 202_269_440,
+                                                   "attn_bwd_dkv": 226_809_088},
+               ("wn2", "bf16", "paired"): {"attn_fwd": 372_274_688, "attn_bwd_dq": 469_790_720,
+                                           "attn_bwd_dkv": 537_186_560}}
 
 
 def peaks():
@@ -264,10 +263,16 @@ def attention_block(args, ranks, workload_name, mode_name, steps, warmup, e2e=Fa
   sf, sb = lf.struct(), lb.struct()
   dref = ctypes.byref(desc)
 
+  side = torch.cuda.Stream(device)
+
   def launch(i, events=None):
+    """One step: forward, delta, then (timed loop) the dQ pass on a side stream concurrent with the dK/dV pass on
+    the main stream, as tiled_attn.attention_backward runs them; with `events`, the four launches one after
+    another, each between events on the main stream."""
     q, k, v, do = sets[i % 3]
     ob = outs[i % 3]
     s = stream.cuda_stream
+    s_dq = s if events is not None else side.cuda_stream
     calls = (
         ("attn_fwd", lambda: lib.fwn_attn_fwd(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(), ctypes.byref(sf),
                                               ob["o"].data_ptr(), ob["lse"].data_ptr(), s)),
@@ -275,7 +280,7 @@ def attention_block(args, ranks, workload_name, mode_name, steps, warmup, e2e=Fa
                                                           ws_bytes, s)),
         ("attn_bwd_dq", lambda: lib.fwn_attn_bwd_dq(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                                     ob["lse"].data_ptr(), do.data_ptr(), ctypes.byref(sf),
-                                                    ob["dq"].data_ptr(), ws.data_ptr(), ws_bytes, s)),
+                                                    ob["dq"].data_ptr(), ws.data_ptr(), ws_bytes, s_dq)),
         ("attn_bwd_dkv", lambda: lib.fwn_attn_bwd_dkv(dref, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                                       ob["lse"].data_ptr(), do.data_ptr(), ctypes.byref(sb),
                                                       ob["dk"].data_ptr(), ob["dv"].data_ptr(), ws.data_ptr(),
@@ -285,11 +290,15 @@ def attention_block(args, ranks, workload_name, mode_name, steps, warmup, e2e=Fa
       if events is not None:
         e0 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+      elif name == "attn_bwd_dq":
+        side.wait_stream(stream)
       _lib.check(fn())
       if events is not None:
         e1 = torch.cuda.Event(enable_timing=True)
         e1.record(stream)
         events.setdefault(name, []).append((e0, e1))
+    if events is None:
+      stream.wait_stream(side)
     return len(calls)
 
   for i in range(warmup):

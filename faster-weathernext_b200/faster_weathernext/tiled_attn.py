@@ -471,8 +471,24 @@ def attention_forward(q, k, v, tiles: AttentionTiles, scale: float, mode: int, w
   return o, lse
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+  """One extra stream per device: the dQ pass runs on it while the dK/dV pass runs on the caller's stream."""
+  st = _SIDE_STREAMS.get(device.index)
+  if st is None:
+    st = _SIDE_STREAMS[device.index] = torch.cuda.Stream(device)
+  return st
+
+
 def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float, mode: int):
-  """(dq, dk, dv), each [B, n, H, D] in q's dtype."""
+  """(dq, dk, dv), each [B, n, H, D] in q's dtype.
+
+  delta = rowsum(o * do) first (fwn_attn_bwd_delta); then the dQ pass (over the forward list) on a side stream
+  and the dK/dV pass (over the transposed list) on the current stream at the same time, joined before return:
+  the two passes read the same inputs and write different outputs, and running them together overlaps their
+  tails (configuration 3: 3 % of the step). The launches are fwn_attn_bwd's, one by one."""
   lib = _lib.lib()
   q, k, v = _canon(q, k, v)
   o, do = _canon(o.contiguous(), do.contiguous())
@@ -483,9 +499,17 @@ def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float,
   dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
   lf, lb = _lists(tiles, q, o)
   sf, sb = lf.struct(), lb.struct()
-  _lib.check(lib.fwn_attn_bwd(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                              lse.data_ptr(), do.data_ptr(), ctypes.byref(sf), ctypes.byref(sb), dq.data_ptr(),
-                              dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(), _stream()))
+  d = ctypes.byref(desc)
+  main = torch.cuda.current_stream(q.device)
+  side = _side_stream(q.device)
+  _lib.check(lib.fwn_attn_bwd_delta(d, o.data_ptr(), do.data_ptr(), ws.data_ptr(), ws.numel(), main.cuda_stream))
+  side.wait_stream(main)
+  _lib.check(lib.fwn_attn_bwd_dq(d, q.data_ptr(), k.data_ptr(), v.data_ptr(), lse.data_ptr(), do.data_ptr(),
+                                 ctypes.byref(sf), dq.data_ptr(), ws.data_ptr(), ws.numel(), side.cuda_stream))
+  _lib.check(lib.fwn_attn_bwd_dkv(d, q.data_ptr(), k.data_ptr(), v.data_ptr(), lse.data_ptr(), do.data_ptr(),
+                                  ctypes.byref(sb), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(),
+                                  main.cuda_stream))
+  main.wait_stream(side)
   return dq, dk, dv
 
 
