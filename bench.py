@@ -515,6 +515,53 @@ def finetune_block(args, ranks, steps, warmup):
   return out
 
 
+def processor_block(args, ranks, steps, warmup):
+  """Configuration 4 (processor inference: 8 members x 2 noise samples = 16 forwards of the 24-block processor, split
+  over the ranks, no communication): ms per step, max over ranks."""
+  import torch
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor, ProcessorConfig
+
+  device = ranks.device
+  mask, _, _ = mesh.config_mask(CFG)
+  n = mask.shape[0]
+  tiles = ta.AttentionTiles.from_mask(mask, device=device)
+  cfg = ProcessorConfig()
+  model = Processor(cfg, seed=0, device=device)
+  forwards = 16
+  local_f = forwards // ranks.world
+  g = torch.Generator(device=device).manual_seed(200 + ranks.rank)
+  x = torch.randn(local_f, n, cfg.d_model, device=device, generator=g)
+  c = torch.randn(local_f, cfg.cond_dim, device=device, generator=g)
+  stream = torch.cuda.current_stream()
+
+  def step():
+    with torch.no_grad():
+      return model(x, c, tiles)
+  for _ in range(warmup):
+    step()
+  ranks.barrier()
+  a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  a.record(stream)
+  for _ in range(steps):
+    y = step()
+  b.record(stream)
+  ranks.barrier()
+  ms = ranks.max(a.elapsed_time(b)) / steps
+  gemm = model.gemm_flops_per_forward(n) * local_f
+  hbm, tc, peak_kind = peaks()
+  out = {"workload": "cfg4: 24 pre-LN blocks d512 8x64 MLP2048 GELU, 16 forwards (8 members x 2 samples) split over "
+                     "the ranks, no communication, level-6 mesh 0.06 rad",
+         "forwards_per_gpu": local_f, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3),
+         "forwards_per_s": round(forwards / (ms * 1e-3), 2),
+         "gemm_tflops_per_gpu": round(gemm / (ms * 1e-3) / 1e12, 1), "gemm_frac_of_peak": round(gemm / (ms * 1e-3) / 1e12 / tc, 4),
+         "output_finite": bool(torch.isfinite(y).all())}
+  del model, x, c, y
+  torch.cuda.empty_cache()
+  return out
+
+
 def run_ours(args):
   import torch
 
@@ -542,8 +589,9 @@ def run_ours(args):
       blk.pop("_mask")
       modes[("cfg3" if wl == "attention" else wl) + "_" + md] = blk
       torch.cuda.empty_cache()
-  finetune = None
+  finetune = processor = None
   if not args.no_finetune and args.workload == "attention" and args.mode == "bf16":
+    processor = processor_block(args, ranks, steps=min(args.steps, 5), warmup=3)
     finetune = finetune_block(args, ranks, steps=min(args.steps, 5), warmup=3)
 
   if ranks.rank == 0:
@@ -567,7 +615,7 @@ def run_ours(args):
                    "l2": head["l2"], "tile_lists": head["tile_lists"]},
         "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"), "gpu_launches": head["gpu_launches"],
         "clocks": clocks.summary(), "kernels": head["kernels"], "issued_tile_tflops": head["issued_tile_tflops"],
-        "modes": modes or None, "finetune": finetune,
+        "modes": modes or None, "processor": processor, "finetune": finetune,
     }
     print(json.dumps(line), flush=True)
   ranks.close()
@@ -822,7 +870,8 @@ def main():
   ap.add_argument("--no-cpu", action="store_true")
   ap.add_argument("--no-blocks", action="store_true",
                   help="default run: skip the TF32 / 3xTF32 / WN2 blocks")
-  ap.add_argument("--no-finetune", action="store_true", help="default run: skip the configuration-5 block")
+  ap.add_argument("--no-finetune", action="store_true",
+                  help="default run: skip the configuration-4 (processor) and configuration-5 (fine-tune) blocks")
   ap.add_argument("--cpu-seconds", type=float, default=15.0)
   ap.add_argument("--ref-seconds", type=float, default=90.0,
                   help="--impl reference: host seconds the warm-up and timed steps take together")

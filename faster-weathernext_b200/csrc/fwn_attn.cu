@@ -684,8 +684,9 @@ fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32
 
 namespace {
 
-fwn_status cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample, const int32_t* out_node,
-                          const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
+fwn_status cond_layernorm(float* x, int64_t rows, int32_t d, int32_t rows_per_sample, const int32_t* out_node,
+                          const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream,
+                          const void* residual = nullptr) {
   if (rows < 0 || rows_per_sample <= 0 || !(eps > 0.f))
     return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld, rows_per_sample=%d or eps", static_cast<long long>(rows),
                 rows_per_sample);
@@ -698,8 +699,9 @@ fwn_status cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_
   if (rows % rows_per_sample != 0)
     return fail(FWN_ERR_INVALID_ARGUMENT, "rows=%lld is not a multiple of rows_per_sample=%d",
                 static_cast<long long>(rows), rows_per_sample);
+  if (residual && rows > 0 && !aligned16(residual)) return fail(FWN_ERR_INVALID_ARGUMENT, "residual must be 16-byte aligned");
   cudaError_t e = fwn::launch_cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out,
-                                             out_dtype == FWN_DTYPE_BF16, static_cast<cudaStream_t>(stream));
+                                             out_dtype == FWN_DTYPE_BF16, residual, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cond_layernorm");
   return ok();
 }
@@ -708,14 +710,23 @@ fwn_status cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_
 
 fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
                               const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
-  return cond_layernorm(x, rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype, stream);
+  return cond_layernorm(const_cast<float*>(x), rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype,
+                        stream);
+}
+
+fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                       const int32_t* out_node, const float* scale_offset, float eps, void* out,
+                                       int32_t out_dtype, void* stream) {
+  if (rows > 0 && !residual) return fail(FWN_ERR_INVALID_ARGUMENT, "null residual");
+  return cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream, residual);
 }
 
 fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
                                       const int32_t* out_node, const float* scale_offset, float eps, void* out,
                                       int32_t out_dtype, void* stream) {
   if (rows > 0 && !out_node) return fail(FWN_ERR_INVALID_ARGUMENT, "null out_node");
-  return cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream);
+  return cond_layernorm(const_cast<float*>(x), rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype,
+                        stream);
 }
 
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }

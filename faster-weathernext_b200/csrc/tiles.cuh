@@ -55,8 +55,9 @@ cudaError_t launch_bitset_csr_fill(const uint32_t* bits, int n_rows, int n_cols,
 
 // Conditioned LayerNorm (norm.cu): out = LN(x) * (1 + scale[s]) + offset[s], s = row / rows_per_sample,
 // scale_offset [samples, 2 d]; d in {128, 256, 512, 1024}; out bf16 or float32; out_node (nullable) maps each
-// row within its sample to its output row.
-cudaError_t launch_cond_layernorm(const float* x, int64_t rows, int d, int rows_per_sample, const int32_t* out_node,
-                                  const float* so, float eps, void* out, bool bf16_out, cudaStream_t stream);
+// row within its sample to its output row; residual (nullable, bf16 [rows, d]) is first added into x in place.
+cudaError_t launch_cond_layernorm(float* x, int64_t rows, int d, int rows_per_sample, const int32_t* out_node,
+                                  const float* so, float eps, void* out, bool bf16_out, const void* residual,
+                                  cudaStream_t stream);
 
 }  // namespace fwn

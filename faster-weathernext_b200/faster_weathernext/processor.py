@@ -142,9 +142,10 @@ class Processor(torch.nn.Module):
     return x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
 
   def _forward_fused(self, x, cond, tiles, perm=None):
-    """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm
-    (fwn_cond_layernorm), bias and GELU in the GEMM epilogue (cuBLASLt), and the residual stream updated in
-    place (float32 += bf16 in one pass). x float32 [B, n, d]; cond [B, cond_dim]; perm checked by forward."""
+    """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm, which also adds
+    the previous sub-block's bf16 output into the float32 residual stream in place (fwn_cond_layernorm_residual: one
+    pass instead of an add and a norm), bias and GELU in the GEMM epilogue (cuBLASLt). x float32 [B, n, d]; cond
+    [B, cond_dim]; perm checked by forward."""
     b, n, d = x.shape
     m_rows = b * n
     lib = _lib.lib()
@@ -156,26 +157,32 @@ class Processor(torch.nn.Module):
     h = torch.empty(m_rows, d, dtype=bf, device=x.device)
     cf = cond.float()
 
-    def norm(w, out, out_dtype):
+    def norm(w, out, out_dtype, residual=None, out_node=None):
+      """out = cond_norm(x) (x += residual first, in the same pass; rows to out_node[row] when given)."""
       so = (cf @ w.float()).contiguous()                    # [B, 2d]: per-sample scale, offset
-      _lib.check(lib.fwn_cond_layernorm(x2.data_ptr(), m_rows, d, n, so.data_ptr(), 1e-5, out.data_ptr(),
-                                        out_dtype, stream))
+      if residual is None and out_node is None:
+        _lib.check(lib.fwn_cond_layernorm(x2.data_ptr(), m_rows, d, n, so.data_ptr(), 1e-5, out.data_ptr(),
+                                          out_dtype, stream))
+      elif residual is None:
+        _lib.check(lib.fwn_cond_layernorm_scatter(x2.data_ptr(), m_rows, d, n, out_node.data_ptr(), so.data_ptr(),
+                                                  1e-5, out.data_ptr(), out_dtype, stream))
+      else:
+        _lib.check(lib.fwn_cond_layernorm_residual(x2.data_ptr(), residual.data_ptr(), m_rows, d, n,
+                                                   out_node.data_ptr() if out_node is not None else None,
+                                                   so.data_ptr(), 1e-5, out.data_ptr(), out_dtype, stream))
 
+    # Each sub-block's output (bf16) is added into the residual stream by the norm that follows it.
+    pending = None
     for blk in self.blocks:
-      norm(blk.cond1, h, _lib.DTYPE_BF16)
-      x2.add_(self._mha(h.view(b, n, d), self._bf16(blk.w_qkv), self._bf16(blk.w_out), tiles).view(m_rows, d))
-      norm(blk.cond2, h, _lib.DTYPE_BF16)
+      norm(blk.cond1, h, _lib.DTYPE_BF16, residual=pending)
+      pending = self._mha(h.view(b, n, d), self._bf16(blk.w_qkv), self._bf16(blk.w_out), tiles).view(m_rows, d)
+      norm(blk.cond2, h, _lib.DTYPE_BF16, residual=pending)
       mlp = torch._addmm_activation(self._bf16(blk.b1), h, self._bf16(blk.w1), use_gelu=True)
-      x2.add_(torch.addmm(self._bf16(blk.b2), mlp, self._bf16(blk.w2)))
+      pending = torch.addmm(self._bf16(blk.b2), mlp, self._bf16(blk.w2))
     out = torch.empty_like(xs)
-    if perm is None:
-      norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32)
-    else:
-      # Final norm with the un-permutation fused into its store: row i of each sample goes to row perm[i].
-      so = (cf @ self.cond_final.float()).contiguous()
-      out_node = perm.to(torch.int32).contiguous()
-      _lib.check(lib.fwn_cond_layernorm_scatter(x2.data_ptr(), m_rows, d, n, out_node.data_ptr(), so.data_ptr(),
-                                                1e-5, out.data_ptr(), _lib.DTYPE_F32, stream))
+    # Final norm; with perm, the un-permutation is fused into its store: row i of each sample goes to row perm[i].
+    out_node = perm.to(torch.int32).contiguous() if perm is not None else None
+    norm(self.cond_final, out.view(m_rows, d), _lib.DTYPE_F32, residual=pending, out_node=out_node)
     return out
 
   def gemm_flops_per_forward(self, n: int) -> float:

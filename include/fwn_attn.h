@@ -196,6 +196,15 @@ FWN_API fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int3
                                               const int32_t* out_node, const float* scale_offset, float eps,
                                               void* out, int32_t out_dtype, void* stream);
 
+/* The pre-LN block's residual add fused into the next norm (src/faster_weathernext/patch.py:238-252, `x = x + f(h)`
+ * followed by the next LayerNorm): x[r, :] += residual[r, :] in place (x float32 [rows, d], residual bf16 [rows, d],
+ * the sub-block's output), then out = the conditioned LayerNorm of the sum, as fwn_cond_layernorm (or, with out_node
+ * non-null, fwn_cond_layernorm_scatter). One pass over the rows instead of an add and a norm. */
+FWN_API fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, int64_t rows, int32_t d,
+                                               int32_t rows_per_sample, const int32_t* out_node,
+                                               const float* scale_offset, float eps, void* out, int32_t out_dtype,
+                                               void* stream);
+
 /* ---- attention --------------------------------------------------------------------------------------- */
 
 /* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)

@@ -259,3 +259,36 @@ def test_processor_remat_gives_the_same_gradients(cuda):
       patch.OPTIONS.remat = False
     grads.append(torch.cat([p.grad.reshape(-1) for p in model.parameters()]))
   assert float((grads[1] - grads[0]).norm() / grads[0].norm()) <= 1e-6
+
+
+def test_cond_layernorm_residual_kernel(cuda):
+  """fwn_cond_layernorm_residual: x += residual (bf16) in place, then the conditioned norm of the sum, bit-equal to a
+  float32 add followed by fwn_cond_layernorm (and, with an output node map, fwn_cond_layernorm_scatter)."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  g = torch.Generator(device=cuda).manual_seed(4)
+  for d in (128, 512, 1024):
+    b, n = 2, 301
+    x = torch.randn(b * n, d, device=cuda, generator=g)
+    r = torch.randn(b * n, d, device=cuda, generator=g).to(torch.bfloat16)
+    so = torch.randn(b, 2 * d, device=cuda, generator=g) * 0.2
+    perm = torch.randperm(n, device=cuda, generator=g).to(torch.int32)
+    for out_node in (None, perm):
+      x_ref = x + r.float()
+      ref = torch.empty(b * n, d, device=cuda, dtype=torch.bfloat16)
+      if out_node is None:
+        _lib.check(lib.fwn_cond_layernorm(x_ref.data_ptr(), b * n, d, n, so.data_ptr(), 1e-5, ref.data_ptr(),
+                                          _lib.DTYPE_BF16, 0))
+      else:
+        _lib.check(lib.fwn_cond_layernorm_scatter(x_ref.data_ptr(), b * n, d, n, out_node.data_ptr(), so.data_ptr(),
+                                                  1e-5, ref.data_ptr(), _lib.DTYPE_BF16, 0))
+      x_got = x.clone()
+      got = torch.empty_like(ref)
+      _lib.check(lib.fwn_cond_layernorm_residual(x_got.data_ptr(), r.data_ptr(), b * n, d, n,
+                                                 out_node.data_ptr() if out_node is not None else None,
+                                                 so.data_ptr(), 1e-5, got.data_ptr(), _lib.DTYPE_BF16, 0))
+      torch.cuda.synchronize()
+      assert torch.equal(x_got, x_ref), d
+      assert torch.equal(got, ref), d
+  assert lib.fwn_cond_layernorm_residual(x.data_ptr(), None, 4, 128, 2, None, so.data_ptr(), 1e-5, x.data_ptr(),
+                                         _lib.DTYPE_F32, 0) == _lib.FWN_ERR_INVALID_ARGUMENT
