@@ -15,6 +15,7 @@
 #include "attn_fwd.cuh"
 #include "attn_fwd_wide.cuh"
 #include "attn_bwd_wide.cuh"
+#include "gemm.cuh"
 #include "tiles.cuh"
 
 namespace {
@@ -727,6 +728,62 @@ fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, i
   if (rows > 0 && !out_node) return fail(FWN_ERR_INVALID_ARGUMENT, "null out_node");
   return cond_layernorm(const_cast<float*>(x), rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype,
                         stream);
+}
+
+namespace {
+
+// 2D map over a row-major bf16 matrix [rows, cols] (cols contiguous): box = 64 columns (128 bytes) x box_rows rows,
+// 128-byte swizzle (the K-major operand layout of the GEMM).
+// box_cols 64 with the 128-byte swizzle (GEMM operands) or 32 with the 64-byte swizzle (GEMM output chunks).
+fwn_status make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows, int box_cols = 64) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FWN_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FWN_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled (2d) failed (%d)", static_cast<int>(r));
+  return FWN_OK;
+}
+
+}  // namespace
+
+fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n, int32_t k,
+                         int32_t act, void* stream) {
+  using C = fwn::GemmCfg;
+  if (m <= 0 || n <= 0 || k <= 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape m=%lld n=%d k=%d", static_cast<long long>(m), n, k);
+  if (n % C::BN != 0 || k % C::BK != 0)
+    return fail(FWN_ERR_UNSUPPORTED, "n=%d must be a multiple of %d and k=%d of %d", n, C::BN, k, C::BK);
+  if (act != FWN_ACT_NONE && act != FWN_ACT_GELU_TANH) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  if (!a || !bt || !c) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(a) || !aligned16(bt) || !aligned16(c) || (bias && !aligned16(bias)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "pointers must be 16-byte aligned");
+  const int64_t m_tiles = (m + C::BM - 1) / C::BM;
+  if (m_tiles * (n / C::BN) >= (int64_t(1) << 31)) return fail(FWN_ERR_UNSUPPORTED, "m=%lld too large", static_cast<long long>(m));
+  CUtensorMap ta, tb, tc;
+  fwn_status s;
+  if ((s = make_map_2d(&ta, a, m, k, C::BM)) != FWN_OK) return s;
+  if ((s = make_map_2d(&tb, bt, n, k, C::BN)) != FWN_OK) return s;
+  if ((s = make_map_2d(&tc, c, m, n, 32, 32)) != FWN_OK) return s;
+  fwn::GemmParams p{};
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.act = act;
+  p.n_tiles = n / C::BN;
+  p.num_tiles = static_cast<int>(m_tiles * p.n_tiles);
+  auto kernel = fwn::gemm_bf16_kernel;
+  int grid = 0;
+  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.num_tiles, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, tc, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return ok();
 }
 
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }

@@ -1,0 +1,260 @@
+// Dense bf16 GEMM with a fused bias / GELU epilogue for the processor's projections around the attention
+// (src/faster_weathernext/patch.py:165-177, 250-252: q / k / v projection, mha_final, the MLP):
+//   C[m, n] = act(A[m, k] B[k, n] + bias[n]),  A row-major [m, k], B given transposed as Bt [n, k] (both operands
+//   K-major), C row-major [m, n] bf16, float32 accumulation, act = identity or GELU in its tanh form.
+//
+// Persistent, one CTA per SM, tiles of 128 x 256 walked in (row block, column block) order so that the CTAs working
+// at the same time share their A rows in L2 (B, a weight, stays in L2):
+//   warp 0      TMA producer: A box 64 x 128 and Bt box 64 x 256 (128-byte swizzle) per K-step of 64, into a
+//               ring of four 48 KB stages;
+//   warp 1      MMA issuer: four tcgen05.mma (M 128, N 256, K 16) per stage into one of two TMEM accumulators
+//               (256 columns each), committing the stage back to the producer and, after the tile's last stage,
+//               the accumulator to the epilogue;
+//   warps 2-9   epilogue: warps w and w+4 share TMEM lane quadrant w % 4 (rows) and take 128 columns each; they
+//               read the accumulator in 64-column steps and release it after the last, so the next tile's MMAs
+//               (into the other accumulator, then this one) overlap the activation and stores; bias, activation,
+//               bf16; each warp's 32 x 32 chunk goes through its own shared-memory buffer (64-byte swizzle, two
+//               per warp) and leaves as one TMA tensor store (rows past m clipped by the tensor map).
+// Measured at m = 655,392, k = 512 (n = 1536): stores of one row per lane straight from registers (32 rows per warp
+// instruction) held the kernel at 0.82 PFLOP/s; 256 x 256 tiles with each 128-row half single-buffered in TMEM made
+// the next tile's MMAs wait for most of the epilogue (1.03 with per-warp TMA stores).
+// Every wait is bounded (mbar_wait); on expiry the CTA's roles leave their loops and the CTA frees TMEM.
+#pragma once
+
+#include "common.cuh"
+
+namespace fwn {
+
+struct GemmParams {
+  const __nv_bfloat16* bias;  // [n] or null
+  __nv_bfloat16* c;           // [m, n]
+  int64_t m;
+  int n, k;
+  int act;                    // 0 identity, 1 GELU (tanh form)
+  int n_tiles, num_tiles;
+};
+
+struct GemmCfg {
+  static constexpr int BM = 128, BN = 256, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int NS = 4;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int THREADS = 320;
+  static constexpr int N_BAR = 2 * NS + 4 + 1;
+  static constexpr int OUT_BYTES = 32 * 32 * 2;                        // one epilogue warp's 32 x 32 chunk
+  static constexpr int OFF_OUT = NS * STAGE_BYTES;                     // 8 warps x 2 buffers
+  static constexpr int OFF_BAR = OFF_OUT + 8 * 2 * OUT_BYTES;
+  static constexpr int SMEM_BYTES = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + TMEM holder / abort word + 1 KB alignment
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB-aligned stages");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+// Box {32 columns, 32 rows} of the output from shared memory (bulk async-group completion).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int c0, int c1, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU, tanh form: 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.f + tanh_approx(u));
+}
+
+// Ten warps: each SM sub-partition holds three, which leaves 168 registers per thread.
+__global__ void __maxnreg__(168)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+  using C = GemmCfg;
+  extern __shared__ uint8_t smem_gemm[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_gemm) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  auto a_st = [&](int s) { return sbase + s * C::STAGE_BYTES; };
+  auto b_st = [&](int s) { return sbase + s * C::STAGE_BYTES + C::A_BYTES; };
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8 * s; };
+  auto empty = [&](int s) { return bar0 + 8 * (C::NS + s); };
+  auto acc_full = [&](int b) { return bar0 + 8 * (2 * C::NS + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8 * (2 * C::NS + 2 + b); };
+  const uint32_t drain = bar0 + 8 * (2 * C::NS + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + C::N_BAR * 8 + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = p.k / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = mbar_wait(empty(st), ((g / C::NS) & 1) ^ 1, abort_flag))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full(st), C::STAGE_BYTES);
+          tma_load_2d(a_st(st), &tm_a, kb * C::BK, mt * C::BM, full(st));
+          tma_load_2d(b_st(st), &tm_b, kb * C::BK, nt * C::BN, full(st));
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok && lane == 0) {
+      // Drain (bounded, ignoring the abort flag): every copy this warp issued lands before TMEM is released.
+      volatile int never = 0;
+      for (uint32_t k = (g >= C::NS ? g - C::NS : 0); k < g; ++k) mbar_wait(full(k % C::NS), (k / C::NS) & 1, &never);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = instr_desc(false, C::BM, C::BN, false, false);
+    uint32_t g = 0, acc_i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++acc_i) {
+      const int buf = acc_i & 1;
+      if (!(ok = warp_wait(acc_empty(buf), ((acc_i >> 1) & 1) ^ 1, abort_flag))) break;
+      tc_fence_after();
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % C::NS;
+        if (!(ok = warp_wait(full(st), (g / C::NS) & 1, abort_flag))) break;
+        tc_fence_after();
+        const uint64_t ad = smem_desc(a_st(st), 16, 1024), bd = smem_desc(b_st(st), 16, 1024);
+        if (elect_one_sync()) {
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 16; ++kk)
+            mma_ss<false>(tmem + buf * C::BN, ad + ((kk * 32) >> 4), bd + ((kk * 32) >> 4), idesc,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(empty(st));
+          if (kb == nk - 1) mma_commit(acc_full(buf));
+        }
+        __syncwarp();
+      }
+    }
+    if (elect_one_sync()) mma_commit(drain);
+    __syncwarp();
+    volatile int never = 0;
+    mbar_wait(drain, 0, &never);
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2-9)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;  // rows 32 quarter + lane, columns 128 half + [0, 128)
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * 128;
+    auto out_buf = [&](int b) { return sbase + C::OFF_OUT + ((warp - 2) * 2 + b) * C::OUT_BYTES; };
+    uint32_t acc_i = 0, nbuf = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++acc_i) {
+      const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+      const int buf = acc_i & 1;
+      if (!(ok = mbar_wait(acc_full(buf), (acc_i >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      const int64_t row0 = static_cast<int64_t>(mt) * C::BM + quarter * 32;  // the warp's first row
+      const int col0 = nt * C::BN + half * 128;
+#pragma unroll 1
+      for (int jp = 0; jp < 2; ++jp) {
+        float v[2][32];
+        tmem_ld32(trow + buf * C::BN + 64 * jp, v[0]);
+        tmem_ld32(trow + buf * C::BN + 64 * jp + 32, v[1]);
+        tmem_wait_ld();
+        reg_fence(v[0]);
+        reg_fence(v[1]);
+        if (jp == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty(buf));
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int c32 = col0 + 64 * jp + 32 * jj;
+          uint32_t bw[16];  // the chunk's 32 bias values as bf16 pairs (the same 64 bytes for every lane)
+          if (p.bias != nullptr) {
+            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + c32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = __ldg(bp + q);
+              bw[4 * q] = w.x;
+              bw[4 * q + 1] = w.y;
+              bw[4 * q + 2] = w.z;
+              bw[4 * q + 3] = w.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) bw[i] = 0u;
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 bf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[i]));
+            float a = v[jj][2 * i] + bf.x, b = v[jj][2 * i + 1] + bf.y;
+            if (p.act == 1) {
+              a = gelu_tanh(a);
+              b = gelu_tanh(b);
+            }
+            pk[i] = pack_bf16(a, b);
+          }
+          // This lane's row of the chunk into the warp's buffer (64-byte swizzle) once the store that last read the
+          // buffer has read it, then one TMA store of the 32 x 32 chunk.
+          const uint32_t ob = out_buf(nbuf & 1);
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) st_shared_v4(ob + sw64_offset(lane, q), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < p.m) {
+            tma_store_2d(&tm_c, c32, static_cast<int>(row0), ob);
+            bulk_commit();
+          }
+          ++nbuf;
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+}  // namespace fwn

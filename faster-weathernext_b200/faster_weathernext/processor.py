@@ -12,8 +12,9 @@ q/k/v/out projections and a GELU MLP. The official modules (`weathernext.utils.s
 the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU in the tanh form that is
 jax.nn.gelu's default; Glorot-uniform weights from a seed), not a numerical copy of the official one. The
 projections run as cuBLAS GEMMs; the attention block is patch.tiled_mha (the B200 kernel; q, k, v are strided
-views of one fused projection, no copies). Without autograd (inference), each norm is one fused kernel and
-bias + GELU run in the GEMM epilogue. With autograd and patch.OPTIONS.remat, each block's activations are
+views of one fused projection, no copies). Without autograd (inference), each norm is one fused kernel that also
+adds the previous sub-block's output into the residual stream, and the MLP up-projection runs on this package's
+tcgen05 GEMM with bias + GELU in its epilogue (faster than cuBLASLt's GELU epilogue at these shapes). With autograd and patch.OPTIONS.remat, each block's activations are
 recomputed in the backward instead of stored (the reference's per-layer rematerialisation, patch.py:69-73).
 
 Node order: the reference's transformer gathers the latents into the mask's node order with `perm` before the
@@ -76,6 +77,30 @@ class Processor(torch.nn.Module):
       self.blocks.append(blk)
     self.cond_final = _glorot(gen, cfg.cond_dim, 2 * d, dev)
     self._bf16_cache = {}
+
+  def _bf16_t(self, p: torch.Tensor) -> torch.Tensor:
+    """bf16 copy of p's transpose (contiguous), the K-major weight operand of fwn_gemm_bf16; cached as _bf16."""
+    key = ("t", id(p))
+    hit = self._bf16_cache.get(key)
+    if hit is not None and hit[0] == p._version and hit[1] == p.data_ptr():
+      return hit[2]
+    w = p.detach().t().contiguous().to(torch.bfloat16)
+    self._bf16_cache[key] = (p._version, p.data_ptr(), w)
+    return w
+
+  def _mlp_up(self, h: torch.Tensor, blk) -> torch.Tensor:
+    """GELU(h @ w1 + b1) in bf16 for the inference path: fwn_gemm_bf16 with bias and GELU in its epilogue where the
+    shapes fit its tiles (hidden a multiple of 256, width of 64), cuBLASLt's bias + GELU epilogue otherwise."""
+    m, d = h.shape
+    hidden = blk.w1.shape[1]
+    if hidden % 256 or d % 64:
+      return torch._addmm_activation(self._bf16(blk.b1), h, self._bf16(blk.w1), use_gelu=True)
+    lib = _lib.lib()
+    out = torch.empty(m, hidden, dtype=torch.bfloat16, device=h.device)
+    _lib.check(lib.fwn_gemm_bf16(h.data_ptr(), self._bf16_t(blk.w1).data_ptr(), self._bf16(blk.b1).data_ptr(),
+                                 out.data_ptr(), m, hidden, d, _lib.ACT_GELU_TANH,
+                                 torch.cuda.current_stream().cuda_stream))
+    return out
 
   def _bf16(self, p: torch.Tensor) -> torch.Tensor:
     """bf16 copy of parameter p for the inference path, cast again only when p has changed: the cache entry
@@ -144,8 +169,9 @@ class Processor(torch.nn.Module):
   def _forward_fused(self, x, cond, tiles, perm=None):
     """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm, which also adds
     the previous sub-block's bf16 output into the float32 residual stream in place (fwn_cond_layernorm_residual: one
-    pass instead of an add and a norm), bias and GELU in the GEMM epilogue (cuBLASLt). x float32 [B, n, d]; cond
-    [B, cond_dim]; perm checked by forward."""
+    pass instead of an add and a norm), the MLP up-projection with bias and GELU in the epilogue of this package's
+    GEMM (fwn_gemm_bf16), the other projections on cuBLAS. x float32 [B, n, d]; cond [B, cond_dim]; perm checked by
+    forward."""
     b, n, d = x.shape
     m_rows = b * n
     lib = _lib.lib()
@@ -177,7 +203,7 @@ class Processor(torch.nn.Module):
       norm(blk.cond1, h, _lib.DTYPE_BF16, residual=pending)
       pending = self._mha(h.view(b, n, d), self._bf16(blk.w_qkv), self._bf16(blk.w_out), tiles).view(m_rows, d)
       norm(blk.cond2, h, _lib.DTYPE_BF16, residual=pending)
-      mlp = torch._addmm_activation(self._bf16(blk.b1), h, self._bf16(blk.w1), use_gelu=True)
+      mlp = self._mlp_up(h, blk)
       pending = torch.addmm(self._bf16(blk.b2), mlp, self._bf16(blk.w2))
     out = torch.empty_like(xs)
     # Final norm; with perm, the un-permutation is fused into its store: row i of each sample goes to row perm[i].

@@ -205,6 +205,15 @@ FWN_API fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, i
                                                const float* scale_offset, float eps, void* out, int32_t out_dtype,
                                                void* stream);
 
+/* Projections around the attention (src/faster_weathernext/patch.py:165-177, 250-252: q / k / v, mha_final, the
+ * MLP): c[m, n] = act(a[m, k] b[k, n] + bias[n]), a row-major bf16 [m, k], b given transposed as bt row-major bf16
+ * [n, k] (the weight with k contiguous), bias bf16 [n] or NULL, c row-major bf16 [m, n]; float32 accumulation on the
+ * tensor cores. n a multiple of 256, k a multiple of 64, pointers 16-byte aligned. act: FWN_ACT_NONE or
+ * FWN_ACT_GELU_TANH (0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), jax.nn.gelu's default form). */
+typedef enum fwn_act { FWN_ACT_NONE = 0, FWN_ACT_GELU_TANH = 1 } fwn_act;
+FWN_API fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n,
+                                 int32_t k, int32_t act, void* stream);
+
 /* ---- attention --------------------------------------------------------------------------------------- */
 
 /* Forward: o = softmax(mask(q k^T * scale)) v over the tiles of `tiles` (128-row list); lse (nullable)
