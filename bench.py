@@ -562,6 +562,60 @@ def processor_block(args, ranks, steps, warmup):
   return out
 
 
+def gnn_block(args, ranks, steps, warmup):
+  """The decoder's grid <-> mesh interaction network at the WeatherNext 2 shape (patch.py:347-509): 40,962 mesh
+  nodes send to the 1,038,240 points of the 0.25-degree grid, each point receiving from its 3 nearest mesh nodes
+  (3,114,720 edges sorted by receiver), latent and hidden width 512; edges in one pass and in the reference's blocks of
+  Options.edge_chunk. ms per step and matmul TFLOP/s."""
+  import torch
+  from scipy.spatial import cKDTree
+  from faster_weathernext import mesh, patch
+  from faster_weathernext.gnn import GNNConfig, InteractionNetwork
+
+  device = ranks.device
+  xyz, _ = mesh.icosphere(6)
+  lat = np.deg2rad(np.linspace(-90.0, 90.0, 721))
+  lon = np.deg2rad(np.arange(1440) * 0.25)
+  la, lo = np.meshgrid(lat, lon, indexing="ij")
+  pts = np.stack([np.cos(la) * np.cos(lo), np.cos(la) * np.sin(lo), np.sin(la)], -1).reshape(-1, 3)
+  t0 = time.perf_counter()
+  _, nn = cKDTree(xyz).query(pts, k=3)
+  build_s = time.perf_counter() - t0
+  ns, nr = xyz.shape[0], pts.shape[0]
+  senders = torch.from_numpy(nn.reshape(-1).astype(np.int32))
+  receivers = torch.from_numpy(np.repeat(np.arange(nr, dtype=np.int32), 3))
+  cfg = GNNConfig(latent=512, hidden=512)
+  net = InteractionNetwork(cfg, seed=0, device=device)
+  g = torch.Generator(device=device).manual_seed(300 + ranks.rank)
+  sx = torch.randn(ns, cfg.latent, device=device, generator=g)
+  rx = torch.randn(nr, cfg.latent, device=device, generator=g)
+  ex = torch.randn(senders.numel(), cfg.latent, device=device, generator=g)
+  stream = torch.cuda.current_stream()
+  out = {"workload": "decoder interaction network: 40,962 mesh nodes -> 1,038,240 grid points (0.25 deg), 3 nearest "
+                     "mesh nodes per point, 3,114,720 edges sorted by receiver, latent / hidden 512",
+         "graph_build_s": round(build_s, 2), "steps": steps, "warmup": warmup,
+         "matmul_gflop": round(net.flops(ns, nr, senders.numel()) / 1e9, 1)}
+  for name, chunk in (("one_pass", 0), ("edge_chunk_default", patch.Options().edge_chunk)):
+    def step():
+      return net(sx, rx, ex, senders, receivers, edge_chunk=chunk)
+    for _ in range(warmup):
+      step()
+    ranks.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+      ys, yr = step()
+    b.record(stream)
+    ranks.barrier()
+    ms = ranks.max(a.elapsed_time(b)) / steps
+    out[name] = {"edge_chunk": chunk, "ms_per_step": round(ms, 3),
+                 "matmul_tflops": round(net.flops(ns, nr, senders.numel()) / (ms * 1e-3) / 1e12, 1),
+                 "output_finite": bool(torch.isfinite(yr).all() and torch.isfinite(ys).all())}
+  del net, sx, rx, ex
+  torch.cuda.empty_cache()
+  return out
+
+
 def run_ours(args):
   import torch
 
@@ -589,6 +643,7 @@ def run_ours(args):
       blk.pop("_mask")
       modes[("cfg3" if wl == "attention" else wl) + "_" + md] = blk
       torch.cuda.empty_cache()
+    modes["gnn_decoder"] = gnn_block(args, ranks, steps=min(args.steps, 5), warmup=3)
   finetune = processor = None
   if not args.no_finetune and args.workload == "attention" and args.mode == "bf16":
     processor = processor_block(args, ranks, steps=min(args.steps, 5), warmup=3)

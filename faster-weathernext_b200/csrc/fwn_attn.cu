@@ -786,6 +786,38 @@ fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* 
   return ok();
 }
 
+fwn_status fwn_gnn_gather_add_act(const void* e_proj, const void* s_proj, const int32_t* senders, const void* r_proj,
+                                  const int32_t* receivers, const void* bias, int64_t rows, int32_t h, int32_t act,
+                                  void* out, void* stream) {
+  if (rows < 0 || h <= 0 || h % 8 != 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld or h=%d (a multiple of 8)",
+                                                    static_cast<long long>(rows), h);
+  if (act != FWN_ACT_NONE && act != FWN_ACT_SWISH) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  if (rows > 0 && !out) return fail(FWN_ERR_INVALID_ARGUMENT, "null out");
+  for (const void* ptr : {e_proj, s_proj, r_proj, bias, static_cast<const void*>(out)})
+    if (ptr && !aligned16(ptr)) return fail(FWN_ERR_INVALID_ARGUMENT, "operands must be 16-byte aligned");
+  cudaError_t e = fwn::launch_gather_add_act(e_proj, s_proj, senders, r_proj, receivers, bias, rows, h,
+                                             act == FWN_ACT_SWISH, out,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather_add_act");
+  return ok();
+}
+
+fwn_status fwn_gnn_ln_segment_sum(const void* m, const int32_t* seg_ptr, int64_t n_out, int32_t f, const void* gamma,
+                                  const void* beta, float eps, float norm, const float* residual, void* out,
+                                  int32_t out_dtype, void* stream) {
+  if (n_out < 0 || !(eps > 0.f)) return fail(FWN_ERR_INVALID_ARGUMENT, "bad n_out=%lld or eps", static_cast<long long>(n_out));
+  if (f != 256 && f != 512 && f != 1024) return fail(FWN_ERR_UNSUPPORTED, "f=%d not built (256, 512, 1024)", f);
+  if (out_dtype != FWN_DTYPE_BF16 && out_dtype != FWN_DTYPE_F32)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown out dtype %d", out_dtype);
+  if (n_out > 0 && (!m || !gamma || !beta || !out)) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  for (const void* ptr : {m, gamma, beta, static_cast<const void*>(residual), static_cast<const void*>(out)})
+    if (ptr && !aligned16(ptr)) return fail(FWN_ERR_INVALID_ARGUMENT, "operands must be 16-byte aligned");
+  cudaError_t e = fwn::launch_ln_segment_sum(m, seg_ptr, n_out, f, gamma, beta, eps, norm, residual, out,
+                                             out_dtype == FWN_DTYPE_BF16, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "ln_segment_sum");
+  return ok();
+}
+
 int32_t fwn_bitset_words(int32_t n_cols) { return n_cols > 0 ? fwn::bitset_words(n_cols) : 0; }
 
 namespace {

@@ -60,4 +60,13 @@ cudaError_t launch_cond_layernorm(float* x, int64_t rows, int d, int rows_per_sa
                                   const float* so, float eps, void* out, bool bf16_out, const void* residual,
                                   cudaStream_t stream);
 
+// Interaction-network pieces (gnn.cu): h = act(E + S[snd] + R[rcv] + bias) (bf16), and out[i] = norm * sum over the
+// receiver's sorted edge run of LN(m[e]) (+ residual[i]).
+cudaError_t launch_gather_add_act(const void* e_proj, const void* s_proj, const int32_t* snd, const void* r_proj,
+                                  const int32_t* rcv, const void* bias, int64_t rows, int h, bool swish, void* out,
+                                  cudaStream_t stream);
+cudaError_t launch_ln_segment_sum(const void* m, const int32_t* seg, int64_t n_out, int f, const void* gamma,
+                                  const void* beta, float eps, float norm, const float* residual, void* out,
+                                  bool bf16_out, cudaStream_t stream);
+
 }  // namespace fwn

@@ -24,6 +24,7 @@ MODE_TF32 = 1
 MODE_TF32X3 = 2
 ACT_NONE = 0
 ACT_GELU_TANH = 1
+ACT_SWISH = 2
 
 # Every symbol include/fwn_attn.h declares.
 SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_rows",
@@ -32,7 +33,7 @@ SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_
            "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv", "fwn_attn_bwd_noalloc",
            "fwn_bitset_words", "fwn_khop_bitset", "fwn_walk_bitset", "fwn_bitset_csr_count", "fwn_bitset_csr_fill",
            "fwn_cond_layernorm", "fwn_cond_layernorm_scatter", "fwn_cond_layernorm_residual",
-           "fwn_gemm_bf16", "fwn_test_attn_fwd_timeout")
+           "fwn_gemm_bf16", "fwn_gnn_gather_add_act", "fwn_gnn_ln_segment_sum", "fwn_test_attn_fwd_timeout")
 
 
 class AttnDesc(ctypes.Structure):
@@ -83,6 +84,8 @@ def _declare(lib):
       "fwn_cond_layernorm_scatter": [_P, ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P],
       "fwn_cond_layernorm_residual": [_P, _P, ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P],
       "fwn_gemm_bf16": [_P, _P, _P, _P, ctypes.c_int64, _I, _I, _I, _P],
+      "fwn_gnn_gather_add_act": [_P, _P, _P, _P, _P, _P, ctypes.c_int64, _I, _I, _P, _P],
+      "fwn_gnn_ln_segment_sum": [_P, _P, ctypes.c_int64, _I, _P, _P, ctypes.c_float, ctypes.c_float, _P, _P, _I, _P],
       "fwn_bitset_csr_count": [_P, _I, _I, _P, _P, _SZ, _P],
       "fwn_bitset_csr_fill": [_P, _I, _I, _P, _P, _P],
       "fwn_attn_fwd": [ctypes.POINTER(AttnDesc), _P, _P, _P, ctypes.POINTER(TileList), _P, _P, _P],

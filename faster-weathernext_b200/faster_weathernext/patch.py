@@ -6,9 +6,10 @@
   reorder       Hilbert order of the mesh nodes in transformer_tiles (patch.py:210-213);
   strict_fp32   passed to the attention as the reference's tiled_mha does (patch.py:173-174): it matters only
                 under default_matmul_precision("highest"), where IEEE float32 dots are asked for (not built);
-  remat         the processor recomputes each block's activations in the backward (patch.py:69-73).
-The others configure parts of the reference outside the attention path (its XLA attention fallback's chunk,
-the grid / mesh GNN, encoder and decoder blocking, Haiku's layer loop, sequential samples in training); they are
+  remat         the processor recomputes each block's activations in the backward (patch.py:69-73);
+  edge_chunk    edges per block of the grid <-> mesh interaction network (faster_weathernext.gnn).
+The others configure parts of the reference this build does not include (its XLA attention fallback's chunk, the
+node blocking of the GNNs, encoder and decoder, Haiku's layer loop, sequential samples in training); they are
 accepted so that option sets written for the reference keep working, and setting one to a non-default value
 warns that it has no effect here.
 
@@ -48,8 +49,8 @@ NO_EFFECT = {
     "replace_attention": "which attention types of the official configs are routed to the fused kernel "
                          "(every attention here is the fused kernel)",
     "attn_chunk": "the query chunk of the reference's XLA attention fallback (not built: no fallback)",
-    "grid_chunk": "the grid / mesh GNN, encoder and decoder blocking (outside the attention path)",
-    "edge_chunk": "the grid -> mesh GNN's edge blocking (outside the attention path)",
+    "grid_chunk": "the node blocking of the grid / mesh GNNs, encoder and decoder (the interaction network here "
+                  "processes all nodes at once; edge_chunk blocks its edges)",
     "layer_loop": "Haiku's scan over the transformer layers (the torch processor runs its layers eagerly)",
     "sequential_samples": "the reference's training loop over samples (DataParallelStep's micro_batch sets "
                           "how many members run together)",

@@ -210,9 +210,30 @@ FWN_API fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, i
  * [n, k] (the weight with k contiguous), bias bf16 [n] or NULL, c row-major bf16 [m, n]; float32 accumulation on the
  * tensor cores. n a multiple of 256, k a multiple of 64, pointers 16-byte aligned. act: FWN_ACT_NONE or
  * FWN_ACT_GELU_TANH (0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), jax.nn.gelu's default form). */
-typedef enum fwn_act { FWN_ACT_NONE = 0, FWN_ACT_GELU_TANH = 1 } fwn_act;
+typedef enum fwn_act { FWN_ACT_NONE = 0, FWN_ACT_GELU_TANH = 1, FWN_ACT_SWISH = 2 } fwn_act;
 FWN_API fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n,
                                  int32_t k, int32_t act, void* stream);
+
+/* ---- grid <-> mesh interaction networks -------------------------------------------------------------------
+ * The blocked GNNs of the encoder / decoder (src/faster_weathernext/patch.py:347-509, ChunkedDeepGNN: edge MLP on
+ * (edge, sender, receiver) features with the first layer's matmul applied per node before the gather, a sorted
+ * segment-sum of the messages into the receivers, a node MLP); the matmuls run on fwn_gemm_bf16.
+ *
+ * h[e, :] = act(e_proj[e, :] + s_proj[senders[e], :] + r_proj[receivers[e], :] + bias), bf16 [rows, h] each (h a
+ * multiple of 8); any of e_proj / s_proj / r_proj / bias may be NULL (left out), senders / receivers may be NULL
+ * (row e itself). act: FWN_ACT_NONE or FWN_ACT_SWISH (x sigmoid(x)). */
+FWN_API fwn_status fwn_gnn_gather_add_act(const void* e_proj, const void* s_proj, const int32_t* senders,
+                                          const void* r_proj, const int32_t* receivers, const void* bias, int64_t rows,
+                                          int32_t h, int32_t act, void* out, void* stream);
+
+/* out[i, :] = norm * sum_{e = seg_ptr[i]}^{seg_ptr[i+1]-1} LN(m[e, :]) (+ residual[i, :]): LayerNorm of each message
+ * row (eps, scale gamma, offset beta: bf16 [f]) summed over the receiver's edges, which the caller sorts by receiver
+ * (seg_ptr [n_out + 1], the CSR offsets of the runs; NULL: row i alone, for a node MLP's output norm); residual
+ * float32 [n_out, f] or NULL; out [n_out, f] float32 or bf16 (out_dtype). m bf16 [edges, f], f in {256, 512, 1024}.
+ * One warp per receiver, no atomics: deterministic. */
+FWN_API fwn_status fwn_gnn_ln_segment_sum(const void* m, const int32_t* seg_ptr, int64_t n_out, int32_t f,
+                                          const void* gamma, const void* beta, float eps, float norm,
+                                          const float* residual, void* out, int32_t out_dtype, void* stream);
 
 /* ---- attention --------------------------------------------------------------------------------------- */
 

@@ -76,7 +76,7 @@ def test_layout_helpers_on_host():
 
 def test_options_without_effect_warn_and_acted_on_options_do_not():
   """Options that configure parts of the reference outside this build warn when set away from their defaults;
-  reorder, strict_fp32, remat and attention are acted on and do not."""
+  reorder, strict_fp32, remat, edge_chunk and attention are acted on and do not."""
   import warnings
   import faster_weathernext
   from faster_weathernext import patch
@@ -84,8 +84,8 @@ def test_options_without_effect_warn_and_acted_on_options_do_not():
     with warnings.catch_warnings():
       warnings.simplefilter("error")
       faster_weathernext.enable(force=True, reorder=False, strict_fp32=True, remat=True, attention="tiled",
-                                grid_chunk=32768)
-    for name, value in (("edge_chunk", 1024), ("layer_loop", False), ("sequential_samples", True),
+                                grid_chunk=32768, edge_chunk=1024)
+    for name, value in (("grid_chunk", 1024), ("layer_loop", False), ("sequential_samples", True),
                         ("replace_attention", False)):
       with pytest.warns(UserWarning, match=name):
         faster_weathernext.enable(force=True, **{name: value})
