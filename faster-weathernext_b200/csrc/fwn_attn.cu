@@ -4,7 +4,9 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -135,7 +137,27 @@ fwn_status check_desc(const fwn_attn_desc* d) {
   if (d->stride_h < d->head_dim || d->stride_n <= 0 || d->stride_b <= 0 || d->out_stride_h < d->head_dim ||
       d->out_stride_n <= 0 || d->out_stride_b <= 0)
     return fail(FWN_ERR_INVALID_ARGUMENT, "strides must be positive and rows must not overlap");
+  if (d->flags & ~static_cast<int32_t>(FWN_DESC_GRAD_STRIDES))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown desc flags 0x%x", static_cast<unsigned>(d->flags));
+  if (d->flags & FWN_DESC_GRAD_STRIDES) {
+    if ((d->grad_stride_h * es) % 16 || (d->grad_stride_n * es) % 16 || (d->grad_stride_b * es) % 16)
+      return fail(FWN_ERR_INVALID_ARGUMENT, "gradient strides must be multiples of 16 bytes");
+    if (d->grad_stride_h < d->head_dim || d->grad_stride_n <= 0 || d->grad_stride_b <= 0)
+      return fail(FWN_ERR_INVALID_ARGUMENT, "gradient strides must be positive and rows must not overlap");
+  }
   return FWN_OK;
+}
+
+// The descriptor with its gradient strides resolved (the out strides unless FWN_DESC_GRAD_STRIDES is set). Reads
+// the grad_stride fields only when the flag is set: a caller's struct may end at out_stride_h.
+fwn_attn_desc resolve_grad_strides(const fwn_attn_desc* desc) {
+  fwn_attn_desc d;
+  std::memcpy(&d, desc, offsetof(fwn_attn_desc, grad_stride_b));
+  const bool own = (desc->flags & FWN_DESC_GRAD_STRIDES) != 0;
+  d.grad_stride_b = own ? desc->grad_stride_b : d.out_stride_b;
+  d.grad_stride_n = own ? desc->grad_stride_n : d.out_stride_n;
+  d.grad_stride_h = own ? desc->grad_stride_h : d.out_stride_h;
+  return d;
 }
 
 fwn_status check_tiles(const fwn_tile_list* t, const fwn_attn_desc* d, const char* name) {
@@ -389,9 +411,9 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   p.delta = delta;
   p.out0 = out0;
   p.out1 = out1;
-  p.o_sb = d.out_stride_b;
-  p.o_sn = d.out_stride_n;
-  p.o_sh = d.out_stride_h;
+  p.o_sb = d.grad_stride_b;  // dq / dk / dv stores
+  p.o_sn = d.grad_stride_n;
+  p.o_sh = d.grad_stride_h;
   p.heads = d.heads;
   p.n = d.n;
   p.np = t.n_blocks;
@@ -449,9 +471,9 @@ fwn_status launch_bwd_wide(const fwn_attn_desc& d, const void* q, const void* k,
   p.delta = delta;
   p.out0 = out0;
   p.out1 = out1;
-  p.o_sb = d.out_stride_b;
-  p.o_sn = d.out_stride_n;
-  p.o_sh = d.out_stride_h;
+  p.o_sb = d.grad_stride_b;  // dq / dk / dv stores
+  p.o_sn = d.grad_stride_n;
+  p.o_sh = d.grad_stride_h;
   p.heads = d.heads;
   p.n = d.n;
   p.np = t.n_blocks;
@@ -685,9 +707,9 @@ fwn_status fwn_hilbert_codes(const double* lat_deg, const double* lon_deg, int32
 
 namespace {
 
-fwn_status cond_layernorm(float* x, int64_t rows, int32_t d, int32_t rows_per_sample, const int32_t* out_node,
-                          const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream,
-                          const void* residual = nullptr) {
+fwn_status cond_layernorm(const float* x, float* x_out, int64_t rows, int32_t d, int32_t rows_per_sample,
+                          const int32_t* out_node, const float* scale_offset, float eps, void* out, int32_t out_dtype,
+                          void* stream, const void* residual = nullptr) {
   if (rows < 0 || rows_per_sample <= 0 || !(eps > 0.f))
     return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld, rows_per_sample=%d or eps", static_cast<long long>(rows),
                 rows_per_sample);
@@ -700,8 +722,9 @@ fwn_status cond_layernorm(float* x, int64_t rows, int32_t d, int32_t rows_per_sa
   if (rows % rows_per_sample != 0)
     return fail(FWN_ERR_INVALID_ARGUMENT, "rows=%lld is not a multiple of rows_per_sample=%d",
                 static_cast<long long>(rows), rows_per_sample);
-  if (residual && rows > 0 && !aligned16(residual)) return fail(FWN_ERR_INVALID_ARGUMENT, "residual must be 16-byte aligned");
-  cudaError_t e = fwn::launch_cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out,
+  if (residual && rows > 0 && (!aligned16(residual) || !x_out || !aligned16(x_out)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "residual and x_out must be non-null and 16-byte aligned");
+  cudaError_t e = fwn::launch_cond_layernorm(x, x_out, rows, d, rows_per_sample, out_node, scale_offset, eps, out,
                                              out_dtype == FWN_DTYPE_BF16, residual, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cond_layernorm");
   return ok();
@@ -711,23 +734,63 @@ fwn_status cond_layernorm(float* x, int64_t rows, int32_t d, int32_t rows_per_sa
 
 fwn_status fwn_cond_layernorm(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
                               const float* scale_offset, float eps, void* out, int32_t out_dtype, void* stream) {
-  return cond_layernorm(const_cast<float*>(x), rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype,
-                        stream);
+  return cond_layernorm(x, nullptr, rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype, stream);
 }
 
 fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, int64_t rows, int32_t d, int32_t rows_per_sample,
                                        const int32_t* out_node, const float* scale_offset, float eps, void* out,
                                        int32_t out_dtype, void* stream) {
   if (rows > 0 && !residual) return fail(FWN_ERR_INVALID_ARGUMENT, "null residual");
-  return cond_layernorm(x, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream, residual);
+  return cond_layernorm(x, x, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream, residual);
+}
+
+fwn_status fwn_cond_layernorm_add(const float* x, const void* residual, float* x_out, int64_t rows, int32_t d,
+                                  int32_t rows_per_sample, const float* scale_offset, float eps, void* out,
+                                  int32_t out_dtype, void* stream) {
+  if (rows > 0 && !residual) return fail(FWN_ERR_INVALID_ARGUMENT, "null residual");
+  return cond_layernorm(x, x_out, rows, d, rows_per_sample, nullptr, scale_offset, eps, out, out_dtype, stream,
+                        residual);
 }
 
 fwn_status fwn_cond_layernorm_scatter(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
                                       const int32_t* out_node, const float* scale_offset, float eps, void* out,
                                       int32_t out_dtype, void* stream) {
   if (rows > 0 && !out_node) return fail(FWN_ERR_INVALID_ARGUMENT, "null out_node");
-  return cond_layernorm(const_cast<float*>(x), rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype,
-                        stream);
+  return cond_layernorm(x, nullptr, rows, d, rows_per_sample, out_node, scale_offset, eps, out, out_dtype, stream);
+}
+
+size_t fwn_cond_layernorm_bwd_workspace(int64_t rows, int32_t d, int32_t rows_per_sample) {
+  if (rows <= 0 || rows_per_sample <= 0 || d <= 0) return 0;
+  return fwn::cond_layernorm_bwd_workspace(rows, d, rows_per_sample);
+}
+
+fwn_status fwn_cond_layernorm_bwd(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                  const float* scale_offset, float eps, const void* dy, int32_t dy_dtype,
+                                  const float* dx_in, float* dx, void* dx_bf16, float* dscale_offset, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (rows < 0 || rows_per_sample <= 0 || !(eps > 0.f))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "bad rows=%lld, rows_per_sample=%d or eps", static_cast<long long>(rows),
+                rows_per_sample);
+  if (d != 128 && d != 256 && d != 512) return fail(FWN_ERR_UNSUPPORTED, "d=%d not built for the backward", d);
+  if (dy_dtype != FWN_DTYPE_BF16 && dy_dtype != FWN_DTYPE_F32)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown dy dtype %d", dy_dtype);
+  if (rows % rows_per_sample != 0)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "rows=%lld is not a multiple of rows_per_sample=%d",
+                static_cast<long long>(rows), rows_per_sample);
+  if (rows == 0) return ok();
+  if (!x || !scale_offset || !dy || !dx || !dscale_offset || !workspace)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(x) || !aligned16(scale_offset) || !aligned16(dy) || !aligned16(dx) ||
+      (dx_in && !aligned16(dx_in)) || (dx_bf16 && !aligned16(dx_bf16)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const size_t need = fwn::cond_layernorm_bwd_workspace(rows, d, rows_per_sample);
+  if (workspace_bytes < need)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  cudaError_t e = fwn::launch_cond_layernorm_bwd(x, rows, d, rows_per_sample, scale_offset, eps, dy,
+                                                 dy_dtype == FWN_DTYPE_BF16, dx_in, dx, dx_bf16, dscale_offset,
+                                                 workspace, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cond_layernorm_bwd");
+  return ok();
 }
 
 namespace {
@@ -1014,7 +1077,7 @@ fwn_status bwd_dispatch(const fwn_attn_desc* desc, const void* q, const void* k,
   if (!ws || ws_bytes < need || !aligned16(ws))
     return fail(FWN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed", need);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const fwn_attn_desc& d = *desc;
+  const fwn_attn_desc d = resolve_grad_strides(desc);
   float* delta = static_cast<float*>(const_cast<void*>(ws));
   if (d.mode == FWN_MODE_BF16) {
     if (d.head_dim == 64) return launch_bwd<64, false>(d, q, k, v, o, lse, d_o, tiles, tiles_t, dq, dk, dv, delta, parts, st);

@@ -20,23 +20,25 @@ namespace fwn {
 namespace {
 
 template <int D, bool BF16_OUT, bool RES>
-__global__ void __launch_bounds__(256) cond_layernorm_kernel(float* __restrict__ x, int64_t rows, int rows_per_sample,
+__global__ void __launch_bounds__(256) cond_layernorm_kernel(const float* x_in, float* x_out, int64_t rows,
+                                                              int rows_per_sample,
                                                               const int32_t* __restrict__ out_node,
                                                               const float* __restrict__ scale_offset, float eps,
                                                               void* __restrict__ out,
                                                               const __nv_bfloat16* __restrict__ residual) {
+  // x_out (RES only) may be x_in itself (the residual stream updated in place): plain loads.
   constexpr int V = D / 128;  // float4 per lane
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;  // whole warps leave together (rows are warp-uniform)
-  float4* xr = reinterpret_cast<float4*>(x + row * D);
+  const float4* xr = reinterpret_cast<const float4*>(x_in + row * D);
   float4 v[V];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
+    v[i] = xr[lane + 32 * i];
     if constexpr (RES) {
-      // x += residual (4 bf16 per lane and step), written back to the residual stream.
-      v[i] = xr[lane + 32 * i];
+      // x_out = x_in + residual (4 bf16 per lane and step).
       const uint2 r = __ldg(reinterpret_cast<const uint2*>(residual + row * D) + lane + 32 * i);
       const float2 r01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
       const float2 r23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
@@ -44,9 +46,7 @@ __global__ void __launch_bounds__(256) cond_layernorm_kernel(float* __restrict__
       v[i].y += r01.y;
       v[i].z += r23.x;
       v[i].w += r23.y;
-      xr[lane + 32 * i] = v[i];
-    } else {
-      v[i] = __ldg(xr + lane + 32 * i);
+      reinterpret_cast<float4*>(x_out + row * D)[lane + 32 * i] = v[i];
     }
     sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
@@ -93,38 +93,202 @@ __global__ void __launch_bounds__(256) cond_layernorm_kernel(float* __restrict__
 }
 
 template <int D, bool RES>
-cudaError_t launch(float* x, int64_t rows, int rows_per_sample, const int32_t* out_node, const float* so, float eps,
-                   void* out, bool bf16_out, const __nv_bfloat16* residual, cudaStream_t stream) {
+cudaError_t launch(const float* x, float* x_out, int64_t rows, int rows_per_sample, const int32_t* out_node,
+                   const float* so, float eps, void* out, bool bf16_out, const __nv_bfloat16* residual,
+                   cudaStream_t stream) {
   const int64_t threads = rows * 32;
   const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
   if (bf16_out)
-    cond_layernorm_kernel<D, true, RES><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, out_node, so, eps, out,
-                                                                  residual);
+    cond_layernorm_kernel<D, true, RES><<<grid, 256, 0, stream>>>(x, x_out, rows, rows_per_sample, out_node, so, eps,
+                                                                  out, residual);
   else
-    cond_layernorm_kernel<D, false, RES><<<grid, 256, 0, stream>>>(x, rows, rows_per_sample, out_node, so, eps, out,
-                                                                   residual);
+    cond_layernorm_kernel<D, false, RES><<<grid, 256, 0, stream>>>(x, x_out, rows, rows_per_sample, out_node, so, eps,
+                                                                   out, residual);
   return cudaGetLastError();
 }
 
 template <int D>
-cudaError_t launch_d(float* x, int64_t rows, int rows_per_sample, const int32_t* out_node, const float* so, float eps,
-                     void* out, bool bf16_out, const __nv_bfloat16* residual, cudaStream_t stream) {
-  return residual ? launch<D, true>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, residual, stream)
-                  : launch<D, false>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, residual, stream);
+cudaError_t launch_d(const float* x, float* x_out, int64_t rows, int rows_per_sample, const int32_t* out_node,
+                     const float* so, float eps, void* out, bool bf16_out, const __nv_bfloat16* residual,
+                     cudaStream_t stream) {
+  return residual ? launch<D, true>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, residual, stream)
+                  : launch<D, false>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, residual,
+                                     stream);
+}
+
+// Backward of y = LN(x) (1 + scale[s]) + offset[s] (x the normalised input, i.e. the residual stream after any add):
+//   g = dy (1 + scale[s]),  dx = dx_in + rstd (g - mean(g) - xhat mean(g xhat))   (one warp per row)
+//   dscale[s, j] = sum over the sample's rows of dy xhat,  doffset[s, j] = sum of dy  (per-CTA column partials: each
+//   CTA takes kBwdRows consecutive rows of one sample; reduced per sample by cond_layernorm_part_sum_kernel).
+constexpr int kBwdRows = 128;
+
+template <int D, bool DY_BF16>
+__global__ void __launch_bounds__(256) cond_layernorm_bwd_kernel(const float* __restrict__ x, int rows_per_sample,
+                                                                  int ctas_per_sample,
+                                                                  const float* __restrict__ scale_offset, float eps,
+                                                                  const void* __restrict__ dy,
+                                                                  const float* dx_in,
+                                                                  float* dx,
+                                                                  __nv_bfloat16* __restrict__ dx_bf16,
+                                                                  float* __restrict__ part) {
+  constexpr int V = D / 128;
+  __shared__ float red[8][2 * D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sample = blockIdx.x / ctas_per_sample, chunk = blockIdx.x % ctas_per_sample;
+  const int64_t r0 = static_cast<int64_t>(sample) * rows_per_sample + static_cast<int64_t>(chunk) * kBwdRows;
+  const int64_t r1 = static_cast<int64_t>(sample) * rows_per_sample +
+                     min(static_cast<int64_t>(chunk + 1) * kBwdRows, static_cast<int64_t>(rows_per_sample));
+  float4 sc[V], ds[V], dof[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    sc[i] = __ldg(reinterpret_cast<const float4*>(scale_offset + static_cast<int64_t>(sample) * 2 * D) + lane + 32 * i);
+    ds[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dof[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t row = r0 + warp; row < r1; row += 8) {
+    float4 v[V], d[V];
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      v[i] = __ldg(reinterpret_cast<const float4*>(x + row * D) + lane + 32 * i);
+      s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      if constexpr (DY_BF16) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(dy) + row * D) + lane + 32 * i);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        d[i] = make_float4(a.x, a.y, b.x, b.y);
+      } else {
+        d[i] = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(dy) + row * D) + lane + 32 * i);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    const float mean = s1 * (1.f / D);
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+      s2 += (a * a + b * b) + (c * c + e * e);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float rstd = rsqrtf(s2 * (1.f / D) + eps);
+    float sg = 0.f, sgx = 0.f;
+    float4 xh[V], g[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      xh[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
+      g[i] = make_float4(d[i].x * (1.f + sc[i].x), d[i].y * (1.f + sc[i].y), d[i].z * (1.f + sc[i].z),
+                         d[i].w * (1.f + sc[i].w));
+      sg += (g[i].x + g[i].y) + (g[i].z + g[i].w);
+      sgx += (g[i].x * xh[i].x + g[i].y * xh[i].y) + (g[i].z * xh[i].z + g[i].w * xh[i].w);
+      ds[i].x += d[i].x * xh[i].x; ds[i].y += d[i].y * xh[i].y; ds[i].z += d[i].z * xh[i].z; ds[i].w += d[i].w * xh[i].w;
+      dof[i].x += d[i].x; dof[i].y += d[i].y; dof[i].z += d[i].z; dof[i].w += d[i].w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sg += __shfl_xor_sync(0xffffffffu, sg, o);
+      sgx += __shfl_xor_sync(0xffffffffu, sgx, o);
+    }
+    const float mg = sg * (1.f / D), mgx = sgx * (1.f / D);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float4 r = make_float4(rstd * (g[i].x - mg - xh[i].x * mgx), rstd * (g[i].y - mg - xh[i].y * mgx),
+                             rstd * (g[i].z - mg - xh[i].z * mgx), rstd * (g[i].w - mg - xh[i].w * mgx));
+      if (dx_in) {
+        const float4 a = reinterpret_cast<const float4*>(dx_in + row * D)[lane + 32 * i];  // may be dx
+        r.x += a.x; r.y += a.y; r.z += a.z; r.w += a.w;
+      }
+      reinterpret_cast<float4*>(dx + row * D)[lane + 32 * i] = r;
+      if (dx_bf16) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(r.x, r.y), hi = __floats2bfloat162_rn(r.z, r.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+        reinterpret_cast<uint2*>(dx_bf16 + row * D)[lane + 32 * i] = pk;
+      }
+    }
+  }
+  // Column partials of the CTA: warps' sums through shared memory, one row of 2 D per CTA.
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    red[warp][c] = ds[i].x; red[warp][c + 1] = ds[i].y; red[warp][c + 2] = ds[i].z; red[warp][c + 3] = ds[i].w;
+    red[warp][D + c] = dof[i].x; red[warp][D + c + 1] = dof[i].y; red[warp][D + c + 2] = dof[i].z;
+    red[warp][D + c + 3] = dof[i].w;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < 2 * D; j += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][j];
+    part[static_cast<int64_t>(blockIdx.x) * 2 * D + j] = t;
+  }
+}
+
+// dso[s, j] = sum over the sample's CTAs of part[cta, j] (fixed order: deterministic).
+__global__ void __launch_bounds__(256) cond_layernorm_part_sum_kernel(const float* __restrict__ part, int samples,
+                                                                       int ctas_per_sample, int width,
+                                                                       float* __restrict__ dso) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(samples) * width) return;
+  const int s = static_cast<int>(idx / width), j = static_cast<int>(idx % width);
+  float t = 0.f;
+  for (int c = 0; c < ctas_per_sample; ++c) t += part[(static_cast<int64_t>(s) * ctas_per_sample + c) * width + j];
+  dso[idx] = t;
+}
+
+template <int D>
+cudaError_t launch_bwd(const float* x, int64_t rows, int rows_per_sample, const float* so, float eps, const void* dy,
+                       bool dy_bf16, const float* dx_in, float* dx, __nv_bfloat16* dx_bf16, float* dso, float* part,
+                       cudaStream_t stream) {
+  const int samples = static_cast<int>(rows / rows_per_sample);
+  const int cps = (rows_per_sample + kBwdRows - 1) / kBwdRows;
+  const unsigned grid = static_cast<unsigned>(samples * cps);
+  if (dy_bf16)
+    cond_layernorm_bwd_kernel<D, true><<<grid, 256, 0, stream>>>(x, rows_per_sample, cps, so, eps, dy, dx_in, dx,
+                                                                 dx_bf16, part);
+  else
+    cond_layernorm_bwd_kernel<D, false><<<grid, 256, 0, stream>>>(x, rows_per_sample, cps, so, eps, dy, dx_in, dx,
+                                                                  dx_bf16, part);
+  const int64_t total = static_cast<int64_t>(samples) * 2 * D;
+  cond_layernorm_part_sum_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(part, samples, cps,
+                                                                                                 2 * D, dso);
+  return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_cond_layernorm(float* x, int64_t rows, int d, int rows_per_sample, const int32_t* out_node,
-                                  const float* so, float eps, void* out, bool bf16_out, const void* residual,
-                                  cudaStream_t stream) {
+cudaError_t launch_cond_layernorm(const float* x, float* x_out, int64_t rows, int d, int rows_per_sample,
+                                  const int32_t* out_node, const float* so, float eps, void* out, bool bf16_out,
+                                  const void* residual, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   const auto* res = static_cast<const __nv_bfloat16*>(residual);
   switch (d) {
-    case 128: return launch_d<128>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
-    case 256: return launch_d<256>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
-    case 512: return launch_d<512>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
-    case 1024: return launch_d<1024>(x, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
+    case 128: return launch_d<128>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
+    case 256: return launch_d<256>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
+    case 512: return launch_d<512>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
+    case 1024: return launch_d<1024>(x, x_out, rows, rows_per_sample, out_node, so, eps, out, bf16_out, res, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+size_t cond_layernorm_bwd_workspace(int64_t rows, int d, int rows_per_sample) {
+  const int64_t samples = rows / rows_per_sample;
+  const int64_t cps = (rows_per_sample + kBwdRows - 1) / kBwdRows;
+  return static_cast<size_t>(samples * cps * 2 * d) * sizeof(float);
+}
+
+cudaError_t launch_cond_layernorm_bwd(const float* x, int64_t rows, int d, int rows_per_sample, const float* so,
+                                      float eps, const void* dy, bool dy_bf16, const float* dx_in, float* dx,
+                                      void* dx_bf16, float* dso, void* ws, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  auto* xb = static_cast<__nv_bfloat16*>(dx_bf16);
+  auto* part = static_cast<float*>(ws);
+  switch (d) {
+    case 128: return launch_bwd<128>(x, rows, rows_per_sample, so, eps, dy, dy_bf16, dx_in, dx, xb, dso, part, stream);
+    case 256: return launch_bwd<256>(x, rows, rows_per_sample, so, eps, dy, dy_bf16, dx_in, dx, xb, dso, part, stream);
+    case 512: return launch_bwd<512>(x, rows, rows_per_sample, so, eps, dy, dy_bf16, dx_in, dx, xb, dso, part, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -56,9 +56,15 @@ cudaError_t launch_bitset_csr_fill(const uint32_t* bits, int n_rows, int n_cols,
 // Conditioned LayerNorm (norm.cu): out = LN(x) * (1 + scale[s]) + offset[s], s = row / rows_per_sample,
 // scale_offset [samples, 2 d]; d in {128, 256, 512, 1024}; out bf16 or float32; out_node (nullable) maps each
 // row within its sample to its output row; residual (nullable, bf16 [rows, d]) is first added into x in place.
-cudaError_t launch_cond_layernorm(float* x, int64_t rows, int d, int rows_per_sample, const int32_t* out_node,
-                                  const float* so, float eps, void* out, bool bf16_out, const void* residual,
-                                  cudaStream_t stream);
+cudaError_t launch_cond_layernorm(const float* x, float* x_out, int64_t rows, int d, int rows_per_sample,
+                                  const int32_t* out_node, const float* so, float eps, void* out, bool bf16_out,
+                                  const void* residual, cudaStream_t stream);
+// Backward of the conditioned norm (x the normalised input): dx (+ dx_in), optional bf16 copy of dx, and the
+// per-sample scale / offset gradients dso [samples, 2 d] through a workspace of per-CTA column partials.
+size_t cond_layernorm_bwd_workspace(int64_t rows, int d, int rows_per_sample);
+cudaError_t launch_cond_layernorm_bwd(const float* x, int64_t rows, int d, int rows_per_sample, const float* so,
+                                      float eps, const void* dy, bool dy_bf16, const float* dx_in, float* dx,
+                                      void* dx_bf16, float* dso, void* ws, cudaStream_t stream);
 
 // Interaction-network pieces (gnn.cu): h = act(E + S[snd] + R[rcv] + bias) (bf16), and out[i] = norm * sum over the
 // receiver's sorted edge run of LN(m[e]) (+ residual[i]).

@@ -22,6 +22,7 @@ DTYPE_F32 = 1
 MODE_BF16 = 0
 MODE_TF32 = 1
 MODE_TF32X3 = 2
+DESC_GRAD_STRIDES = 1
 ACT_NONE = 0
 ACT_GELU_TANH = 1
 ACT_SWISH = 2
@@ -33,15 +34,17 @@ SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_
            "fwn_attn_bwd_delta", "fwn_attn_bwd_dq", "fwn_attn_bwd_dkv", "fwn_attn_bwd_noalloc",
            "fwn_bitset_words", "fwn_khop_bitset", "fwn_walk_bitset", "fwn_bitset_csr_count", "fwn_bitset_csr_fill",
            "fwn_cond_layernorm", "fwn_cond_layernorm_scatter", "fwn_cond_layernorm_residual",
+           "fwn_cond_layernorm_add", "fwn_cond_layernorm_bwd_workspace", "fwn_cond_layernorm_bwd",
            "fwn_gemm_bf16", "fwn_gnn_gather_add_act", "fwn_gnn_ln_segment_sum", "fwn_test_attn_fwd_timeout")
 
 
 class AttnDesc(ctypes.Structure):
   _fields_ = [("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("n", ctypes.c_int32),
               ("head_dim", ctypes.c_int32), ("scale", ctypes.c_float), ("dtype", ctypes.c_int32),
-              ("mode", ctypes.c_int32), ("reserved", ctypes.c_int32), ("stride_b", ctypes.c_int64),
+              ("mode", ctypes.c_int32), ("flags", ctypes.c_int32), ("stride_b", ctypes.c_int64),
               ("stride_n", ctypes.c_int64), ("stride_h", ctypes.c_int64), ("out_stride_b", ctypes.c_int64),
-              ("out_stride_n", ctypes.c_int64), ("out_stride_h", ctypes.c_int64)]
+              ("out_stride_n", ctypes.c_int64), ("out_stride_h", ctypes.c_int64), ("grad_stride_b", ctypes.c_int64),
+              ("grad_stride_n", ctypes.c_int64), ("grad_stride_h", ctypes.c_int64)]
 
 
 class TileList(ctypes.Structure):
@@ -68,6 +71,8 @@ def _declare(lib):
   lib.fwn_lse_rows.restype = _I
   lib.fwn_bitset_words.argtypes = [_I]
   lib.fwn_bitset_words.restype = _I
+  lib.fwn_cond_layernorm_bwd_workspace.argtypes = [ctypes.c_int64, _I, _I]
+  lib.fwn_cond_layernorm_bwd_workspace.restype = _SZ
   sigs = {
       "fwn_device_error": [_P, ctypes.POINTER(_I)],
       "fwn_tiles_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
@@ -83,6 +88,9 @@ def _declare(lib):
       "fwn_cond_layernorm": [_P, ctypes.c_int64, _I, _I, _P, ctypes.c_float, _P, _I, _P],
       "fwn_cond_layernorm_scatter": [_P, ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P],
       "fwn_cond_layernorm_residual": [_P, _P, ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P],
+      "fwn_cond_layernorm_add": [_P, _P, _P, ctypes.c_int64, _I, _I, _P, ctypes.c_float, _P, _I, _P],
+      "fwn_cond_layernorm_bwd": [_P, ctypes.c_int64, _I, _I, _P, ctypes.c_float, _P, _I, _P, _P, _P, _P, _P,
+                                 ctypes.c_size_t, _P],
       "fwn_gemm_bf16": [_P, _P, _P, _P, ctypes.c_int64, _I, _I, _I, _P],
       "fwn_gnn_gather_add_act": [_P, _P, _P, _P, _P, _P, ctypes.c_int64, _I, _I, _P, _P],
       "fwn_gnn_ln_segment_sum": [_P, _P, ctypes.c_int64, _I, _P, _P, ctypes.c_float, ctypes.c_float, _P, _P, _I, _P],

@@ -115,11 +115,11 @@ def tiled_mha(x, w_qkv, w_out, tiles: "tiled_attn.AttentionTiles", heads: int, k
   tiled_attn.default_matmul_precision block), then the output projection.
 
   x [B, n, d]; w_qkv [d, heads * 3 * key_size], output columns ordered [head, (q, k, v), key_size] so that q, k, v
-  are strided [B, n, heads, key_size] views of one GEMM's output (the kernels read them in place, no copies);
+  are strided [B, n, heads, key_size] views of one GEMM's output (the kernels read them in place, no copies, and
+  the backward writes their gradients into one [B, n, heads, 3, key_size] tensor, tiled_attn.attention_qkv);
   w_out [heads * key_size, d_out]; b_out [d_out] or None. Returns [B, n, d_out] in x's dtype."""
   b, n, _ = x.shape
   qkv = (x @ w_qkv).view(b, n, heads, 3, key_size)
-  q, k, v = qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2]
-  out = tiled_attn.attention(q, k, v, tiles, scale=key_size ** -0.5, strict_fp32=OPTIONS.strict_fp32)
+  out = tiled_attn.attention_qkv(qkv, tiles, scale=key_size ** -0.5, strict_fp32=OPTIONS.strict_fp32)
   out = out.reshape(b, n, heads * key_size)
   return out @ w_out if b_out is None else torch.addmm(b_out, out.view(b * n, -1), w_out).view(b, n, -1)

@@ -52,6 +52,64 @@ def _glorot(gen, fan_in, fan_out, device):
   return torch.nn.Parameter(w)
 
 
+class _CondNorm(torch.autograd.Function):
+  """Differentiable fused conditioned norm of the training path: h = cond_norm(x) or, with a sub-block output a,
+  (x + a, cond_norm(x + a)). x float32 [M, d] (M = samples x rows_per_sample), a bf16 [M, d] or None, so float32
+  [samples, 2 d] (per-sample scale, offset). Forward: one pass (fwn_cond_layernorm / fwn_cond_layernorm_add);
+  backward: one pass for dx (plus the incoming gradient of x + a, plus the bf16 gradient of a) and one small
+  deterministic reduction for the scale / offset gradient (fwn_cond_layernorm_bwd). Replaces the add, LayerNorm,
+  multiply-add, casts and their backward kernels of the composed torch form, _cond_norm."""
+
+  @staticmethod
+  def forward(ctx, x, a, so, rows_per_sample, out_dtype):
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    m, d = x.shape
+    h = torch.empty(m, d, dtype=out_dtype, device=x.device)
+    code = _lib.DTYPE_BF16 if out_dtype == torch.bfloat16 else _lib.DTYPE_F32
+    ctx.rows_per_sample = rows_per_sample
+    ctx.has_a = a is not None
+    ctx.set_materialize_grads(False)
+    if a is None:
+      _lib.check(lib.fwn_cond_layernorm(x.data_ptr(), m, d, rows_per_sample, so.data_ptr(), _EPS, h.data_ptr(), code,
+                                        stream))
+      ctx.save_for_backward(x, so)
+      return h
+    xn = torch.empty_like(x)
+    _lib.check(lib.fwn_cond_layernorm_add(x.data_ptr(), a.data_ptr(), xn.data_ptr(), m, d, rows_per_sample,
+                                          so.data_ptr(), _EPS, h.data_ptr(), code, stream))
+    ctx.save_for_backward(xn, so)
+    return xn, h
+
+  @staticmethod
+  def backward(ctx, *grads):
+    xn, so = ctx.saved_tensors
+    g_xn, g_h = (grads[0], grads[1]) if ctx.has_a else (None, grads[0])
+    m, d = xn.shape
+    if g_h is None:
+      g_h = torch.zeros(m, d, dtype=torch.float32, device=xn.device)
+    if g_h.dtype not in (torch.bfloat16, torch.float32):
+      g_h = g_h.float()
+    g_h = g_h.contiguous()
+    if g_xn is not None:
+      g_xn = g_xn.float().contiguous()
+    lib = _lib.lib()
+    dx = torch.empty_like(xn)
+    da = torch.empty(m, d, dtype=torch.bfloat16, device=xn.device) if ctx.has_a else None
+    dso = torch.empty_like(so)
+    nbytes = lib.fwn_cond_layernorm_bwd_workspace(m, d, ctx.rows_per_sample)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=xn.device)
+    _lib.check(lib.fwn_cond_layernorm_bwd(
+        xn.data_ptr(), m, d, ctx.rows_per_sample, so.data_ptr(), _EPS, g_h.data_ptr(),
+        _lib.DTYPE_BF16 if g_h.dtype == torch.bfloat16 else _lib.DTYPE_F32,
+        g_xn.data_ptr() if g_xn is not None else None, dx.data_ptr(), da.data_ptr() if da is not None else None,
+        dso.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream))
+    return dx, da, dso, None, None
+
+
+_EPS = 1e-5
+
+
 class Processor(torch.nn.Module):
   """Random-init processor; parameters float32, compute in `dtype` (bf16 by default)."""
 
@@ -77,6 +135,9 @@ class Processor(torch.nn.Module):
       self.blocks.append(blk)
     self.cond_final = _glorot(gen, cfg.cond_dim, 2 * d, dev)
     self._bf16_cache = {}
+    # With autograd and bf16 compute: the fused differentiable norms (_forward_train); False selects the composed
+    # torch form of the same blocks (_block), which other dtypes and widths take.
+    self.fused_training = True
 
   def _bf16_t(self, p: torch.Tensor) -> torch.Tensor:
     """bf16 copy of p's transpose (contiguous), the K-major weight operand of fwn_gemm_bf16; cached as _bf16."""
@@ -144,6 +205,8 @@ class Processor(torch.nn.Module):
     fused_ok = x.dtype == torch.float32 and d in (128, 256, 512, 1024)
     if not torch.is_grad_enabled() and dtype == torch.bfloat16 and fused_ok:
       return self._forward_fused(x, cond.expand(b, -1), tiles, perm)
+    if dtype == torch.bfloat16 and fused_ok and d <= 512 and self.fused_training:
+      return self._forward_train(x, cond.expand(b, -1), tiles, perm)
     c = cond.to(dtype)
     if perm is not None:
       x = x.index_select(1, perm)
@@ -165,6 +228,48 @@ class Processor(torch.nn.Module):
     h = self._cond_norm(x, c, blk.cond2).to(dtype)
     m = F.gelu(h @ blk.w1.to(dtype) + blk.b1.to(dtype), approximate="tanh")
     return x + (m @ blk.w2.to(dtype) + blk.b2.to(dtype)).to(x.dtype)
+
+  def _forward_train(self, x, cond, tiles, perm=None):
+    """The autograd path with the fused differentiable norms (_CondNorm): each norm also adds the previous
+    sub-block's bf16 output into the float32 residual stream, and its backward is one pass plus a per-sample
+    reduction. The projections and the MLP are torch ops (cuBLAS), the attention is patch.tiled_mha; the
+    conditioning's scale / offset are computed in float32. x float32 [B, n, d]; cond [B, cond_dim]."""
+    b, n, d = x.shape
+    if perm is not None:
+      x = x.index_select(1, perm)
+    xs = x.reshape(b * n, d).contiguous()
+    cf = cond.float()
+    remat = patch.OPTIONS.remat
+    pending = None
+    for blk in self.blocks:
+      so1 = cf @ blk.cond1.float()
+      so2 = cf @ blk.cond2.float()
+      if remat:
+        xs, pending = torch.utils.checkpoint.checkpoint(self._block_train, xs, pending, so1, so2, blk, tiles, b, n,
+                                                        use_reentrant=False)
+      else:
+        xs, pending = self._block_train(xs, pending, so1, so2, blk, tiles, b, n)
+    so = cf @ self.cond_final.float()
+    y = _CondNorm.apply(xs, pending, so, n, torch.float32)[1] if pending is not None else \
+        _CondNorm.apply(xs, None, so, n, torch.float32)
+    y = y.view(b, n, d)
+    if perm is not None:
+      y = y.index_select(1, torch.argsort(perm))
+    return y
+
+  def _block_train(self, xs, pending, so1, so2, blk, tiles, b, n):
+    """One pre-LN block on the fused norms: returns the residual stream after the attention's add and the MLP's
+    bf16 output, which the next norm adds (xs float32 [b n, d]; pending bf16 [b n, d] or None)."""
+    bf = torch.bfloat16
+    d = xs.shape[1]
+    if pending is None:
+      h = _CondNorm.apply(xs, None, so1, n, bf)
+    else:
+      xs, h = _CondNorm.apply(xs, pending, so1, n, bf)
+    a = self._mha(h.view(b, n, d), blk.w_qkv.to(bf), blk.w_out.to(bf), tiles).reshape(b * n, d)
+    xs, h = _CondNorm.apply(xs, a, so2, n, bf)
+    mlp = F.gelu(torch.addmm(blk.b1.to(bf), h, blk.w1.to(bf)), approximate="tanh")
+    return xs, torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf))
 
   def _forward_fused(self, x, cond, tiles, perm=None):
     """Inference: the same blocks with the LayerNorm, conditioning and cast in one kernel per norm, which also adds

@@ -408,15 +408,22 @@ def _mode_for(dtype: torch.dtype, precision: Optional[str], strict_fp32: bool) -
   return _lib.MODE_TF32
 
 
-def _desc(q: torch.Tensor, o: torch.Tensor, scale: float, mode: int) -> _lib.AttnDesc:
-  """q's strides for q, k, v; o's strides for o, d_o, dq, dk, dv."""
+def _desc(q: torch.Tensor, o: torch.Tensor, scale: float, mode: int, grad: torch.Tensor = None) -> _lib.AttnDesc:
+  """q's strides for q, k, v; o's strides for o, d_o and, unless `grad` (a [B, n, H, D] view with the gradients'
+  strides) is given, for dq, dk, dv."""
   b, n, h, d = q.shape
   sb, sn, sh, sd = q.stride()
   ob, on, oh, od = o.stride()
   if sd != 1 or od != 1:
     raise ValueError("head_dim must be contiguous")
   dt = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_F32
-  return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh, ob, on, oh)
+  if grad is None:
+    return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, 0, sb, sn, sh, ob, on, oh)
+  gb, gn, gh, gd = grad.stride()
+  if gd != 1:
+    raise ValueError("head_dim of the gradients must be contiguous")
+  return _lib.AttnDesc(b, h, n, d, float(scale), dt, mode, _lib.DESC_GRAD_STRIDES, sb, sn, sh, ob, on, oh, gb, gn,
+                       gh)
 
 
 def _gather_layout(t: torch.Tensor) -> int:
@@ -482,8 +489,10 @@ def _side_stream(device: torch.device) -> torch.cuda.Stream:
   return st
 
 
-def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float, mode: int):
-  """(dq, dk, dv), each [B, n, H, D] in q's dtype.
+def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float, mode: int, dqkv=None):
+  """(dq, dk, dv), each [B, n, H, D] in q's dtype; with dqkv ([B, n, H, 3, D], q's dtype and device) the kernels
+  write them into its slices [..., 0, :], [..., 1, :], [..., 2, :] (the gradient of a fused projection's output)
+  and the slices are returned.
 
   delta = rowsum(o * do) first (fwn_attn_bwd_delta); then the dQ pass (over the forward list) on a side stream
   and the dK/dV pass (over the transposed list) on the current stream at the same time, joined before return:
@@ -492,11 +501,15 @@ def attention_backward(q, k, v, o, lse, do, tiles: AttentionTiles, scale: float,
   lib = _lib.lib()
   q, k, v = _canon(q, k, v)
   o, do = _canon(o.contiguous(), do.contiguous())
-  desc = _desc(q, o, scale, mode)
+  if dqkv is not None:
+    dq, dk, dv = dqkv[:, :, :, 0], dqkv[:, :, :, 1], dqkv[:, :, :, 2]
+    desc = _desc(q, o, scale, mode, grad=dq)
+  else:
+    dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
+    desc = _desc(q, o, scale, mode)
   ws_bytes = ctypes.c_size_t(0)
   _lib.check(lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)))
   ws = torch.empty(max(ws_bytes.value, 16), dtype=torch.uint8, device=q.device)
-  dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
   lf, lb = _lists(tiles, q, o)
   sf, sb = lf.struct(), lb.struct()
   d = ctypes.byref(desc)
@@ -533,7 +546,46 @@ class _TiledAttention(torch.autograd.Function):
     return dq, dk, dv, None, None, None
 
 
+class _TiledAttentionQKV(torch.autograd.Function):
+  """The same attention over q, k, v given as one fused projection output qkv [B, n, H, 3, D] (q, k, v its slices
+  along dim 3, read in place): the backward writes dq, dk, dv straight into one [B, n, H, 3, D] gradient
+  (FWN_DESC_GRAD_STRIDES), where autograd would otherwise zero-fill a full-size buffer per slice, copy each slice
+  gradient into it and sum the three."""
+
+  @staticmethod
+  def forward(ctx, qkv, tiles, scale, mode):
+    q, k, v = qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2]
+    needs = ctx.needs_input_grad[0]
+    o, lse = attention_forward(q, k, v, tiles, scale, mode, with_lse=needs)
+    if needs:
+      ctx.save_for_backward(qkv, o, lse)
+    ctx.tiles, ctx.scale, ctx.mode = tiles, scale, mode
+    return o
+
+  @staticmethod
+  def backward(ctx, do):
+    qkv, o, lse = ctx.saved_tensors
+    dqkv = torch.empty(qkv.shape, dtype=qkv.dtype, device=qkv.device)
+    q, k, v = qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2]
+    attention_backward(q, k, v, o, lse, do, ctx.tiles, ctx.scale, ctx.mode, dqkv=dqkv)
+    return dqkv, None, None, None
+
+
 _BUILT_HEAD_DIMS = (64, 128)
+
+
+def attention_qkv(qkv, tiles: AttentionTiles, *, scale: float, precision: Optional[str] = None,
+                  strict_fp32: bool = False):
+  """attention() over a fused projection output qkv [B, n, H, 3, D] (q, k, v = qkv[:, :, :, i]) -> [B, n, H, D];
+  its gradient is one [B, n, H, 3, D] tensor written by the backward kernels. Head dims other than 64 and 128 take
+  attention() on the slices (zero padding)."""
+  if qkv.dim() != 5 or qkv.shape[3] != 3:
+    raise ValueError(f"qkv has shape {tuple(qkv.shape)}, expected [B, n, H, 3, D]")
+  mode = _mode_for(qkv.dtype, precision, strict_fp32)
+  if qkv.shape[-1] not in _BUILT_HEAD_DIMS or qkv.stride(-1) != 1:
+    return attention(qkv[:, :, :, 0], qkv[:, :, :, 1], qkv[:, :, :, 2], tiles, scale=scale, precision=precision,
+                     strict_fp32=strict_fp32)
+  return _TiledAttentionQKV.apply(qkv, tiles, float(scale), mode)
 
 
 def attention(q, k, v, tiles: AttentionTiles, *, scale: float, precision: Optional[str] = None,

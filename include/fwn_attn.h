@@ -68,14 +68,21 @@ typedef struct fwn_attn_desc {
   float scale;        /* softmax scale; the reference passes key_size ** -0.5 (patch.py:174) */
   int32_t dtype;      /* fwn_dtype of q, k, v, o, d_o, dq, dk, dv */
   int32_t mode;       /* fwn_mode */
-  int32_t reserved;
+  int32_t flags;      /* fwn_desc_flags bits; 0: the fields up to out_stride_h are all that is read */
   int64_t stride_b;   /* element strides of q, k, v ([batch, n, heads, head_dim], head_dim contiguous) */
   int64_t stride_n;
   int64_t stride_h;
-  int64_t out_stride_b; /* element strides of o, d_o, dq, dk, dv */
+  int64_t out_stride_b; /* element strides of o, d_o, and of dq, dk, dv unless FWN_DESC_GRAD_STRIDES is set */
   int64_t out_stride_n;
   int64_t out_stride_h;
+  int64_t grad_stride_b; /* with FWN_DESC_GRAD_STRIDES only: element strides of dq, dk, dv, e.g. views of one */
+  int64_t grad_stride_n; /* [batch, n, heads, 3, head_dim] gradient of a fused q / k / v projection's output */
+  int64_t grad_stride_h; /* (the reference's patch.py:165-177 projections), written in place by the backward */
 } fwn_attn_desc;
+
+/* fwn_attn_desc.flags. A caller built against a header without the grad_stride fields passes flags = 0 and its
+ * shorter struct is read only up to out_stride_h. */
+typedef enum fwn_desc_flags { FWN_DESC_GRAD_STRIDES = 1 } fwn_desc_flags;
 
 typedef struct fwn_tile_list {
   const int32_t* ptr;   /* [n_blocks + 1] */
@@ -204,6 +211,27 @@ FWN_API fwn_status fwn_cond_layernorm_residual(float* x, const void* residual, i
                                                int32_t rows_per_sample, const int32_t* out_node,
                                                const float* scale_offset, float eps, void* out, int32_t out_dtype,
                                                void* stream);
+
+/* Out-of-place form for the training path (autograd keeps the block's input): x_out = x + residual (x float32, residual
+ * bf16, x_out float32, all [rows, d]; x_out may be x), out = the conditioned LayerNorm of x_out as fwn_cond_layernorm. */
+FWN_API fwn_status fwn_cond_layernorm_add(const float* x, const void* residual, float* x_out, int64_t rows, int32_t d,
+                                          int32_t rows_per_sample, const float* scale_offset, float eps, void* out,
+                                          int32_t out_dtype, void* stream);
+
+/* Backward of the conditioned LayerNorm (the VJP the reference's training path takes through the blocks' norms under
+ * jax.grad, src/faster_weathernext/patch.py:238-252, 288-290), x the norm's input (after any residual add), dy the
+ * gradient of out ([rows, d] in dy_dtype, bf16 or float32):
+ *   g = dy (1 + scale[s]),  xhat = (x - mean) rstd,
+ *   dx[r, :] = rstd (g - mean(g) - xhat mean(g xhat)) + dx_in[r, :]     (dx_in float32 or NULL; dx may be dx_in)
+ *   dscale_offset[s, :d] = sum over the sample's rows of dy xhat,  dscale_offset[s, d:] = sum of dy   (float32)
+ * dx_bf16 (bf16 [rows, d] or NULL) receives a bf16 copy of dx: the gradient of a bf16 residual that was added into x.
+ * d in {128, 256, 512}. The per-sample sums are taken in a fixed order (per-CTA partials in `workspace`, then one
+ * reduction kernel): deterministic. workspace: fwn_cond_layernorm_bwd_workspace bytes, 16-byte aligned. */
+FWN_API size_t fwn_cond_layernorm_bwd_workspace(int64_t rows, int32_t d, int32_t rows_per_sample);
+FWN_API fwn_status fwn_cond_layernorm_bwd(const float* x, int64_t rows, int32_t d, int32_t rows_per_sample,
+                                          const float* scale_offset, float eps, const void* dy, int32_t dy_dtype,
+                                          const float* dx_in, float* dx, void* dx_bf16, float* dscale_offset,
+                                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* Projections around the attention (src/faster_weathernext/patch.py:165-177, 250-252: q / k / v, mha_final, the
  * MLP): c[m, n] = act(a[m, k] b[k, n] + bias[n]), a row-major bf16 [m, k], b given transposed as bt row-major bf16

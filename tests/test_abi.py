@@ -41,3 +41,21 @@ def test_host_only_entry_points_need_no_gpu():
   desc.head_dim = 64
   desc.mode = _lib.MODE_TF32  # TF32 needs float32 tensors
   assert lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(size)) == _lib.FWN_ERR_INVALID_ARGUMENT
+
+
+def test_desc_flags_are_checked_before_any_cuda_call():
+  """fwn_attn_desc.flags: unknown bits are refused; FWN_DESC_GRAD_STRIDES makes the gradient strides checked (16-byte
+  multiples, rows not overlapping); flags = 0 never reads them."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  size = ctypes.c_size_t(0)
+  desc = _lib.AttnDesc(1, 2, 300, 64, 0.125, _lib.DTYPE_BF16, _lib.MODE_BF16, 0, 600 * 64, 2 * 64, 64,
+                       600 * 64, 2 * 64, 64, 1, 1, 1)   # bad gradient strides, ignored without the flag
+  assert lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(size)) == _lib.FWN_OK
+  desc.flags = 4
+  assert lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(size)) == _lib.FWN_ERR_INVALID_ARGUMENT
+  assert b"flags" in lib.fwn_last_error_string()
+  desc.flags = _lib.DESC_GRAD_STRIDES
+  assert lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(size)) == _lib.FWN_ERR_INVALID_ARGUMENT
+  desc.grad_stride_b, desc.grad_stride_n, desc.grad_stride_h = 300 * 2 * 3 * 64, 2 * 3 * 64, 3 * 64
+  assert lib.fwn_attn_bwd_workspace_size(ctypes.byref(desc), ctypes.byref(size)) == _lib.FWN_OK

@@ -283,3 +283,40 @@ def test_autograd_fused_qkv_layout_dense_mask(cuda, head_dim):
   got = gx.float().cpu().numpy()
   for i, name in enumerate(("dq", "dk", "dv")):
     assert oa.rel_rms(got[:, :, :, i], ref[i]) < TOL["bf16"], (name, oa.rel_rms(got[:, :, :, i], ref[i]))
+
+
+@pytest.mark.parametrize("mode", ["bf16", "tf32"])
+@pytest.mark.parametrize("mask_kind", ["ref_nonsym", "khop"])
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_attention_qkv_writes_the_fused_gradient_in_place(golden, cuda, mode, mask_kind, head_dim):
+  """tiled_attn.attention_qkv (the backward writes dq, dk, dv into one [B, n, H, 3, D] gradient through
+  FWN_DESC_GRAD_STRIDES) gives bit-identical outputs and gradients to attention() on the three slices (the same
+  kernels, whose per-slice gradients autograd assembles), and the gradient matches the oracle's VJP."""
+  from faster_weathernext import _lib
+  from faster_weathernext import tiled_attn as ta
+  if mask_kind == "khop":
+    m = _khop_mask(4, 6)
+  else:
+    m = golden_mask(golden["tiles"], "k_nonsym")
+  n = m.shape[0]
+  dt = torch.bfloat16 if mode == "bf16" else torch.float32
+  g = torch.Generator(device=cuda).manual_seed(21)
+  x = torch.randn(2, n, 2, 3, head_dim, device=cuda, generator=g).to(dt)
+  do = torch.randn(2, n, 2, head_dim, device=cuda, generator=g).to(dt)
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  scale = head_dim ** -0.5
+  xa = x.clone().requires_grad_(True)
+  oa_ = ta.attention_qkv(xa, tiles, scale=scale)
+  (ga,) = torch.autograd.grad(oa_, xa, do)
+  xb = x.clone().requires_grad_(True)
+  ob = ta.attention(xb[:, :, :, 0], xb[:, :, :, 1], xb[:, :, :, 2], tiles, scale=scale)
+  (gb,) = torch.autograd.grad(ob, xb, do)
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  assert torch.equal(oa_, ob)
+  assert torch.equal(ga, gb)
+  q, k, v = (x[:, :, :, i].float().cpu().numpy() for i in range(3))
+  ref = oa.sparse_attention_vjp(q, k, v, do.float().cpu().numpy(), m, scale)
+  got = ga.float().cpu().numpy()
+  for i, name in enumerate(("dq", "dk", "dv")):
+    assert oa.rel_rms(got[:, :, :, i], ref[i]) < TOL[mode], (name, oa.rel_rms(got[:, :, :, i], ref[i]))

@@ -292,3 +292,119 @@ def test_cond_layernorm_residual_kernel(cuda):
       assert torch.equal(got, ref), d
   assert lib.fwn_cond_layernorm_residual(x.data_ptr(), None, 4, 128, 2, None, so.data_ptr(), 1e-5, x.data_ptr(),
                                          _lib.DTYPE_F32, 0) == _lib.FWN_ERR_INVALID_ARGUMENT
+
+
+def _cond_norm_torch(x, a, so, n):
+  """Composed float32 torch form of the conditioned norm: xn = x (+ a), y = LN(xn) (1 + scale) + offset."""
+  b = so.shape[0]
+  d = x.shape[1]
+  xn = x + a.float() if a is not None else x
+  y = torch.nn.functional.layer_norm(xn.view(b, n, d), (d,), eps=1e-5)
+  scale, offset = so.unsqueeze(1).chunk(2, dim=-1)
+  return xn, (y * (1 + scale) + offset).view(b * n, d)
+
+
+def test_cond_layernorm_backward_matches_torch_autograd(cuda):
+  """fwn_cond_layernorm_bwd through the processor's autograd Function against torch autograd of the composed
+  float32 form, for d in {128, 256, 512}, 301 rows per sample (ragged against the kernel's 128-row CTAs), with and
+  without a residual input, bf16 and float32 output: dx and d(scale, offset) within 1e-4 of the gradient's scale
+  (float32, different summation orders), d(residual) the bf16 rounding of dx exactly; two calls give identical
+  scale / offset gradients (fixed reduction order)."""
+  from faster_weathernext.processor import _CondNorm
+  g = torch.Generator(device=cuda).manual_seed(11)
+  b, n = 3, 301
+  for d in (128, 256, 512):
+    for with_a in (False, True):
+      for out_dtype in (torch.bfloat16, torch.float32):
+        x = torch.randn(b * n, d, device=cuda, generator=g) * 2 + 0.5
+        a = (torch.randn(b * n, d, device=cuda, generator=g)).to(torch.bfloat16) if with_a else None
+        so = torch.randn(b, 2 * d, device=cuda, generator=g) * 0.3
+        dy = torch.randn(b * n, d, device=cuda, generator=g).to(out_dtype)
+        dxn = torch.randn(b * n, d, device=cuda, generator=g) if with_a else None
+        # ours
+        xo = x.clone().requires_grad_()
+        ao = a.clone().requires_grad_() if with_a else None
+        soo = so.clone().requires_grad_()
+        out = _CondNorm.apply(xo, ao, soo, n, out_dtype)
+        if with_a:
+          xn_o, h_o = out
+          torch.autograd.backward([xn_o, h_o], [dxn, dy])
+        else:
+          h_o = out
+          h_o.backward(dy)
+        # torch
+        xr = x.clone().requires_grad_()
+        ar = a.float().clone().requires_grad_() if with_a else None
+        sor = so.clone().requires_grad_()
+        xn_r, h_r = _cond_norm_torch(xr, ar, sor, n)
+        if with_a:
+          torch.autograd.backward([xn_r, h_r], [dxn, dy.float()])
+        else:
+          h_r.backward(dy.float())
+        torch.testing.assert_close(h_o.float(), h_r.detach().to(out_dtype).float(), atol=1e-2 if out_dtype ==
+                                   torch.bfloat16 else 1e-5, rtol=1e-2 if out_dtype == torch.bfloat16 else 1e-5)
+        scale_dx = float(xr.grad.abs().max())
+        assert float((xo.grad - xr.grad).abs().max()) <= 1e-4 * scale_dx, (d, with_a, out_dtype)
+        scale_ds = float(sor.grad.abs().max())
+        assert float((soo.grad - sor.grad).abs().max()) <= 1e-4 * scale_ds, (d, with_a, out_dtype)
+        if with_a:
+          assert ao.grad.dtype == torch.bfloat16
+          assert torch.equal(ao.grad, xo.grad.to(torch.bfloat16))
+        first = soo.grad.clone()
+        soo.grad = None
+        out = _CondNorm.apply(xo, ao, soo, n, out_dtype)
+        (out[1] if with_a else out).backward(dy)
+        assert torch.equal(soo.grad, first)
+
+
+def test_cond_layernorm_backward_abi_checks(cuda):
+  """fwn_cond_layernorm_bwd rejects an unbuilt width, a short workspace and rows that are not whole samples."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  x = torch.zeros(8, 1024, device=cuda)
+  so = torch.zeros(2, 2048, device=cuda)
+  dy, dx, dso = torch.zeros_like(x), torch.empty_like(x), torch.empty_like(so)
+  ws = torch.zeros(1 << 16, dtype=torch.uint8, device=cuda)
+  args = lambda d, rps, nbytes: (x.data_ptr(), 8, d, rps, so.data_ptr(), 1e-5, dy.data_ptr(), _lib.DTYPE_F32, None,
+                                 dx.data_ptr(), None, dso.data_ptr(), ws.data_ptr(), nbytes, 0)
+  assert lib.fwn_cond_layernorm_bwd(*args(1024, 4, ws.numel())) == _lib.FWN_ERR_UNSUPPORTED
+  assert lib.fwn_cond_layernorm_bwd(*args(512, 3, ws.numel())) == _lib.FWN_ERR_INVALID_ARGUMENT
+  need = lib.fwn_cond_layernorm_bwd_workspace(8, 512, 4)
+  assert need == 2 * 1 * 2 * 512 * 4
+  assert lib.fwn_cond_layernorm_bwd(*args(512, 4, need - 4)) == _lib.FWN_ERR_INVALID_ARGUMENT
+  assert lib.fwn_cond_layernorm_bwd(*args(512, 4, need)) == _lib.FWN_OK
+  torch.cuda.synchronize()
+  assert not bool(dso.view(-1)[:2 * 1024].any())
+
+
+def test_processor_fused_training_matches_composed_path(cuda):
+  """The autograd path on the fused norms (fused_training, the default) against the composed torch form of the same
+  blocks (fused_training = False): outputs within rel RMS 1e-2 and all parameter and input gradients within 3e-2
+  global relative L2 (bf16 compute; the fused path computes the conditioning's scale / offset in float32, the
+  composed one in bf16)."""
+  from faster_weathernext import mesh
+  from faster_weathernext import tiled_attn as ta
+  from faster_weathernext.processor import Processor
+  m, _, _ = mesh.config_mask(1)
+  n = m.shape[0]
+  tiles = ta.AttentionTiles.from_mask(m, device=cuda)
+  cfg = _small()
+  model = Processor(cfg, seed=6, device=cuda)
+  g = torch.Generator(device=cuda).manual_seed(8)
+  x = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  c = torch.randn(2, cfg.cond_dim, device=cuda, generator=g)
+  t = torch.randn(2, n, cfg.d_model, device=cuda, generator=g)
+  ys, grads = [], []
+  for fused in (True, False):
+    model.fused_training = fused
+    model.zero_grad(set_to_none=True)
+    xi = x.clone().requires_grad_()
+    ci = c.clone().requires_grad_()
+    y = model(xi, ci, tiles)
+    torch.nn.functional.mse_loss(y, t).backward()
+    ys.append(y.detach())
+    grads.append(torch.cat([p.grad.reshape(-1) for p in model.parameters()] + [xi.grad.reshape(-1),
+                                                                                ci.grad.reshape(-1)]))
+  model.fused_training = True
+  assert _rel(ys[0], ys[1]) < 1e-2
+  assert float((grads[0] - grads[1]).norm() / grads[1].norm()) < 3e-2
