@@ -59,6 +59,12 @@ EncodeTiledFn encode_fn() {
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
+  // The driver call needs a current context. A thread whose runtime calls so far needed none (autograd's device
+  // thread running a backward whose allocations all came from the caching allocator, for one) has its device set but
+  // no context bound: cudaSetDevice on the thread's current device binds that device's primary context (and changes
+  // nothing when it is bound already).
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
   return fn;
 }
 
@@ -814,39 +820,64 @@ fwn_status make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
 
 }  // namespace
 
-fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n, int32_t k,
-                         int32_t act, void* stream) {
+namespace {
+
+fwn_status gemm_bf16(const void* a, const void* bt, const void* bias, void* c, void* aux, int64_t m, int32_t n,
+                     int32_t k, int32_t act, void* stream) {
   using C = fwn::GemmCfg;
   if (m <= 0 || n <= 0 || k <= 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape m=%lld n=%d k=%d", static_cast<long long>(m), n, k);
   if (n % C::BN != 0 || k % C::BK != 0)
     return fail(FWN_ERR_UNSUPPORTED, "n=%d must be a multiple of %d and k=%d of %d", n, C::BN, k, C::BK);
-  if (act != FWN_ACT_NONE && act != FWN_ACT_GELU_TANH) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
   if (!a || !bt || !c) return fail(FWN_ERR_INVALID_ARGUMENT, "null pointer");
-  if (!aligned16(a) || !aligned16(bt) || !aligned16(c) || (bias && !aligned16(bias)))
+  const bool uses_aux = act == FWN_ACT_GELU_TANH_AUX || act == FWN_ACT_GELU_TANH_GRAD;
+  if (uses_aux && !aux) return fail(FWN_ERR_INVALID_ARGUMENT, "activation %d needs the aux tensor", act);
+  if (!aligned16(a) || !aligned16(bt) || !aligned16(c) || (bias && !aligned16(bias)) || (uses_aux && !aligned16(aux)))
     return fail(FWN_ERR_INVALID_ARGUMENT, "pointers must be 16-byte aligned");
   const int64_t m_tiles = (m + C::BM - 1) / C::BM;
   if (m_tiles * (n / C::BN) >= (int64_t(1) << 31)) return fail(FWN_ERR_UNSUPPORTED, "m=%lld too large", static_cast<long long>(m));
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb, tc, taux;
   fwn_status s;
   if ((s = make_map_2d(&ta, a, m, k, C::BM)) != FWN_OK) return s;
   if ((s = make_map_2d(&tb, bt, n, k, C::BN)) != FWN_OK) return s;
   if ((s = make_map_2d(&tc, c, m, n, 32, 32)) != FWN_OK) return s;
+  taux = tc;
+  if (uses_aux && (s = make_map_2d(&taux, aux, m, n, 32, 32)) != FWN_OK) return s;
   fwn::GemmParams p{};
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.c = static_cast<__nv_bfloat16*>(c);
+  p.aux_in = act == FWN_ACT_GELU_TANH_GRAD ? static_cast<const __nv_bfloat16*>(aux) : nullptr;
   p.m = m;
   p.n = n;
   p.k = k;
   p.act = act;
   p.n_tiles = n / C::BN;
   p.num_tiles = static_cast<int>(m_tiles * p.n_tiles);
-  auto kernel = fwn::gemm_bf16_kernel;
+  auto kernel = act == FWN_ACT_GELU_TANH        ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH>
+                : act == FWN_ACT_GELU_TANH_AUX  ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH_AUX>
+                : act == FWN_ACT_GELU_TANH_GRAD ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH_GRAD>
+                                                : fwn::gemm_bf16_kernel<FWN_ACT_NONE>;
+  const int smem = act == FWN_ACT_GELU_TANH_GRAD ? fwn::GemmCfgT<FWN_ACT_GELU_TANH_GRAD>::SMEM_BYTES : C::SMEM_BYTES;
   int grid = 0;
-  if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.num_tiles, &grid)) != FWN_OK) return s;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, tc, p);
+  if ((s = persistent_grid(kernel, C::THREADS, smem, C::TMEM_COLS, p.num_tiles, &grid)) != FWN_OK) return s;
+  kernel<<<grid, C::THREADS, smem, static_cast<cudaStream_t>(stream)>>>(ta, tb, tc, taux, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return ok();
+}
+
+}  // namespace
+
+fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n, int32_t k,
+                         int32_t act, void* stream) {
+  if (act != FWN_ACT_NONE && act != FWN_ACT_GELU_TANH) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  return gemm_bf16(a, bt, bias, c, nullptr, m, n, k, act, stream);
+}
+
+fwn_status fwn_gemm_bf16_aux(const void* a, const void* bt, const void* bias, void* c, void* aux, int64_t m, int32_t n,
+                             int32_t k, int32_t act, void* stream) {
+  if (act != FWN_ACT_NONE && act != FWN_ACT_GELU_TANH && act != FWN_ACT_GELU_TANH_AUX && act != FWN_ACT_GELU_TANH_GRAD)
+    return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  return gemm_bf16(a, bt, bias, c, aux, m, n, k, act, stream);
 }
 
 fwn_status fwn_gnn_gather_add_act(const void* e_proj, const void* s_proj, const int32_t* senders, const void* r_proj,

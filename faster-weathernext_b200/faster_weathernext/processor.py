@@ -110,6 +110,50 @@ class _CondNorm(torch.autograd.Function):
 _EPS = 1e-5
 
 
+class _GeluMLP(torch.autograd.Function):
+  """The training path's MLP, GELU(h w1 + b1) w2 + b2 in bf16 (h bf16 [M, d]; w1 [d, hidden], b1, w2 [hidden, d],
+  b2 float32 parameters), with the GELU in the epilogues of this package's GEMM: forward fwn_gemm_bf16_aux with
+  FWN_ACT_GELU_TANH_AUX (the activation, and the pre-activation kept for the backward, in one pass); backward
+  d_pre = (d_out w2^T) GELU'(pre) by the same GEMM with FWN_ACT_GELU_TANH_GRAD (w2 as stored is its K-major
+  operand). The down-projection and the weight / input gradients are cuBLAS GEMMs; the bias gradients are float32
+  column sums. Replaces torch's bias + GELU forward and GELU backward passes over the [M, hidden] activations.
+  Requires hidden % 256 == 0 and d % 64 == 0."""
+
+  @staticmethod
+  def forward(ctx, h, w1, b1, w2, b2):
+    bf = torch.bfloat16
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    m, d = h.shape
+    hidden = w1.shape[1]
+    w1t = w1.detach().t().contiguous().to(bf)           # [hidden, d]: K-major operand of the up-projection
+    w2h = w2.detach().to(bf)                            # [hidden, d]
+    pre = torch.empty(m, hidden, dtype=bf, device=h.device)
+    act = torch.empty(m, hidden, dtype=bf, device=h.device)
+    _lib.check(lib.fwn_gemm_bf16_aux(h.data_ptr(), w1t.data_ptr(), b1.detach().to(bf).data_ptr(), act.data_ptr(),
+                                     pre.data_ptr(), m, hidden, d, _lib.ACT_GELU_TANH_AUX, stream))
+    out = torch.addmm(b2.detach().to(bf), act, w2h)
+    ctx.save_for_backward(h, pre, act, w1t, w2h)
+    return out
+
+  @staticmethod
+  def backward(ctx, d_out):
+    h, pre, act, w1t, w2h = ctx.saved_tensors
+    lib = _lib.lib()
+    m, hidden = pre.shape
+    d = h.shape[1]
+    d_out = d_out.to(torch.bfloat16).contiguous()
+    d_pre = torch.empty_like(pre)
+    _lib.check(lib.fwn_gemm_bf16_aux(d_out.data_ptr(), w2h.data_ptr(), None, d_pre.data_ptr(), pre.data_ptr(), m,
+                                     hidden, d, _lib.ACT_GELU_TANH_GRAD, torch.cuda.current_stream().cuda_stream))
+    d_b2 = torch.sum(d_out, 0, dtype=torch.float32)
+    d_w2 = torch.mm(act.t(), d_out).float()
+    d_b1 = torch.sum(d_pre, 0, dtype=torch.float32)
+    d_w1 = torch.mm(h.t(), d_pre).float()
+    d_h = torch.mm(d_pre, w1t)
+    return d_h, d_w1, d_b1, d_w2, d_b2
+
+
 class Processor(torch.nn.Module):
   """Random-init processor; parameters float32, compute in `dtype` (bf16 by default)."""
 
@@ -232,8 +276,9 @@ class Processor(torch.nn.Module):
   def _forward_train(self, x, cond, tiles, perm=None):
     """The autograd path with the fused differentiable norms (_CondNorm): each norm also adds the previous
     sub-block's bf16 output into the float32 residual stream, and its backward is one pass plus a per-sample
-    reduction. The projections and the MLP are torch ops (cuBLAS), the attention is patch.tiled_mha; the
-    conditioning's scale / offset are computed in float32. x float32 [B, n, d]; cond [B, cond_dim]."""
+    reduction. The MLP is _GeluMLP (GELU and its backward in this package's GEMM epilogues) where its shapes fit the
+    GEMM's tiles, the other projections are cuBLAS GEMMs, the attention is patch.tiled_mha; the conditioning's
+    scale / offset are computed in float32. x float32 [B, n, d]; cond [B, cond_dim]."""
     b, n, d = x.shape
     if perm is not None:
       x = x.index_select(1, perm)
@@ -268,6 +313,8 @@ class Processor(torch.nn.Module):
       xs, h = _CondNorm.apply(xs, pending, so1, n, bf)
     a = self._mha(h.view(b, n, d), blk.w_qkv.to(bf), blk.w_out.to(bf), tiles).reshape(b * n, d)
     xs, h = _CondNorm.apply(xs, a, so2, n, bf)
+    if blk.w1.shape[1] % 256 == 0 and d % 64 == 0:
+      return xs, _GeluMLP.apply(h, blk.w1, blk.b1, blk.w2, blk.b2)
     mlp = F.gelu(torch.addmm(blk.b1.to(bf), h, blk.w1.to(bf)), approximate="tanh")
     return xs, torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf))
 

@@ -238,9 +238,24 @@ FWN_API fwn_status fwn_cond_layernorm_bwd(const float* x, int64_t rows, int32_t 
  * [n, k] (the weight with k contiguous), bias bf16 [n] or NULL, c row-major bf16 [m, n]; float32 accumulation on the
  * tensor cores. n a multiple of 256, k a multiple of 64, pointers 16-byte aligned. act: FWN_ACT_NONE or
  * FWN_ACT_GELU_TANH (0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), jax.nn.gelu's default form). */
-typedef enum fwn_act { FWN_ACT_NONE = 0, FWN_ACT_GELU_TANH = 1, FWN_ACT_SWISH = 2 } fwn_act;
+typedef enum fwn_act {
+  FWN_ACT_NONE = 0,
+  FWN_ACT_GELU_TANH = 1,
+  FWN_ACT_SWISH = 2,
+  FWN_ACT_GELU_TANH_AUX = 3,  /* fwn_gemm_bf16_aux: c = GELU(x) and aux = x (x = a b + bias), both bf16 [m, n] */
+  FWN_ACT_GELU_TANH_GRAD = 4  /* fwn_gemm_bf16_aux: c = x GELU'(aux), aux the bf16 [m, n] input GELU was applied to */
+} fwn_act;
 FWN_API fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias, void* c, int64_t m, int32_t n,
                                  int32_t k, int32_t act, void* stream);
+
+/* The MLP of the processor's training path (src/faster_weathernext/patch.py:250-252 under jax.grad): the same GEMM
+ * with an aux tensor (bf16 [m, n], 16-byte aligned). act FWN_ACT_GELU_TANH_AUX: c = GELU(x), aux = x, x = a b + bias
+ * (the forward, keeping the pre-activation for the backward); FWN_ACT_GELU_TANH_GRAD: c = x GELU'(aux), x = a b (+ bias)
+ * (the backward: a = the gradient of the MLP's output, bt = the down-projection weight as stored, [hidden, d], so x is
+ * the gradient of the activation, and c the gradient of the pre-activation). FWN_ACT_NONE / FWN_ACT_GELU_TANH ignore
+ * aux. */
+FWN_API fwn_status fwn_gemm_bf16_aux(const void* a, const void* bt, const void* bias, void* c, void* aux, int64_t m,
+                                     int32_t n, int32_t k, int32_t act, void* stream);
 
 /* ---- grid <-> mesh interaction networks -------------------------------------------------------------------
  * The blocked GNNs of the encoder / decoder (src/faster_weathernext/patch.py:347-509, ChunkedDeepGNN: edge MLP on
