@@ -26,22 +26,32 @@ __global__ void __launch_bounds__(256) cond_layernorm_kernel(const float* x_in, 
                                                               const float* __restrict__ scale_offset, float eps,
                                                               void* __restrict__ out,
                                                               const __nv_bfloat16* __restrict__ residual) {
-  // x_out (RES only) may be x_in itself (the residual stream updated in place): plain loads.
+  // x_out (RES only) may be x_in itself (the residual stream updated in place): every load of the row is issued
+  // before the first store (the compiler may not move a load across a store that can alias it), and x_in is read
+  // through the read-only path only without a residual.
   constexpr int V = D / 128;  // float4 per lane
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;  // whole warps leave together (rows are warp-uniform)
   const float4* xr = reinterpret_cast<const float4*>(x_in + row * D);
   float4 v[V];
+  uint2 r[V];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    v[i] = xr[lane + 32 * i];
+    if constexpr (RES) {
+      v[i] = xr[lane + 32 * i];
+      r[i] = __ldg(reinterpret_cast<const uint2*>(residual + row * D) + lane + 32 * i);
+    } else {
+      v[i] = __ldg(xr + lane + 32 * i);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
     if constexpr (RES) {
       // x_out = x_in + residual (4 bf16 per lane and step).
-      const uint2 r = __ldg(reinterpret_cast<const uint2*>(residual + row * D) + lane + 32 * i);
-      const float2 r01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
-      const float2 r23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+      const float2 r01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[i].x));
+      const float2 r23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[i].y));
       v[i].x += r01.x;
       v[i].y += r01.y;
       v[i].z += r23.x;
