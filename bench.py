@@ -779,7 +779,7 @@ def run_model_workload(args):
                                 "cfg4: 24 pre-LN blocks d512 8x64 MLP2048 GELU, 16 forwards") +
                                f", level-6 mesh 0.06 rad", "members": members, "members_per_gpu": local_m,
                    "parallelism": f"{'dp' if finetune else 'replicas'}{world}"},
-        "roofline": {"bound": "tensor", "kernel": "processor GEMMs (cuBLAS bf16) per GPU", "achieved": round(achieved, 1),
+        "roofline": {"bound": "tensor", "kernel": "processor GEMMs (cuBLAS and fwn_gemm_bf16, bf16) per GPU", "achieved": round(achieved, 1),
                      "peak": tc, "unit": "TFLOP/s", "frac": round(achieved / tc, 4), "peak_source": peak_kind,
                      "traffic": None},
         "attention_useful_gflop_per_gpu": round(attn / 1e9, 1), "gemm_gflop_per_gpu": round(gemm / 1e9, 1),

@@ -11,10 +11,13 @@ q/k/v/out projections and a GELU MLP. The official modules (`weathernext.utils.s
 `dense.LinearNormConditioning`) are third-party and not available here, so this is a synthetic processor of
 the configurations' shape (24 blocks, width 512, 8 x 64 heads, MLP 2048, GELU in the tanh form that is
 jax.nn.gelu's default; Glorot-uniform weights from a seed), not a numerical copy of the official one. The
-projections run as cuBLAS GEMMs; the attention block is patch.tiled_mha (the B200 kernel; q, k, v are strided
-views of one fused projection, no copies). Without autograd (inference), each norm is one fused kernel that also
-adds the previous sub-block's output into the residual stream, and the MLP up-projection runs on this package's
-tcgen05 GEMM with bias + GELU in its epilogue (faster than cuBLASLt's GELU epilogue at these shapes). With autograd and patch.OPTIONS.remat, each block's activations are
+q/k/v, output and down projections run as cuBLAS GEMMs; the attention block is patch.tiled_mha (the B200 kernel;
+q, k, v are strided views of one fused projection, no copies, and its backward writes their gradients into one
+tensor). Without autograd (inference), each norm is one fused kernel that also adds the previous sub-block's output
+into the residual stream, and the MLP up-projection runs on this package's tcgen05 GEMM with bias + GELU in its
+epilogue (faster than cuBLASLt's GELU epilogue at these shapes). With autograd in bf16 (training), the norms are a
+differentiable fused kernel pair (_CondNorm: residual add + norm forward, one-pass backward) and the MLP's GELU and its
+backward live in the same GEMM's epilogues (_GeluMLP). With patch.OPTIONS.remat, each block's activations are
 recomputed in the backward instead of stored (the reference's per-layer rematerialisation, patch.py:69-73).
 
 Node order: the reference's transformer gathers the latents into the mask's node order with `perm` before the
