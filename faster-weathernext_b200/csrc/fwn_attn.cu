@@ -602,7 +602,7 @@ fwn_status fwn_device_error(void* stream, int32_t* code) {
   if (e != cudaSuccess) return cuda_fail(e, "read device error word");
   e = cudaMemcpyToSymbol(fwn::g_device_error, &zero, sizeof(zero));
   if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
-  *code = word ? FWN_ERR_DEVICE_TIMEOUT : 0;
+  *code = !word ? 0 : (word & 0x400u) ? FWN_ERR_INVALID_ARGUMENT : FWN_ERR_DEVICE_TIMEOUT;
   return ok();
 }
 
@@ -822,8 +822,11 @@ fwn_status make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
 
 namespace {
 
+// act: the public FWN_ACT_* value, or kGemmGatherAdd (the gathered-add epilogue, whose fields `adds` carries).
+constexpr int32_t kGemmGatherAdd = 5;
+
 fwn_status gemm_bf16(const void* a, const void* bt, const void* bias, void* c, void* aux, int64_t m, int32_t n,
-                     int32_t k, int32_t act, void* stream) {
+                     int32_t k, int32_t act, void* stream, const fwn::GemmParams* adds = nullptr) {
   using C = fwn::GemmCfg;
   if (m <= 0 || n <= 0 || k <= 0) return fail(FWN_ERR_INVALID_ARGUMENT, "bad shape m=%lld n=%d k=%d", static_cast<long long>(m), n, k);
   if (n % C::BN != 0 || k % C::BK != 0)
@@ -846,6 +849,15 @@ fwn_status gemm_bf16(const void* a, const void* bt, const void* bias, void* c, v
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.c = static_cast<__nv_bfloat16*>(c);
   p.aux_in = act == FWN_ACT_GELU_TANH_GRAD ? static_cast<const __nv_bfloat16*>(aux) : nullptr;
+  if (adds != nullptr) {
+    p.add0 = adds->add0;
+    p.idx0 = adds->idx0;
+    p.rows0 = adds->rows0;
+    p.add1 = adds->add1;
+    p.idx1 = adds->idx1;
+    p.rows1 = adds->rows1;
+    p.swish = adds->swish;
+  }
   p.m = m;
   p.n = n;
   p.k = k;
@@ -855,6 +867,7 @@ fwn_status gemm_bf16(const void* a, const void* bt, const void* bias, void* c, v
   auto kernel = act == FWN_ACT_GELU_TANH        ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH>
                 : act == FWN_ACT_GELU_TANH_AUX  ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH_AUX>
                 : act == FWN_ACT_GELU_TANH_GRAD ? fwn::gemm_bf16_kernel<FWN_ACT_GELU_TANH_GRAD>
+                : act == kGemmGatherAdd         ? fwn::gemm_bf16_kernel<kGemmGatherAdd>
                                                 : fwn::gemm_bf16_kernel<FWN_ACT_NONE>;
   const int smem = act == FWN_ACT_GELU_TANH_GRAD ? fwn::GemmCfgT<FWN_ACT_GELU_TANH_GRAD>::SMEM_BYTES : C::SMEM_BYTES;
   int grid = 0;
@@ -878,6 +891,25 @@ fwn_status fwn_gemm_bf16_aux(const void* a, const void* bt, const void* bias, vo
   if (act != FWN_ACT_NONE && act != FWN_ACT_GELU_TANH && act != FWN_ACT_GELU_TANH_AUX && act != FWN_ACT_GELU_TANH_GRAD)
     return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
   return gemm_bf16(a, bt, bias, c, aux, m, n, k, act, stream);
+}
+
+fwn_status fwn_gemm_bf16_gather(const void* a, const void* bt, const void* bias, void* c, const void* add0,
+                                const int32_t* idx0, int64_t rows0, const void* add1, const int32_t* idx1,
+                                int64_t rows1, int64_t m, int32_t n, int32_t k, int32_t act, void* stream) {
+  if (act != FWN_ACT_NONE && act != FWN_ACT_SWISH) return fail(FWN_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  if ((add0 && (!aligned16(add0) || rows0 <= 0)) || (add1 && (!aligned16(add1) || rows1 <= 0)))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "added tensors must be 16-byte aligned with a positive row count");
+  if ((add0 && !idx0 && rows0 < m) || (add1 && !idx1 && rows1 < m))
+    return fail(FWN_ERR_INVALID_ARGUMENT, "an added tensor without an index needs m rows");
+  fwn::GemmParams adds{};
+  adds.add0 = static_cast<const __nv_bfloat16*>(add0);
+  adds.idx0 = add0 ? idx0 : nullptr;
+  adds.rows0 = rows0;
+  adds.add1 = static_cast<const __nv_bfloat16*>(add1);
+  adds.idx1 = add1 ? idx1 : nullptr;
+  adds.rows1 = rows1;
+  adds.swish = act == FWN_ACT_SWISH;
+  return gemm_bf16(a, bt, bias, c, nullptr, m, n, k, kGemmGatherAdd, stream, &adds);
 }
 
 fwn_status fwn_gnn_gather_add_act(const void* e_proj, const void* s_proj, const int32_t* senders, const void* r_proj,

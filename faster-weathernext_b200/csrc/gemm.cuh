@@ -32,10 +32,19 @@ struct GemmParams {
   const __nv_bfloat16* bias;    // [n] or null
   __nv_bfloat16* c;             // [m, n]
   const __nv_bfloat16* aux_in;  // act 4: the pre-activation [m, n] the GELU was applied to
+  // act 5: rows added before the activation, c[i] = act(a b + bias + add0[idx0[i]] + add1[idx1[i]]); an add tensor
+  // may be null, an index null (row i itself); rows0 / rows1 bound the indices.
+  const __nv_bfloat16* add0;
+  const int32_t* idx0;
+  const __nv_bfloat16* add1;
+  const int32_t* idx1;
+  int64_t rows0, rows1;
+  int swish;                    // act 5: swish (x sigmoid(x)) after the adds, else identity
   int64_t m;
   int n, k;
   int act;                      // 0 identity, 1 GELU (tanh form), 3 GELU and x itself to the aux output (tm_aux),
-                                // 4 x GELU'(aux_in): the backward of GELU, x the incoming gradient
+                                // 4 x GELU'(aux_in): the backward of GELU, x the incoming gradient, 5 gathered adds
+                                // and optional swish (the interaction network's edge and node MLP input layers)
   int n_tiles, num_tiles;
 };
 
@@ -89,6 +98,13 @@ __device__ __forceinline__ float tanh_approx(float x) {
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.f + tanh_approx(u));
+}
+
+// swish(x) = x sigmoid(x) = 0.5 x + 0.5 x tanh(x / 2): one hardware tanh and two FMAs (x / (1 + exp(-x)) costs an
+// exponential and a full-precision division per element, which made the epilogue the GEMM's bottleneck).
+__device__ __forceinline__ float swish(float x) {
+  const float h = 0.5f * x;
+  return fmaf(h, tanh_approx(h), h);
 }
 
 // d/dx of the tanh-form GELU: 0.5 (1 + t) + 0.5 x (1 - t^2) sqrt(2 / pi) (1 + 3 * 0.044715 x^2), t = tanh(u).
@@ -233,6 +249,21 @@ __global__ void __maxnreg__(168)
         aux_pending = false;
       }
       tc_fence_after();
+      // act 5: this lane's row of each added tensor (its index read once per tile); -1: no row (past m, or no tensor).
+      int64_t ar0 = -1, ar1 = -1;
+      if constexpr (ACT == 5) {
+        const int64_t r = row0 + lane;
+        if (r < p.m) {
+          if (p.add0 != nullptr) ar0 = p.idx0 != nullptr ? static_cast<int64_t>(__ldg(p.idx0 + r)) : r;
+          if (p.add1 != nullptr) ar1 = p.idx1 != nullptr ? static_cast<int64_t>(__ldg(p.idx1 + r)) : r;
+          if ((p.add0 != nullptr && static_cast<uint64_t>(ar0) >= static_cast<uint64_t>(p.rows0)) ||
+              (p.add1 != nullptr && static_cast<uint64_t>(ar1) >= static_cast<uint64_t>(p.rows1))) {
+            // An index outside its tensor: add nothing for this row and report it (fwn_device_error).
+            atomicOr(&g_device_error, 0x400u);
+            ar0 = ar1 = -1;
+          }
+        }
+      }
 #pragma unroll 1
       for (int jp = 0; jp < 2; ++jp) {
         float v[2][32];
@@ -275,6 +306,26 @@ __global__ void __maxnreg__(168)
               aw[4 * q + 3] = w.w;
             }
           }
+          if constexpr (ACT == 5) {
+            // The chunk's 32 columns of this lane's rows of the added tensors, into the bias pairs.
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int64_t ar = t == 0 ? ar0 : ar1;
+              if (ar < 0) continue;
+              const uint4* ap = reinterpret_cast<const uint4*>((t == 0 ? p.add0 : p.add1) + ar * p.n + c32);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint4 w = __ldg(ap + q);
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+                  v[jj][8 * q + 2 * e] += x.x;
+                  v[jj][8 * q + 2 * e + 1] += x.y;
+                }
+              }
+            }
+          }
           uint32_t pk[16], px[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -288,6 +339,11 @@ __global__ void __maxnreg__(168)
               const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[i]));
               a *= gelu_tanh_grad(x.x);
               b *= gelu_tanh_grad(x.y);
+            } else if constexpr (ACT == 5) {
+              if (p.swish) {
+                a = swish(a);
+                b = swish(b);
+              }
             }
             pk[i] = pack_bf16(a, b);
           }

@@ -37,7 +37,7 @@ SYMBOLS = ("fwn_version", "fwn_last_error_string", "fwn_device_error", "fwn_lse_
            "fwn_bitset_words", "fwn_khop_bitset", "fwn_walk_bitset", "fwn_bitset_csr_count", "fwn_bitset_csr_fill",
            "fwn_cond_layernorm", "fwn_cond_layernorm_scatter", "fwn_cond_layernorm_residual",
            "fwn_cond_layernorm_add", "fwn_cond_layernorm_bwd_workspace", "fwn_cond_layernorm_bwd",
-           "fwn_gemm_bf16", "fwn_gemm_bf16_aux", "fwn_gnn_gather_add_act", "fwn_gnn_ln_segment_sum", "fwn_test_attn_fwd_timeout")
+           "fwn_gemm_bf16", "fwn_gemm_bf16_aux", "fwn_gemm_bf16_gather", "fwn_gnn_gather_add_act", "fwn_gnn_ln_segment_sum", "fwn_test_attn_fwd_timeout")
 
 
 class AttnDesc(ctypes.Structure):
@@ -95,6 +95,8 @@ def _declare(lib):
                                  ctypes.c_size_t, _P],
       "fwn_gemm_bf16": [_P, _P, _P, _P, ctypes.c_int64, _I, _I, _I, _P],
       "fwn_gemm_bf16_aux": [_P, _P, _P, _P, _P, ctypes.c_int64, _I, _I, _I, _P],
+      "fwn_gemm_bf16_gather": [_P, _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, ctypes.c_int64, ctypes.c_int64, _I, _I,
+                               _I, _P],
       "fwn_gnn_gather_add_act": [_P, _P, _P, _P, _P, _P, ctypes.c_int64, _I, _I, _P, _P],
       "fwn_gnn_ln_segment_sum": [_P, _P, ctypes.c_int64, _I, _P, _P, ctypes.c_float, ctypes.c_float, _P, _P, _I, _P],
       "fwn_bitset_csr_count": [_P, _I, _I, _P, _P, _SZ, _P],

@@ -12,9 +12,11 @@ the structure with the conventional interaction-network MLPs (one hidden layer, 
     r_i'  = r_i + LN_r(swish(r_i U_r + agg_i U_a + c1) U2 + c2)
     s_j'  = s_j + LN_s(swish(s_j V_s + d1) V2 + d2)                                  (senders: no messages)
 
-Kernels: the matmuls on fwn_gemm_bf16 (this package's tcgen05 GEMM; cuBLAS where a width does not fit its tiles),
-the gather of the pre-gathered projections with the bias and swish in one pass (fwn_gnn_gather_add_act), and the
-message LayerNorm with the sorted segment-sum in one pass, one warp per receiver, no atomics
+Kernels: the matmuls on fwn_gemm_bf16 (this package's tcgen05 GEMM; cuBLAS where a width does not fit its tiles);
+the MLPs' input layers as fwn_gemm_bf16_gather, whose epilogue adds the gathered pre-projected sender / receiver
+rows (edge MLP) or the aggregate's projection (receiver MLP) and the bias, then swish, so that the layer's own
+product never goes to memory (fwn_gnn_gather_add_act does the same adds after a plain GEMM where the widths do not
+fit the tiles); and the message LayerNorm with the sorted segment-sum in one pass, one warp per receiver, no atomics
 (fwn_gnn_ln_segment_sum). Edges are processed in blocks of patch.OPTIONS.edge_chunk (0: all at once): a block's
 receivers are a contiguous id range, and their running sums accumulate in float32. Features [n, F] for one sample
 (the reference's [n, batch, F] is a loop over the batch here), bf16 matmuls with float32 accumulation, float32
@@ -105,6 +107,23 @@ class InteractionNetwork(torch.nn.Module):
       y = torch.nn.functional.gelu(y, approximate="tanh")
     return y
 
+  def _mm_add_act(self, x, w, bias, add0=None, idx0=None, add1=None, idx1=None):
+    """swish(x w + bias + add0[idx0] + add1[idx1]) in bf16: fwn_gemm_bf16_gather (the adds and swish in the GEMM's
+    epilogue, one pass) where the widths fit its tiles; else the GEMM, then fwn_gnn_gather_add_act. idx None: the
+    row itself."""
+    m, k = x.shape
+    n = w.shape[1]
+    if n % 256 == 0 and k % 64 == 0 and m > 0:
+      out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+      ptr = lambda t: t.data_ptr() if t is not None else None
+      rows = lambda t: t.shape[0] if t is not None else 0
+      _lib.check(_lib.lib().fwn_gemm_bf16_gather(
+          x.data_ptr(), self._bf(w, True).data_ptr(), self._bf(bias).data_ptr(), out.data_ptr(), ptr(add0), ptr(idx0),
+          rows(add0), ptr(add1), ptr(idx1), rows(add1), m, n, k, _lib.ACT_SWISH, torch.cuda.current_stream().cuda_stream))
+      return out
+    return self._gather_act(m, n, e_proj=self._mm(x, w), s_proj=add0, snd=idx0, r_proj=add1, rcv=idx1,
+                            bias=self._bf(bias))
+
   def _gather_act(self, rows, h, e_proj=None, s_proj=None, snd=None, r_proj=None, rcv=None, bias=None, act=True):
     out = torch.empty(rows, h, dtype=torch.bfloat16, device=self.b1.device)
     p = lambda t: t.data_ptr() if t is not None else None
@@ -126,9 +145,8 @@ class InteractionNetwork(torch.nn.Module):
   def _node_mlp(self, x32, x16, w_in, b_in, w_out, b_out, ln_g, ln_b, agg16=None, w_agg=None):
     """x + LN(swish(x w_in (+ agg w_agg) + b_in) w_out + b_out), x float32 [n, F] (x16 its bf16 copy)."""
     n = x32.shape[0]
-    hx = self._mm(x16, w_in)
     ha = self._mm(agg16, w_agg) if agg16 is not None else None
-    hid = self._gather_act(n, self.cfg.hidden, e_proj=hx, s_proj=ha, bias=self._bf(b_in))
+    hid = self._mm_add_act(x16, w_in, b_in, add0=ha)
     y = self._mm(hid, w_out, b_out)
     return self._ln_sum(y, None, n, ln_g, ln_b, residual=x32)
 
@@ -174,9 +192,8 @@ class InteractionNetwork(torch.nn.Module):
     for e0, e1, r_lo, r_hi, off in plan:
       if e1 <= e0:
         continue
-      e_proj = self._mm(e16[e0:e1], self.w_e)
-      hid = self._gather_act(e1 - e0, cfg.hidden, e_proj=e_proj, s_proj=s_proj, snd=snd[e0:e1], r_proj=r_proj,
-                             rcv=rcv[e0:e1], bias=self._bf(self.b1))
+      hid = self._mm_add_act(e16[e0:e1], self.w_e, self.b1, add0=s_proj, idx0=snd[e0:e1], add1=r_proj,
+                             idx1=rcv[e0:e1])
       msg = self._mm(hid, self.w2, self.b2)
       if off is None:
         self._ln_sum(msg, seg, nr, self.ln_e_g, self.ln_e_b, norm=norm, out=agg)

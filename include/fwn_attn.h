@@ -105,8 +105,9 @@ FWN_API const char* fwn_version(void);
 /* Description of the last error returned to the calling thread ("" if none). */
 FWN_API const char* fwn_last_error_string(void);
 
-/* Synchronises `stream`, reads and clears the device error word written by bounded waits.
- * *code receives 0 or FWN_ERR_DEVICE_TIMEOUT. */
+/* Synchronises `stream`, reads and clears the device error word written by bounded waits (and by
+ * fwn_gemm_bf16_gather on an index out of range). *code receives 0, FWN_ERR_DEVICE_TIMEOUT, or FWN_ERR_INVALID_ARGUMENT
+ * for such an index. */
 FWN_API fwn_status fwn_device_error(void* stream, int32_t* code);
 
 /* Rows of the lse buffer per (batch, head): n rounded up to a multiple of 128. */
@@ -256,6 +257,18 @@ FWN_API fwn_status fwn_gemm_bf16(const void* a, const void* bt, const void* bias
  * aux. */
 FWN_API fwn_status fwn_gemm_bf16_aux(const void* a, const void* bt, const void* bias, void* c, void* aux, int64_t m,
                                      int32_t n, int32_t k, int32_t act, void* stream);
+
+/* The interaction network's MLP input layers (src/faster_weathernext/patch.py:347-509: the edge MLP over (edge, sender,
+ * receiver) features with the pre-gather projections, pre_gather_{senders,receivers,edges}_for_edges_fn; the node MLP
+ * over (node, aggregate)): the same GEMM with rows of two more tensors added before the activation,
+ *   c[i, :] = act(a[i, :] bt^T + bias + add0[idx0[i], :] + add1[idx1[i], :]),
+ * add0 / add1 bf16 [rows0 / rows1, n] row-major (either may be NULL), idx0 / idx1 int32 [m] (NULL: row i itself, which
+ * then needs rows >= m); act FWN_ACT_NONE or FWN_ACT_SWISH (x sigmoid(x)). One pass instead of the GEMM's output
+ * written and read back by a separate gather-add. An index outside [0, rows) adds nothing to its row and is reported by
+ * fwn_device_error as FWN_ERR_INVALID_ARGUMENT. */
+FWN_API fwn_status fwn_gemm_bf16_gather(const void* a, const void* bt, const void* bias, void* c, const void* add0,
+                                        const int32_t* idx0, int64_t rows0, const void* add1, const int32_t* idx1,
+                                        int64_t rows1, int64_t m, int32_t n, int32_t k, int32_t act, void* stream);
 
 /* ---- grid <-> mesh interaction networks -------------------------------------------------------------------
  * The blocked GNNs of the encoder / decoder (src/faster_weathernext/patch.py:347-509, ChunkedDeepGNN: edge MLP on

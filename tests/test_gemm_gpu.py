@@ -124,3 +124,43 @@ def test_gelu_mlp_function_matches_torch_autograd(cuda):
   for x, y in zip(pa, pb):
     assert x.grad.dtype == torch.float32
     assert _rel(x.grad, y.grad.double()) <= 1e-2
+
+
+@pytest.mark.parametrize("m,n,k,idx", [(3001, 512, 512, True), (40_962 + 77, 256, 512, False)])
+def test_gemm_gather_add_swish(cuda, m, n, k, idx):
+  """fwn_gemm_bf16_gather: c = swish(a bt^T + bias + add0[idx0] + add1[idx1]) against float64 on the same bf16
+  operands (rel RMS <= 5e-3), gathered indices (the interaction network's edge MLP) or the rows themselves (its node
+  MLP); an index out of range is reported as FWN_ERR_INVALID_ARGUMENT by fwn_device_error, in bounds."""
+  from faster_weathernext import _lib
+  lib = _lib.lib()
+  g = torch.Generator(device=cuda).manual_seed(m)
+  a = torch.randn(m, k, device=cuda, generator=g).to(torch.bfloat16)
+  bt = (torch.randn(n, k, device=cuda, generator=g) * k ** -0.5).to(torch.bfloat16)
+  b = (torch.randn(n, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+  r0, r1 = (97, 2 * m) if idx else (m, m)
+  add0 = torch.randn(r0, n, device=cuda, generator=g).to(torch.bfloat16)
+  add1 = torch.randn(r1, n, device=cuda, generator=g).to(torch.bfloat16)
+  i0 = torch.randint(0, r0, (m,), device=cuda, generator=g, dtype=torch.int32) if idx else None
+  i1 = torch.randint(0, r1, (m,), device=cuda, generator=g, dtype=torch.int32) if idx else None
+  c = torch.full((m, n), float("nan"), device=cuda, dtype=torch.bfloat16)
+  st = torch.cuda.current_stream().cuda_stream
+  ptr = lambda t: t.data_ptr() if t is not None else None
+  _lib.check(lib.fwn_gemm_bf16_gather(a.data_ptr(), bt.data_ptr(), b.data_ptr(), c.data_ptr(), add0.data_ptr(), ptr(i0),
+                                      r0, add1.data_ptr(), ptr(i1), r1, m, n, k, _lib.ACT_SWISH, st))
+  torch.cuda.synchronize()
+  assert _lib.device_error() == 0
+  g0 = add0.double()[i0.long()] if idx else add0.double()
+  g1 = add1.double()[i1.long()] if idx else add1.double()
+  x = _ref(a, bt, b, 0) + g0 + g1
+  assert _rel(c, x * torch.sigmoid(x)) <= 5e-3
+  if idx:
+    bad = i0.clone()
+    bad[m // 2] = r0                                  # one past the last row
+    _lib.check(lib.fwn_gemm_bf16_gather(a.data_ptr(), bt.data_ptr(), b.data_ptr(), c.data_ptr(), add0.data_ptr(),
+                                        bad.data_ptr(), r0, add1.data_ptr(), i1.data_ptr(), r1, m, n, k, _lib.ACT_SWISH,
+                                        st))
+    code = ctypes.c_int32(0)
+    _lib.check(lib.fwn_device_error(st, ctypes.byref(code)))
+    assert code.value == _lib.FWN_ERR_INVALID_ARGUMENT
+  assert lib.fwn_gemm_bf16_gather(a.data_ptr(), bt.data_ptr(), b.data_ptr(), c.data_ptr(), add0.data_ptr(), None,
+                                  m - 1, None, None, 0, m, n, k, _lib.ACT_SWISH, st) == _lib.FWN_ERR_INVALID_ARGUMENT
