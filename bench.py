@@ -39,8 +39,8 @@ CFG = 3
 USEFUL_PER_PAIR = 14
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of each workload on the
 # current kernels (summaries under profiles/): configuration 3 bf16 and the WN2 shape bf16.
-NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 149_179_648, "attn_bwd_dq": 202_269_440,
-                                                   "attn_bwd_dkv": 226_809_088},
+NCU_TRAFFIC = {("attention", "bf16", "gathered"): {"attn_fwd": 151_399_936, "attn_bwd_dq": 198_163_712,
+                                                   "attn_bwd_dkv": 228_230_400},
                ("wn2", "bf16", "paired"): {"attn_fwd": 372_274_688, "attn_bwd_dq": 469_790_720,
                                            "attn_bwd_dkv": 537_186_560}}
 
