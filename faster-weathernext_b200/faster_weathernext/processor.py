@@ -316,7 +316,7 @@ class Processor(torch.nn.Module):
       xs, h = _CondNorm.apply(xs, pending, so1, n, bf)
     a = self._mha(h.view(b, n, d), blk.w_qkv.to(bf), blk.w_out.to(bf), tiles).reshape(b * n, d)
     xs, h = _CondNorm.apply(xs, a, so2, n, bf)
-    if blk.w1.shape[1] % 256 == 0 and d % 64 == 0:
+    if blk.w1.shape[1] % 256 == 0 and d % 64 == 0 and h.shape[0] > 0:
       return xs, _GeluMLP.apply(h, blk.w1, blk.b1, blk.w2, blk.b2)
     mlp = F.gelu(torch.addmm(blk.b1.to(bf), h, blk.w1.to(bf)), approximate="tanh")
     return xs, torch.addmm(blk.b2.to(bf), mlp, blk.w2.to(bf))
