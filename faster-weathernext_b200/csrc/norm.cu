@@ -155,44 +155,48 @@ __global__ void __launch_bounds__(256) cond_layernorm_bwd_kernel(const float* __
     ds[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     dof[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  // A row's loads (x, dy, the incoming gradient) are all issued before any of its stores: dx may be dx_in, and the
+  // compiler may not move a load across a store that can alias it, which otherwise serialises the row's memory round
+  // trips. xhat and g are recomputed in the last loop instead of kept, to stay within two CTAs' registers per SM.
   for (int64_t row = r0 + warp; row < r1; row += 8) {
-    float4 v[V], d[V];
-    float s1 = 0.f;
+    float4 v[V], d[V], a[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       v[i] = __ldg(reinterpret_cast<const float4*>(x + row * D) + lane + 32 * i);
-      s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
       if constexpr (DY_BF16) {
         const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(dy) + row * D) + lane + 32 * i);
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-        d[i] = make_float4(a.x, a.y, b.x, b.y);
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        d[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
       } else {
         d[i] = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(dy) + row * D) + lane + 32 * i);
       }
+      a[i] = dx_in ? reinterpret_cast<const float4*>(dx_in + row * D)[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     const float mean = s1 * (1.f / D);
     float s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
-      s2 += (a * a + b * b) + (c * c + e * e);
+      v[i] = make_float4(v[i].x - mean, v[i].y - mean, v[i].z - mean, v[i].w - mean);  // centred from here on
+      s2 += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
     const float rstd = rsqrtf(s2 * (1.f / D) + eps);
     float sg = 0.f, sgx = 0.f;
-    float4 xh[V], g[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      xh[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
-      g[i] = make_float4(d[i].x * (1.f + sc[i].x), d[i].y * (1.f + sc[i].y), d[i].z * (1.f + sc[i].z),
-                         d[i].w * (1.f + sc[i].w));
-      sg += (g[i].x + g[i].y) + (g[i].z + g[i].w);
-      sgx += (g[i].x * xh[i].x + g[i].y * xh[i].y) + (g[i].z * xh[i].z + g[i].w * xh[i].w);
-      ds[i].x += d[i].x * xh[i].x; ds[i].y += d[i].y * xh[i].y; ds[i].z += d[i].z * xh[i].z; ds[i].w += d[i].w * xh[i].w;
+      const float4 xh = make_float4(v[i].x * rstd, v[i].y * rstd, v[i].z * rstd, v[i].w * rstd);
+      const float4 g = make_float4(d[i].x * (1.f + sc[i].x), d[i].y * (1.f + sc[i].y), d[i].z * (1.f + sc[i].z),
+                                   d[i].w * (1.f + sc[i].w));
+      sg += (g.x + g.y) + (g.z + g.w);
+      sgx += (g.x * xh.x + g.y * xh.y) + (g.z * xh.z + g.w * xh.w);
+      ds[i].x += d[i].x * xh.x; ds[i].y += d[i].y * xh.y; ds[i].z += d[i].z * xh.z; ds[i].w += d[i].w * xh.w;
       dof[i].x += d[i].x; dof[i].y += d[i].y; dof[i].z += d[i].z; dof[i].w += d[i].w;
     }
 #pragma unroll
@@ -203,12 +207,12 @@ __global__ void __launch_bounds__(256) cond_layernorm_bwd_kernel(const float* __
     const float mg = sg * (1.f / D), mgx = sgx * (1.f / D);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float4 r = make_float4(rstd * (g[i].x - mg - xh[i].x * mgx), rstd * (g[i].y - mg - xh[i].y * mgx),
-                             rstd * (g[i].z - mg - xh[i].z * mgx), rstd * (g[i].w - mg - xh[i].w * mgx));
-      if (dx_in) {
-        const float4 a = reinterpret_cast<const float4*>(dx_in + row * D)[lane + 32 * i];  // may be dx
-        r.x += a.x; r.y += a.y; r.z += a.z; r.w += a.w;
-      }
+      const float4 xh = make_float4(v[i].x * rstd, v[i].y * rstd, v[i].z * rstd, v[i].w * rstd);
+      const float4 g = make_float4(d[i].x * (1.f + sc[i].x), d[i].y * (1.f + sc[i].y), d[i].z * (1.f + sc[i].z),
+                                   d[i].w * (1.f + sc[i].w));
+      float4 r = make_float4(rstd * (g.x - mg - xh.x * mgx), rstd * (g.y - mg - xh.y * mgx),
+                             rstd * (g.z - mg - xh.z * mgx), rstd * (g.w - mg - xh.w * mgx));
+      r.x += a[i].x; r.y += a[i].y; r.z += a[i].z; r.w += a[i].w;
       reinterpret_cast<float4*>(dx + row * D)[lane + 32 * i] = r;
       if (dx_bf16) {
         const __nv_bfloat162 lo = __floats2bfloat162_rn(r.x, r.y), hi = __floats2bfloat162_rn(r.z, r.w);
