@@ -142,6 +142,16 @@ __global__ void __launch_bounds__(256) ln_segment_sum_kernel(const __nv_bfloat16
       for (int k = 0; k < 8; ++k) sum[q][k] += (v[q][k] - mean) * rstd * g[q][k] + bt[q][k];
     }
   }
+  // The residual rows before any store (residual may be out itself: a load may not pass a store that can alias it).
+  float4 res[G][2];
+  if (residual) {
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+      const float4* rp = reinterpret_cast<const float4*>(residual + i * F + (q * 32 + lane) * 8);
+      res[q][0] = rp[0];
+      res[q][1] = rp[1];
+    }
+  }
 #pragma unroll
   for (int q = 0; q < G; ++q) {
     const int c = (q * 32 + lane) * 8;
@@ -149,8 +159,7 @@ __global__ void __launch_bounds__(256) ln_segment_sum_kernel(const __nv_bfloat16
 #pragma unroll
     for (int k = 0; k < 8; ++k) r[k] = sum[q][k] * norm;
     if (residual) {
-      const float4 a = reinterpret_cast<const float4*>(residual + i * F + c)[0];
-      const float4 b = reinterpret_cast<const float4*>(residual + i * F + c)[1];
+      const float4 a = res[q][0], b = res[q][1];
       r[0] += a.x; r[1] += a.y; r[2] += a.z; r[3] += a.w;
       r[4] += b.x; r[5] += b.y; r[6] += b.z; r[7] += b.w;
     }
