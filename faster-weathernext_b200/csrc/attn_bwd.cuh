@@ -185,6 +185,8 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ o, 
   constexpr int ES = F32 ? 4 : 2;
   constexpr int LPR = D * ES / 16;          // lanes per row
   constexpr int RPW = 32 / LPR;             // rows per warp
+  grid_dependency_wait();  // o comes from the forward (launched with programmatic serialization)
+  allow_dependents();
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int row_id = gwarp * RPW + lane / LPR, part = lane % LPR;
   float acc = 0.f;
@@ -312,6 +314,9 @@ __global__ void __launch_bounds__(BwdCfg<KIND, D, F32, CH, X3>::THREADS) __maxnr
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int per_bh = p.np;
+  // Launched with programmatic serialization after the delta pass: its prologue above (barriers, TMEM, descriptor
+  // prefetch) may overlap the delta pass; nothing the earlier kernels wrote is read before this.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (whole warp)

@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(FwdCfg<D, F32, X3>::THREADS) __maxnreg__((FwdC
   const uint32_t tmem = *tmem_holder;
 
   const int per_bh = p.np;
+  allow_dependents();  // the delta pass may be scheduled now; it waits for this grid before reading o
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (whole warp)
     // Tile metadata is prefetched two chunks ahead, and the next item's list range one item ahead.

@@ -306,6 +306,12 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
+// Programmatic dependent launch (griddepcontrol): a kernel launched with programmatic stream serialization may start
+// while the kernel before it in the stream is finishing; grid_dependency_wait() returns once that kernel has completed
+// and its memory operations are visible (a no-op for a normal launch). allow_dependents() lets the next such launch
+// begin its prologue early; it never lets it read this kernel's results before they are complete.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Registers written by tcgen05.ld are valid only after tcgen05.wait::ld; this empty asm makes every later use
 // depend on a point after the wait, so that the compiler cannot move a use above it.

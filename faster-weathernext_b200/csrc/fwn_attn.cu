@@ -441,8 +441,20 @@ fwn_status launch_bwd_pass(const fwn_attn_desc& d, const void* q, const void* k,
   auto kernel = fwn::attn_bwd_kernel<KIND, D, F32, CH, GATHER, X3>;
   int grid = 0;
   if ((s = persistent_grid(kernel, C::THREADS, C::SMEM_BYTES, C::TMEM_COLS, p.n_items, &grid)) != FWN_OK) return s;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(r0, r1, c0, c1, c0mn, c1mn, c0r, c1r, c0mnr, c1mnr, p);
-  cudaError_t e = cudaGetLastError();
+  // Programmatic serialization: the launch and prologue may overlap the end of the kernel before it in the stream
+  // (the delta pass); the kernel waits for that kernel (griddepcontrol.wait) before its first dependent read.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, r0, r1, c0, c1, c0mn, c1mn, c0r, c1r, c0mnr, c1mnr, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   static const char* const kNames[] = {"attn_bwd dq launch", "attn_bwd dkv launch", "attn_bwd dv launch",
                                        "attn_bwd dk launch"};
   if (e != cudaSuccess) return cuda_fail(e, kNames[KIND]);
@@ -525,9 +537,19 @@ fwn_status launch_delta(const fwn_attn_desc& d, const void* o, const void* d_o, 
   const int total = d.batch * d.heads * lse_rows;
   constexpr int rows_per_warp = 32 / (D * (F32 ? 4 : 2) / 16);
   const int warps = (total + rows_per_warp - 1) / rows_per_warp;
-  fwn::delta_kernel<F32, D><<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
-      o, d_o, delta, d.heads, d.n, lse_rows, d.out_stride_b, d.out_stride_n, d.out_stride_h, total);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((warps * 32 + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap the launch with the forward's tail
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fwn::delta_kernel<F32, D>, o, d_o, delta, static_cast<int>(d.heads),
+                                     static_cast<int>(d.n), lse_rows, static_cast<int64_t>(d.out_stride_b),
+                                     static_cast<int64_t>(d.out_stride_n), static_cast<int64_t>(d.out_stride_h), total);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "delta launch");
   return FWN_OK;
 }
